@@ -1,0 +1,567 @@
+// Grouped (per-expert) GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// One persistent, warp-specialised kernel template covers every expert GEMM of the
+// MoE layer, forward and backward:
+//
+//   mode        A (rows x K)            B                         D
+//   fwd         X_perm  K-major         W[e] [N,K] K-major        [rows, N]   ragged M
+//   dgrad       dY_perm K-major         W[e] [K,N] MN-major       [rows, N]   ragged M
+//   wgrad       dY^T    MN-major        Z^T      MN-major         [G, M, N]   ragged K
+//
+// Ragged dimension = rows of each expert group, taken from device-side offsets
+// (`group_off`, 64-row aligned, zero-filled padding) so that no host sync is needed.
+//
+// Warp roles (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer (one elected lane): A/B tiles, 128B swizzle, STAGES deep.
+//   warp 1      TMEM allocator + MMA issuer (one lane): tcgen05.mma M=128, N=BN, K=16.
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, fused SwiGLU fwd/bwd,
+//               bf16/fp32 stores. Two TMEM accumulators so the epilogue of tile i
+//               overlaps the MMAs of tile i+1.
+//
+// All pipeline waits are bounded (see sm100.cuh); a timeout aborts the CTA cleanly and
+// leaves an error code in `status`.
+//
+// Reference parity: the reference runs experts through a user callback
+// (`expert(rows, expert_ids)`, src/rbd.py:485) and, in its model path, DeepSpeed's
+// grouped_mm (configs/qwen_ep8.json:7). This kernel is that expert computation.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include "sm100.cuh"
+#include "grouped_gemm.h"
+
+namespace sepx {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
+  static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
+  static constexpr int PREFIX_OFF = MISC_OFF + 16;
+  static size_t bytes(int G) { return 1024 + PREFIX_OFF + 4 * (size_t)(G + 1); }
+};
+
+struct TileInfo {
+  int g;        // group
+  int row0;     // ragged-M: first row of the tile; ragged-K: m0
+  int row_end;  // ragged-M: end of the group's rows
+  int n0;       // first output column (in units of accumulator columns)
+  int k0;       // ragged-K: first reduction row of the group
+  int num_kb;   // k-blocks
+};
+
+template <bool RAGGED_K, int BN>
+__device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, const int* s_prefix) {
+  TileInfo ti;
+  if (!RAGGED_K) {
+    // binary search: largest g with prefix[g] <= t
+    int lo = 0, hi = p.G;  // prefix[G] = total > t
+    while (hi - lo > 1) {
+      int mid = (lo + hi) >> 1;
+      if (s_prefix[mid] <= t) lo = mid; else hi = mid;
+    }
+    int g = lo;
+    int local = t - s_prefix[g];
+    int m_tile = local / p.n_tiles;
+    int n_tile = local - m_tile * p.n_tiles;
+    int off0 = __ldg(p.group_off + g);
+    ti.g = g;
+    ti.row0 = off0 + m_tile * kBM;
+    ti.row_end = __ldg(p.group_off + g + 1);
+    ti.n0 = n_tile * BN;
+    ti.k0 = 0;
+    ti.num_kb = p.K / kBK;
+  } else {
+    int m_tiles = p.M / kBM;
+    int per_group = m_tiles * p.n_tiles;
+    int g = t / per_group;
+    int local = t - g * per_group;
+    int m_tile = local / p.n_tiles;
+    int n_tile = local - m_tile * p.n_tiles;
+    int off0 = __ldg(p.group_off + g);
+    int off1 = __ldg(p.group_off + g + 1);
+    ti.g = g;
+    ti.row0 = m_tile * kBM;
+    ti.row_end = p.M;
+    ti.n0 = n_tile * BN;
+    ti.k0 = off0;
+    ti.num_kb = (off1 - off0) / kBK;
+  }
+  return ti;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+  int* s_prefix = reinterpret_cast<int*>(smem + L::PREFIX_OFF);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- tile prefix (ragged M): tiles of group g = ceil(rows_g / BM) * n_tiles ----
+  int total_tiles;
+  if (!RAGGED_K) {
+    if (threadIdx.x == 0) {
+      int acc = 0;
+      for (int g = 0; g < p.G; ++g) {
+        s_prefix[g] = acc;
+        int rows = __ldg(p.group_off + g + 1) - __ldg(p.group_off + g);
+        acc += ((rows + kBM - 1) / kBM) * p.n_tiles;
+      }
+      s_prefix[p.G] = acc;
+    }
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (!RAGGED_K) {
+    total_tiles = s_prefix[p.G];
+  } else {
+    total_tiles = p.G * (p.M / kBM) * p.n_tiles;
+  }
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer -------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        TileInfo ti = decode_tile<RAGGED_K, BN>(t, p, s_prefix);
+        for (int kb = 0; kb < ti.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, s_abort, p.status, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * L::STAGE_BYTES;
+          uint8_t* sB = sA + L::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], L::STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_2d(sA, &tmA, &full_bar[stage], kb * kBK, ti.row0);
+          } else {
+            // A[m, k] stored as [k rows, m contiguous]: two 64-wide MN chunks
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j)
+              tma_load_2d(sA + j * 8192, &tmA, &full_bar[stage], ti.row0 + j * 64,
+                          ti.k0 + kb * kBK);
+          }
+          if (!B_MN) {
+            if (EPI == kEpiSwigluFwd) {
+              // gate rows [i0, i0+128) and up rows [I + i0, ...) of expert g
+              const int i0 = ti.n0 / 2;
+              const int base = ti.g * p.b_rows_per_group;
+              tma_load_2d(sB, &tmB, &full_bar[stage], kb * kBK, base + i0);
+              tma_load_2d(sB + 128 * 128, &tmB, &full_bar[stage], kb * kBK, base + p.I + i0);
+            } else {
+              const int base = ti.g * p.b_rows_per_group + ti.n0;
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j)
+                tma_load_2d(sB + j * 128 * 128, &tmB, &full_bar[stage], kb * kBK, base + j * 128);
+            }
+          } else {
+            const int krow = RAGGED_K ? (ti.k0 + kb * kBK) : (ti.g * p.b_rows_per_group + kb * kBK);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + j * 8192, &tmB, &full_bar[stage], ti.n0 + j * 64, krow);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer --------------------------------
+    constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      TileInfo ti = decode_tile<RAGGED_K, BN>(t, p, s_prefix);
+      if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1, s_abort, p.status, p.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < ti.num_kb; ++kb) {
+        if (!mbar_wait_bounded(&full_bar[stage], phase, s_abort, p.status, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            uint64_t adesc, bdesc;
+            if (!A_MN) adesc = make_smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            else adesc = make_smem_desc_sw128(a_addr + kk * 2048, 8192, 1024);
+            if (!B_MN) bdesc = make_smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+            else bdesc = make_smem_desc_sw128(b_addr + kk * 2048, 8192, 1024);
+            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&tfull_bar[acc]);
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  } else {
+    // --------------------------------- epilogue --------------------------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      TileInfo ti = decode_tile<RAGGED_K, BN>(t, p, s_prefix);
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, s_abort, p.status, p.timeout_ns)) break;
+      tc_fence_after();
+      const int r = ti.row0 + q * 32 + lane;
+      const bool valid = r < ti.row_end;
+      const uint32_t t_row = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
+      const bool zero = ti.num_kb == 0;
+
+      if (EPI == kEpiBf16) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(t_row + c * 32, v);
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(out + (size_t)r * p.ldo + ti.n0 + c * 32);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 w;
+              w.x = pack_bf16x2(zero ? 0.f : v[8 * j + 0], zero ? 0.f : v[8 * j + 1]);
+              w.y = pack_bf16x2(zero ? 0.f : v[8 * j + 2], zero ? 0.f : v[8 * j + 3]);
+              w.z = pack_bf16x2(zero ? 0.f : v[8 * j + 4], zero ? 0.f : v[8 * j + 5]);
+              w.w = pack_bf16x2(zero ? 0.f : v[8 * j + 6], zero ? 0.f : v[8 * j + 7]);
+              dst[j] = w;
+            }
+          }
+        }
+      } else if (EPI == kEpiF32) {
+        float* out = reinterpret_cast<float*>(p.out);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(t_row + c * 32, v);
+          if (valid) {
+            float4* dst = reinterpret_cast<float4*>(
+                out + ((size_t)ti.g * p.M + r) * p.ldo + ti.n0 + c * 32);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 w;
+              w.x = zero ? 0.f : v[4 * j + 0];
+              w.y = zero ? 0.f : v[4 * j + 1];
+              w.z = zero ? 0.f : v[4 * j + 2];
+              w.w = zero ? 0.f : v[4 * j + 3];
+              dst[j] = w;
+            }
+          }
+        }
+      } else if (EPI == kEpiSwigluFwd) {
+        // accumulator columns [0,128) = gate, [128,256) = up, for I-range [i0, i0+128)
+        const int i0 = ti.n0 / 2;
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out);
+        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.aux);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float g[32], u[32];
+          tmem_ld32(t_row + c * 32, g);
+          tmem_ld32(t_row + 128 + c * 32, u);
+          if (valid) {
+            uint4* dh = reinterpret_cast<uint4*>(h + (size_t)r * p.ldo + i0 + c * 32);
+            uint4* dg = reinterpret_cast<uint4*>(gu + (size_t)r * p.ld_aux + i0 + c * 32);
+            uint4* du = reinterpret_cast<uint4*>(gu + (size_t)r * p.ld_aux + p.I + i0 + c * 32);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float gg[8], uu[8], hh[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                // round g/u to bf16 first so h is consistent with the stored pre-activation
+                gg[e] = __bfloat162float(__float2bfloat16(g[8 * j + e]));
+                uu[e] = __bfloat162float(__float2bfloat16(u[8 * j + e]));
+                hh[e] = silu_f(gg[e]) * uu[e];
+              }
+              dg[j] = make_uint4(pack_bf16x2(gg[0], gg[1]), pack_bf16x2(gg[2], gg[3]),
+                                 pack_bf16x2(gg[4], gg[5]), pack_bf16x2(gg[6], gg[7]));
+              du[j] = make_uint4(pack_bf16x2(uu[0], uu[1]), pack_bf16x2(uu[2], uu[3]),
+                                 pack_bf16x2(uu[4], uu[5]), pack_bf16x2(uu[6], uu[7]));
+              dh[j] = make_uint4(pack_bf16x2(hh[0], hh[1]), pack_bf16x2(hh[2], hh[3]),
+                                 pack_bf16x2(hh[4], hh[5]), pack_bf16x2(hh[6], hh[7]));
+            }
+          }
+        }
+      } else if (EPI == kEpiSwigluBwd) {
+        // accumulator = dh_unweighted[r, i0 : i0+BN]; gate weight w = row_w[r]
+        const int i0 = ti.n0;
+        const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux);
+        __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(p.out);
+        __nv_bfloat16* hw = reinterpret_cast<__nv_bfloat16*>(p.aux2);
+        const float w = valid ? __ldg(p.row_w + r) : 0.f;
+        float dw_part = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float d[32];
+          tmem_ld32(t_row + c * 32, d);
+          if (valid) {
+            const uint4* sg = reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + i0 + c * 32);
+            const uint4* su =
+                reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + p.I + i0 + c * 32);
+            uint4* og = reinterpret_cast<uint4*>(dgu + (size_t)r * p.ldo + i0 + c * 32);
+            uint4* ou = reinterpret_cast<uint4*>(dgu + (size_t)r * p.ldo + p.I + i0 + c * 32);
+            uint4* oh = reinterpret_cast<uint4*>(hw + (size_t)r * p.ld_aux2 + i0 + c * 32);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 gv = sg[j], uv = su[j];
+              uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+              uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+              uint32_t rg[4], ru[4], rh[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 g2 = unpack_bf16x2(gw[e]);
+                float2 u2 = unpack_bf16x2(uw[e]);
+                float dd0 = d[8 * j + 2 * e], dd1 = d[8 * j + 2 * e + 1];
+                float s0 = 1.f / (1.f + __expf(-g2.x)), s1 = 1.f / (1.f + __expf(-g2.y));
+                float si0 = g2.x * s0, si1 = g2.y * s1;
+                float h0 = si0 * u2.x, h1 = si1 * u2.y;
+                dw_part += dd0 * h0 + dd1 * h1;
+                float wd0 = w * dd0, wd1 = w * dd1;
+                float dg0 = wd0 * u2.x * s0 * (1.f + g2.x * (1.f - s0));
+                float dg1 = wd1 * u2.y * s1 * (1.f + g2.y * (1.f - s1));
+                rg[e] = pack_bf16x2(dg0, dg1);
+                ru[e] = pack_bf16x2(wd0 * si0, wd1 * si1);
+                rh[e] = pack_bf16x2(w * h0, w * h1);
+              }
+              og[j] = make_uint4(rg[0], rg[1], rg[2], rg[3]);
+              ou[j] = make_uint4(ru[0], ru[1], ru[2], ru[3]);
+              oh[j] = make_uint4(rh[0], rh[1], rh[2], rh[3]);
+            }
+          }
+        }
+        if (valid && p.row_dw) atomicAdd(p.row_dw + r, dw_part);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    if (*s_abort) {
+      // drain: wait (bounded) for any MMA this thread issued before releasing TMEM
+      if (lane == 0) umma_commit(drain_bar);
+      __syncwarp();
+      uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain_bar, 0) && globaltimer_ns() - t0 < p.timeout_ns) {
+      }
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// =====================================================================================
+// Host side
+// =====================================================================================
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with a {64, box_rows} box and
+// 128-byte swizzle. `cols` is the contiguous dimension.
+static CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t ld_elems,
+                                  int box_rows) {
+  CUtensorMap tm;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld_elems * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld_elems * 2) & 15))
+    throw std::runtime_error("TMA operand must be 16-byte aligned with 16-byte row stride");
+  CUresult r = get_encode_fn()(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return tm;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                   int max_tiles, cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, RAGGED_K, EPI>;
+  size_t smem = L::bytes(p.G);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    configured = true;
+  }
+  int grid = num_sms();
+  if (max_tiles > 0 && max_tiles < grid) grid = max_tiles;
+  if (grid < 1) grid = 1;
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("grouped_gemm launch: ") + cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------------
+// Forward / dgrad: D[rows, N] = A[rows, K] . B_g   (ragged M)
+//   b_kmajor: B stored [G * N_b, K] (weights as [out, in]);  else B stored [G * K, N].
+// ---------------------------------------------------------------------------------
+void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream) {
+  GemmParams p = c.p;
+  if (p.K % kBK) throw std::runtime_error("K must be a multiple of 64");
+  CUtensorMap ta = make_tmap_bf16(c.A, c.a_rows, p.K, c.lda, 128);
+  // upper bound on tiles, used only to size the grid
+  int max_tiles = 0;
+  if (c.epi == kEpiSwigluFwd) {
+    if (!c.b_kmajor) throw std::runtime_error("swiglu fwd expects K-major weights");
+    if (p.I % 128) throw std::runtime_error("SwiGLU intermediate must be a multiple of 128");
+    p.n_tiles = p.I / 128;
+    max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
+    CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
+    launch<256, 4, false, false, false, kEpiSwigluFwd>(ta, tb, p, max_tiles, stream);
+    return;
+  }
+  if (c.epi == kEpiSwigluBwd) {
+    if (c.b_kmajor) throw std::runtime_error("swiglu bwd expects MN-major weights");
+    if (p.N % 256) throw std::runtime_error("N must be a multiple of 256");
+    p.n_tiles = p.N / 256;
+    max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
+    CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
+    launch<256, 4, false, true, false, kEpiSwigluBwd>(ta, tb, p, max_tiles, stream);
+    return;
+  }
+  if (c.epi != kEpiBf16) throw std::runtime_error("unsupported epilogue for ragged-M GEMM");
+  if (p.N % 256 == 0) {
+    p.n_tiles = p.N / 256;
+    max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
+    if (c.b_kmajor) {
+      CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
+      launch<256, 4, false, false, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
+    } else {
+      CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
+      launch<256, 4, false, true, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
+    }
+  } else if (p.N % 128 == 0) {
+    p.n_tiles = p.N / 128;
+    max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
+    if (c.b_kmajor) {
+      CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
+      launch<128, 6, false, false, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
+    } else {
+      CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
+      launch<128, 6, false, true, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
+    }
+  } else {
+    throw std::runtime_error("N must be a multiple of 128");
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Weight gradient: D[g][M, N] = sum_{r in group g} A[r, m] * B[r, n]   (ragged K)
+//   A stored [rows, M], B stored [rows, N] (both row-major, so MN-major operands).
+// ---------------------------------------------------------------------------------
+void grouped_gemm_ragged_k(const GemmCall& c, cudaStream_t stream) {
+  GemmParams p = c.p;
+  if (p.M % 128) throw std::runtime_error("M must be a multiple of 128");
+  CUtensorMap ta = make_tmap_bf16(c.A, c.a_rows, p.M, c.lda, 64);
+  CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
+  if (p.N % 256 == 0) {
+    p.n_tiles = p.N / 256;
+    int max_tiles = p.G * (p.M / 128) * p.n_tiles;
+    launch<256, 4, true, true, true, kEpiF32>(ta, tb, p, max_tiles, stream);
+  } else if (p.N % 128 == 0) {
+    p.n_tiles = p.N / 128;
+    int max_tiles = p.G * (p.M / 128) * p.n_tiles;
+    launch<128, 6, true, true, true, kEpiF32>(ta, tb, p, max_tiles, stream);
+  } else {
+    throw std::runtime_error("N must be a multiple of 128");
+  }
+}
+
+}  // namespace sepx
