@@ -1,0 +1,721 @@
+// Memory-bound hot ops of the Qwen3-MoE block, written for sm_100a:
+//   RMSNorm fwd/bwd, fused per-head q/k RMSNorm + RoPE fwd/bwd, SwiGLU fwd/bwd,
+//   router softmax/top-k/renorm fwd/bwd, fused AdamW (fp32 or block-wise 8-bit state),
+//   fused cross-entropy (loss + dlogits in one pass pair).
+// All use 16-byte vector accesses and fp32 math; transcendental functions are CUDA's
+// own intrinsics (__expf, rsqrtf, __logf).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "elementwise.h"
+#include "sm100.cuh"
+
+namespace sepx {
+
+static void check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  uint4 v = *reinterpret_cast<const uint4*>(p);
+  float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 v;
+  v.x = pack_bf16x2(f[0], f[1]);
+  v.y = pack_bf16x2(f[2], f[3]);
+  v.z = pack_bf16x2(f[4], f[5]);
+  v.w = pack_bf16x2(f[6], f[7]);
+  *reinterpret_cast<uint4*>(p) = v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffff, v, o));
+  return v;
+}
+
+// =====================================================================================
+// RMSNorm: y = w * x * rsqrt(mean(x^2) + eps). One warp per row; D % 256 == 0, D <= 8192.
+// =====================================================================================
+template <int VPL>  // 8-element vectors per lane
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ w,
+                                                          __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
+                                                          int N, int D, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= N) return;
+  float v[VPL][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    load8(x + (size_t)row * D + (i * 32 + lane) * 8, v[i]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / D + eps);
+  if (lane == 0) rstd[row] = r;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    float wv[8], o[8];
+    load8(w + (i * 32 + lane) * 8, wv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = v[i][e] * r * wv[e];
+    store8(y + (size_t)row * D + (i * 32 + lane) * 8, o);
+  }
+}
+
+// dx = r * (w*dy - xhat * mean(xhat * w*dy)); dw += sum_rows dy * xhat (fp32, per-block
+// reduction in shared memory then one atomicAdd per element per block).
+template <int VPL>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ w,
+                                                          const float* __restrict__ rstd,
+                                                          const __nv_bfloat16* __restrict__ dy,
+                                                          __nv_bfloat16* __restrict__ dx, float* __restrict__ dw,
+                                                          int N, int D) {
+  extern __shared__ float s_dw[];  // [D]
+  for (int i = threadIdx.x; i < D; i += blockDim.x) s_dw[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  float acc[VPL][8];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+  for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < N; row += nw) {
+    const float r = rstd[row];
+    float xv[VPL][8], g[VPL][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      float wv[8];
+      load8(x + (size_t)row * D + (i * 32 + lane) * 8, xv[i]);
+      load8(dy + (size_t)row * D + (i * 32 + lane) * 8, g[i]);
+      load8(w + (i * 32 + lane) * 8, wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xh = xv[i][e] * r;
+        acc[i][e] += g[i][e] * xh;
+        g[i][e] *= wv[e];
+        xv[i][e] = xh;
+        dot += xh * g[i][e];
+      }
+    }
+    dot = warp_sum(dot) / D;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = r * (g[i][e] - xv[i][e] * dot);
+      store8(dx + (size_t)row * D + (i * 32 + lane) * 8, o);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) atomicAdd(&s_dw[(i * 32 + lane) * 8 + e], acc[i][e]);
+  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += blockDim.x) atomicAdd(dw + i, s_dw[i]);
+}
+
+void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int N, int D, float eps, cudaStream_t st) {
+  if (D % 256 || D > 8192) throw std::runtime_error("rmsnorm: D must be a multiple of 256, <= 8192");
+  const int blocks = (N + 7) / 8;
+  auto X = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto Wt = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto Y = reinterpret_cast<__nv_bfloat16*>(y);
+  switch (D / 256) {
+    case 1: rmsnorm_fwd_kernel<1><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
+    case 2: rmsnorm_fwd_kernel<2><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
+    case 4: rmsnorm_fwd_kernel<4><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
+    case 8: rmsnorm_fwd_kernel<8><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
+    case 16: rmsnorm_fwd_kernel<16><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
+    case 32: rmsnorm_fwd_kernel<32><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
+    default: throw std::runtime_error("rmsnorm: unsupported D");
+  }
+  check("rmsnorm_fwd");
+}
+
+void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, void* dx, float* dw, int N, int D,
+                 int num_sms, cudaStream_t st) {
+  if (D % 256 || D > 8192) throw std::runtime_error("rmsnorm: D must be a multiple of 256, <= 8192");
+  const int blocks = std::min((N + 7) / 8, num_sms * 2);
+  auto X = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto Wt = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
+  auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
+  const size_t sm = D * sizeof(float);
+  switch (D / 256) {
+    case 1: rmsnorm_bwd_kernel<1><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D); break;
+    case 2: rmsnorm_bwd_kernel<2><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D); break;
+    case 4: rmsnorm_bwd_kernel<4><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D); break;
+    case 8: rmsnorm_bwd_kernel<8><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D); break;
+    default: throw std::runtime_error("rmsnorm_bwd: unsupported D");
+  }
+  check("rmsnorm_bwd");
+}
+
+// =====================================================================================
+// Fused per-head RMSNorm + rotary embedding (rotate-half convention, Qwen3):
+//   in  qkv [T, (Hq + 2*Hkv) * 128]  (output of the fused QKV projection)
+//   out q [T, Hq, 128], k [T, Hkv, 128] normalised and rotated; v [T, Hkv, 128] copied.
+// One warp per (token, head); lane l owns elements {2l, 2l+1} and {64+2l, 64+2l+1}... we
+// use the pairing (i, i+64) of rotate-half: lane l owns i = 2l, 2l+1 and their partners.
+// =====================================================================================
+__device__ __forceinline__ void rope_cs(int pos, int i, float log2_theta, float* c, float* s) {
+  // inv_freq_i = theta^(-2i/128), angle = pos * inv_freq
+  const float inv = exp2f(-(2.f * i / 128.f) * log2_theta);
+  const float ang = (float)pos * inv;
+  sincosf(ang, s, c);
+}
+
+__global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(
+    const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ wq, const __nv_bfloat16* __restrict__ wk,
+    __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v,
+    float* __restrict__ rstd_q, float* __restrict__ rstd_k, const int* __restrict__ pos_ids, int T, int Hq, int Hkv,
+    float eps, float log2_theta) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int Ht = Hq + 2 * Hkv;
+  if (gw >= T * Ht) return;
+  const int t = gw / Ht, h = gw % Ht;
+  const __nv_bfloat16* src = qkv + ((size_t)t * Ht + h) * 128;
+  // lane owns lo = (2l, 2l+1) and hi = (64+2l, 64+2l+1)
+  float2 lo = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[lane]);
+  float2 hi = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src + 64)[lane]);
+  if (h >= Hq + Hkv) {  // value head: plain copy
+    __nv_bfloat16* dst = v + ((size_t)t * Hkv + (h - Hq - Hkv)) * 128;
+    reinterpret_cast<__nv_bfloat162*>(dst)[lane] = __floats2bfloat162_rn(lo.x, lo.y);
+    reinterpret_cast<__nv_bfloat162*>(dst + 64)[lane] = __floats2bfloat162_rn(hi.x, hi.y);
+    return;
+  }
+  const bool is_q = h < Hq;
+  const __nv_bfloat16* w = is_q ? wq : wk;
+  float ss = lo.x * lo.x + lo.y * lo.y + hi.x * hi.x + hi.y * hi.y;
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / 128.f + eps);
+  float2 wl = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(w)[lane]);
+  float2 wh = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(w + 64)[lane]);
+  float a0 = lo.x * r * wl.x, a1 = lo.y * r * wl.y, b0 = hi.x * r * wh.x, b1 = hi.y * r * wh.y;
+  const int pos = pos_ids ? pos_ids[t] : t;
+  float c0, s0, c1, s1;
+  rope_cs(pos, 2 * lane, log2_theta, &c0, &s0);
+  rope_cs(pos, 2 * lane + 1, log2_theta, &c1, &s1);
+  // out_lo = a*cos - b*sin ; out_hi = b*cos + a*sin
+  float o0 = a0 * c0 - b0 * s0, o1 = a1 * c1 - b1 * s1;
+  float p0 = b0 * c0 + a0 * s0, p1 = b1 * c1 + a1 * s1;
+  __nv_bfloat16* dst;
+  if (is_q) {
+    dst = q + ((size_t)t * Hq + h) * 128;
+    if (lane == 0) rstd_q[(size_t)t * Hq + h] = r;
+  } else {
+    dst = k + ((size_t)t * Hkv + (h - Hq)) * 128;
+    if (lane == 0) rstd_k[(size_t)t * Hkv + (h - Hq)] = r;
+  }
+  reinterpret_cast<__nv_bfloat162*>(dst)[lane] = __floats2bfloat162_rn(o0, o1);
+  reinterpret_cast<__nv_bfloat162*>(dst + 64)[lane] = __floats2bfloat162_rn(p0, p1);
+}
+
+// Backward: dq/dk (post-rotation) -> un-rotate -> RMSNorm backward -> dqkv; dv copied.
+// dwq/dwk accumulate per-element weight gradients (fp32).
+__global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(
+    const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ wq, const __nv_bfloat16* __restrict__ wk,
+    const float* __restrict__ rstd_q, const float* __restrict__ rstd_k, const __nv_bfloat16* __restrict__ dq,
+    const __nv_bfloat16* __restrict__ dk, const __nv_bfloat16* __restrict__ dv, __nv_bfloat16* __restrict__ dqkv,
+    float* __restrict__ dwq, float* __restrict__ dwk, const int* __restrict__ pos_ids, int T, int Hq, int Hkv,
+    float log2_theta) {
+  __shared__ float s_dw[2][128];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) (&s_dw[0][0])[i] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int Ht = Hq + 2 * Hkv;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  float aq[4] = {0, 0, 0, 0}, ak[4] = {0, 0, 0, 0};
+  for (int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); gw < T * Ht; gw += nw) {
+    const int t = gw / Ht, h = gw % Ht;
+    __nv_bfloat16* out = dqkv + ((size_t)t * Ht + h) * 128;
+    if (h >= Hq + Hkv) {
+      const __nv_bfloat16* g = dv + ((size_t)t * Hkv + (h - Hq - Hkv)) * 128;
+      reinterpret_cast<__nv_bfloat162*>(out)[lane] = reinterpret_cast<const __nv_bfloat162*>(g)[lane];
+      reinterpret_cast<__nv_bfloat162*>(out + 64)[lane] = reinterpret_cast<const __nv_bfloat162*>(g + 64)[lane];
+      continue;
+    }
+    const bool is_q = h < Hq;
+    const __nv_bfloat16* w = is_q ? wq : wk;
+    const __nv_bfloat16* g = is_q ? dq + ((size_t)t * Hq + h) * 128 : dk + ((size_t)t * Hkv + (h - Hq)) * 128;
+    const float r = is_q ? rstd_q[(size_t)t * Hq + h] : rstd_k[(size_t)t * Hkv + (h - Hq)];
+    float2 glo = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(g)[lane]);
+    float2 ghi = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(g + 64)[lane]);
+    const int pos = pos_ids ? pos_ids[t] : t;
+    float c0, s0, c1, s1;
+    rope_cs(pos, 2 * lane, log2_theta, &c0, &s0);
+    rope_cs(pos, 2 * lane + 1, log2_theta, &c1, &s1);
+    // inverse rotation: da = glo*cos + ghi*sin ; db = ghi*cos - glo*sin
+    float da0 = glo.x * c0 + ghi.x * s0, da1 = glo.y * c1 + ghi.y * s1;
+    float db0 = ghi.x * c0 - glo.x * s0, db1 = ghi.y * c1 - glo.y * s1;
+    const __nv_bfloat16* src = qkv + ((size_t)t * Ht + h) * 128;
+    float2 lo = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[lane]);
+    float2 hi = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src + 64)[lane]);
+    float2 wl = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(w)[lane]);
+    float2 wh = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(w + 64)[lane]);
+    float xh[4] = {lo.x * r, lo.y * r, hi.x * r, hi.y * r};
+    float gy[4] = {da0, da1, db0, db1};
+    float wv[4] = {wl.x, wl.y, wh.x, wh.y};
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (is_q) aq[e] += gy[e] * xh[e]; else ak[e] += gy[e] * xh[e];
+      gy[e] *= wv[e];
+      dot += gy[e] * xh[e];
+    }
+    dot = warp_sum(dot) / 128.f;
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = r * (gy[e] - xh[e] * dot);
+    reinterpret_cast<__nv_bfloat162*>(out)[lane] = __floats2bfloat162_rn(o[0], o[1]);
+    reinterpret_cast<__nv_bfloat162*>(out + 64)[lane] = __floats2bfloat162_rn(o[2], o[3]);
+  }
+  atomicAdd(&s_dw[0][2 * lane], aq[0]);
+  atomicAdd(&s_dw[0][2 * lane + 1], aq[1]);
+  atomicAdd(&s_dw[0][64 + 2 * lane], aq[2]);
+  atomicAdd(&s_dw[0][64 + 2 * lane + 1], aq[3]);
+  atomicAdd(&s_dw[1][2 * lane], ak[0]);
+  atomicAdd(&s_dw[1][2 * lane + 1], ak[1]);
+  atomicAdd(&s_dw[1][64 + 2 * lane], ak[2]);
+  atomicAdd(&s_dw[1][64 + 2 * lane + 1], ak[3]);
+  __syncthreads();
+  for (int i = threadIdx.x; i < 128; i += blockDim.x) {
+    atomicAdd(dwq + i, s_dw[0][i]);
+    atomicAdd(dwk + i, s_dw[1][i]);
+  }
+}
+
+void qk_norm_rope_fwd(const void* qkv, const void* wq, const void* wk, void* q, void* k, void* v, float* rstd_q,
+                      float* rstd_k, const int* pos_ids, int T, int Hq, int Hkv, float eps, float theta,
+                      cudaStream_t st) {
+  const int warps = T * (Hq + 2 * Hkv);
+  qk_norm_rope_fwd_kernel<<<(warps + 7) / 8, 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(wq),
+      reinterpret_cast<const __nv_bfloat16*>(wk), reinterpret_cast<__nv_bfloat16*>(q),
+      reinterpret_cast<__nv_bfloat16*>(k), reinterpret_cast<__nv_bfloat16*>(v), rstd_q, rstd_k, pos_ids, T, Hq, Hkv,
+      eps, log2f(theta));
+  check("qk_norm_rope_fwd");
+}
+
+void qk_norm_rope_bwd(const void* qkv, const void* wq, const void* wk, const float* rstd_q, const float* rstd_k,
+                      const void* dq, const void* dk, const void* dv, void* dqkv, float* dwq, float* dwk,
+                      const int* pos_ids, int T, int Hq, int Hkv, float theta, int num_sms, cudaStream_t st) {
+  const int warps = T * (Hq + 2 * Hkv);
+  const int blocks = std::min((warps + 7) / 8, num_sms * 4);
+  qk_norm_rope_bwd_kernel<<<blocks, 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(wq),
+      reinterpret_cast<const __nv_bfloat16*>(wk), rstd_q, rstd_k, reinterpret_cast<const __nv_bfloat16*>(dq),
+      reinterpret_cast<const __nv_bfloat16*>(dk), reinterpret_cast<const __nv_bfloat16*>(dv),
+      reinterpret_cast<__nv_bfloat16*>(dqkv), dwq, dwk, pos_ids, T, Hq, Hkv, log2f(theta));
+  check("qk_norm_rope_bwd");
+}
+
+// =====================================================================================
+// SwiGLU on a [N, 2I] gate|up tensor: h = silu(g) * u; backward gives d[g|u].
+// =====================================================================================
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ h, int N, int I) {
+  const size_t total = (size_t)N * I / 8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = i / (I / 8), c = (i % (I / 8)) * 8;
+    float g[8], u[8], o[8];
+    load8(gu + row * 2 * I + c, g);
+    load8(gu + row * 2 * I + I + c, u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = g[e] / (1.f + __expf(-g[e])) * u[e];
+    store8(h + row * I + c, o);
+  }
+}
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ dh,
+                                  __nv_bfloat16* __restrict__ dgu, int N, int I) {
+  const size_t total = (size_t)N * I / 8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = i / (I / 8), c = (i % (I / 8)) * 8;
+    float g[8], u[8], d[8], og[8], ou[8];
+    load8(gu + row * 2 * I + c, g);
+    load8(gu + row * 2 * I + I + c, u);
+    load8(dh + row * I + c, d);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float s = 1.f / (1.f + __expf(-g[e]));
+      og[e] = d[e] * u[e] * s * (1.f + g[e] * (1.f - s));
+      ou[e] = d[e] * g[e] * s;
+    }
+    store8(dgu + row * 2 * I + c, og);
+    store8(dgu + row * 2 * I + I + c, ou);
+  }
+}
+void swiglu_fwd(const void* gu, void* h, int N, int I, int num_sms, cudaStream_t st) {
+  if (I % 8) throw std::runtime_error("swiglu: I must be a multiple of 8");
+  swiglu_fwd_kernel<<<num_sms * 8, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(gu),
+                                                 reinterpret_cast<__nv_bfloat16*>(h), N, I);
+  check("swiglu_fwd");
+}
+void swiglu_bwd(const void* gu, const void* dh, void* dgu, int N, int I, int num_sms, cudaStream_t st) {
+  if (I % 8) throw std::runtime_error("swiglu: I must be a multiple of 8");
+  swiglu_bwd_kernel<<<num_sms * 8, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(gu),
+                                                 reinterpret_cast<const __nv_bfloat16*>(dh),
+                                                 reinterpret_cast<__nv_bfloat16*>(dgu), N, I);
+  check("swiglu_bwd");
+}
+
+// =====================================================================================
+// Router: p = softmax(logits) (fp32), top-k, optional renormalisation over the top-k.
+// One warp per token; E <= 1024 (E/32 values per lane in registers).
+// =====================================================================================
+template <int EPL>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits,
+                                                          const float* __restrict__ bias, int T, int E, int k,
+                                                          int renorm, int* __restrict__ topk_e,
+                                                          float* __restrict__ topk_w, float* __restrict__ probs) {
+  const int lane = threadIdx.x & 31;
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t >= T) return;
+  float p[EPL];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    p[i] = e < E ? logits[(size_t)t * E + e] : -INFINITY;
+    mx = fmaxf(mx, p[i]);
+  }
+  mx = warp_max(mx);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    p[i] = (i * 32 + lane) < E ? __expf(p[i] - mx) : 0.f;
+    s += p[i];
+  }
+  s = warp_sum(s);
+  const float inv = 1.f / s;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    p[i] *= inv;
+    if (probs && (i * 32 + lane) < E) probs[(size_t)t * E + i * 32 + lane] = p[i];
+  }
+  // selection score = p (+ optional per-expert bias, used for skewed synthetic routing)
+  float sc[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    sc[i] = e < E ? p[i] + (bias ? bias[e] : 0.f) : -INFINITY;
+  }
+  float sel_sum = 0.f;
+  int my_e = -1;
+  float my_w = 0.f;
+  for (int j = 0; j < k; ++j) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = i * 32 + lane;
+      if (sc[i] > best || (sc[i] == best && e < bi)) { best = sc[i]; bi = e; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ob = __shfl_xor_sync(0xffffffff, best, o);
+      int oi = __shfl_xor_sync(0xffffffff, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    // owner lane removes it and reports its probability
+    float pw = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      if (i * 32 + lane == bi) { pw = p[i]; sc[i] = -INFINITY; }
+    }
+    pw = warp_sum(pw);
+    sel_sum += pw;
+    if (lane == j) { my_e = bi; my_w = pw; }
+  }
+  if (lane < k) {
+    topk_e[(size_t)t * k + lane] = my_e;
+    topk_w[(size_t)t * k + lane] = renorm ? my_w / sel_sum : my_w;
+  }
+}
+
+// Backward through renorm + softmax: dlogits[t, :] given dw[t, j] for the chosen experts.
+template <int EPL>
+__global__ void __launch_bounds__(256) router_bwd_kernel(const float* __restrict__ probs, const int* __restrict__ topk_e,
+                                                         const float* __restrict__ dw, int T, int E, int k, int renorm,
+                                                         float* __restrict__ dlogits) {
+  const int lane = threadIdx.x & 31;
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t >= T) return;
+  // dp_i for chosen experts
+  float S = 0.f, gw = 0.f;
+  int e_l = -1;
+  float g_l = 0.f, p_l = 0.f;
+  if (lane < k) {
+    e_l = topk_e[(size_t)t * k + lane];
+    g_l = dw[(size_t)t * k + lane];
+    p_l = probs[(size_t)t * E + e_l];
+  }
+  S = warp_sum(lane < k ? p_l : 0.f);
+  // with renorm: w_j = p_j / S; dL/dp_i = (g_i - sum_j g_j w_j) / S for chosen i
+  gw = warp_sum(lane < k ? g_l * p_l : 0.f) / S;
+  float dp_l = lane < k ? (renorm ? (g_l - gw) / S : g_l) : 0.f;
+  // softmax backward: dlogit_i = p_i * (dp_i - sum_j p_j dp_j)
+  float pdp = warp_sum(lane < k ? p_l * dp_l : 0.f);
+  float p[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    p[i] = e < E ? probs[(size_t)t * E + e] : 0.f;
+  }
+  float dpv[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) dpv[i] = 0.f;
+  for (int j = 0; j < k; ++j) {
+    const int ej = __shfl_sync(0xffffffff, e_l, j);
+    const float dj = __shfl_sync(0xffffffff, dp_l, j);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i)
+      if (i * 32 + lane == ej) dpv[i] += dj;
+  }
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    if (e < E) dlogits[(size_t)t * E + e] = p[i] * (dpv[i] - pdp);
+  }
+}
+
+void router_topk(const float* logits, const float* bias, int T, int E, int k, bool renorm, int* topk_e, float* topk_w,
+                 float* probs, cudaStream_t st) {
+  if (k > 32) throw std::runtime_error("router: top-k above 32");
+  const int blocks = (T + 7) / 8;
+  const int epl = (E + 31) / 32;
+  if (epl <= 2) router_topk_kernel<2><<<blocks, 256, 0, st>>>(logits, bias, T, E, k, renorm, topk_e, topk_w, probs);
+  else if (epl <= 4) router_topk_kernel<4><<<blocks, 256, 0, st>>>(logits, bias, T, E, k, renorm, topk_e, topk_w, probs);
+  else if (epl <= 8) router_topk_kernel<8><<<blocks, 256, 0, st>>>(logits, bias, T, E, k, renorm, topk_e, topk_w, probs);
+  else if (epl <= 16) router_topk_kernel<16><<<blocks, 256, 0, st>>>(logits, bias, T, E, k, renorm, topk_e, topk_w, probs);
+  else throw std::runtime_error("router: at most 512 experts");
+  check("router_topk");
+}
+
+void router_bwd(const float* probs, const int* topk_e, const float* dw, int T, int E, int k, bool renorm,
+                float* dlogits, cudaStream_t st) {
+  const int blocks = (T + 7) / 8;
+  const int epl = (E + 31) / 32;
+  if (epl <= 2) router_bwd_kernel<2><<<blocks, 256, 0, st>>>(probs, topk_e, dw, T, E, k, renorm, dlogits);
+  else if (epl <= 4) router_bwd_kernel<4><<<blocks, 256, 0, st>>>(probs, topk_e, dw, T, E, k, renorm, dlogits);
+  else if (epl <= 8) router_bwd_kernel<8><<<blocks, 256, 0, st>>>(probs, topk_e, dw, T, E, k, renorm, dlogits);
+  else if (epl <= 16) router_bwd_kernel<16><<<blocks, 256, 0, st>>>(probs, topk_e, dw, T, E, k, renorm, dlogits);
+  else throw std::runtime_error("router: at most 512 experts");
+  check("router_bwd");
+}
+
+// =====================================================================================
+// Fused AdamW.
+//  * fp32 state: master (optional, fp32), m, v fp32. Param stored bf16 (and the master
+//    copy when present).
+//  * 8-bit state: m and v quantised per block of 128 values with an fp32 absmax scale
+//    (block-wise quantisation, Dettmers et al., ICLR 2022): m linearly as int8, v as
+//    uint8 of sqrt(v) (sqrt keeps the dynamic range of the second moment). No master
+//    copy; the bf16 parameter is updated with stochastic rounding.
+// =====================================================================================
+__device__ __forceinline__ uint32_t hash32(uint32_t x) {
+  // integer finaliser (murmur3 fmix32)
+  x ^= x >> 16;
+  x *= 0x85ebca6bu;
+  x ^= x >> 13;
+  x *= 0xc2b2ae35u;
+  x ^= x >> 16;
+  return x;
+}
+__device__ __forceinline__ __nv_bfloat16 bf16_stochastic(float x, uint32_t rnd) {
+  uint32_t u = __float_as_uint(x);
+  // add random bits below the bf16 mantissa, then truncate
+  u += (rnd & 0xFFFFu);
+  u &= 0xFFFF0000u;
+  return __ushort_as_bfloat16((unsigned short)(u >> 16));
+}
+
+__global__ void adamw_fp32_kernel(__nv_bfloat16* __restrict__ p, float* __restrict__ master, const float* __restrict__ g,
+                                  float* __restrict__ m, float* __restrict__ v, size_t n, AdamWHyper h) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float gi = g[i] * h.grad_scale;
+    const float mi = h.beta1 * m[i] + (1.f - h.beta1) * gi;
+    const float vi = h.beta2 * v[i] + (1.f - h.beta2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    float w = master ? master[i] : __bfloat162float(p[i]);
+    w = w * (1.f - h.lr * h.weight_decay) - h.lr * (mi * h.bc1) / (sqrtf(vi * h.bc2) + h.eps);
+    if (master) master[i] = w;
+    p[i] = __float2bfloat16(w);
+  }
+}
+
+__global__ void __launch_bounds__(256) adamw_8bit_kernel(__nv_bfloat16* __restrict__ p, const float* __restrict__ g,
+                                                         int8_t* __restrict__ mq, float* __restrict__ ms,
+                                                         uint8_t* __restrict__ vq, float* __restrict__ vs, size_t n,
+                                                         AdamWHyper h) {
+  // one warp per block of 128 values (4 per lane)
+  const int lane = threadIdx.x & 31;
+  const size_t nb = (n + 127) / 128;
+  const size_t nw = (size_t)gridDim.x * (blockDim.x >> 5);
+  for (size_t b = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5; b < nb; b += nw) {
+    const float msc = ms[b], vsc = vs[b];
+    float mi[4], vi[4];
+    float mmax = 0.f, vmax = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const size_t i = b * 128 + e * 32 + lane;
+      if (i < n) {
+        const float gi = g[i] * h.grad_scale;
+        const float m0 = (float)mq[i] * msc * (1.f / 127.f);
+        const float sv = (float)vq[i] * vsc * (1.f / 255.f);
+        const float v0 = sv * sv;
+        mi[e] = h.beta1 * m0 + (1.f - h.beta1) * gi;
+        vi[e] = h.beta2 * v0 + (1.f - h.beta2) * gi * gi;
+        float w = __bfloat162float(p[i]);
+        w = w * (1.f - h.lr * h.weight_decay) - h.lr * (mi[e] * h.bc1) / (sqrtf(vi[e] * h.bc2) + h.eps);
+        p[i] = bf16_stochastic(w, hash32((uint32_t)i * 2654435761u ^ (uint32_t)h.step * 0x9E3779B9u ^ h.seed));
+      } else {
+        mi[e] = 0.f;
+        vi[e] = 0.f;
+      }
+      mmax = fmaxf(mmax, fabsf(mi[e]));
+      vmax = fmaxf(vmax, sqrtf(vi[e]));
+    }
+    mmax = warp_max(mmax);
+    vmax = warp_max(vmax);
+    const float minv = mmax > 0.f ? 127.f / mmax : 0.f;
+    const float vinv = vmax > 0.f ? 255.f / vmax : 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const size_t i = b * 128 + e * 32 + lane;
+      if (i < n) {
+        mq[i] = (int8_t)__float2int_rn(mi[e] * minv);
+        vq[i] = (uint8_t)min(255, __float2int_rn(sqrtf(vi[e]) * vinv));
+      }
+    }
+    if (lane == 0) {
+      ms[b] = mmax;
+      vs[b] = vmax;
+    }
+  }
+}
+
+void adamw_fp32(void* p, float* master, const float* g, float* m, float* v, size_t n, const AdamWHyper& h, int num_sms,
+                cudaStream_t st) {
+  adamw_fp32_kernel<<<num_sms * 8, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(p), master, g, m, v, n, h);
+  check("adamw_fp32");
+}
+void adamw_8bit(void* p, const float* g, int8_t* mq, float* ms, uint8_t* vq, float* vs, size_t n, const AdamWHyper& h,
+                int num_sms, cudaStream_t st) {
+  adamw_8bit_kernel<<<num_sms * 8, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(p), g, mq, ms, vq, vs, n, h);
+  check("adamw_8bit");
+}
+
+// =====================================================================================
+// Cross-entropy (mean over valid labels) fused with its gradient:
+//   loss[t] = logsumexp(z_t) - z_t[y_t];  dz_t = (softmax(z_t) - onehot(y_t)) * scale,
+// written in place over the bf16 logits. One block per row; labels < 0 are ignored.
+// =====================================================================================
+__global__ void __launch_bounds__(512) xent_fwd_bwd_kernel(__nv_bfloat16* __restrict__ logits, const int* __restrict__ labels,
+                                                           int V, float scale, float* __restrict__ loss) {
+  const int t = blockIdx.x;
+  __nv_bfloat16* z = logits + (size_t)t * V;
+  const int y = labels[t];
+  __shared__ float s_m[16], s_s[16];
+  float m = -INFINITY, s = 0.f;
+  const int nvec = V / 8;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    float f[8];
+    load8(z + i * 8, f);
+    float lm = f[0];
+#pragma unroll
+    for (int e = 1; e < 8; ++e) lm = fmaxf(lm, f[e]);
+    const float nm = fmaxf(m, lm);
+    float acc = s * __expf(m - nm);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc += __expf(f[e] - nm);
+    m = nm;
+    s = acc;
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    const float f = __bfloat162float(z[i]);
+    const float nm = fmaxf(m, f);
+    s = s * __expf(m - nm) + __expf(f - nm);
+    m = nm;
+  }
+  // block reduce (m, s)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffff, m, o);
+    const float os = __shfl_xor_sync(0xffffffff, s, o);
+    const float nm = fmaxf(m, om);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+    m = nm;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_s[warp] = s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? s_m[lane] : -INFINITY;
+    s = lane < nw ? s_s[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffff, m, o);
+      const float os = __shfl_xor_sync(0xffffffff, s, o);
+      const float nm = fmaxf(m, om);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+      m = nm;
+    }
+    if (lane == 0) {
+      s_m[0] = m;
+      s_s[0] = s;
+    }
+  }
+  __syncthreads();
+  m = s_m[0];
+  s = s_s[0];
+  const float lse = m + __logf(s);
+  const float zy = (y >= 0) ? __bfloat162float(z[y]) : 0.f;
+  __syncthreads();
+  if (threadIdx.x == 0) loss[t] = (y >= 0) ? (lse - zy) : 0.f;
+  const float sc = (y >= 0) ? scale : 0.f;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    float f[8], o[8];
+    load8(z + i * 8, f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int col = i * 8 + e;
+      o[e] = (__expf(f[e] - lse) - (col == y ? 1.f : 0.f)) * sc;
+    }
+    store8(z + i * 8, o);
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    const float f = __bfloat162float(z[i]);
+    z[i] = __float2bfloat16((__expf(f - lse) - (i == y ? 1.f : 0.f)) * sc);
+  }
+}
+
+void xent_fwd_bwd(void* logits, const int* labels, int T, int V, float scale, float* loss, cudaStream_t st) {
+  xent_fwd_bwd_kernel<<<T, 512, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), labels, V, scale, loss);
+  check("xent_fwd_bwd");
+}
+
+}  // namespace sepx

@@ -1,0 +1,171 @@
+// Python bindings of the memory-bound kernels (elementwise.cu).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "elementwise.h"
+
+namespace {
+
+cudaStream_t cs() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+int num_sms() {
+  static int n = 0;
+  if (!n) n = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  return n;
+}
+
+void req(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
+}
+
+const int* opt_int(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr<int>() : nullptr; }
+const float* opt_f(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr<float>() : nullptr; }
+
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, double eps) {
+  req(x, at::kBFloat16, "x");
+  req(w, at::kBFloat16, "w");
+  req(y, at::kBFloat16, "y");
+  req(rstd, at::kFloat, "rstd");
+  const int D = x.size(-1);
+  const int N = x.numel() / D;
+  sepx::rmsnorm_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr<float>(), N, D, (float)eps, cs());
+}
+
+void rmsnorm_bwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd, const at::Tensor& dy, at::Tensor& dx,
+                 at::Tensor& dw) {
+  req(x, at::kBFloat16, "x");
+  req(dy, at::kBFloat16, "dy");
+  req(dx, at::kBFloat16, "dx");
+  req(dw, at::kFloat, "dw");
+  const int D = x.size(-1);
+  const int N = x.numel() / D;
+  sepx::rmsnorm_bwd(x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(), dx.data_ptr(),
+                    dw.data_ptr<float>(), N, D, num_sms(), cs());
+}
+
+void qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, at::Tensor& q, at::Tensor& k,
+                      at::Tensor& v, at::Tensor& rstd_q, at::Tensor& rstd_k, const c10::optional<at::Tensor>& pos,
+                      int64_t Hq, int64_t Hkv, double eps, double theta) {
+  req(qkv, at::kBFloat16, "qkv");
+  const int T = qkv.size(0);
+  TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * 128, "qkv width must be (Hq + 2 Hkv) * 128");
+  sepx::qk_norm_rope_fwd(qkv.data_ptr(), wq.data_ptr(), wk.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                         rstd_q.data_ptr<float>(), rstd_k.data_ptr<float>(), opt_int(pos), T, Hq, Hkv, (float)eps,
+                         (float)theta, cs());
+}
+
+void qk_norm_rope_bwd(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& rstd_q,
+                      const at::Tensor& rstd_k, const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv,
+                      at::Tensor& dqkv, at::Tensor& dwq, at::Tensor& dwk, const c10::optional<at::Tensor>& pos,
+                      int64_t Hq, int64_t Hkv, double theta) {
+  req(dq, at::kBFloat16, "dq");
+  req(dk, at::kBFloat16, "dk");
+  req(dv, at::kBFloat16, "dv");
+  req(dqkv, at::kBFloat16, "dqkv");
+  const int T = qkv.size(0);
+  sepx::qk_norm_rope_bwd(qkv.data_ptr(), wq.data_ptr(), wk.data_ptr(), rstd_q.data_ptr<float>(),
+                         rstd_k.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dqkv.data_ptr(),
+                         dwq.data_ptr<float>(), dwk.data_ptr<float>(), opt_int(pos), T, Hq, Hkv, (float)theta,
+                         num_sms(), cs());
+}
+
+void swiglu_fwd(const at::Tensor& gu, at::Tensor& h) {
+  req(gu, at::kBFloat16, "gu");
+  req(h, at::kBFloat16, "h");
+  const int I = h.size(-1);
+  sepx::swiglu_fwd(gu.data_ptr(), h.data_ptr(), h.numel() / I, I, num_sms(), cs());
+}
+
+void swiglu_bwd(const at::Tensor& gu, const at::Tensor& dh, at::Tensor& dgu) {
+  req(gu, at::kBFloat16, "gu");
+  req(dh, at::kBFloat16, "dh");
+  req(dgu, at::kBFloat16, "dgu");
+  const int I = dh.size(-1);
+  sepx::swiglu_bwd(gu.data_ptr(), dh.data_ptr(), dgu.data_ptr(), dh.numel() / I, I, num_sms(), cs());
+}
+
+void router_topk(const at::Tensor& logits, const c10::optional<at::Tensor>& bias, int64_t k, bool renorm,
+                 at::Tensor& topk_e, at::Tensor& topk_w, const c10::optional<at::Tensor>& probs) {
+  req(logits, at::kFloat, "logits");
+  req(topk_e, at::kInt, "topk_e");
+  req(topk_w, at::kFloat, "topk_w");
+  sepx::router_topk(logits.data_ptr<float>(), opt_f(bias), logits.size(0), logits.size(1), k, renorm,
+                    topk_e.data_ptr<int>(), topk_w.data_ptr<float>(),
+                    probs.has_value() ? probs->data_ptr<float>() : nullptr, cs());
+}
+
+void router_bwd(const at::Tensor& probs, const at::Tensor& topk_e, const at::Tensor& dw, bool renorm, at::Tensor& dlogits) {
+  req(probs, at::kFloat, "probs");
+  req(dw, at::kFloat, "dw");
+  req(dlogits, at::kFloat, "dlogits");
+  sepx::router_bwd(probs.data_ptr<float>(), topk_e.data_ptr<int>(), dw.data_ptr<float>(), probs.size(0), probs.size(1),
+                   topk_e.size(1), renorm, dlogits.data_ptr<float>(), cs());
+}
+
+sepx::AdamWHyper hyper(double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale,
+                       int64_t seed) {
+  sepx::AdamWHyper h;
+  h.lr = lr;
+  h.beta1 = b1;
+  h.beta2 = b2;
+  h.eps = eps;
+  h.weight_decay = wd;
+  h.step = step;
+  h.bc1 = 1.0 / (1.0 - std::pow(b1, (double)step));
+  h.bc2 = 1.0 / (1.0 - std::pow(b2, (double)step));
+  h.grad_scale = grad_scale;
+  h.seed = (uint32_t)seed;
+  return h;
+}
+
+void adamw_fp32(at::Tensor& p, const c10::optional<at::Tensor>& master, const at::Tensor& g, at::Tensor& m, at::Tensor& v,
+                double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale) {
+  req(p, at::kBFloat16, "param");
+  req(g, at::kFloat, "grad");
+  req(m, at::kFloat, "exp_avg");
+  req(v, at::kFloat, "exp_avg_sq");
+  TORCH_CHECK(g.numel() == p.numel() && m.numel() == p.numel(), "size mismatch");
+  float* mp = master.has_value() ? master->data_ptr<float>() : nullptr;
+  sepx::adamw_fp32(p.data_ptr(), mp, g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), p.numel(),
+                   hyper(lr, b1, b2, eps, wd, step, grad_scale, 0), num_sms(), cs());
+}
+
+void adamw_8bit(at::Tensor& p, const at::Tensor& g, at::Tensor& mq, at::Tensor& ms, at::Tensor& vq, at::Tensor& vs,
+                double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale, int64_t seed) {
+  req(p, at::kBFloat16, "param");
+  req(g, at::kFloat, "grad");
+  req(mq, at::kChar, "exp_avg_q");
+  req(vq, at::kByte, "exp_avg_sq_q");
+  TORCH_CHECK(ms.numel() >= (p.numel() + 127) / 128, "scale size");
+  sepx::adamw_8bit(p.data_ptr(), g.data_ptr<float>(), mq.data_ptr<int8_t>(), ms.data_ptr<float>(),
+                   vq.data_ptr<uint8_t>(), vs.data_ptr<float>(), p.numel(),
+                   hyper(lr, b1, b2, eps, wd, step, grad_scale, seed), num_sms(), cs());
+}
+
+void xent_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, double scale, at::Tensor& loss) {
+  req(logits, at::kBFloat16, "logits");
+  req(labels, at::kInt, "labels");
+  req(loss, at::kFloat, "loss");
+  TORCH_CHECK(logits.size(1) % 8 == 0, "vocab must be a multiple of 8");
+  sepx::xent_fwd_bwd(logits.data_ptr(), labels.data_ptr<int>(), logits.size(0), logits.size(1), (float)scale,
+                     loss.data_ptr<float>(), cs());
+}
+
+}  // namespace
+
+void register_elementwise(pybind11::module& m) {
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("router_topk", &router_topk);
+  m.def("router_bwd", &router_bwd);
+  m.def("adamw_fp32", &adamw_fp32);
+  m.def("adamw_8bit", &adamw_8bit);
+  m.def("xent_fwd_bwd", &xent_fwd_bwd);
+}

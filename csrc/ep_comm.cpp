@@ -1,0 +1,201 @@
+// Native expert-parallel communicator: a symmetric device heap shared over CUDA IPC and
+// the launch wrappers of the dispatch/combine kernels (moe_ep.cu).
+//
+// Every rank allocates one heap of identical size and layout with cudaMalloc, exports
+// its IPC handle, and maps every peer's heap (cudaIpcOpenMemHandle). Kernels then store
+// straight into peer memory over NVLink. The handle exchange itself is done by the
+// Python caller over torch.distributed (any backend), so this class has no dependency on
+// a particular bootstrap.
+//
+// Reference parity: replaces the NCCL all_to_all_single calls of src/rbd.py:71-133 (and
+// the plan metadata exchanges of src/rbd.py:271-297) with peer stores + epoch headers.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+
+namespace {
+
+#define CUDA_OK(expr)                                                                     \
+  do {                                                                                    \
+    cudaError_t _e = (expr);                                                              \
+    TORCH_CHECK(_e == cudaSuccess, #expr " failed: ", cudaGetErrorString(_e));            \
+  } while (0)
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+class EpComm {
+ public:
+  EpComm(int world, int rank, int cap, int k, int hidden, int device)
+      : world_(world), rank_(rank), device_(device) {
+    TORCH_CHECK(world >= 1 && world <= 64, "EP world size must be in [1, 64]");
+    TORCH_CHECK(rank >= 0 && rank < world, "bad rank");
+    TORCH_CHECK(hidden % 8 == 0, "hidden size must be a multiple of 8");
+    TORCH_CHECK(k >= 1 && k <= 8, "top-k must be in [1, 8]");
+    c10::cuda::CUDAGuard g(device);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+      size_t o = off;
+      off = align_up(off + bytes, 256);
+      return o;
+    };
+    args_.W = world;
+    args_.rank = rank;
+    args_.cap = cap;
+    args_.k = k;
+    args_.H = hidden;
+    args_.off_hdr = take(sizeof(uint64_t) * 4 * world);
+    args_.off_recv_e = take(sizeof(int16_t) * (size_t)world * cap * k);
+    args_.off_recv_w = take(sizeof(float) * (size_t)world * cap * k);
+    args_.off_ret_w = take(sizeof(float) * (size_t)world * cap * k);
+    args_.off_recv_x = take((size_t)2 * world * cap * hidden);
+    args_.off_ret_x = take((size_t)2 * world * cap * hidden);
+    bytes_ = off;
+    CUDA_OK(cudaMalloc(&heap_, bytes_));
+    CUDA_OK(cudaMemset(heap_, 0, bytes_));
+    for (int i = 0; i < 64; ++i) args_.peer_base[i] = nullptr;
+    args_.peer_base[rank] = heap_;
+  }
+
+  ~EpComm() { close(); }
+
+  void close() {
+    if (!heap_) return;
+    c10::cuda::CUDAGuard g(device_);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < world_; ++r)
+      if (r != rank_ && args_.peer_base[r]) cudaIpcCloseMemHandle(args_.peer_base[r]);
+    cudaFree(heap_);
+    heap_ = nullptr;
+  }
+
+  size_t heap_bytes() const { return bytes_; }
+
+  py::bytes ipc_handle() const {
+    cudaIpcMemHandle_t h;
+    CUDA_OK(cudaIpcGetMemHandle(&h, heap_));
+    return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+  }
+
+  void open_peers(const std::vector<py::bytes>& handles) {
+    TORCH_CHECK((int)handles.size() == world_, "need one handle per rank");
+    c10::cuda::CUDAGuard g(device_);
+    for (int r = 0; r < world_; ++r) {
+      if (r == rank_) continue;
+      std::string s = handles[r];
+      TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+      cudaIpcMemHandle_t h;
+      memcpy(&h, s.data(), sizeof(h));
+      void* p = nullptr;
+      CUDA_OK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+      args_.peer_base[r] = p;
+    }
+  }
+
+  int64_t peer_base(int r) const { return reinterpret_cast<int64_t>(args_.peer_base[r]); }
+
+  // -------------------------------------------------------------------------------
+  sepx::EpArgs call_args(int T, int phase, int64_t epoch, at::Tensor& done, at::Tensor& status,
+                         double timeout_s) const {
+    sepx::EpArgs a = args_;
+    TORCH_CHECK(T <= a.cap, "more tokens than the communicator capacity");
+    a.T = T;
+    a.phase = phase;
+    a.epoch = (uint32_t)epoch;
+    a.done_counter = reinterpret_cast<unsigned int*>(done.data_ptr<int>());
+    a.status = status.data_ptr<int>();
+    a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+    return a;
+  }
+
+  void route_plan(const at::Tensor& topk_e, const at::Tensor& e2r, at::Tensor& slot, at::Tensor& send_count) {
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_route_plan(topk_e.data_ptr<int>(), topk_e.size(0), topk_e.size(1), e2r.data_ptr<int>(), world_,
+                        slot.data_ptr<int>(), send_count.data_ptr<int>(), st);
+  }
+
+  void dispatch(const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w, const at::Tensor& slot,
+                const at::Tensor& e2r, const at::Tensor& e2l, at::Tensor& self_tok, const at::Tensor& send_count,
+                bool with_meta, int64_t epoch, at::Tensor& done, at::Tensor& status, double timeout_s) {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x must be contiguous bf16");
+    TORCH_CHECK(x.size(1) == args_.H, "hidden size mismatch");
+    auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_dispatch(a, x.data_ptr(), topk_e.data_ptr<int>(), topk_w.data_ptr<float>(), slot.data_ptr<int>(),
+                      e2r.data_ptr<int>(), e2l.data_ptr<int>(), self_tok.data_ptr<int>(),
+                      send_count.data_ptr<int>(), with_meta, st);
+  }
+
+  void recv_plan(const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w, const at::Tensor& self_tok,
+                 const at::Tensor& e2r, const at::Tensor& e2l, const at::Tensor& send_count, int G, int64_t epoch,
+                 at::Tensor& rows_from, at::Tensor& chunk_cnt, at::Tensor& group_off, at::Tensor& group_cnt,
+                 at::Tensor& pad_off, at::Tensor& xp, at::Tensor& row_w, at::Tensor& row_src, at::Tensor& inv_rows,
+                 at::Tensor& done, at::Tensor& status, double timeout_s) {
+    auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_recv_plan(a, x.data_ptr(), topk_e.data_ptr<int>(), topk_w.data_ptr<float>(), self_tok.data_ptr<int>(),
+                       e2r.data_ptr<int>(), e2l.data_ptr<int>(), send_count.data_ptr<int>(), G, (int)xp.size(0),
+                       rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(), group_off.data_ptr<int>(),
+                       group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(), xp.data_ptr(), row_w.data_ptr<float>(),
+                       row_src.data_ptr<int>(), inv_rows.data_ptr<int>(), st);
+  }
+
+  void recv_gather(const at::Tensor& x, const at::Tensor& self_tok, const at::Tensor& row_src,
+                   const at::Tensor& group_off, const at::Tensor& send_count, at::Tensor& xp, int64_t epoch,
+                   at::Tensor& done, at::Tensor& status, double timeout_s) {
+    auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    const int G = group_off.size(0) - 1;
+    sepx::ep_recv_gather(a, x.data_ptr(), self_tok.data_ptr<int>(), row_src.data_ptr<int>(),
+                         group_off.data_ptr<int>() + G, send_count.data_ptr<int>(), xp.data_ptr(), (int)xp.size(0), st);
+  }
+
+  void combine(const at::Tensor& y, const at::Tensor& inv_rows, const at::Tensor& row_w, const at::Tensor& rows_from,
+               bool weighted, const c10::optional<at::Tensor>& row_val, int T, int64_t epoch, at::Tensor& done,
+               at::Tensor& status, double timeout_s) {
+    auto a = call_args(T, 1, epoch, done, status, timeout_s);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_combine(a, y.data_ptr(), inv_rows.data_ptr<int>(), row_w.data_ptr<float>(), rows_from.data_ptr<int>(),
+                     weighted, row_val.has_value() ? row_val->data_ptr<float>() : nullptr, st);
+  }
+
+  void source_reduce(const at::Tensor& slot, const at::Tensor& topk_e, const at::Tensor& e2r,
+                     const c10::optional<at::Tensor>& residual, at::Tensor& out, const c10::optional<at::Tensor>& val,
+                     int64_t epoch, at::Tensor& done, at::Tensor& status, double timeout_s) {
+    auto a = call_args(out.size(0), 1, epoch, done, status, timeout_s);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_source_reduce(a, slot.data_ptr<int>(), topk_e.data_ptr<int>(), e2r.data_ptr<int>(),
+                           residual.has_value() ? residual->data_ptr() : nullptr, out.data_ptr(),
+                           val.has_value() ? val->data_ptr<float>() : nullptr, st);
+  }
+
+ private:
+  int world_, rank_, device_;
+  void* heap_ = nullptr;
+  size_t bytes_ = 0;
+  sepx::EpArgs args_;
+};
+
+}  // namespace
+
+void register_ep_comm(pybind11::module& m) {
+  py::class_<EpComm>(m, "EpComm")
+      .def(py::init<int, int, int, int, int, int>(), py::arg("world"), py::arg("rank"), py::arg("cap"),
+           py::arg("k"), py::arg("hidden"), py::arg("device"))
+      .def("close", &EpComm::close)
+      .def("heap_bytes", &EpComm::heap_bytes)
+      .def("ipc_handle", &EpComm::ipc_handle)
+      .def("open_peers", &EpComm::open_peers)
+      .def("peer_base", &EpComm::peer_base)
+      .def("route_plan", &EpComm::route_plan)
+      .def("dispatch", &EpComm::dispatch)
+      .def("recv_plan", &EpComm::recv_plan)
+      .def("recv_gather", &EpComm::recv_gather)
+      .def("combine", &EpComm::combine)
+      .def("source_reduce", &EpComm::source_reduce);
+}

@@ -1,5 +1,47 @@
-// Launchers for the non-GEMM sm_100a kernels (norms, RoPE, SwiGLU, MoE routing and
-// dispatch/combine, optimizer, loss). Each takes raw device pointers and a stream.
+// Launchers for the non-GEMM sm_100a kernels (MoE dispatch/combine, norms, RoPE,
+// SwiGLU, optimizer, loss). Each takes raw device pointers and a stream.
 #pragma once
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
+
+namespace sepx {
+
+// ---------------------------------------------------------------------------------
+// Expert-parallel dispatch/combine (moe_ep.cu)
+// ---------------------------------------------------------------------------------
+struct EpArgs {
+  void* peer_base[64];  // base of every rank's symmetric region (this rank's included)
+  size_t off_recv_x = 0, off_recv_e = 0, off_recv_w = 0;
+  size_t off_ret_x = 0, off_ret_w = 0, off_hdr = 0;
+  int W = 1, rank = 0;
+  int cap = 0;  // slots per source (max tokens per rank per call)
+  int k = 1;
+  int H = 0;
+  int T = 0;      // tokens of this rank in this call
+  int phase = 0;  // header row used by this call
+  uint32_t epoch = 0;
+  unsigned int* done_counter = nullptr;
+  int* status = nullptr;
+  unsigned long long timeout_ns = 5000000000ull;
+};
+
+void ep_route_plan(const int* topk_e, int T, int k, const int* e2r, int W, int* slot,
+                   int* send_count, cudaStream_t st);
+void ep_dispatch(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
+                 const int* slot, const int* e2r, const int* e2l, int* self_tok,
+                 const int* send_count, bool with_meta, cudaStream_t st);
+void ep_recv_plan(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
+                  const int* self_tok, const int* e2r, const int* e2l, const int* send_count,
+                  int G, int cap_rows, int* rows_from, int* chunk_cnt, int* group_off,
+                  int* group_cnt, int* pad_off, void* xp, float* row_w, int* row_src,
+                  int* inv_rows, cudaStream_t st);
+void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const int* row_src,
+                    const int* total_rows, const int* send_count, void* xp, int cap_rows,
+                    cudaStream_t st);
+void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float* row_w,
+                const int* rows_from, bool weighted, const float* row_val, cudaStream_t st);
+void ep_source_reduce(const EpArgs& a, const int* slot, const int* topk_e, const int* e2r,
+                      const void* residual, void* out, float* val, cudaStream_t st);
+
+}  // namespace sepx

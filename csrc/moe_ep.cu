@@ -1,0 +1,676 @@
+// Expert-parallel dispatch / combine over NVLink peer memory (one process per GPU).
+//
+// Data plane: every rank owns the same symmetric layout (see symm_heap.cpp) and the
+// kernels write straight into peers' buffers with 16-byte stores, then publish an
+// epoch-tagged header with a system-scope release store. Receivers acquire-poll the
+// headers with a deadline; on timeout they record kErrTimeoutPeer and return.
+//
+// Per-rank deduplication: a token is sent to a destination rank at most once, whatever
+// number of its top-k experts live there (the reference sends one row per (token,
+// expert) inside a node, src/rbd.py:229-236, and one pilot per (token, node) between
+// nodes, src/rbd.py:238-252). The receiving rank fans the row out to its local experts
+// in HBM (permute kernel), applies the gate weights, reduces a token's co-resident
+// experts and returns ONE partial row per (token, rank).
+//
+// Symmetric slabs (per rank, indexed [src][slot]):
+//   recv_x   [W][cap][H] bf16   rows received from each source
+//   recv_e   [W][cap][k] int16  local expert slot of each of the row's k choices (-1: other rank)
+//   recv_w   [W][cap][k] f32    gate weight of each choice
+//   ret_x    [W][cap][H] bf16   partial outputs returned by each expert rank
+//   ret_w    [W][cap][k] f32    per-choice router-weight gradients (backward)
+//   hdr      [4][W]      u64    (epoch << 32 | rows) per phase: 0 dispatch, 1 combine
+//
+// Rows a rank sends to itself never cross the slab: the permute reads x directly and
+// the slot->token map for self rows is kept locally.
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace sepx {
+
+constexpr int kMaxW = 64;
+
+__device__ __forceinline__ bool wait_header(const uint64_t* hdr, uint32_t epoch, uint32_t* rows,
+                                            int* status, uint64_t timeout_ns) {
+  uint64_t v = ld_acquire_sys_u64(hdr);
+  if ((uint32_t)(v >> 32) == epoch) {
+    *rows = (uint32_t)v;
+    return true;
+  }
+  uint64_t t0 = globaltimer_ns();
+  while (true) {
+    v = ld_acquire_sys_u64(hdr);
+    if ((uint32_t)(v >> 32) == epoch) {
+      *rows = (uint32_t)v;
+      return true;
+    }
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      record_error(status, kErrTimeoutPeer);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// K1: route plan. slot[t][d] = ordinal of token t among tokens sent to rank d (-1 if
+// none of t's experts is on d). Single block; T up to a few 10^4 tokens.
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict__ topk_e, int T,
+                                                          int k, const int* __restrict__ e2r,
+                                                          int W, int* __restrict__ slot,
+                                                          int* __restrict__ send_count) {
+  __shared__ int s_part[1024 / 32][kMaxW];  // per-warp totals per destination
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (T + blockDim.x - 1) / blockDim.x;
+  const int t_begin = tid * per, t_end = min(T, t_begin + per);
+  // pass 1: mask per token, thread-local counts per destination (W <= 64: 64-bit mask)
+  int cnt[kMaxW];
+#pragma unroll 1
+  for (int d = 0; d < W; ++d) cnt[d] = 0;
+  for (int t = t_begin; t < t_end; ++t) {
+    unsigned long long m = 0;
+    for (int j = 0; j < k; ++j) m |= 1ull << e2r[topk_e[t * k + j]];
+    for (int d = 0; d < W; ++d) cnt[d] += (m >> d) & 1;
+  }
+  // exclusive scan of cnt[d] across threads (warp shuffle + per-warp totals)
+  for (int d = 0; d < W; ++d) {
+    int v = cnt[d];
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int n = __shfl_up_sync(0xffffffff, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) s_part[warp][d] = incl;
+    cnt[d] = incl - v;  // exclusive within warp
+  }
+  __syncthreads();
+  if (tid < W) {
+    int acc = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      int v = s_part[w][tid];
+      s_part[w][tid] = acc;
+      acc += v;
+    }
+    send_count[tid] = acc;
+  }
+  __syncthreads();
+  for (int d = 0; d < W; ++d) cnt[d] += s_part[warp][d];
+  // pass 2: write slots
+  for (int t = t_begin; t < t_end; ++t) {
+    unsigned long long m = 0;
+    for (int j = 0; j < k; ++j) m |= 1ull << e2r[topk_e[t * k + j]];
+    for (int d = 0; d < W; ++d) {
+      if ((m >> d) & 1) slot[(size_t)t * W + d] = cnt[d]++;
+      else slot[(size_t)t * W + d] = -1;
+    }
+  }
+}
+
+// Publish helper: the last CTA to finish writes the headers (release, system scope).
+__device__ __forceinline__ void publish_last_cta(unsigned int* done_counter, const EpArgs& a,
+                                                 int phase, const int* counts_per_dst,
+                                                 bool counts_are_per_src) {
+  __syncthreads();
+  __shared__ bool s_last;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    unsigned int prev = atomicAdd(done_counter, 1u);
+    s_last = ((prev + 1) % gridDim.x) == 0;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x < a.W) {
+    __threadfence_system();
+    const int d = threadIdx.x;
+    char* base = reinterpret_cast<char*>(a.peer_base[d]);
+    uint64_t* hdr = reinterpret_cast<uint64_t*>(base + a.off_hdr) + (size_t)phase * a.W + a.rank;
+    uint32_t rows = (uint32_t)counts_per_dst[d];
+    (void)counts_are_per_src;
+    st_release_sys_u64(hdr, ((uint64_t)a.epoch << 32) | rows);
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// K3: dispatch. One warp per (token): loads the row once, stores it to every remote
+// destination's recv_x[rank][slot], with the k (local expert, weight) entries.
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x,
+                                                       const int* __restrict__ topk_e,
+                                                       const float* __restrict__ topk_w,
+                                                       const int* __restrict__ slot,
+                                                       const int* __restrict__ e2r,
+                                                       const int* __restrict__ e2l,
+                                                       int* __restrict__ self_tok,
+                                                       const int* __restrict__ send_count,
+                                                       int with_meta) {
+  const int lane = threadIdx.x & 31;
+  const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  const int vec = a.H / 8;  // uint4 per row
+  for (int t = gwarp; t < a.T; t += nwarps) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * a.H);
+    // destinations of this token
+    unsigned long long m = 0;
+    for (int j = 0; j < a.k; ++j) m |= 1ull << __ldg(e2r + __ldg(topk_e + t * a.k + j));
+    if ((m >> a.rank) & 1) {
+      if (lane == 0) self_tok[__ldg(slot + (size_t)t * a.W + a.rank)] = t;
+    }
+    unsigned long long remote = m & ~(1ull << a.rank);
+    if (!remote) continue;
+    for (int c0 = 0; c0 < vec; c0 += 32 * 8) {
+      uint4 r[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        int c = c0 + i * 32 + lane;
+        if (c < vec) r[i] = __ldg(src + c);
+      }
+      unsigned long long rm = remote;
+      while (rm) {
+        int d = __ffsll(rm) - 1;
+        rm &= rm - 1;
+        int s = __ldg(slot + (size_t)t * a.W + d);
+        char* base = reinterpret_cast<char*>(a.peer_base[d]);
+        uint4* dst = reinterpret_cast<uint4*>(base + a.off_recv_x) +
+                     ((size_t)a.rank * a.cap + s) * vec;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          int c = c0 + i * 32 + lane;
+          if (c < vec) dst[c] = r[i];
+        }
+      }
+    }
+    if (with_meta && lane < a.k) {
+      const int j = lane;
+      const int e = __ldg(topk_e + t * a.k + j);
+      const int owner = __ldg(e2r + e);
+      const float w = __ldg(topk_w + t * a.k + j);
+      unsigned long long rm = remote;
+      while (rm) {
+        int d = __ffsll(rm) - 1;
+        rm &= rm - 1;
+        int s = __ldg(slot + (size_t)t * a.W + d);
+        char* base = reinterpret_cast<char*>(a.peer_base[d]);
+        int16_t* re = reinterpret_cast<int16_t*>(base + a.off_recv_e) + ((size_t)a.rank * a.cap + s) * a.k;
+        float* rw = reinterpret_cast<float*>(base + a.off_recv_w) + ((size_t)a.rank * a.cap + s) * a.k;
+        re[j] = (owner == d) ? (int16_t)__ldg(e2l + e) : (int16_t)-1;
+        rw[j] = w;
+      }
+    }
+  }
+  publish_last_cta(a.done_counter, a, a.phase, send_count, false);
+}
+
+// ------------------------------------------------------------------------------------
+// Receive side. Rows are enumerated src-major: (src, slot) for slot < rows_from[src].
+// K4a count: per chunk of 128 rows, rows per local expert -> chunk_cnt[chunk][G].
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void row_meta(const EpArgs& a, const int* topk_e, const float* topk_w,
+                                         const int* self_tok, const int* e2r, const int* e2l,
+                                         int src, int s, int j, int* le, float* w) {
+  if (src == a.rank) {
+    const int t = self_tok[s];
+    const int e = __ldg(topk_e + t * a.k + j);
+    *le = (__ldg(e2r + e) == a.rank) ? __ldg(e2l + e) : -1;
+    *w = __ldg(topk_w + t * a.k + j);
+  } else {
+    const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+    const int16_t* re = reinterpret_cast<const int16_t*>(base + a.off_recv_e) + ((size_t)src * a.cap + s) * a.k;
+    const float* rw = reinterpret_cast<const float*>(base + a.off_recv_w) + ((size_t)src * a.cap + s) * a.k;
+    *le = re[j];
+    *w = rw[j];
+  }
+}
+
+constexpr int kChunk = 128;
+
+__global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int* __restrict__ topk_e,
+                                                            const float* __restrict__ topk_w,
+                                                            const int* __restrict__ self_tok,
+                                                            const int* __restrict__ e2r,
+                                                            const int* __restrict__ e2l,
+                                                            const int* __restrict__ send_count,
+                                                            int* __restrict__ rows_from,
+                                                            int* __restrict__ chunk_cnt, int G) {
+  // blockIdx.x = src * chunks_per_src + chunk
+  const int chunks_per_src = (a.cap + kChunk - 1) / kChunk;
+  const int src = blockIdx.x / chunks_per_src;
+  const int chunk = blockIdx.x % chunks_per_src;
+  __shared__ int s_rows;
+  __shared__ int s_cnt[1024];
+  for (int g = threadIdx.x; g < G; g += blockDim.x) s_cnt[g] = 0;
+  if (threadIdx.x == 0) {
+    uint32_t rows = 0;
+    if (src == a.rank) {
+      rows = (uint32_t)send_count[a.rank];
+    } else {
+      const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+      const uint64_t* hdr = reinterpret_cast<const uint64_t*>(base + a.off_hdr) + (size_t)a.phase * a.W + src;
+      if (!wait_header(hdr, a.epoch, &rows, a.status, a.timeout_ns)) rows = 0;
+    }
+    if (rows > (uint32_t)a.cap) {
+      record_error(a.status, kErrOverflow);
+      rows = a.cap;
+    }
+    s_rows = (int)rows;
+    if (chunk == 0) rows_from[src] = (int)rows;
+  }
+  __syncthreads();
+  const int s = chunk * kChunk + threadIdx.x;
+  if (s < s_rows) {
+    for (int j = 0; j < a.k; ++j) {
+      int le;
+      float w;
+      row_meta(a, topk_e, topk_w, self_tok, e2r, e2l, src, s, j, &le, &w);
+      if (le >= 0) atomicAdd(&s_cnt[le], 1);
+    }
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < G; g += blockDim.x)
+    chunk_cnt[(size_t)blockIdx.x * G + g] = s_cnt[g];
+}
+
+// K4b scan (one block): chunk_base[chunk][g] = group_off[g] + rows of g in earlier chunks.
+// group_off is 64-row aligned; pad_off[g] lists the padding rows after each group.
+__global__ void __launch_bounds__(1024) recv_scan_kernel(EpArgs a, int* __restrict__ chunk_cnt,
+                                                         int nchunks, int G,
+                                                         int* __restrict__ group_off,
+                                                         int* __restrict__ group_cnt,
+                                                         int* __restrict__ pad_off,
+                                                         int cap_rows) {
+  __shared__ int s_tot[1024];
+  const int g = threadIdx.x;
+  int tot = 0;
+  if (g < G) {
+    for (int c = 0; c < nchunks; ++c) {
+      int v = chunk_cnt[(size_t)c * G + g];
+      chunk_cnt[(size_t)c * G + g] = tot;  // exclusive within group
+      tot += v;
+    }
+    s_tot[g] = tot;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, pacc = 0;
+    for (int i = 0; i < G; ++i) {
+      group_off[i] = acc;
+      group_cnt[i] = s_tot[i];
+      int padded = (s_tot[i] + 63) & ~63;
+      pad_off[i] = pacc;
+      pacc += padded - s_tot[i];
+      acc += padded;
+    }
+    if (acc > cap_rows) {
+      record_error(a.status, kErrOverflow);
+      // clamp: groups past the capacity become empty
+      int run = 0;
+      for (int i = 0; i < G; ++i) {
+        int padded = (group_cnt[i] + 63) & ~63;
+        if (run + padded > cap_rows) { group_cnt[i] = 0; padded = 0; }
+        group_off[i] = run;
+        run += padded;
+      }
+      acc = run;
+      pacc = 0;
+      for (int i = 0; i < G; ++i) {
+        pad_off[i] = pacc;
+        pacc += ((group_cnt[i] + 63) & ~63) - group_cnt[i];
+      }
+    }
+    group_off[G] = acc;
+    pad_off[G] = pacc;
+  }
+  __syncthreads();
+  if (g < G) {
+    for (int c = 0; c < nchunks; ++c) chunk_cnt[(size_t)c * G + g] += group_off[g];
+  }
+}
+
+// K4c permute: place every (row, local choice) at its deterministic position inside its
+// expert group, copy the row (from the slab or, for self rows, from x), record maps.
+// Also zero-fills the group padding rows.
+__global__ void __launch_bounds__(kChunk) recv_permute_kernel(
+    EpArgs a, const __nv_bfloat16* __restrict__ x, const int* __restrict__ topk_e,
+    const float* __restrict__ topk_w, const int* __restrict__ self_tok, const int* __restrict__ e2r,
+    const int* __restrict__ e2l, const int* __restrict__ rows_from, const int* __restrict__ chunk_base,
+    int G, const int* __restrict__ group_off, const int* __restrict__ group_cnt,
+    const int* __restrict__ pad_off, __nv_bfloat16* __restrict__ xp, float* __restrict__ row_w,
+    int* __restrict__ row_src, int* __restrict__ inv_rows) {
+  const int chunks_per_src = (a.cap + kChunk - 1) / kChunk;
+  const int src = blockIdx.x / chunks_per_src;
+  const int chunk = blockIdx.x % chunks_per_src;
+  const int s = chunk * kChunk + threadIdx.x;
+  const int rows = rows_from[src];
+  __shared__ int s_base[1024];
+  for (int g = threadIdx.x; g < G; g += blockDim.x) s_base[g] = chunk_base[(size_t)blockIdx.x * G + g];
+  __syncthreads();
+  const int vec = a.H / 8;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ int s_pos[kChunk][8];
+  __shared__ int s_le[kChunk];
+  // Positions are deterministic: within an expert group, entries of this chunk are
+  // ordered by (choice j, slot). Each pass j ranks the block's threads sharing a group.
+  for (int j = 0; j < a.k; ++j) {
+    int le = -1;
+    float w = 0.f;
+    if (s < rows) row_meta(a, topk_e, topk_w, self_tok, e2r, e2l, src, s, j, &le, &w);
+    if (le >= G) le = -1;
+    s_le[threadIdx.x] = le;
+    __syncthreads();
+    int pos = -1, before = 0, total = 0;
+    if (le >= 0) {
+      for (int i = 0; i < kChunk; ++i) {
+        const int same = (s_le[i] == le);
+        before += (i < (int)threadIdx.x) & same;
+        total += same;
+      }
+      pos = s_base[le] + before;
+      if (pos - group_off[le] < group_cnt[le]) {
+        row_w[pos] = w;
+        row_src[pos] = src * a.cap + s;
+      } else {
+        pos = -1;  // beyond capacity: dropped (overflow already recorded)
+      }
+    }
+    __syncthreads();  // every thread has read s_base for this pass
+    if (le >= 0 && before == total - 1) s_base[le] += total;  // last of its group advances
+    s_pos[threadIdx.x][j] = pos;
+    if (s < rows) inv_rows[((size_t)src * a.cap + s) * a.k + j] = pos;
+    __syncthreads();
+  }
+  // copy rows: one warp per slot, fanning out to its positions
+  for (int i = warp; i < kChunk; i += blockDim.x / 32) {
+    const int ss = chunk * kChunk + i;
+    if (ss >= rows) break;
+    const uint4* srow;
+    if (src == a.rank) {
+      srow = reinterpret_cast<const uint4*>(x + (size_t)self_tok[ss] * a.H);
+    } else {
+      const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+      srow = reinterpret_cast<const uint4*>(base + a.off_recv_x) + ((size_t)src * a.cap + ss) * vec;
+    }
+    int npos = 0, plist[8];
+    for (int j = 0; j < a.k && j < 8; ++j) {
+      int p = s_pos[i][j];
+      if (p >= 0) plist[npos++] = p;
+    }
+    if (npos == 0) continue;
+    for (int c = lane; c < vec; c += 32) {
+      uint4 v = srow[c];
+      for (int q = 0; q < npos; ++q) reinterpret_cast<uint4*>(xp + (size_t)plist[q] * a.H)[c] = v;
+    }
+  }
+  // zero the padding rows (spread over all blocks)
+  const int npad = pad_off[G];
+  const int gwarp = blockIdx.x * (blockDim.x / 32) + warp;
+  const int nw = gridDim.x * (blockDim.x / 32);
+  for (int q = gwarp; q < npad; q += nw) {
+    // find group: largest g with pad_off[g] <= q
+    int lo = 0, hi = G;
+    while (hi - lo > 1) {
+      int mid = (lo + hi) >> 1;
+      if (pad_off[mid] <= q) lo = mid; else hi = mid;
+    }
+    const int r = group_off[lo] + group_cnt[lo] + (q - pad_off[lo]);
+    uint4 z = make_uint4(0, 0, 0, 0);
+    for (int c = lane; c < vec; c += 32) reinterpret_cast<uint4*>(xp + (size_t)r * a.H)[c] = z;
+    if (lane == 0) {
+      row_w[r] = 0.f;
+      row_src[r] = -1;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Plain gather for the backward: xp[p] = slab row (or dy[self]) for p in every group;
+// padding rows zero.
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) recv_gather_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x,
+                                                          const int* __restrict__ self_tok,
+                                                          const int* __restrict__ row_src,
+                                                          const int* __restrict__ total_rows,
+                                                          const int* __restrict__ send_count,
+                                                          __nv_bfloat16* __restrict__ xp) {
+  // every block first waits for all peers' headers of this phase
+  if (threadIdx.x < a.W) {
+    const int src = threadIdx.x;
+    if (src != a.rank) {
+      const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+      const uint64_t* hdr = reinterpret_cast<const uint64_t*>(base + a.off_hdr) + (size_t)a.phase * a.W + src;
+      uint32_t rows;
+      wait_header(hdr, a.epoch, &rows, a.status, a.timeout_ns);
+    }
+  }
+  __syncthreads();
+  (void)send_count;
+  const int vec = a.H / 8;
+  const int lane = threadIdx.x & 31;
+  const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int R = *total_rows;
+  for (int p = gwarp; p < R; p += nw) {
+    const int code = row_src[p];
+    uint4* dst = reinterpret_cast<uint4*>(xp + (size_t)p * a.H);
+    if (code < 0) {
+      for (int c = lane; c < vec; c += 32) dst[c] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const int src = code / a.cap, s = code % a.cap;
+    const uint4* srow;
+    if (src == a.rank) {
+      srow = reinterpret_cast<const uint4*>(x + (size_t)self_tok[s] * a.H);
+    } else {
+      const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+      srow = reinterpret_cast<const uint4*>(base + a.off_recv_x) + ((size_t)src * a.cap + s) * vec;
+    }
+    for (int c = lane; c < vec; c += 32) dst[c] = srow[c];
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// K6: combine. For each received (src, slot): out = sum_j scale_j * y[inv_rows[j]]
+// (scale_j = gate weight in the forward, 1 in the backward), one bf16 partial row
+// returned to the source's ret_x[rank][slot]; optional per-choice values (router-weight
+// gradients) returned to ret_w.
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) combine_kernel(EpArgs a, const __nv_bfloat16* __restrict__ y,
+                                                      const int* __restrict__ inv_rows,
+                                                      const float* __restrict__ row_w,
+                                                      const int* __restrict__ rows_from,
+                                                      int weighted, const float* __restrict__ row_val,
+                                                      int* __restrict__ done_rows) {
+  const int lane = threadIdx.x & 31;
+  const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int vec = a.H / 8;
+  for (int src = 0; src < a.W; ++src) {
+    const int rows = rows_from[src];
+    char* dbase = reinterpret_cast<char*>(a.peer_base[src]);
+    uint4* ret = reinterpret_cast<uint4*>(dbase + a.off_ret_x) + (size_t)a.rank * a.cap * vec;
+    for (int s = gwarp; s < rows; s += nw) {
+      const int* inv = inv_rows + ((size_t)src * a.cap + s) * a.k;
+      int plist[8];
+      float wl[8];
+      int np = 0;
+      for (int j = 0; j < a.k && j < 8; ++j) {
+        int p = inv[j];
+        if (p >= 0) {
+          plist[np] = p;
+          wl[np] = weighted ? row_w[p] : 1.f;
+          ++np;
+        }
+      }
+      if (row_val && lane < a.k) {
+        int p = inv[lane];
+        float* rw = reinterpret_cast<float*>(dbase + a.off_ret_w) + ((size_t)a.rank * a.cap + s) * a.k;
+        rw[lane] = p >= 0 ? row_val[p] : 0.f;
+      }
+      for (int c = lane; c < vec; c += 32) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int q = 0; q < np; ++q) {
+          uint4 v = reinterpret_cast<const uint4*>(y + (size_t)plist[q] * a.H)[c];
+          float2 f0 = unpack_bf16x2(v.x), f1 = unpack_bf16x2(v.y), f2 = unpack_bf16x2(v.z),
+                 f3 = unpack_bf16x2(v.w);
+          const float w = wl[q];
+          acc[0] += w * f0.x; acc[1] += w * f0.y; acc[2] += w * f1.x; acc[3] += w * f1.y;
+          acc[4] += w * f2.x; acc[5] += w * f2.y; acc[6] += w * f3.x; acc[7] += w * f3.y;
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        ret[(size_t)s * vec + c] = o;
+      }
+    }
+  }
+  publish_last_cta(a.done_counter, a, a.phase, rows_from, true);
+  (void)done_rows;
+}
+
+// ------------------------------------------------------------------------------------
+// K7: source reduce. out[t] = sum_d ret_x[d][slot[t][d]] over the ranks t was sent to,
+// in rank order (deterministic), plus optional residual; per-choice values gathered
+// back into val[t][j] from the rank that owns choice j.
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) source_reduce_kernel(EpArgs a, const int* __restrict__ slot,
+                                                            const int* __restrict__ topk_e,
+                                                            const int* __restrict__ e2r,
+                                                            const __nv_bfloat16* __restrict__ residual,
+                                                            __nv_bfloat16* __restrict__ out,
+                                                            float* __restrict__ val) {
+  if (threadIdx.x < a.W) {
+    const int d = threadIdx.x;
+    const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+    const uint64_t* hdr = reinterpret_cast<const uint64_t*>(base + a.off_hdr) + (size_t)a.phase * a.W + d;
+    uint32_t rows;
+    wait_header(hdr, a.epoch, &rows, a.status, a.timeout_ns);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int vec = a.H / 8;
+  const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+  const uint4* ret = reinterpret_cast<const uint4*>(base + a.off_ret_x);
+  const float* retw = reinterpret_cast<const float*>(base + a.off_ret_w);
+  for (int t = gwarp; t < a.T; t += nw) {
+    int sl[kMaxW];
+    for (int d = 0; d < a.W; ++d) sl[d] = __ldg(slot + (size_t)t * a.W + d);
+    if (val && lane < a.k) {
+      const int j = lane;
+      const int d = __ldg(e2r + __ldg(topk_e + t * a.k + j));
+      val[t * a.k + j] = retw[((size_t)d * a.cap + sl[d]) * a.k + j];
+    }
+    for (int c = lane; c < vec; c += 32) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (residual) {
+        uint4 v = reinterpret_cast<const uint4*>(residual + (size_t)t * a.H)[c];
+        float2 f0 = unpack_bf16x2(v.x), f1 = unpack_bf16x2(v.y), f2 = unpack_bf16x2(v.z), f3 = unpack_bf16x2(v.w);
+        acc[0] = f0.x; acc[1] = f0.y; acc[2] = f1.x; acc[3] = f1.y;
+        acc[4] = f2.x; acc[5] = f2.y; acc[6] = f3.x; acc[7] = f3.y;
+      }
+      for (int d = 0; d < a.W; ++d) {
+        if (sl[d] < 0) continue;
+        uint4 v = ret[((size_t)d * a.cap + sl[d]) * vec + c];
+        float2 f0 = unpack_bf16x2(v.x), f1 = unpack_bf16x2(v.y), f2 = unpack_bf16x2(v.z), f3 = unpack_bf16x2(v.w);
+        acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
+        acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      reinterpret_cast<uint4*>(out + (size_t)t * a.H)[c] = o;
+    }
+  }
+}
+
+// =====================================================================================
+// launchers
+// =====================================================================================
+static void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+void ep_route_plan(const int* topk_e, int T, int k, const int* e2r, int W, int* slot, int* send_count,
+                   cudaStream_t st) {
+  if (W > kMaxW) throw std::runtime_error("EP world size above 64 is not supported");
+  route_plan_kernel<<<1, 1024, 0, st>>>(topk_e, T, k, e2r, W, slot, send_count);
+  check_launch("route_plan");
+}
+
+void ep_dispatch(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w, const int* slot,
+                 const int* e2r, const int* e2l, int* self_tok, const int* send_count, bool with_meta,
+                 cudaStream_t st) {
+  if (a.H % 8) throw std::runtime_error("hidden size must be a multiple of 8");
+  if (a.k > 32) throw std::runtime_error("top-k above 32 is not supported");
+  int blocks = sm_count() * 2;
+  dispatch_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w,
+                                          slot, e2r, e2l, self_tok, send_count, with_meta ? 1 : 0);
+  check_launch("dispatch");
+}
+
+void ep_recv_plan(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w, const int* self_tok,
+                  const int* e2r, const int* e2l, const int* send_count, int G, int cap_rows,
+                  int* rows_from, int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, void* xp,
+                  float* row_w, int* row_src, int* inv_rows, cudaStream_t st) {
+  if (G > 1024) throw std::runtime_error("at most 1024 local experts");
+  if (a.k > 8) throw std::runtime_error("top-k above 8 is not supported by the permute kernel");
+  const int chunks_per_src = (a.cap + kChunk - 1) / kChunk;
+  const int nchunks = chunks_per_src * a.W;
+  recv_count_kernel<<<nchunks, kChunk, 0, st>>>(a, topk_e, topk_w, self_tok, e2r, e2l, send_count, rows_from,
+                                                chunk_cnt, G);
+  check_launch("recv_count");
+  recv_scan_kernel<<<1, 1024, 0, st>>>(a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows);
+  check_launch("recv_scan");
+  recv_permute_kernel<<<nchunks, kChunk, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w,
+                                                  self_tok, e2r, e2l, rows_from, chunk_cnt, G, group_off,
+                                                  group_cnt, pad_off, reinterpret_cast<__nv_bfloat16*>(xp), row_w,
+                                                  row_src, inv_rows);
+  check_launch("recv_permute");
+}
+
+void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const int* row_src, const int* total_rows,
+                    const int* send_count, void* xp, int cap_rows, cudaStream_t st) {
+  int blocks = sm_count() * 2;
+  (void)cap_rows;
+  recv_gather_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), self_tok, row_src,
+                                             total_rows, send_count, reinterpret_cast<__nv_bfloat16*>(xp));
+  check_launch("recv_gather");
+}
+
+void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float* row_w, const int* rows_from,
+                bool weighted, const float* row_val, cudaStream_t st) {
+  int blocks = sm_count() * 2;
+  combine_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(y), inv_rows, row_w, rows_from,
+                                         weighted ? 1 : 0, row_val, nullptr);
+  check_launch("combine");
+}
+
+void ep_source_reduce(const EpArgs& a, const int* slot, const int* topk_e, const int* e2r, const void* residual,
+                      void* out, float* val, cudaStream_t st) {
+  int blocks = sm_count() * 2;
+  source_reduce_kernel<<<blocks, 256, 0, st>>>(a, slot, topk_e, e2r,
+                                               reinterpret_cast<const __nv_bfloat16*>(residual),
+                                               reinterpret_cast<__nv_bfloat16*>(out), val);
+  check_launch("source_reduce");
+}
+
+}  // namespace sepx

@@ -1,0 +1,116 @@
+"""Fused AdamW on the sm_100a kernel (csrc/elementwise.cu).
+
+State precision per parameter:
+
+* ``"fp32"``: fp32 master weights + fp32 moments (16 bytes/param with the bf16 weight).
+* ``"8bit"``: block-wise 8-bit moments (Dettmers et al., ICLR 2022: int8 first moment and
+  uint8 sqrt-second moment, one fp32 absmax scale per 128 values) and stochastic
+  rounding of the bf16 weight (4 bytes/param with the bf16 weight). Used where fp32
+  state does not fit, e.g. all 128 experts of a 30B-parameter MoE on one GPU.
+
+Parameters may also be updated *inside the backward pass* through :meth:`apply_now`:
+the MoE layer hands over each expert weight gradient as soon as its wgrad GEMM is done,
+so no full-model gradient buffer ever exists (the gradient of one layer is transient).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._ext import load
+
+
+class FusedAdamW:
+    def __init__(self, params, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                 state_precision: str | dict = "fp32", max_grad_norm: float | None = None):
+        self.params = [p for p in params]
+        self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
+        self.step_count = 0
+        self.max_grad_norm = max_grad_norm
+        self.state: dict[int, dict] = {}
+        self._precision = state_precision
+        for p in self.params:
+            self._init_state(p)
+
+    def precision_of(self, p) -> str:
+        if isinstance(self._precision, dict):
+            return self._precision.get(id(p), self._precision.get("default", "fp32"))
+        return self._precision
+
+    def _init_state(self, p):
+        prec = getattr(p, "_sepx_state_precision", None) or self.precision_of(p)
+        dev = p.device
+        if prec == "fp32":
+            st = dict(prec="fp32", master=p.detach().float().clone(),
+                      m=torch.zeros(p.shape, device=dev, dtype=torch.float32),
+                      v=torch.zeros(p.shape, device=dev, dtype=torch.float32))
+        elif prec == "8bit":
+            nb = (p.numel() + 127) // 128
+            st = dict(prec="8bit",
+                      mq=torch.zeros(p.numel(), device=dev, dtype=torch.int8),
+                      ms=torch.zeros(nb, device=dev, dtype=torch.float32),
+                      vq=torch.zeros(p.numel(), device=dev, dtype=torch.uint8),
+                      vs=torch.zeros(nb, device=dev, dtype=torch.float32))
+        else:
+            raise ValueError(f"unknown optimizer state precision {prec!r}")
+        self.state[id(p)] = st
+
+    def state_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for st in self.state.values()
+                   for t in st.values() if torch.is_tensor(t))
+
+    # ---------------------------------------------------------------------------
+    def _update(self, p, g, step, grad_scale=1.0):
+        st = self.state[id(p)]
+        C = load()
+        b1, b2 = self.betas
+        g = g.contiguous()
+        if g.dtype != torch.float32:
+            g = g.float()
+        if st["prec"] == "fp32":
+            C.adamw_fp32(p.data, st["master"], g, st["m"], st["v"], self.lr, b1, b2, self.eps, self.wd,
+                         step, grad_scale)
+        else:
+            C.adamw_8bit(p.data, g, st["mq"], st["ms"], st["vq"], st["vs"], self.lr, b1, b2, self.eps,
+                         self.wd, step, grad_scale, id(p) & 0x7FFFFFFF)
+
+    def apply_now(self, p, grad_fp32):
+        """Update ``p`` immediately with ``grad_fp32`` (optimizer-in-backward)."""
+        self._update(p, grad_fp32, self.step_count + 1)
+
+    def step(self):
+        """Update every parameter that has a ``.grad`` (those updated in backward have none)."""
+        self.step_count += 1
+        scale = 1.0
+        if self.max_grad_norm is not None:
+            grads = [p.grad for p in self.params if p.grad is not None]
+            if grads:
+                norm = torch.linalg.vector_norm(torch.stack([g.float().norm() for g in grads]))
+                scale_t = (self.max_grad_norm / (norm + 1e-6)).clamp(max=1.0)
+                for g in grads:
+                    g.mul_(scale_t.to(g.dtype))
+        for p in self.params:
+            if p.grad is None:
+                continue
+            self._update(p, p.grad, self.step_count, scale)
+            p.grad = None
+
+    def zero_grad(self):
+        for p in self.params:
+            p.grad = None
+
+
+def adamw_reference(p, g, m, v, lr, b1, b2, eps, wd, step):
+    """fp32 PyTorch oracle of one AdamW step; returns (p, m, v)."""
+    m = b1 * m + (1 - b1) * g
+    v = b2 * v + (1 - b2) * g * g
+    mh = m / (1 - b1**step)
+    vh = v / (1 - b2**step)
+    p = p * (1 - lr * wd) - lr * mh / (vh.sqrt() + eps)
+    return p, m, v
+
+
+def bytes_per_param(precision: str) -> int:
+    """Optimizer state bytes per parameter (excluding the bf16 weight itself)."""
+    return {"fp32": 12, "8bit": 2}[precision] + (0 if precision == "fp32" else math.ceil(8 / 128))

@@ -1,0 +1,240 @@
+"""Fused expert-parallel MoE over NVLink peer memory (one process per GPU).
+
+Forward of one MoE layer on rank r (all on the device, no host sync):
+
+  route_plan   slot[t][d]: ordinal of token t among the tokens r sends to rank d
+  dispatch     one row per (token, destination rank) stored into the peer's slab,
+               plus the row's (local expert, gate weight) choices; epoch header
+  recv_plan    wait for every source's header, count rows per local expert,
+               place each (row, choice) at a deterministic position of its expert group
+               (64-row aligned, zero padding) and copy the rows (HBM fan-out)
+  gate_up      tcgen05 grouped GEMM + SwiGLU epilogue  -> h, and gu saved for backward
+  down         tcgen05 grouped GEMM                    -> y
+  combine      gate-weighted sum of a token's co-resident experts, ONE partial row
+               per (token, rank) stored back into the source's slab
+  source_reduce  sum of the <= W partials per token in rank order (deterministic)
+
+Backward mirrors it: dy is dispatched to the same slots, gathered into expert order,
+then the fused down-dgrad + SwiGLU-backward GEMM (which also produces the router-weight
+gradient and w*h), the two weight-gradient GEMMs, the gate_up dgrad, and a combine of
+dx plus the router-weight gradients back to the sources.
+
+Reference parity: this is the B200 version of ``RBD_combine_dispatch``
+(src/rbd.py:417-506) with per-rank rather than per-node dedup (one NVSwitch domain);
+the torch reference of the same semantics is ``spec_ep.rbd.dedup_combine_dispatch``.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from ..ops import grouped_gemm as gg
+from ..ops._ext import load
+
+ERRORS = {1: "pipeline barrier timeout", 2: "peer rank never signalled (timeout)", 3: "receive capacity overflow",
+          4: "bad argument"}
+
+
+class EPError(RuntimeError):
+    pass
+
+
+def contiguous_placement(num_experts: int, world: int):
+    """Expert e lives on rank e // (E / world) in local slot e % (E / world) (src/rbd.py:200-202)."""
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not split over {world} ranks")
+    epr = num_experts // world
+    e = torch.arange(num_experts)
+    return (e // epr).int(), (e % epr).int(), [epr] * world
+
+
+@dataclass
+class EPState:
+    """Per-layer plan saved from forward for backward (all device tensors)."""
+
+    T: int
+    slot: torch.Tensor
+    send_count: torch.Tensor
+    self_tok: torch.Tensor
+    topk_e: torch.Tensor
+    topk_w: torch.Tensor
+    rows_from: torch.Tensor
+    group_off: torch.Tensor
+    group_cnt: torch.Tensor
+    xp: torch.Tensor
+    row_w: torch.Tensor
+    row_src: torch.Tensor
+    inv_rows: torch.Tensor
+
+
+class ExpertParallel:
+    """Communicator + plan for one expert-parallel group.
+
+    Args:
+        num_experts: experts of the layer (E).
+        top_k: experts per token.
+        hidden: model width (H).
+        max_tokens: most tokens a rank passes in one call (sizes the symmetric slabs).
+        group: process group of the EP ranks (None = default group, or single GPU).
+        placement: optional ``(e2r, e2l, experts_per_rank)`` from the placement planner.
+        capacity_factor: receive capacity in units of ``max_tokens * top_k`` rows.
+        timeout_s: device-side wait limit before a peer is declared lost.
+    """
+
+    def __init__(self, num_experts, top_k, hidden, max_tokens, group=None, placement=None,
+                 capacity_factor=2.0, timeout_s=10.0, device=None):
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device)
+        self.group = group
+        if dist.is_available() and dist.is_initialized():
+            self.world = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        self.E, self.k, self.H, self.cap = num_experts, top_k, hidden, max_tokens
+        if placement is None:
+            placement = contiguous_placement(num_experts, self.world)
+        e2r, e2l, per_rank = placement
+        self.e2r = e2r.to(self.device, torch.int32)
+        self.e2l = e2l.to(self.device, torch.int32)
+        self.G = int(per_rank[self.rank])
+        C = load()
+        self.comm = C.EpComm(self.world, self.rank, max_tokens, top_k, hidden, self.device.index or 0)
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self.comm.ipc_handle(), group=group)
+            self.comm.open_peers(handles)
+            dist.barrier(group=group)
+        rows = max_tokens * top_k
+        self.cap_rows = min(self.world * rows, int(math.ceil(capacity_factor * rows))) + self.G * 64
+        self.cap_rows = (self.cap_rows + 127) // 128 * 128
+        self.nchunks = self.world * ((max_tokens + 127) // 128)
+        self.timeout_s = float(timeout_s)
+        self.epoch = 0
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.done = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.bytes_sent = 0  # host-side running estimate, updated by stats()
+
+    # -------------------------------------------------------------------------------
+    def check(self):
+        """Raise if any kernel recorded an error (one small device->host read)."""
+        code = int(self.status.item())
+        if code:
+            self.status.zero_()
+            raise EPError(f"expert-parallel kernel error {code}: {ERRORS.get(code, 'unknown')}")
+
+    def close(self):
+        self.comm.close()
+
+    def _args(self):
+        return self.done, self.status, self.timeout_s
+
+    def dispatch_fwd(self, x, topk_e, topk_w) -> EPState:
+        T, dev, W, k = x.shape[0], self.device, self.world, self.k
+        if T > self.cap:
+            raise ValueError(f"{T} tokens exceed the communicator capacity {self.cap}")
+        self.epoch += 1
+        ep = self.epoch
+        slot = torch.empty(T, W, dtype=torch.int32, device=dev)
+        send_count = torch.empty(W, dtype=torch.int32, device=dev)
+        self_tok = torch.empty(self.cap, dtype=torch.int32, device=dev)
+        topk_e = topk_e.int().contiguous()
+        topk_w = topk_w.float().contiguous()
+        self.comm.route_plan(topk_e, self.e2r, slot, send_count)
+        self.comm.dispatch(x, topk_e, topk_w, slot, self.e2r, self.e2l, self_tok, send_count, True, ep,
+                           self.done[0:1], self.status, self.timeout_s)
+        G, R = self.G, self.cap_rows
+        rows_from = torch.empty(W, dtype=torch.int32, device=dev)
+        chunk_cnt = torch.empty(self.nchunks * G, dtype=torch.int32, device=dev)
+        group_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
+        group_cnt = torch.empty(G, dtype=torch.int32, device=dev)
+        pad_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
+        xp = torch.empty(R, self.H, dtype=torch.bfloat16, device=dev)
+        row_w = torch.empty(R, dtype=torch.float32, device=dev)
+        row_src = torch.empty(R, dtype=torch.int32, device=dev)
+        inv_rows = torch.empty(W, self.cap, k, dtype=torch.int32, device=dev)
+        self.comm.recv_plan(x, topk_e, topk_w, self_tok, self.e2r, self.e2l, send_count, G, ep, rows_from,
+                            chunk_cnt, group_off, group_cnt, pad_off, xp, row_w, row_src, inv_rows,
+                            self.done[0:1], self.status, self.timeout_s)
+        return EPState(T, slot, send_count, self_tok, topk_e, topk_w, rows_from, group_off, group_cnt, xp, row_w,
+                       row_src, inv_rows)
+
+    def combine_fwd(self, y, st: EPState, residual=None):
+        out = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
+        self.comm.combine(y, st.inv_rows, st.row_w, st.rows_from, True, None, st.T, self.epoch, self.done[1:2],
+                          self.status, self.timeout_s)
+        self.comm.source_reduce(st.slot, st.topk_e, self.e2r, residual, out, None, self.epoch, self.done[1:2],
+                                self.status, self.timeout_s)
+        return out
+
+    def dispatch_bwd(self, dy, st: EPState):
+        self.epoch += 1
+        ep = self.epoch
+        self.comm.dispatch(dy, st.topk_e, st.topk_w, st.slot, self.e2r, self.e2l, st.self_tok, st.send_count,
+                           False, ep, self.done[0:1], self.status, self.timeout_s)
+        dyp = torch.empty(self.cap_rows, self.H, dtype=torch.bfloat16, device=self.device)
+        self.comm.recv_gather(dy, st.self_tok, st.row_src, st.group_off, st.send_count, dyp, ep, self.done[0:1],
+                              self.status, self.timeout_s)
+        return dyp
+
+    def combine_bwd(self, dxp, row_dw, st: EPState):
+        dx = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
+        dw = torch.empty(st.T, self.k, dtype=torch.float32, device=self.device)
+        self.comm.combine(dxp, st.inv_rows, st.row_w, st.rows_from, False, row_dw, st.T, self.epoch,
+                          self.done[1:2], self.status, self.timeout_s)
+        self.comm.source_reduce(st.slot, st.topk_e, self.e2r, None, dx, dw, self.epoch, self.done[1:2],
+                                self.status, self.timeout_s)
+        return dx, dw
+
+
+class _EPMoE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, topk_w, w_gu, w_d, topk_e, ep: ExpertParallel, grad_sink, residual):
+        st = ep.dispatch_fwd(x.contiguous(), topk_e, topk_w)
+        h, gu = gg.gg_swiglu_fwd(st.xp, w_gu, st.group_off, status=ep.status)
+        y = gg.gg_fwd(h, w_d, st.group_off, status=ep.status)
+        del h
+        out = ep.combine_fwd(y, st, residual)
+        ctx.ep, ctx.st, ctx.sink = ep, st, grad_sink
+        ctx.has_residual = residual is not None
+        ctx.save_for_backward(w_gu, w_d, gu)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        ep, st, sink = ctx.ep, ctx.st, ctx.sink
+        w_gu, w_d, gu = ctx.saved_tensors
+        dout = dout.contiguous()
+        dyp = ep.dispatch_bwd(dout, st)
+        row_dw = torch.zeros(ep.cap_rows, dtype=torch.float32, device=dout.device)
+        dgu, hw, row_dw = gg.gg_swiglu_bwd(dyp, w_d, st.group_off, gu, st.row_w, row_dw=row_dw, status=ep.status)
+        dwd = gg.gg_wgrad(dyp, hw, st.group_off, ep.G, status=ep.status)
+        del hw, dyp
+        dxp = gg.gg_dgrad(dgu, w_gu, st.group_off, status=ep.status)
+        dwgu = gg.gg_wgrad(dgu, st.xp, st.group_off, ep.G, status=ep.status)
+        del dgu
+        dx, dtopk_w = ep.combine_bwd(dxp, row_dw, st)
+        g_gu = g_d = None
+        if sink is not None:
+            sink(w_d, dwd)
+            sink(w_gu, dwgu)
+        else:
+            g_d = dwd.to(w_d.dtype) if ctx.needs_input_grad[3] else None
+            g_gu = dwgu.to(w_gu.dtype) if ctx.needs_input_grad[2] else None
+        ctx.st = None
+        dres = dout if ctx.has_residual else None
+        return dx, dtopk_w, g_gu, g_d, None, None, None, dres
+
+
+def ep_moe(x, topk_e, topk_w, w_gu, w_d, ep: ExpertParallel, grad_sink=None, residual=None):
+    """Expert-parallel SwiGLU MoE: ``out[t] = residual[t] + sum_j w[t,j] * FFN_{e[t,j]}(x[t])``.
+
+    ``w_gu [G, 2I, H]`` and ``w_d [G, H, I]`` hold this rank's ``G`` local experts.
+    ``grad_sink(param, fp32_grad)``, when given, receives the expert weight gradients
+    (e.g. an optimizer applying them immediately) instead of autograd.
+    """
+    return _EPMoE.apply(x, topk_w, w_gu, w_d, topk_e, ep, grad_sink, residual)

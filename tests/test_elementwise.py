@@ -1,0 +1,128 @@
+"""sm_100a memory-bound kernels against fp32 PyTorch references."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
+
+
+@pytest.mark.parametrize("D", [256, 2048])
+def test_rmsnorm_fwd_bwd(D):
+    from spec_ep.ops.norm import rms_norm, rms_norm_reference
+
+    torch.manual_seed(0)
+    x = torch.randn(1000, D, device="cuda").bfloat16().requires_grad_()
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16().requires_grad_()
+    y = rms_norm(x, w)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr, wr = x.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+    yr = rms_norm_reference(xr, wr)
+    yr.backward(g.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(x.grad, xr.grad) < 2e-2
+    assert _rel(w.grad, wr.grad) < 2e-2
+
+
+def test_qk_norm_rope_fwd_bwd():
+    from spec_ep.ops.rope import qk_norm_rope, qk_norm_rope_reference
+
+    torch.manual_seed(0)
+    T, Hq, Hkv = 300, 4, 2
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device="cuda").bfloat16().requires_grad_()
+    wq = (1 + 0.1 * torch.randn(128, device="cuda")).bfloat16().requires_grad_()
+    wk = (1 + 0.1 * torch.randn(128, device="cuda")).bfloat16().requires_grad_()
+    q, k, v = qk_norm_rope(qkv, wq, wk, Hq, Hkv, theta=1e6)
+    gq, gk, gv = torch.randn_like(q), torch.randn_like(k), torch.randn_like(v)
+    (q.float() * gq).sum().add((k.float() * gk).sum()).add((v.float() * gv).sum()).backward()
+    xr = qkv.detach().float().requires_grad_()
+    wqr, wkr = wq.detach().float().requires_grad_(), wk.detach().float().requires_grad_()
+    qr, kr, vr = qk_norm_rope_reference(xr, wqr, wkr, Hq, Hkv, theta=1e6)
+    ((qr * gq.float()).sum() + (kr * gk.float()).sum() + (vr * gv.float()).sum()).backward()
+    assert _rel(q, qr) < 1e-2 and _rel(k, kr) < 1e-2 and _rel(v, vr) < 1e-2
+    assert _rel(qkv.grad, xr.grad) < 2e-2
+    assert _rel(wq.grad, wqr.grad) < 2e-2 and _rel(wk.grad, wkr.grad) < 2e-2
+
+
+def test_swiglu():
+    from spec_ep.ops._ext import load
+
+    C = load()
+    gu = torch.randn(333, 2 * 768, device="cuda").bfloat16()
+    h = torch.empty(333, 768, device="cuda", dtype=torch.bfloat16)
+    C.swiglu_fwd(gu, h)
+    g, u = gu.float()[:, :768], gu.float()[:, 768:]
+    assert _rel(h, torch.nn.functional.silu(g) * u) < 1e-2
+    dh = torch.randn_like(h)
+    dgu = torch.empty_like(gu)
+    C.swiglu_bwd(gu, dh, dgu)
+    gr, ur = g.clone().requires_grad_(), u.clone().requires_grad_()
+    (torch.nn.functional.silu(gr) * ur * dh.float()).sum().backward()
+    assert _rel(dgu[:, :768], gr.grad) < 2e-2 and _rel(dgu[:, 768:], ur.grad) < 2e-2
+
+
+@pytest.mark.parametrize("E,k", [(128, 8), (8, 2), (64, 6)])
+def test_router_topk_fwd_bwd(E, k):
+    from spec_ep.ops.router import router_topk, router_topk_reference
+
+    torch.manual_seed(0)
+    logits = torch.randn(500, E, device="cuda").requires_grad_()
+    w, e = router_topk(logits, k)
+    lr = logits.detach().clone().requires_grad_()
+    wr, er = router_topk_reference(lr, k)
+    assert torch.equal(e.long().sort(-1).values, er.long().sort(-1).values)
+    # align order (both are descending by probability)
+    assert _rel(w, wr) < 1e-5
+    g = torch.randn_like(w)
+    (w * g).sum().backward()
+    (wr * g).sum().backward()
+    assert _rel(logits.grad, lr.grad) < 1e-4
+
+
+def test_xent():
+    from spec_ep.ops.loss import lm_head_xent, lm_head_xent_reference
+
+    torch.manual_seed(0)
+    T, H, V = 256, 256, 4096 + 8
+    h = (torch.randn(T, H, device="cuda") / 4).bfloat16().requires_grad_()
+    w = (torch.randn(V, H, device="cuda") / 16).bfloat16().requires_grad_()
+    labels = torch.randint(0, V, (T,), device="cuda")
+    labels[-3:] = -1
+    loss = lm_head_xent(h, w, labels, num_valid=T - 3)
+    loss.backward()
+    hr, wr = h.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+    lr_ = lm_head_xent_reference(hr, wr, labels)
+    lr_.backward()
+    assert abs(loss.item() - lr_.item()) < 1e-2 * abs(lr_.item())
+    assert _rel(h.grad, hr.grad) < 3e-2
+    assert _rel(w.grad, wr.grad) < 3e-2
+
+
+@pytest.mark.parametrize("prec", ["fp32", "8bit"])
+def test_fused_adamw(prec):
+    from spec_ep.ops.optim import FusedAdamW, adamw_reference
+
+    torch.manual_seed(0)
+    p = torch.nn.Parameter(torch.randn(10000, device="cuda").bfloat16())
+    p0 = p.detach().float().clone()
+    opt = FusedAdamW([p], lr=1e-2, weight_decay=0.1, state_precision=prec)
+    m = torch.zeros_like(p0)
+    v = torch.zeros_like(p0)
+    ref = p0.clone()
+    for step in range(1, 4):
+        g = torch.randn(10000, device="cuda")
+        p.grad = g.bfloat16()
+        opt.step()
+        ref, m, v = adamw_reference(ref, g.bfloat16().float(), m, v, 1e-2, 0.9, 0.95, 1e-8, 0.1, step)
+    st = opt.state[id(p)]
+    if prec == "fp32":
+        assert _rel(st["master"] - p0, ref - p0) < 1e-3
+        assert torch.equal(p.detach(), st["master"].bfloat16())
+    else:
+        # block-wise 8-bit moments + stochastic rounding: mean error well below the update
+        upd = (ref - p0).abs().mean()
+        err = (p.detach().float() - ref).abs().mean()
+        assert err < 0.15 * upd
