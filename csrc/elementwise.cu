@@ -11,11 +11,13 @@
 #include <string>
 
 #include "elementwise.h"
+#include "kernels.h"
 #include "sm100.cuh"
 
 namespace sepx {
 
 static void check(const char* what) {
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }

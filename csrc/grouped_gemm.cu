@@ -34,6 +34,7 @@
 
 #include "sm100.cuh"
 #include "grouped_gemm.h"
+#include "kernels.h"
 
 namespace sepx {
 
@@ -484,6 +485,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
   if (max_tiles > 0 && max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
   kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("grouped_gemm launch: ") + cudaGetErrorString(e));
 }

@@ -7,6 +7,10 @@
 
 namespace sepx {
 
+// Number of kernels launched by this library (incremented by every launcher).
+void note_launch();
+long long launch_count();
+
 // ---------------------------------------------------------------------------------
 // Expert-parallel dispatch/combine (moe_ep.cu)
 // ---------------------------------------------------------------------------------

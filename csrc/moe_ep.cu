@@ -595,6 +595,7 @@ __global__ void __launch_bounds__(256) source_reduce_kernel(EpArgs a, const int*
 // launchers
 // =====================================================================================
 static void check_launch(const char* what) {
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }

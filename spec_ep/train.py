@@ -1,0 +1,95 @@
+"""Training engine: one step = forward, backward, gradient sync, optimizer.
+
+* Expert weights are sharded over the EP group and updated *inside* the backward pass
+  (the MoE layer hands each expert gradient to the optimizer the moment its wgrad GEMM
+  is done), so a full-model expert gradient buffer never exists.
+* Dense weights (attention, router, norms, embeddings) are replicated on every rank;
+  their gradients are all-reduced (NCCL, bucketed) over the data-parallel group, which
+  for pure EP is every rank.
+* Expert replicas across DP groups (EP < world) are all-reduced over the replica group
+  before their in-backward update.
+* Optimizer state precision is chosen per parameter group to fit the memory budget:
+  fp32 master + moments where they fit, block-wise 8-bit moments otherwise.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .ops.optim import FusedAdamW
+
+
+def choose_state_precision(expert_params: int, dense_params: int, budget_bytes: int,
+                           activation_bytes: int) -> str:
+    """Most precise expert optimizer state that fits next to weights and activations."""
+    weights = 2 * (expert_params + dense_params)
+    dense_state = 12 * dense_params
+    for prec, per in (("fp32", 12), ("8bit", 2)):
+        if weights + dense_state + per * expert_params + activation_bytes <= budget_bytes:
+            return prec
+    return "8bit"
+
+
+class Trainer:
+    def __init__(self, model, lr=3e-4, weight_decay=0.1, betas=(0.9, 0.95), expert_state="fp32",
+                 dp_group=None, expert_dp_group=None, bucket_mb=256):
+        self.model = model
+        self.dense = model.dense_parameters()
+        self.experts = model.expert_parameters()
+        for p in self.experts:
+            p._sepx_state_precision = expert_state
+        self.opt = FusedAdamW(self.dense + self.experts, lr=lr, betas=betas, weight_decay=weight_decay,
+                              state_precision="fp32")
+        self.dp_group = dp_group
+        self.expert_dp_group = expert_dp_group
+        self.world = dist.get_world_size(dp_group) if dist.is_initialized() else 1
+        self.expert_world = dist.get_world_size(expert_dp_group) if (dist.is_initialized() and expert_dp_group
+                                                                      is not None) else 1
+        self.bucket_bytes = bucket_mb << 20
+        model.set_grad_sink(self._expert_sink)
+
+    def _expert_sink(self, p, g):
+        if self.expert_world > 1:
+            dist.all_reduce(g, group=self.expert_dp_group)
+            g.mul_(1.0 / self.expert_world)
+        self.opt.apply_now(p, g)
+
+    def _sync_dense_grads(self):
+        if self.world <= 1:
+            return
+        grads = [p.grad for p in self.dense if p.grad is not None]
+        bucket, size = [], 0
+        for g in grads:
+            bucket.append(g)
+            size += g.numel() * g.element_size()
+            if size >= self.bucket_bytes:
+                self._reduce_bucket(bucket)
+                bucket, size = [], 0
+        if bucket:
+            self._reduce_bucket(bucket)
+
+    def _reduce_bucket(self, bucket):
+        flat = torch.cat([g.reshape(-1) for g in bucket])
+        dist.all_reduce(flat, group=self.dp_group)
+        flat.mul_(1.0 / self.world)
+        off = 0
+        for g in bucket:
+            n = g.numel()
+            g.copy_(flat[off:off + n].view_as(g))
+            off += n
+
+    def train_step(self, input_ids, labels, num_valid=None):
+        """One optimizer step on a device-resident batch; returns the (device) loss."""
+        loss = self.model(input_ids, labels, num_valid)
+        loss.backward()
+        self._sync_dense_grads()
+        self.opt.step()
+        return loss.detach()
+
+    def train_step_from_host(self, input_ids_cpu, labels_cpu, num_valid=None):
+        """End-to-end step: pinned host batch -> device, step, loss read back to the host."""
+        dev = self.model.ep.device
+        ids = input_ids_cpu.to(dev, non_blocking=True)
+        lab = labels_cpu.to(dev, non_blocking=True)
+        loss = self.train_step(ids, lab, num_valid)
+        return float(loss.to("cpu"))

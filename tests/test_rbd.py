@@ -1,0 +1,150 @@
+"""CPU / gloo tests of the redundancy-bypassing dispatch/combine API (``spec_ep.rbd``).
+
+Multi-process: each test spawns ranks that rendezvous through a file in tmp_path, and
+simulates nodes with ``dist.new_subgroups`` (as the reference's tests/test_rbd.py:40-43).
+"""
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _init(rank, world, init_file, gpn):
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+    local_group, _ = dist.new_subgroups(group_size=gpn)
+    return local_group
+
+
+def _check_identity(rank, init_file, concurrent):
+    from spec_ep.rbd import RBD_combine_dispatch
+
+    local_group = _init(rank, 4, init_file, 2)
+    torch.manual_seed(rank)
+    T, H, E, k = 16, 4, 8, 3
+    tokens = torch.randn(T, H)
+    weights = torch.rand(T, k)
+    route = torch.rand(T, E).topk(k, dim=-1).indices
+    out = RBD_combine_dispatch(tokens, weights, lambda x, ids: x, route, E=E, gpus_per_node=2,
+                               local_group=local_group, concurrent=concurrent)
+    torch.testing.assert_close(out, tokens * weights.sum(-1, keepdim=True))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("concurrent", [False, True])
+def test_identity_expert_returns_weighted_tokens(tmp_path: Path, concurrent: bool):
+    mp.spawn(_check_identity, args=(tmp_path / "init", concurrent), nprocs=4)
+
+
+def _expert_fn(e_ids, x, w_gu, w_d):
+    I = w_d.shape[2]
+    out = torch.empty_like(x)
+    for e in e_ids.unique().tolist():
+        m = e_ids == e
+        gu = x[m] @ w_gu[e].t()
+        out[m] = (torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]) @ w_d[e].t()
+    return out
+
+
+def _check_config1(rank, init_file, world, gpn, result_q):
+    """Config: hidden 256, 8 SwiGLU experts (inter 512), top-2 softmax, 1024 tokens/rank, fp32."""
+    from spec_ep.rbd import RBD_combine_dispatch, dedup_combine_dispatch, naive_combine_dispatch, plan_traffic
+
+    local_group = _init(rank, world, init_file, gpn)
+    T, H, E, k, I = 1024, 256, 8, 2, 512
+    g = torch.Generator().manual_seed(0)
+    w_router = torch.randn(H, E, generator=g) * 0.02
+    w_gu = torch.randn(E, 2 * I, H, generator=g) / H**0.5
+    w_d = torch.randn(E, H, I, generator=g) / I**0.5
+    torch.manual_seed(100 + rank)
+    tokens = torch.randn(T, H)
+    p = torch.softmax(tokens @ w_router, -1)
+    weights, route = p.topk(k, -1)
+
+    def expert(x, ids):
+        # ids are global expert ids; each rank holds E // world experts
+        return _expert_fn(ids, x, w_gu, w_d)
+
+    out_rbd = RBD_combine_dispatch(tokens, weights, expert, route, E, gpn, local_group, concurrent=True)
+    out_naive = naive_combine_dispatch(tokens, weights, expert, route, E)
+    out_dedup = dedup_combine_dispatch(tokens, weights, expert, route, E)
+    # single-process oracle (all experts local)
+    ref = torch.zeros_like(tokens)
+    for j in range(k):
+        ref += weights[:, j:j + 1] * _expert_fn(route[:, j], tokens, w_gu, w_d)
+    torch.testing.assert_close(out_rbd, ref, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(out_naive, ref, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(out_dedup, ref, rtol=1e-4, atol=1e-5)
+    traffic = plan_traffic(route, E, world, rank, gpn)
+    assert traffic["rank_dedup"] <= traffic["naive"]
+    assert traffic["rbd_inter"] <= traffic["naive"]
+    result_q.put((rank, traffic))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,gpn", [(2, 1), (4, 2)])
+def test_config1_rbd_matches_naive_all2all_with_fewer_rows(tmp_path, world, gpn):
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.spawn(_check_config1, args=(tmp_path / "init", world, gpn, q), nprocs=world)
+    rows = [q.get() for _ in range(world)]
+    naive = sum(t["naive"] for _, t in rows)
+    dedup = sum(t["rank_dedup"] for _, t in rows)
+    assert dedup < naive  # top-2 over 8 experts puts both copies on one rank for some tokens
+
+
+def _check_autograd(rank, init_file):
+    from spec_ep.rbd import RBD_combine_dispatch
+
+    local_group = _init(rank, 4, init_file, 2)
+    T, H, E, k, I = 32, 8, 8, 3, 16
+    g = torch.Generator().manual_seed(0)
+    w_gu = (torch.randn(E, 2 * I, H, generator=g) / 4).requires_grad_()
+    w_d = (torch.randn(E, H, I, generator=g) / 4).requires_grad_()
+    torch.manual_seed(rank)
+    tokens = torch.randn(T, H, requires_grad=True)
+    weights = torch.rand(T, k, requires_grad=True)
+    route = torch.rand(T, E).topk(k, -1).indices
+    out = RBD_combine_dispatch(tokens, weights, lambda x, ids: _expert_fn(ids, x, w_gu, w_d), route, E, 2,
+                               local_group, concurrent=False)
+    gout = torch.randn_like(out)
+    (out * gout).sum().backward()
+    # oracle on this rank's tokens with all experts local; expert grads are summed over
+    # ranks, so compare input grads here and expert grads after an all-reduce
+    t2 = tokens.detach().clone().requires_grad_()
+    w2 = weights.detach().clone().requires_grad_()
+    gu2 = w_gu.detach().clone().requires_grad_()
+    d2 = w_d.detach().clone().requires_grad_()
+    ref = sum(w2[:, j:j + 1] * _expert_fn(route[:, j], t2, gu2, d2) for j in range(k))
+    (ref * gout).sum().backward()
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(tokens.grad, t2.grad, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(weights.grad, w2.grad, rtol=1e-4, atol=1e-5)
+    # expert grads in RBD land on the rank that ran the expert: sum over ranks of both
+    for a, b in ((w_gu.grad, gu2.grad), (w_d.grad, d2.grad)):
+        a = a.clone()
+        dist.all_reduce(a)
+        dist.all_reduce(b)
+        torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5)
+    dist.destroy_process_group()
+
+
+def test_rbd_backward_reaches_tokens_weights_and_experts(tmp_path):
+    mp.spawn(_check_autograd, args=(tmp_path / "init",), nprocs=4)
+
+
+def test_plan_traffic_counts_single_process():
+    from spec_ep.rbd import plan_traffic
+
+    route = torch.tensor([[0, 1, 2], [0, 4, 5], [6, 7, 3]])
+    # E=8, world=4 -> 2 experts per rank; rank 0 owns {0,1}; nodes of 2 ranks
+    t = plan_traffic(route, 8, 4, 0, 2)
+    # naive: copies not on rank 0: [2]->1, [4,5]->2, [6,7,3]->3 => 1+2+3 = 6
+    assert t["naive"] == 6
+    # dedup: token0 -> {1}, token1 -> {2}, token2 -> {3,1} => 4
+    assert t["rank_dedup"] == 4
+    # rbd_inter: other node = ranks {2,3}: token1 (node1), token2 (node1) => 2
+    assert t["rbd_inter"] == 2
+    # rbd_intra: same-node copies to rank 1: token0 expert 2, token2 expert 3 => 2
+    assert t["rbd_intra"] == 2
