@@ -1,5 +1,5 @@
 // Inline-PTX wrappers for the Blackwell (sm_100a) features the kernels use:
-// mbarriers, TMA tiled loads (no multicast anywhere), tcgen05 MMA / TMEM, and
+// mbarriers, TMA tiled loads (single-CTA destinations only), tcgen05 MMA / TMEM, and
 // bounded waits that report a timeout instead of spinning forever.
 //
 // Every wait in this file has a deadline measured with %globaltimer. On expiry the
@@ -94,7 +94,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ----------------------------------------------------------------------------------
-// TMA (tiled, local memory only, never multicast)
+// TMA (tiled, local memory only, one destination CTA)
 // ----------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");

@@ -1,0 +1,103 @@
+"""Expert parallelism over NVLink peer memory on 2+ GPUs (child processes, NCCL bootstrap).
+
+Each rank holds E / world experts; outputs and gradients are compared with an fp32
+single-process reference that holds all experts.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
+
+
+def _moe_ref(x, te, tw, w_gu, w_d):
+    I = w_d.shape[2]
+    out = torch.zeros(x.shape, device=x.device)
+    for j in range(te.shape[1]):
+        for e in te[:, j].unique().tolist():
+            m = te[:, j] == e
+            gu = x[m] @ w_gu[e].t()
+            out[m] += tw[m, j:j + 1] * ((torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]) @ w_d[e].t())
+    return out
+
+
+def _worker(rank, world, port, T, E, k, H, I, skew, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        from spec_ep.parallel.ep import ExpertParallel, ep_moe
+
+        g = torch.Generator().manual_seed(0)
+        w_gu_full = (torch.randn(E, 2 * I, H, generator=g) / H**0.5).bfloat16().to(dev)
+        w_d_full = (torch.randn(E, H, I, generator=g) / I**0.5).bfloat16().to(dev)
+        epr = E // world
+        w_gu = w_gu_full[rank * epr:(rank + 1) * epr].clone().requires_grad_()
+        w_d = w_d_full[rank * epr:(rank + 1) * epr].clone().requires_grad_()
+        torch.manual_seed(10 + rank)
+        x = torch.randn(T, H, device=dev).bfloat16().requires_grad_()
+        logits = torch.randn(T, E, device=dev)
+        if skew:  # make rank 0's experts hot
+            logits[:, :epr] += 2.0
+        p = torch.softmax(logits, -1)
+        tw, te = p.topk(k, -1)
+        tw = (tw / tw.sum(-1, keepdim=True)).requires_grad_()
+        ep = ExpertParallel(E, k, H, max_tokens=T, device=dev, capacity_factor=float(world))
+        for _ in range(2):  # run twice: epochs advance, buffers are reused
+            out = ep_moe(x, te.int(), tw, w_gu, w_d, ep)
+            gout = torch.randn(out.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(rank))
+            x.grad = tw.grad = w_gu.grad = w_d.grad = None
+            out.backward(gout.bfloat16())
+        torch.cuda.synchronize()
+        ep.check()
+        xr = x.detach().float().requires_grad_()
+        twr = tw.detach().clone().requires_grad_()
+        gur = w_gu_full.float().requires_grad_()
+        dr = w_d_full.float().requires_grad_()
+        ref = _moe_ref(xr, te, twr, gur, dr)
+        ref.backward(gout.bfloat16().float())
+        gg, dd = gur.grad.clone(), dr.grad.clone()
+        dist.all_reduce(gg)
+        dist.all_reduce(dd)
+        assert _rel(out, ref) < 2e-2, _rel(out, ref)
+        assert _rel(x.grad, xr.grad) < 3e-2
+        assert _rel(tw.grad, twr.grad) < 3e-2
+        assert _rel(w_gu.grad, gg[rank * epr:(rank + 1) * epr]) < 3e-2
+        assert _rel(w_d.grad, dd[rank * epr:(rank + 1) * epr]) < 3e-2
+        dist.barrier()
+        ep.close()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent, never hang it
+        import traceback
+
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+@pytest.mark.parametrize("skew", [False, True])
+def test_ep_moe_two_or_more_gpus(skew):
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(n, 4)
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.spawn(_worker, args=(world, _free_port(), 1024, 16, 4, 512, 256, skew, errq), nprocs=world, join=True)
+    assert errq.empty()
