@@ -675,3 +675,116 @@ void ep_source_reduce(const EpArgs& a, const int* slot, const int* topk_e, const
 }
 
 }  // namespace sepx
+
+// =====================================================================================
+// Allocation-free variant of the world-size-1 dispatch (declared in moe_noalloc.h; it has
+// no counterpart in the reference). Every temporary lives in one static device array;
+// the entry point calls no allocator. See moe_noalloc.h for limits and semantics.
+// =====================================================================================
+#include <cstdio>
+#include <mutex>
+
+#include "moe_noalloc.h"
+
+namespace {
+
+constexpr int kNaMaxT = 8192;
+constexpr int kNaMaxE = 256;
+constexpr int kNaMaxChunks = kNaMaxT / sepx::kChunk;
+// word offsets inside the scratch array
+constexpr int kNaSlot = 0;                              // [T]   slot of each token (all go to rank 0)
+constexpr int kNaSelfTok = kNaSlot + kNaMaxT;           // [T]   slot -> token
+constexpr int kNaSendCount = kNaSelfTok + kNaMaxT;      // [1]
+constexpr int kNaRowsFrom = kNaSendCount + 64;          // [1]
+constexpr int kNaGroupCnt = kNaRowsFrom + 64;           // [E]
+constexpr int kNaPadOff = kNaGroupCnt + kNaMaxE;        // [E + 1]
+constexpr int kNaE2R = kNaPadOff + kNaMaxE + 64;        // [E]   expert -> rank (all 0)
+constexpr int kNaE2L = kNaE2R + kNaMaxE;                // [E]   expert -> local slot (identity)
+constexpr int kNaChunkCnt = kNaE2L + kNaMaxE;           // [chunks * E]
+constexpr int kNaWords = kNaChunkCnt + kNaMaxChunks * kNaMaxE;  // 34,176 words = 136,704 bytes
+
+}  // namespace
+
+static __device__ __align__(256) int g_sepx_noalloc_scratch[kNaWords];
+
+namespace {
+
+__global__ void noalloc_init_kernel(int* scratch, int T, int E) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kNaMaxT; i += gridDim.x * blockDim.x) {
+    if (i < T) scratch[kNaSelfTok + i] = i;  // world size 1: token t has slot t
+    if (i < E) {
+      scratch[kNaE2R + i] = 0;
+      scratch[kNaE2L + i] = i;
+    }
+  }
+}
+
+int* noalloc_scratch_for_current_device(int* dev_out) {
+  static int* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  *dev_out = dev;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_sepx_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+int noalloc_fail(int code, const char* msg) {
+  std::fprintf(stderr, "sepx_moe_permute_noalloc: %s (code %d)\n", msg, code);
+  return code;
+}
+
+}  // namespace
+
+extern "C" int sepx_moe_permute_noalloc(const void* x, const int* topk_e, const float* topk_w, int T, int k,
+                                        int H, int E, void* xp, int cap_rows, int* group_off, float* row_w,
+                                        int* row_src, int* inv_rows, int* status, cudaStream_t stream) {
+  using namespace sepx;
+  if (T < 1 || T > kNaMaxT) return noalloc_fail(1, "T must be in [1, 8192]");
+  if (k < 1 || k > 8) return noalloc_fail(2, "k must be in [1, 8]");
+  if (E < 1 || E > kNaMaxE) return noalloc_fail(3, "E must be in [1, 256]");
+  if (H < 8 || H % 8) return noalloc_fail(4, "H must be a positive multiple of 8");
+  if ((long long)cap_rows < (long long)T * k + 64LL * E) return noalloc_fail(5, "cap_rows must be >= T*k + 64*E");
+  if (!x || !topk_e || !topk_w || !xp || !group_off || !row_w || !row_src || !inv_rows || !status)
+    return noalloc_fail(6, "null pointer argument");
+  int dev = -1;
+  int* s = noalloc_scratch_for_current_device(&dev);
+  if (!s) return noalloc_fail(7, "cudaGetSymbolAddress failed for the scratch array on the current device");
+
+  const int nchunks = (T + kChunk - 1) / kChunk;
+  EpArgs a;
+  for (int i = 0; i < 64; ++i) a.peer_base[i] = nullptr;
+  a.W = 1;
+  a.rank = 0;
+  a.cap = T;
+  a.k = k;
+  a.H = H;
+  a.T = T;
+  a.phase = 0;
+  a.epoch = 0;
+  a.status = status;
+
+  cudaMemsetAsync(status, 0, sizeof(int), stream);
+  noalloc_init_kernel<<<(kNaMaxT + 255) / 256, 256, 0, stream>>>(s, T, E);
+  route_plan_kernel<<<1, 1024, 0, stream>>>(topk_e, T, k, s + kNaE2R, 1, s + kNaSlot, s + kNaSendCount);
+  recv_count_kernel<<<nchunks, kChunk, 0, stream>>>(a, topk_e, topk_w, s + kNaSelfTok, s + kNaE2R, s + kNaE2L,
+                                                    s + kNaSendCount, s + kNaRowsFrom, s + kNaChunkCnt, E);
+  recv_scan_kernel<<<1, 1024, 0, stream>>>(a, s + kNaChunkCnt, nchunks, E, group_off, s + kNaGroupCnt,
+                                           s + kNaPadOff, cap_rows);
+  recv_permute_kernel<<<nchunks, kChunk, 0, stream>>>(
+      a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w, s + kNaSelfTok, s + kNaE2R, s + kNaE2L,
+      s + kNaRowsFrom, s + kNaChunkCnt, E, group_off, s + kNaGroupCnt, s + kNaPadOff,
+      reinterpret_cast<__nv_bfloat16*>(xp), row_w, row_src, inv_rows);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "sepx_moe_permute_noalloc: launch failed: %s\n", cudaGetErrorString(e));
+    return 100 + (int)e;
+  }
+  return 0;
+}
