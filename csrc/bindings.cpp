@@ -7,6 +7,7 @@
 
 #include "grouped_gemm.h"
 #include "kernels.h"
+#include "opt_bind.h"
 
 namespace {
 
@@ -186,6 +187,37 @@ void gg_wgrad(const at::Tensor& A, const at::Tensor& B, const at::Tensor& group_
   sepx::grouped_gemm_ragged_k(c, cur_stream());
 }
 
+// W[g] <- AdamW(W[g], A[rows_g]^T . B[rows_g]): weight gradient with the optimizer update
+// fused into the GEMM epilogue (the gradient never reaches HBM). W is [G, M, N].
+void gg_wgrad_adamw(const at::Tensor& A, const at::Tensor& B, const at::Tensor& group_off, at::Tensor& W,
+                    int64_t kind, const c10::optional<at::Tensor>& master, at::Tensor& m, at::Tensor& v,
+                    const c10::optional<at::Tensor>& ms, const c10::optional<at::Tensor>& vs, double lr, double b1,
+                    double b2, double eps, double wd, int64_t step, double grad_scale, int64_t seed,
+                    const c10::optional<at::Tensor>& status) {
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_BF16(W);
+  TORCH_CHECK(W.dim() == 3, "W must be [G, M, N]");
+  const c10::cuda::CUDAGuard guard(A.device());
+  sepx::GemmCall c;
+  c.epi = sepx::kEpiAdamW;
+  c.A = A.data_ptr();
+  c.a_rows = A.size(0);
+  c.lda = A.size(1);
+  c.B = B.data_ptr();
+  c.b_rows = B.size(0);
+  c.ldb = B.size(1);
+  c.b_kmajor = false;
+  c.p.group_off = group_off.data_ptr<int>();
+  c.p.G = W.size(0);
+  c.p.M = W.size(1);
+  c.p.N = W.size(2);
+  TORCH_CHECK(A.size(1) == c.p.M && B.size(1) == c.p.N, "shape mismatch");
+  c.p.status = status_ptr(status);
+  c.p.opt = sepx::make_opt(W, kind, master, m, v, ms, vs, lr, b1, b2, eps, wd, step, grad_scale, seed);
+  sepx::grouped_gemm_wgrad_adamw(c, cur_stream());
+}
+
 }  // namespace
 
 void register_kernels(pybind11::module& m);
@@ -197,5 +229,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gg_swiglu_fwd", &gg_swiglu_fwd);
   m.def("gg_swiglu_bwd", &gg_swiglu_bwd);
   m.def("gg_wgrad", &gg_wgrad);
+  m.def("gg_wgrad_adamw", &gg_wgrad_adamw);
   register_kernels(m);
 }

@@ -10,6 +10,7 @@
 #include <stdexcept>
 #include <string>
 
+#include "adamw_math.cuh"
 #include "elementwise.h"
 #include "kernels.h"
 #include "sm100.cuh"
@@ -525,106 +526,75 @@ void router_bwd(const float* probs, const int* topk_e, const float* dw, int T, i
 }
 
 // =====================================================================================
-// Fused AdamW.
-//  * fp32 state: master (optional, fp32), m, v fp32. Param stored bf16 (and the master
-//    copy when present).
-//  * 8-bit state: m and v quantised per block of 128 values with an fp32 absmax scale
-//    (block-wise quantisation, Dettmers et al., ICLR 2022): m linearly as int8, v as
-//    uint8 of sqrt(v) (sqrt keeps the dynamic range of the second moment). No master
-//    copy; the bf16 parameter is updated with stochastic rounding.
+// Fused AdamW (standalone). The per-block math is adamw_block32 (adamw_math.cuh), shared
+// with the weight-gradient GEMM epilogue that applies the same update in place.
+//  * fp32 state: one thread per 4 elements (vectorised), any size; grads fp32 or bf16.
+//  * 8-bit state: one thread per 32-element quantisation block; size % 32 == 0.
 // =====================================================================================
-__device__ __forceinline__ uint32_t hash32(uint32_t x) {
-  // integer finaliser (murmur3 fmix32)
-  x ^= x >> 16;
-  x *= 0x85ebca6bu;
-  x ^= x >> 13;
-  x *= 0xc2b2ae35u;
-  x ^= x >> 16;
-  return x;
-}
-__device__ __forceinline__ __nv_bfloat16 bf16_stochastic(float x, uint32_t rnd) {
-  uint32_t u = __float_as_uint(x);
-  // add random bits below the bf16 mantissa, then truncate
-  u += (rnd & 0xFFFFu);
-  u &= 0xFFFF0000u;
-  return __ushort_as_bfloat16((unsigned short)(u >> 16));
+template <typename G>
+__device__ __forceinline__ float grad_at(const G* g, size_t i);
+template <>
+__device__ __forceinline__ float grad_at<float>(const float* g, size_t i) { return g[i]; }
+template <>
+__device__ __forceinline__ float grad_at<__nv_bfloat16>(const __nv_bfloat16* g, size_t i) {
+  return __bfloat162float(g[i]);
 }
 
-__global__ void adamw_fp32_kernel(__nv_bfloat16* __restrict__ p, float* __restrict__ master, const float* __restrict__ g,
-                                  float* __restrict__ m, float* __restrict__ v, size_t n, AdamWHyper h) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-    const float gi = g[i] * h.grad_scale;
-    const float mi = h.beta1 * m[i] + (1.f - h.beta1) * gi;
-    const float vi = h.beta2 * v[i] + (1.f - h.beta2) * gi * gi;
-    m[i] = mi;
-    v[i] = vi;
-    float w = master ? master[i] : __bfloat162float(p[i]);
-    w = w * (1.f - h.lr * h.weight_decay) - h.lr * (mi * h.bc1) / (sqrtf(vi * h.bc2) + h.eps);
-    if (master) master[i] = w;
-    p[i] = __float2bfloat16(w);
-  }
-}
-
-__global__ void __launch_bounds__(256) adamw_8bit_kernel(__nv_bfloat16* __restrict__ p, const float* __restrict__ g,
-                                                         int8_t* __restrict__ mq, float* __restrict__ ms,
-                                                         uint8_t* __restrict__ vq, float* __restrict__ vs, size_t n,
-                                                         AdamWHyper h) {
-  // one warp per block of 128 values (4 per lane)
-  const int lane = threadIdx.x & 31;
-  const size_t nb = (n + 127) / 128;
-  const size_t nw = (size_t)gridDim.x * (blockDim.x >> 5);
-  for (size_t b = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5; b < nb; b += nw) {
-    const float msc = ms[b], vsc = vs[b];
-    float mi[4], vi[4];
-    float mmax = 0.f, vmax = 0.f;
+template <typename G>
+__device__ __forceinline__ void load_grad32(const G* g, size_t base, float (&out)[32]) {
+  if constexpr (sizeof(G) == 4) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const size_t i = b * 128 + e * 32 + lane;
-      if (i < n) {
-        const float gi = g[i] * h.grad_scale;
-        const float m0 = (float)mq[i] * msc * (1.f / 127.f);
-        const float sv = (float)vq[i] * vsc * (1.f / 255.f);
-        const float v0 = sv * sv;
-        mi[e] = h.beta1 * m0 + (1.f - h.beta1) * gi;
-        vi[e] = h.beta2 * v0 + (1.f - h.beta2) * gi * gi;
-        float w = __bfloat162float(p[i]);
-        w = w * (1.f - h.lr * h.weight_decay) - h.lr * (mi[e] * h.bc1) / (sqrtf(vi[e] * h.bc2) + h.eps);
-        p[i] = bf16_stochastic(w, hash32((uint32_t)i * 2654435761u ^ (uint32_t)h.step * 0x9E3779B9u ^ h.seed));
-      } else {
-        mi[e] = 0.f;
-        vi[e] = 0.f;
-      }
-      mmax = fmaxf(mmax, fabsf(mi[e]));
-      vmax = fmaxf(vmax, sqrtf(vi[e]));
+    for (int q = 0; q < 8; ++q) {
+      float4 g4 = reinterpret_cast<const float4*>(g + base)[q];
+      out[4 * q] = g4.x; out[4 * q + 1] = g4.y; out[4 * q + 2] = g4.z; out[4 * q + 3] = g4.w;
     }
-    mmax = warp_max(mmax);
-    vmax = warp_max(vmax);
-    const float minv = mmax > 0.f ? 127.f / mmax : 0.f;
-    const float vinv = vmax > 0.f ? 255.f / vmax : 0.f;
+  } else {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const size_t i = b * 128 + e * 32 + lane;
-      if (i < n) {
-        mq[i] = (int8_t)__float2int_rn(mi[e] * minv);
-        vq[i] = (uint8_t)min(255, __float2int_rn(sqrtf(vi[e]) * vinv));
+    for (int q = 0; q < 4; ++q) {
+      uint4 g8 = reinterpret_cast<const uint4*>(g + base)[q];
+      uint32_t w4[4] = {g8.x, g8.y, g8.z, g8.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = unpack_bf16x2(w4[e]);
+        out[8 * q + 2 * e] = f.x;
+        out[8 * q + 2 * e + 1] = f.y;
       }
-    }
-    if (lane == 0) {
-      ms[b] = mmax;
-      vs[b] = vmax;
     }
   }
 }
 
-void adamw_fp32(void* p, float* master, const float* g, float* m, float* v, size_t n, const AdamWHyper& h, int num_sms,
-                cudaStream_t st) {
-  adamw_fp32_kernel<<<num_sms * 8, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(p), master, g, m, v, n, h);
-  check("adamw_fp32");
+// One thread per 32-element block (fp32 or 8-bit state); scalar tail for fp32 state.
+template <typename G>
+__global__ void __launch_bounds__(256) adamw_kernel(const G* __restrict__ g, size_t n, OptHyper h) {
+  const size_t nb = n / 32;
+  for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < nb; b += (size_t)gridDim.x * blockDim.x) {
+    float gg[32];
+    load_grad32(g, b * 32, gg);
+    adamw_block32(gg, b * 32, h);
+  }
+  if (h.kind == kOptFp32) {
+    float* mm = reinterpret_cast<float*>(h.m);
+    float* vv = reinterpret_cast<float*>(h.v);
+    for (size_t i = nb * 32 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+      float m = mm[i], v = vv[i], sq;
+      const float w = adamw_step_elem(h.master[i], __fmul_rn(grad_at(g, i), h.grad_scale), m, v, sq, h);
+      h.master[i] = w;
+      mm[i] = m;
+      vv[i] = v;
+      h.param[i] = __float2bfloat16(w);
+    }
+  }
 }
-void adamw_8bit(void* p, const float* g, int8_t* mq, float* ms, uint8_t* vq, float* vs, size_t n, const AdamWHyper& h,
-                int num_sms, cudaStream_t st) {
-  adamw_8bit_kernel<<<num_sms * 8, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(p), g, mq, ms, vq, vs, n, h);
-  check("adamw_8bit");
+
+void adamw_update(const OptHyper& h, const void* g, bool g_bf16, size_t n, int num_sms, cudaStream_t st) {
+  if (h.kind != kOptFp32 && h.kind != kOpt8bit) throw std::runtime_error("unknown optimizer state kind");
+  if (h.kind == kOpt8bit && n % 32) throw std::runtime_error("8-bit AdamW needs a multiple of 32 elements");
+  const size_t blocks_needed = (n / 32 + 255) / 256 + 1;
+  const int grid = (int)std::min<size_t>(blocks_needed, (size_t)num_sms * 16);
+  if (g_bf16) adamw_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(g), n, h);
+  else adamw_kernel<float><<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(g), n, h);
+  check("adamw");
 }
 
 // =====================================================================================

@@ -4,15 +4,9 @@
 #include <stddef.h>
 #include <stdint.h>
 
-namespace sepx {
+#include "opt_hyper.h"
 
-struct AdamWHyper {
-  float lr = 1e-4f, beta1 = 0.9f, beta2 = 0.95f, eps = 1e-8f, weight_decay = 0.1f;
-  float bc1 = 1.f, bc2 = 1.f;  // 1/(1-beta1^t), 1/(1-beta2^t)
-  float grad_scale = 1.f;
-  int step = 1;
-  uint32_t seed = 0;
-};
+namespace sepx {
 
 void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int N, int D, float eps, cudaStream_t st);
 void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, void* dx, float* dw, int N, int D,
@@ -29,10 +23,8 @@ void router_topk(const float* logits, const float* bias, int T, int E, int k, bo
                  float* topk_w, float* probs, cudaStream_t st);
 void router_bwd(const float* probs, const int* topk_e, const float* dw, int T, int E, int k, bool renorm,
                 float* dlogits, cudaStream_t st);
-void adamw_fp32(void* p, float* master, const float* g, float* m, float* v, size_t n, const AdamWHyper& h,
-                int num_sms, cudaStream_t st);
-void adamw_8bit(void* p, const float* g, int8_t* mq, float* ms, uint8_t* vq, float* vs, size_t n,
-                const AdamWHyper& h, int num_sms, cudaStream_t st);
+// AdamW over n contiguous elements; h.kind selects fp32 or block-wise 8-bit state.
+void adamw_update(const OptHyper& h, const void* g, bool g_bf16, size_t n, int num_sms, cudaStream_t st);
 void xent_fwd_bwd(void* logits, const int* labels, int T, int V, float scale, float* loss, cudaStream_t st);
 
 }  // namespace sepx

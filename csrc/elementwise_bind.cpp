@@ -4,6 +4,7 @@
 #include <torch/extension.h>
 
 #include "elementwise.h"
+#include "opt_bind.h"
 
 namespace {
 
@@ -105,44 +106,14 @@ void router_bwd(const at::Tensor& probs, const at::Tensor& topk_e, const at::Ten
                    topk_e.size(1), renorm, dlogits.data_ptr<float>(), cs());
 }
 
-sepx::AdamWHyper hyper(double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale,
-                       int64_t seed) {
-  sepx::AdamWHyper h;
-  h.lr = lr;
-  h.beta1 = b1;
-  h.beta2 = b2;
-  h.eps = eps;
-  h.weight_decay = wd;
-  h.step = step;
-  h.bc1 = 1.0 / (1.0 - std::pow(b1, (double)step));
-  h.bc2 = 1.0 / (1.0 - std::pow(b2, (double)step));
-  h.grad_scale = grad_scale;
-  h.seed = (uint32_t)seed;
-  return h;
-}
-
-void adamw_fp32(at::Tensor& p, const c10::optional<at::Tensor>& master, const at::Tensor& g, at::Tensor& m, at::Tensor& v,
-                double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale) {
-  req(p, at::kBFloat16, "param");
-  req(g, at::kFloat, "grad");
-  req(m, at::kFloat, "exp_avg");
-  req(v, at::kFloat, "exp_avg_sq");
-  TORCH_CHECK(g.numel() == p.numel() && m.numel() == p.numel(), "size mismatch");
-  float* mp = master.has_value() ? master->data_ptr<float>() : nullptr;
-  sepx::adamw_fp32(p.data_ptr(), mp, g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), p.numel(),
-                   hyper(lr, b1, b2, eps, wd, step, grad_scale, 0), num_sms(), cs());
-}
-
-void adamw_8bit(at::Tensor& p, const at::Tensor& g, at::Tensor& mq, at::Tensor& ms, at::Tensor& vq, at::Tensor& vs,
-                double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale, int64_t seed) {
-  req(p, at::kBFloat16, "param");
-  req(g, at::kFloat, "grad");
-  req(mq, at::kChar, "exp_avg_q");
-  req(vq, at::kByte, "exp_avg_sq_q");
-  TORCH_CHECK(ms.numel() >= (p.numel() + 127) / 128, "scale size");
-  sepx::adamw_8bit(p.data_ptr(), g.data_ptr<float>(), mq.data_ptr<int8_t>(), ms.data_ptr<float>(),
-                   vq.data_ptr<uint8_t>(), vs.data_ptr<float>(), p.numel(),
-                   hyper(lr, b1, b2, eps, wd, step, grad_scale, seed), num_sms(), cs());
+void adamw_update(at::Tensor& p, const at::Tensor& g, int64_t kind, const c10::optional<at::Tensor>& master,
+                  at::Tensor& m, at::Tensor& v, const c10::optional<at::Tensor>& ms, const c10::optional<at::Tensor>& vs,
+                  double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale,
+                  int64_t seed) {
+  TORCH_CHECK(g.is_cuda() && g.is_contiguous() && g.numel() == p.numel(), "grad must match the parameter");
+  TORCH_CHECK(g.scalar_type() == at::kFloat || g.scalar_type() == at::kBFloat16, "grad must be fp32 or bf16");
+  auto h = sepx::make_opt(p, kind, master, m, v, ms, vs, lr, b1, b2, eps, wd, step, grad_scale, seed);
+  sepx::adamw_update(h, g.data_ptr(), g.scalar_type() == at::kBFloat16, p.numel(), num_sms(), cs());
 }
 
 void xent_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, double scale, at::Tensor& loss) {
@@ -165,7 +136,6 @@ void register_elementwise(pybind11::module& m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("router_topk", &router_topk);
   m.def("router_bwd", &router_bwd);
-  m.def("adamw_fp32", &adamw_fp32);
-  m.def("adamw_8bit", &adamw_8bit);
+  m.def("adamw_update", &adamw_update);
   m.def("xent_fwd_bwd", &xent_fwd_bwd);
 }

@@ -32,6 +32,7 @@
 #include <stdexcept>
 #include <string>
 
+#include "adamw_math.cuh"
 #include "sm100.cuh"
 #include "grouped_gemm.h"
 #include "kernels.h"
@@ -40,14 +41,18 @@ namespace sepx {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                 // two warps per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI>
 struct GemmSmem {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  // epilogues that transpose 32x32 accumulator blocks through shared memory
+  static constexpr int EPI_STAGE_OFF = STAGES * STAGE_BYTES;
+  static constexpr int EPI_STAGE_BYTES = (EPI == kEpiAdamW || EPI == kEpiF32) ? kEpiWarps * 32 * 33 * 4 : 0;
+  static constexpr int BAR_OFF = EPI_STAGE_OFF + EPI_STAGE_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
   static constexpr int PREFIX_OFF = MISC_OFF + 16;
@@ -109,7 +114,7 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -146,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);
+      mbar_init(&tempty_bar[a], kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     *s_abort = 0;
@@ -268,6 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // --------------------------------- epilogue --------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which of the two warps on this quarter
+    constexpr int kCStep = kEpiWarps / 4;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
@@ -282,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (EPI == kEpiBf16) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += kCStep) {
           float v[32];
           tmem_ld32(t_row + c * 32, v);
           if (valid) {
@@ -299,24 +306,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if (EPI == kEpiF32) {
+        // Transpose each 32x32 fp32 block through shared memory so every store is one
+        // row's 32 contiguous floats (128 bytes per warp instruction).
         float* out = reinterpret_cast<float*>(p.out);
+        float* tile = reinterpret_cast<float*>(smem + L::EPI_STAGE_OFF) + (warp - 2) * 32 * 33;
+        const size_t row_base = ((size_t)ti.g * p.M + ti.row0 + q * 32) * (size_t)p.ldo;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += kCStep) {
           float v[32];
           tmem_ld32(t_row + c * 32, v);
-          if (valid) {
-            float4* dst = reinterpret_cast<float4*>(
-                out + ((size_t)ti.g * p.M + r) * p.ldo + ti.n0 + c * 32);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float4 w;
-              w.x = zero ? 0.f : v[4 * j + 0];
-              w.y = zero ? 0.f : v[4 * j + 1];
-              w.z = zero ? 0.f : v[4 * j + 2];
-              w.w = zero ? 0.f : v[4 * j + 3];
-              dst[j] = w;
-            }
-          }
+          for (int e = 0; e < 32; ++e) tile[lane * 33 + e] = zero ? 0.f : v[e];
+          __syncwarp();
+          float* dst = out + row_base + ti.n0 + c * 32 + lane;
+#pragma unroll 8
+          for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldo] = tile[i * 33 + lane];
+          __syncwarp();
         }
       } else if (EPI == kEpiSwigluFwd) {
         // accumulator columns [0,128) = gate, [128,256) = up, for I-range [i0, i0+128)
@@ -324,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out);
         __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.aux);
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = half; c < 4; c += kCStep) {
           float g[32], u[32];
           tmem_ld32(t_row + c * 32, g);
           tmem_ld32(t_row + 128 + c * 32, u);
@@ -360,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float w = valid ? __ldg(p.row_w + r) : 0.f;
         float dw_part = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += kCStep) {
           float d[32];
           tmem_ld32(t_row + c * 32, d);
           if (valid) {
@@ -399,6 +404,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (valid && p.row_dw) atomicAdd(p.row_dw + r, dw_part);
+      } else if (EPI == kEpiAdamW) {
+        // The weight gradient never leaves the SM. Each 32x32 fp32 block (32 rows of this
+        // warp's lane quarter x 32 columns) is transposed through shared memory so that
+        // the warp then updates one row's 32 contiguous weights per step, one per lane
+        // (coalesced; the 8-bit quantisation block is exactly those 32 elements).
+        float* tile = reinterpret_cast<float*>(smem + L::EPI_STAGE_OFF) + (warp - 2) * 32 * 33;
+        const size_t row_base = ((size_t)ti.g * p.M + ti.row0 + q * 32) * (size_t)p.N;
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += kCStep) {
+          float v[32];
+          tmem_ld32(t_row + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) tile[lane * 33 + e] = zero ? 0.f : v[e];
+          __syncwarp();
+          const size_t col = (size_t)ti.n0 + c * 32 + lane;
+#pragma unroll 1
+          for (int i = 0; i < 32; i += 4) {
+            float g4[4];
+            size_t idx[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              g4[u] = tile[(i + u) * 33 + lane];
+              idx[u] = row_base + (size_t)(i + u) * p.N + col;
+            }
+            adamw_warp_blocks<4>(g4, idx, p.opt);
+          }
+          __syncwarp();
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -473,7 +506,7 @@ static int num_sms() {
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                    int max_tiles, cudaStream_t stream) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, EPI>;
   auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, RAGGED_K, EPI>;
   size_t smem = L::bytes(p.G);
   static bool configured = false;
@@ -556,11 +589,32 @@ void grouped_gemm_ragged_k(const GemmCall& c, cudaStream_t stream) {
   if (p.N % 256 == 0) {
     p.n_tiles = p.N / 256;
     int max_tiles = p.G * (p.M / 128) * p.n_tiles;
-    launch<256, 4, true, true, true, kEpiF32>(ta, tb, p, max_tiles, stream);
+    launch<256, 3, true, true, true, kEpiF32>(ta, tb, p, max_tiles, stream);
   } else if (p.N % 128 == 0) {
     p.n_tiles = p.N / 128;
     int max_tiles = p.G * (p.M / 128) * p.n_tiles;
-    launch<128, 6, true, true, true, kEpiF32>(ta, tb, p, max_tiles, stream);
+    launch<128, 5, true, true, true, kEpiF32>(ta, tb, p, max_tiles, stream);
+  } else {
+    throw std::runtime_error("N must be a multiple of 128");
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Weight gradient + AdamW: W[g] <- AdamW(W[g], sum_{r in group g} A[r, :]^T B[r, :]).
+// The fp32 gradient tile goes from TMEM straight into the optimizer update.
+// ---------------------------------------------------------------------------------
+void grouped_gemm_wgrad_adamw(const GemmCall& c, cudaStream_t stream) {
+  GemmParams p = c.p;
+  if (p.M % 128) throw std::runtime_error("M must be a multiple of 128");
+  if (p.opt.kind != kOptFp32 && p.opt.kind != kOpt8bit) throw std::runtime_error("bad optimizer kind");
+  CUtensorMap ta = make_tmap_bf16(c.A, c.a_rows, p.M, c.lda, 64);
+  CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
+  if (p.N % 256 == 0) {
+    p.n_tiles = p.N / 256;
+    launch<256, 3, true, true, true, kEpiAdamW>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream);
+  } else if (p.N % 128 == 0) {
+    p.n_tiles = p.N / 128;
+    launch<128, 5, true, true, true, kEpiAdamW>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream);
   } else {
     throw std::runtime_error("N must be a multiple of 128");
   }

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "opt_hyper.h"
+
 namespace sepx {
 
 enum : int {
@@ -10,6 +12,7 @@ enum : int {
   kEpiSwigluFwd = 1,  // D = [gate | up] -> h = silu(g) * u (out), pre-activation gu (aux)
   kEpiSwigluBwd = 2,  // D = dh (unweighted) -> dgu (out), w*h (aux2), dw += <dh, h> (row_dw)
   kEpiF32 = 3,        // D -> fp32 [G, M, ldo] (weight gradients)
+  kEpiAdamW = 4,      // D = weight gradient -> AdamW update of W[G, M, N] in place
 };
 
 struct GemmParams {
@@ -31,6 +34,7 @@ struct GemmParams {
   float* row_dw = nullptr;
   int* status = nullptr;
   unsigned long long timeout_ns = 2000000000ull;
+  OptHyper opt;  // kEpiAdamW
 };
 
 struct GemmCall {
@@ -47,5 +51,7 @@ struct GemmCall {
 
 void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream);
 void grouped_gemm_ragged_k(const GemmCall& c, cudaStream_t stream);
+// weight gradient with the AdamW update fused into the epilogue (c.p.opt describes W)
+void grouped_gemm_wgrad_adamw(const GemmCall& c, cudaStream_t stream);
 
 }  // namespace sepx

@@ -348,9 +348,6 @@ __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
   __shared__ int s_base[1024];
   for (int g = threadIdx.x; g < G; g += blockDim.x) s_base[g] = chunk_base[(size_t)blockIdx.x * G + g];
   __syncthreads();
-  const int vec = a.H / 8;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __shared__ int s_pos[kChunk][8];
   __shared__ int s_le[kChunk];
   // Positions are deterministic: within an expert group, entries of this chunk are
   // ordered by (choice j, slot). Each pass j ranks the block's threads sharing a group.
@@ -378,50 +375,20 @@ __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
     }
     __syncthreads();  // every thread has read s_base for this pass
     if (le >= 0 && before == total - 1) s_base[le] += total;  // last of its group advances
-    s_pos[threadIdx.x][j] = pos;
     if (s < rows) inv_rows[((size_t)src * a.cap + s) * a.k + j] = pos;
     __syncthreads();
   }
-  // copy rows: one warp per slot, fanning out to its positions
-  for (int i = warp; i < kChunk; i += blockDim.x / 32) {
-    const int ss = chunk * kChunk + i;
-    if (ss >= rows) break;
-    const uint4* srow;
-    if (src == a.rank) {
-      srow = reinterpret_cast<const uint4*>(x + (size_t)self_tok[ss] * a.H);
-    } else {
-      const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
-      srow = reinterpret_cast<const uint4*>(base + a.off_recv_x) + ((size_t)src * a.cap + ss) * vec;
-    }
-    int npos = 0, plist[8];
-    for (int j = 0; j < a.k && j < 8; ++j) {
-      int p = s_pos[i][j];
-      if (p >= 0) plist[npos++] = p;
-    }
-    if (npos == 0) continue;
-    for (int c = lane; c < vec; c += 32) {
-      uint4 v = srow[c];
-      for (int q = 0; q < npos; ++q) reinterpret_cast<uint4*>(xp + (size_t)plist[q] * a.H)[c] = v;
-    }
-  }
-  // zero the padding rows (spread over all blocks)
+  // padding rows: weight 0, no source (the gather kernel zero-fills their data)
   const int npad = pad_off[G];
-  const int gwarp = blockIdx.x * (blockDim.x / 32) + warp;
-  const int nw = gridDim.x * (blockDim.x / 32);
-  for (int q = gwarp; q < npad; q += nw) {
-    // find group: largest g with pad_off[g] <= q
-    int lo = 0, hi = G;
+  for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < npad; q += gridDim.x * blockDim.x) {
+    int lo = 0, hi = G;  // largest g with pad_off[g] <= q
     while (hi - lo > 1) {
       int mid = (lo + hi) >> 1;
       if (pad_off[mid] <= q) lo = mid; else hi = mid;
     }
     const int r = group_off[lo] + group_cnt[lo] + (q - pad_off[lo]);
-    uint4 z = make_uint4(0, 0, 0, 0);
-    for (int c = lane; c < vec; c += 32) reinterpret_cast<uint4*>(xp + (size_t)r * a.H)[c] = z;
-    if (lane == 0) {
-      row_w[r] = 0.f;
-      row_src[r] = -1;
-    }
+    row_w[r] = 0.f;
+    row_src[r] = -1;
   }
 }
 
@@ -646,11 +613,14 @@ void ep_recv_plan(const EpArgs& a, const void* x, const int* topk_e, const float
                                                   group_cnt, pad_off, reinterpret_cast<__nv_bfloat16*>(xp), row_w,
                                                   row_src, inv_rows);
   check_launch("recv_permute");
+  recv_gather_kernel<<<sm_count() * 4, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), self_tok, row_src,
+                                                     group_off + G, send_count, reinterpret_cast<__nv_bfloat16*>(xp));
+  check_launch("recv_gather");
 }
 
 void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const int* row_src, const int* total_rows,
                     const int* send_count, void* xp, int cap_rows, cudaStream_t st) {
-  int blocks = sm_count() * 2;
+  int blocks = sm_count() * 4;
   (void)cap_rows;
   recv_gather_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), self_tok, row_src,
                                              total_rows, send_count, reinterpret_cast<__nv_bfloat16*>(xp));
@@ -781,6 +751,11 @@ extern "C" int sepx_moe_permute_noalloc(const void* x, const int* topk_e, const 
       a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w, s + kNaSelfTok, s + kNaE2R, s + kNaE2L,
       s + kNaRowsFrom, s + kNaChunkCnt, E, group_off, s + kNaGroupCnt, s + kNaPadOff,
       reinterpret_cast<__nv_bfloat16*>(xp), row_w, row_src, inv_rows);
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  recv_gather_kernel<<<(sms > 0 ? sms : 148) * 4, 256, 0, stream>>>(
+      a, reinterpret_cast<const __nv_bfloat16*>(x), s + kNaSelfTok, row_src, group_off + E, s + kNaSendCount,
+      reinterpret_cast<__nv_bfloat16*>(xp));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     std::fprintf(stderr, "sepx_moe_permute_noalloc: launch failed: %s\n", cudaGetErrorString(e));

@@ -4,13 +4,16 @@ State precision per parameter:
 
 * ``"fp32"``: fp32 master weights + fp32 moments (16 bytes/param with the bf16 weight).
 * ``"8bit"``: block-wise 8-bit moments (Dettmers et al., ICLR 2022: int8 first moment and
-  uint8 sqrt-second moment, one fp32 absmax scale per 128 values) and stochastic
-  rounding of the bf16 weight (4 bytes/param with the bf16 weight). Used where fp32
+  uint8 sqrt-second moment, one fp32 absmax scale per 32 values) and stochastic
+  rounding of the bf16 weight (4.25 bytes/param with the bf16 weight). Used where fp32
   state does not fit, e.g. all 128 experts of a 30B-parameter MoE on one GPU.
 
 Parameters may also be updated *inside the backward pass* through :meth:`apply_now`:
 the MoE layer hands over each expert weight gradient as soon as its wgrad GEMM is done,
-so no full-model gradient buffer ever exists (the gradient of one layer is transient).
+so no full-model gradient buffer ever exists (the gradient of one layer is transient),
+or, through :meth:`fused_wgrad`, inside the weight-gradient GEMM itself: the tcgen05
+kernel applies AdamW to each output tile in its epilogue and the gradient never reaches
+HBM.
 """
 from __future__ import annotations
 
@@ -30,6 +33,8 @@ class FusedAdamW:
         self.max_grad_norm = max_grad_norm
         self.state: dict[int, dict] = {}
         self._precision = state_precision
+        # stochastic-rounding seed of each parameter: its position in the optimizer
+        self._seed = {id(p): i for i, p in enumerate(self.params)}
         for p in self.params:
             self._init_state(p)
 
@@ -46,7 +51,9 @@ class FusedAdamW:
                       m=torch.zeros(p.shape, device=dev, dtype=torch.float32),
                       v=torch.zeros(p.shape, device=dev, dtype=torch.float32))
         elif prec == "8bit":
-            nb = (p.numel() + 127) // 128
+            if p.numel() % 32:
+                raise ValueError("8-bit optimizer state needs a multiple of 32 elements")
+            nb = p.numel() // 32
             st = dict(prec="8bit",
                       mq=torch.zeros(p.numel(), device=dev, dtype=torch.int8),
                       ms=torch.zeros(nb, device=dev, dtype=torch.float32),
@@ -61,23 +68,28 @@ class FusedAdamW:
                    for t in st.values() if torch.is_tensor(t))
 
     # ---------------------------------------------------------------------------
-    def _update(self, p, g, step, grad_scale=1.0):
+    def _kernel_state(self, p):
         st = self.state[id(p)]
-        C = load()
-        b1, b2 = self.betas
-        g = g.contiguous()
-        if g.dtype != torch.float32:
-            g = g.float()
         if st["prec"] == "fp32":
-            C.adamw_fp32(p.data, st["master"], g, st["m"], st["v"], self.lr, b1, b2, self.eps, self.wd,
-                         step, grad_scale)
-        else:
-            C.adamw_8bit(p.data, g, st["mq"], st["ms"], st["vq"], st["vs"], self.lr, b1, b2, self.eps,
-                         self.wd, step, grad_scale, id(p) & 0x7FFFFFFF)
+            return 1, st["master"], st["m"], st["v"], None, None
+        return 2, None, st["mq"], st["vq"], st["ms"], st["vs"]
 
-    def apply_now(self, p, grad_fp32):
-        """Update ``p`` immediately with ``grad_fp32`` (optimizer-in-backward)."""
-        self._update(p, grad_fp32, self.step_count + 1)
+    def _update(self, p, g, step, grad_scale=1.0):
+        b1, b2 = self.betas
+        kind, master, m, v, ms, vs = self._kernel_state(p)
+        load().adamw_update(p.data, g.contiguous(), kind, master, m, v, ms, vs, self.lr, b1, b2, self.eps, self.wd,
+                            step, grad_scale, self._seed[id(p)])
+
+    def apply_now(self, p, grad):
+        """Update ``p`` immediately with ``grad`` (optimizer-in-backward)."""
+        self._update(p, grad, self.step_count + 1)
+
+    def fused_wgrad(self, p, a, b, group_off, status=None):
+        """``p[g] <- AdamW(p[g], a[rows_g]^T @ b[rows_g])`` in one tcgen05 GEMM (p is [G, M, N])."""
+        b1, b2 = self.betas
+        kind, master, m, v, ms, vs = self._kernel_state(p)
+        load().gg_wgrad_adamw(a, b, group_off, p.data, kind, master, m, v, ms, vs, self.lr, b1, b2, self.eps,
+                              self.wd, self.step_count + 1, 1.0, self._seed[id(p)], status)
 
     def step(self):
         """Update every parameter that has a ``.grad`` (those updated in backward have none)."""
@@ -111,6 +123,6 @@ def adamw_reference(p, g, m, v, lr, b1, b2, eps, wd, step):
     return p, m, v
 
 
-def bytes_per_param(precision: str) -> int:
+def bytes_per_param(precision: str) -> float:
     """Optimizer state bytes per parameter (excluding the bf16 weight itself)."""
-    return {"fp32": 12, "8bit": 2}[precision] + (0 if precision == "fp32" else math.ceil(8 / 128))
+    return {"fp32": 12.0, "8bit": 2.25}[precision]

@@ -212,19 +212,27 @@ class _EPMoE(torch.autograd.Function):
         dyp = ep.dispatch_bwd(dout, st)
         row_dw = torch.zeros(ep.cap_rows, dtype=torch.float32, device=dout.device)
         dgu, hw, row_dw = gg.gg_swiglu_bwd(dyp, w_d, st.group_off, gu, st.row_w, row_dw=row_dw, status=ep.status)
-        dwd = gg.gg_wgrad(dyp, hw, st.group_off, ep.G, status=ep.status)
+        fused = getattr(sink, "fused_wgrad", None) if sink is not None else None
+        g_gu = g_d = None
+        if fused is not None:  # optimizer applied inside the wgrad GEMM epilogue
+            fused(w_d, dyp, hw, st.group_off, ep.status)
+        else:
+            dwd = gg.gg_wgrad(dyp, hw, st.group_off, ep.G, status=ep.status)
         del hw, dyp
         dxp = gg.gg_dgrad(dgu, w_gu, st.group_off, status=ep.status)
-        dwgu = gg.gg_wgrad(dgu, st.xp, st.group_off, ep.G, status=ep.status)
+        if fused is not None:
+            fused(w_gu, dgu, st.xp, st.group_off, ep.status)
+        else:
+            dwgu = gg.gg_wgrad(dgu, st.xp, st.group_off, ep.G, status=ep.status)
         del dgu
         dx, dtopk_w = ep.combine_bwd(dxp, row_dw, st)
-        g_gu = g_d = None
-        if sink is not None:
-            sink(w_d, dwd)
-            sink(w_gu, dwgu)
-        else:
-            g_d = dwd.to(w_d.dtype) if ctx.needs_input_grad[3] else None
-            g_gu = dwgu.to(w_gu.dtype) if ctx.needs_input_grad[2] else None
+        if fused is None:
+            if sink is not None:
+                sink(w_d, dwd)
+                sink(w_gu, dwgu)
+            else:
+                g_d = dwd.to(w_d.dtype) if ctx.needs_input_grad[3] else None
+                g_gu = dwgu.to(w_gu.dtype) if ctx.needs_input_grad[2] else None
         ctx.st = None
         dres = dout if ctx.has_residual else None
         return dx, dtopk_w, g_gu, g_d, None, None, None, dres

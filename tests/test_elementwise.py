@@ -106,14 +106,14 @@ def test_fused_adamw(prec):
     from spec_ep.ops.optim import FusedAdamW, adamw_reference
 
     torch.manual_seed(0)
-    p = torch.nn.Parameter(torch.randn(10000, device="cuda").bfloat16())
+    p = torch.nn.Parameter(torch.randn(10240, device="cuda").bfloat16())
     p0 = p.detach().float().clone()
     opt = FusedAdamW([p], lr=1e-2, weight_decay=0.1, state_precision=prec)
     m = torch.zeros_like(p0)
     v = torch.zeros_like(p0)
     ref = p0.clone()
     for step in range(1, 4):
-        g = torch.randn(10000, device="cuda")
+        g = torch.randn(10240, device="cuda")
         p.grad = g.bfloat16()
         opt.step()
         ref, m, v = adamw_reference(ref, g.bfloat16().float(), m, v, 1e-2, 0.9, 0.95, 1e-8, 0.1, step)

@@ -146,3 +146,44 @@ def test_large_fwd_perf_sanity():
     ref = torch.bmm(a.view(G, per, H), w.transpose(1, 2)).float().reshape(-1, 2 * I)
     torch.cuda.synchronize()
     assert _rel_err(gu, ref) < 1e-2
+
+
+@pytest.mark.parametrize("kind", ["fp32", "8bit"])
+def test_wgrad_adamw_fused_matches_unfused(kind):
+    """AdamW applied in the wgrad epilogue == wgrad to HBM followed by the standalone update."""
+    from spec_ep.ops.grouped_gemm import gg_wgrad
+    from spec_ep.ops.optim import FusedAdamW
+
+    torch.manual_seed(6)
+    sizes = [128, 0, 64, 300]
+    off = _offsets(sizes, 64)
+    R, M, N, G = off[-1], 256, 384, len(sizes)
+    a = torch.zeros(R, M, device="cuda")
+    b = torch.zeros(R, N, device="cuda")
+    for g, s in enumerate(sizes):
+        a[off[g]:off[g] + s] = torch.randn(s, M, device="cuda")
+        b[off[g]:off[g] + s] = torch.randn(s, N, device="cuda")
+    a, b = a.bfloat16(), b.bfloat16()
+    go = torch.tensor(off, dtype=torch.int32, device="cuda")
+    w0 = (torch.randn(G, M, N, device="cuda") * 0.02).bfloat16()
+    p1 = torch.nn.Parameter(w0.clone())
+    p2 = torch.nn.Parameter(w0.clone())
+    p1._sepx_state_precision = kind
+    p2._sepx_state_precision = kind
+    o1 = FusedAdamW([p1], lr=1e-3, weight_decay=0.1)
+    o2 = FusedAdamW([p2], lr=1e-3, weight_decay=0.1)
+    st = _status()
+    for step in range(3):
+        o1.fused_wgrad(p1, a, b, go, st)
+        o1.step_count += 1
+        g = gg_wgrad(a, b, go, G)
+        o2.apply_now(p2, g)
+        o2.step_count += 1
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    assert torch.equal(p1.detach(), p2.detach())
+    for k_ in o1.state[id(p1)]:
+        if torch.is_tensor(o1.state[id(p1)][k_]):
+            assert torch.equal(o1.state[id(p1)][k_], o2.state[id(p2)][k_]), k_
+    # the empty group still got weight decay + moment decay, and parameters moved
+    assert not torch.equal(p1.detach(), w0)
