@@ -58,6 +58,7 @@ class Qwen3MoeLayer(nn.Module):
             p._sepx_expert = True
         self.grad_sink = None
         self.router_bias = None  # optional selection bias (synthetic skew studies)
+        self.routing_callback = None  # receives topk expert ids (routing capture)
 
     def forward(self, x, pos=None):
         cfg = self.cfg
@@ -70,6 +71,8 @@ class Qwen3MoeLayer(nn.Module):
         h = rms_norm(x, self.post_norm, cfg.rms_norm_eps)
         logits = F.linear(h, self.w_router).float()
         topk_w, topk_e = router_topk(logits, cfg.top_k, cfg.norm_topk_prob, self.router_bias)
+        if self.routing_callback is not None:
+            self.routing_callback(topk_e)
         return ep_moe(h, topk_e, topk_w, self.w_gu, self.w_d, self.ep, self.grad_sink, residual=x)
 
 

@@ -79,7 +79,8 @@ class ExpertParallel:
         hidden: model width (H).
         max_tokens: most tokens a rank passes in one call (sizes the symmetric slabs).
         group: process group of the EP ranks (None = default group, or single GPU).
-        placement: optional ``(e2r, e2l, experts_per_rank)`` from the placement planner.
+        placement: a ``Placement`` from ``spec_ep.parallel.placement`` (or raw
+            ``(e2r, e2l, experts_per_rank)`` tables); default: contiguous experts.
         capacity_factor: receive capacity in units of ``max_tokens * top_k`` rows.
         timeout_s: device-side wait limit before a peer is declared lost.
     """
@@ -98,7 +99,12 @@ class ExpertParallel:
         self.E, self.k, self.H, self.cap = num_experts, top_k, hidden, max_tokens
         if placement is None:
             placement = contiguous_placement(num_experts, self.world)
-        e2r, e2l, per_rank = placement
+        if hasattr(placement, "tables"):  # a spec_ep.parallel.placement.Placement
+            self.placement = placement
+            e2r, e2l, per_rank = placement.tables(self.rank)
+        else:
+            self.placement = None
+            e2r, e2l, per_rank = placement
         self.e2r = e2r.to(self.device, torch.int32)
         self.e2l = e2l.to(self.device, torch.int32)
         self.G = int(per_rank[self.rank])

@@ -1,0 +1,193 @@
+"""Speculative expert placement: routing histograms -> expert-to-rank map + replica set.
+
+The reference only sketches this idea (docs/plan.md:3-21: predict the hot experts, keep a
+copy of every expert somewhere, replicate/shuffle experts for load balance). Here it is a
+host planner whose output drives the dispatch kernels directly:
+
+* Every expert has exactly one *primary* rank (so every expert exists somewhere).
+* ``plan_balanced`` assigns primaries by greedy longest-processing-time bin packing of
+  the measured per-expert loads, ``E / world`` slots per rank.
+* ``replicate_top`` hot experts additionally get a *replica* slot on every rank; a token
+  routed to a replicated expert is served by its own rank's copy (no transfer at all).
+* ``Placement.tables(rank)`` returns the per-rank ``(e2r, e2l)`` lookup tables the
+  dispatch kernel uses: destination rank and local slot for each expert, as seen from
+  that source rank.
+* ``reshard`` moves expert weights between ranks when the placement changes.
+"""
+from __future__ import annotations
+
+import heapq
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass
+class Placement:
+    num_experts: int
+    world: int
+    owner: list[int]                      # primary rank of each expert
+    local_experts: list[list[int]]        # per rank: global expert id of each local slot
+    replicated: list[int] = field(default_factory=list)  # experts with a copy on every rank
+
+    # -----------------------------------------------------------------------------
+    def slots(self, rank: int) -> int:
+        return len(self.local_experts[rank])
+
+    def per_rank(self) -> list[int]:
+        return [len(x) for x in self.local_experts]
+
+    def slot_of(self, rank: int, expert: int) -> int:
+        return self.local_experts[rank].index(expert)
+
+    def tables(self, rank: int) -> tuple[torch.Tensor, torch.Tensor, list[int]]:
+        """(e2r, e2l, experts_per_rank) seen from source ``rank``.
+
+        A replicated expert resolves to this rank's own copy; any other expert to its
+        primary rank and the primary's slot.
+        """
+        E = self.num_experts
+        e2r = torch.empty(E, dtype=torch.int32)
+        e2l = torch.empty(E, dtype=torch.int32)
+        mine = {e: i for i, e in enumerate(self.local_experts[rank])}
+        for e in range(E):
+            if e in mine and (e in self.replicated or self.owner[e] == rank):
+                e2r[e], e2l[e] = rank, mine[e]
+            else:
+                o = self.owner[e]
+                e2r[e], e2l[e] = o, self.local_experts[o].index(e)
+        return e2r, e2l, self.per_rank()
+
+    def expected_rows(self, load: torch.Tensor, source_share: torch.Tensor | None = None) -> torch.Tensor:
+        """Rows each rank computes for per-expert ``load`` (tokens routed to each expert).
+
+        Replicated experts are served locally, so their load splits across ranks in the
+        proportion ``source_share`` (uniform by default).
+        """
+        load = load.double()
+        share = source_share.double() if source_share is not None else torch.full((self.world,), 1.0 / self.world,
+                                                                                 dtype=torch.float64)
+        rows = torch.zeros(self.world, dtype=torch.float64)
+        for e in range(self.num_experts):
+            if e in self.replicated:
+                rows += load[e] * share
+            else:
+                rows[self.owner[e]] += load[e]
+        return rows
+
+    def imbalance(self, load: torch.Tensor) -> float:
+        rows = self.expected_rows(load)
+        return float(rows.max() / rows.mean().clamp_min(1e-9))
+
+    def to_dict(self) -> dict:
+        return {"num_experts": self.num_experts, "world": self.world, "owner": list(self.owner),
+                "local_experts": [list(x) for x in self.local_experts], "replicated": list(self.replicated)}
+
+    @staticmethod
+    def from_dict(d: dict) -> "Placement":
+        return Placement(d["num_experts"], d["world"], list(d["owner"]), [list(x) for x in d["local_experts"]],
+                         list(d.get("replicated", [])))
+
+
+def contiguous(num_experts: int, world: int) -> Placement:
+    """Expert e on rank e // (E / world) (the reference's fixed layout, src/rbd.py:200-202)."""
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not split over {world} ranks")
+    epr = num_experts // world
+    owner = [e // epr for e in range(num_experts)]
+    return Placement(num_experts, world, owner, [list(range(r * epr, (r + 1) * epr)) for r in range(world)])
+
+
+def plan_balanced(load: torch.Tensor, world: int, replicate_top: int = 0) -> Placement:
+    """Greedy LPT packing of per-expert ``load`` onto ranks with E / world primary slots each,
+    plus a replica of the ``replicate_top`` most loaded experts on every rank.
+
+    Replicated experts' load is spread evenly across ranks before packing the rest, since
+    each source serves them locally.
+    """
+    E = load.numel()
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    cap = E // world
+    load = load.double().cpu()
+    order = torch.argsort(load, descending=True).tolist()
+    replicated = sorted(order[:replicate_top])
+    base = torch.zeros(world, dtype=torch.float64)
+    for e in replicated:
+        base += load[e] / world
+    heap = [(float(base[r]), r) for r in range(world)]
+    heapq.heapify(heap)
+    owner = [-1] * E
+    slots = [[] for _ in range(world)]
+    for e in order:
+        full = []
+        while True:
+            cur, r = heapq.heappop(heap)
+            if len(slots[r]) < cap:
+                break
+            full.append((cur, r))
+        slots[r].append(e)
+        owner[e] = r
+        add = 0.0 if e in replicated else float(load[e])
+        heapq.heappush(heap, (cur + add, r))
+        for item in full:
+            heapq.heappush(heap, item)
+    local = []
+    for r in range(world):
+        prim = sorted(slots[r])
+        reps = [e for e in replicated if owner[e] != r]
+        local.append(prim + reps)
+    return Placement(E, world, owner, local, replicated)
+
+
+def loads_from_routing(route: torch.Tensor, num_experts: int) -> torch.Tensor:
+    """Per-layer expert loads from a ``[L, T, K]`` routing dump -> ``[L, E]``."""
+    L = route.shape[0]
+    return torch.stack([torch.bincount(route[l].reshape(-1).long(), minlength=num_experts) for l in range(L)])
+
+
+def plan_from_routing(route: torch.Tensor, num_experts: int, world: int, replicate_top: int = 0) -> list[Placement]:
+    """One placement per layer from recorded routing (the experts_rank*.pt format)."""
+    return [plan_balanced(l, world, replicate_top) for l in loads_from_routing(route, num_experts)]
+
+
+# ---------------------------------------------------------------------------------------
+def gather_expert_rows(w_local: torch.Tensor, placement: Placement, rank: int, experts: list[int]) -> torch.Tensor:
+    """Rows of ``w_local`` ([slots, ...]) holding the given global experts."""
+    idx = [placement.slot_of(rank, e) for e in experts]
+    return w_local[idx]
+
+
+def reshard(w_local: torch.Tensor, old: Placement, new: Placement, group=None) -> torch.Tensor:
+    """Move expert weights from ``old`` to ``new`` placement (collective over ``group``).
+
+    Every slot of the new layout is filled from the old primary copy of its expert, over
+    one variable-size all-to-all. Works on any backend (gloo for tests, NCCL on GPUs).
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    per = w_local[0].numel()
+    # what each rank needs, ordered by source (old primary)
+    need = [[[] for _ in range(world)] for _ in range(world)]  # need[dst][src] = experts
+    for dst in range(world):
+        for e in new.local_experts[dst]:
+            need[dst][old.owner[e]].append(e)
+    send_rows = []
+    send_counts = []
+    for dst in range(world):
+        es = need[dst][rank]
+        send_counts.append(len(es) * per)
+        if es:
+            send_rows.append(gather_expert_rows(w_local, old, rank, es).reshape(-1))
+    recv_counts = [len(need[rank][src]) * per for src in range(world)]
+    send = torch.cat(send_rows) if send_rows else w_local.new_empty(0)
+    recv = w_local.new_empty(sum(recv_counts))
+    dist.all_to_all_single(recv, send.contiguous(), recv_counts, send_counts, group=group)
+    got = {}
+    off = 0
+    for src in range(world):
+        for e in need[rank][src]:
+            got[e] = recv[off:off + per].view_as(w_local[0])
+            off += per
+    return torch.stack([got[e] for e in new.local_experts[rank]])

@@ -101,3 +101,71 @@ def test_ep_moe_two_or_more_gpus(skew):
     errq = ctx.SimpleQueue()
     mp.spawn(_worker, args=(world, _free_port(), 1024, 16, 4, 512, 256, skew, errq), nprocs=world, join=True)
     assert errq.empty()
+
+
+def _placement_worker(rank, world, port, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        from spec_ep.parallel.ep import ExpertParallel, ep_moe
+        from spec_ep.parallel.placement import plan_balanced
+
+        T, E, k, H, I = 1024, 16, 4, 512, 256
+        load = torch.arange(E, 0, -1).double() ** 1.5  # skewed popularity
+        plan = plan_balanced(load, world, replicate_top=2)
+        g = torch.Generator().manual_seed(0)
+        w_gu_full = (torch.randn(E, 2 * I, H, generator=g) / H**0.5).bfloat16().to(dev)
+        w_d_full = (torch.randn(E, H, I, generator=g) / I**0.5).bfloat16().to(dev)
+        mine = plan.local_experts[rank]
+        w_gu = w_gu_full[mine].clone().requires_grad_()
+        w_d = w_d_full[mine].clone().requires_grad_()
+        torch.manual_seed(20 + rank)
+        x = torch.randn(T, H, device=dev).bfloat16().requires_grad_()
+        p = torch.softmax(torch.randn(T, E, device=dev) + torch.log(load.float().to(dev)), -1)
+        tw, te = p.topk(k, -1)
+        tw = (tw / tw.sum(-1, keepdim=True)).requires_grad_()
+        ep = ExpertParallel(E, k, H, max_tokens=T, device=dev, placement=plan, capacity_factor=float(world))
+        out = ep_moe(x, te.int(), tw, w_gu, w_d, ep)
+        gout = torch.randn(out.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(rank))
+        out.backward(gout.bfloat16())
+        torch.cuda.synchronize()
+        ep.check()
+        xr = x.detach().float().requires_grad_()
+        twr = tw.detach().clone().requires_grad_()
+        gur = w_gu_full.float().requires_grad_()
+        dr = w_d_full.float().requires_grad_()
+        ref = _moe_ref(xr, te, twr, gur, dr)
+        ref.backward(gout.bfloat16().float())
+        assert _rel(out, ref) < 2e-2
+        assert _rel(x.grad, xr.grad) < 3e-2
+        assert _rel(tw.grad, twr.grad) < 3e-2
+        # expert gradients: sum the local copies' gradients over holders, per global expert
+        acc_gu = torch.zeros_like(gur.grad)
+        acc_d = torch.zeros_like(dr.grad)
+        acc_gu[mine] += w_gu.grad.float()
+        acc_d[mine] += w_d.grad.float()
+        for t in (acc_gu, acc_d, gur.grad, dr.grad):
+            dist.all_reduce(t)
+        assert _rel(acc_gu, gur.grad) < 3e-2
+        assert _rel(acc_d, dr.grad) < 3e-2
+        dist.barrier()
+        ep.close()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+def test_ep_moe_balanced_placement_with_replicas():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(n, 4)
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.spawn(_placement_worker, args=(world, _free_port(), errq), nprocs=world, join=True)
+    assert errq.empty()
