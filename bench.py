@@ -144,7 +144,10 @@ def run_spec_ep(args):
     total, expert = cfg.param_counts()
     dense = total - expert
     local_expert = expert // world
-    act = cfg.num_layers * (T * cfg.hidden_size * 2 * 12 + ep.cap_rows * (cfg.hidden_size + 2 * cfg.moe_intermediate_size) * 2)
+    # saved activations per layer: ~12 [T, H] tensors + the expert rows (x and gate|up),
+    # with 1.5x headroom for routing imbalance
+    rows = int(1.5 * T * cfg.top_k) + ep.G * 64
+    act = cfg.num_layers * (T * cfg.hidden_size * 2 * 12 + rows * (cfg.hidden_size + 2 * cfg.moe_intermediate_size) * 2)
     budget = int(0.92 * torch.cuda.get_device_properties(dev).total_memory)
     prec = args.expert_state
     if prec == "auto":

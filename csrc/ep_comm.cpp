@@ -145,6 +145,36 @@ class EpComm {
                        row_src.data_ptr<int>(), inv_rows.data_ptr<int>(), st);
   }
 
+  void recv_count_scan(const at::Tensor& topk_e, const at::Tensor& topk_w, const at::Tensor& self_tok,
+                       const at::Tensor& e2r, const at::Tensor& e2l, const at::Tensor& send_count, int G, int T,
+                       int cap_rows, int64_t epoch, at::Tensor& rows_from, at::Tensor& chunk_cnt,
+                       at::Tensor& group_off, at::Tensor& group_cnt, at::Tensor& pad_off, at::Tensor& done,
+                       at::Tensor& status, double timeout_s) {
+    auto a = call_args(T, 0, epoch, done, status, timeout_s);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_recv_count_scan(a, topk_e.data_ptr<int>(), topk_w.data_ptr<float>(), self_tok.data_ptr<int>(),
+                             e2r.data_ptr<int>(), e2l.data_ptr<int>(), send_count.data_ptr<int>(), G, cap_rows,
+                             rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(), group_off.data_ptr<int>(),
+                             group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(), st);
+  }
+
+  void recv_permute_gather(const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w,
+                           const at::Tensor& self_tok, const at::Tensor& e2r, const at::Tensor& e2l,
+                           const at::Tensor& send_count, int G, int64_t epoch, const at::Tensor& rows_from,
+                           const at::Tensor& chunk_cnt, const at::Tensor& group_off, const at::Tensor& group_cnt,
+                           const at::Tensor& pad_off, at::Tensor& xp, at::Tensor& row_w, at::Tensor& row_src,
+                           at::Tensor& inv_rows, at::Tensor& done, at::Tensor& status, double timeout_s) {
+    TORCH_CHECK(xp.size(1) == args_.H && xp.is_contiguous(), "xp must be [rows, H]");
+    auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_recv_permute_gather(a, x.data_ptr(), topk_e.data_ptr<int>(), topk_w.data_ptr<float>(),
+                                 self_tok.data_ptr<int>(), e2r.data_ptr<int>(), e2l.data_ptr<int>(),
+                                 send_count.data_ptr<int>(), G, rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(),
+                                 group_off.data_ptr<int>(), group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(),
+                                 xp.data_ptr(), row_w.data_ptr<float>(), row_src.data_ptr<int>(),
+                                 inv_rows.data_ptr<int>(), st);
+  }
+
   void recv_gather(const at::Tensor& x, const at::Tensor& self_tok, const at::Tensor& row_src,
                    const at::Tensor& group_off, const at::Tensor& send_count, at::Tensor& xp, int64_t epoch,
                    at::Tensor& done, at::Tensor& status, double timeout_s) {
@@ -195,6 +225,8 @@ void register_ep_comm(pybind11::module& m) {
       .def("route_plan", &EpComm::route_plan)
       .def("dispatch", &EpComm::dispatch)
       .def("recv_plan", &EpComm::recv_plan)
+      .def("recv_count_scan", &EpComm::recv_count_scan)
+      .def("recv_permute_gather", &EpComm::recv_permute_gather)
       .def("recv_gather", &EpComm::recv_gather)
       .def("combine", &EpComm::combine)
       .def("source_reduce", &EpComm::source_reduce);

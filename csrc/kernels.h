@@ -40,6 +40,16 @@ void ep_recv_plan(const EpArgs& a, const void* x, const int* topk_e, const float
                   int G, int cap_rows, int* rows_from, int* chunk_cnt, int* group_off,
                   int* group_cnt, int* pad_off, void* xp, float* row_w, int* row_src,
                   int* inv_rows, cudaStream_t st);
+// Receive plan in two halves so the caller can size buffers between them: count+scan
+// produce group_off (group_off[G] = rows needed), permute+gather fill them.
+void ep_recv_count_scan(const EpArgs& a, const int* topk_e, const float* topk_w, const int* self_tok,
+                        const int* e2r, const int* e2l, const int* send_count, int G, int cap_rows, int* rows_from,
+                        int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, cudaStream_t st);
+void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
+                            const int* self_tok, const int* e2r, const int* e2l, const int* send_count, int G,
+                            const int* rows_from, const int* chunk_cnt, const int* group_off, const int* group_cnt,
+                            const int* pad_off, void* xp, float* row_w, int* row_src, int* inv_rows,
+                            cudaStream_t st);
 void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const int* row_src,
                     const int* total_rows, const int* send_count, void* xp, int cap_rows,
                     cudaStream_t st);

@@ -618,6 +618,35 @@ void ep_recv_plan(const EpArgs& a, const void* x, const int* topk_e, const float
   check_launch("recv_gather");
 }
 
+void ep_recv_count_scan(const EpArgs& a, const int* topk_e, const float* topk_w, const int* self_tok,
+                        const int* e2r, const int* e2l, const int* send_count, int G, int cap_rows, int* rows_from,
+                        int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, cudaStream_t st) {
+  if (G > 1024) throw std::runtime_error("at most 1024 local experts");
+  if (a.k > 8) throw std::runtime_error("top-k above 8 is not supported by the permute kernel");
+  const int nchunks = ((a.cap + kChunk - 1) / kChunk) * a.W;
+  recv_count_kernel<<<nchunks, kChunk, 0, st>>>(a, topk_e, topk_w, self_tok, e2r, e2l, send_count, rows_from,
+                                                chunk_cnt, G);
+  check_launch("recv_count");
+  recv_scan_kernel<<<1, 1024, 0, st>>>(a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows);
+  check_launch("recv_scan");
+}
+
+void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
+                            const int* self_tok, const int* e2r, const int* e2l, const int* send_count, int G,
+                            const int* rows_from, const int* chunk_cnt, const int* group_off, const int* group_cnt,
+                            const int* pad_off, void* xp, float* row_w, int* row_src, int* inv_rows,
+                            cudaStream_t st) {
+  const int nchunks = ((a.cap + kChunk - 1) / kChunk) * a.W;
+  recv_permute_kernel<<<nchunks, kChunk, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w,
+                                                  self_tok, e2r, e2l, rows_from, chunk_cnt, G, group_off, group_cnt,
+                                                  pad_off, reinterpret_cast<__nv_bfloat16*>(xp), row_w, row_src,
+                                                  inv_rows);
+  check_launch("recv_permute");
+  recv_gather_kernel<<<sm_count() * 4, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), self_tok, row_src,
+                                                     group_off + G, send_count, reinterpret_cast<__nv_bfloat16*>(xp));
+  check_launch("recv_gather");
+}
+
 void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const int* row_src, const int* total_rows,
                     const int* send_count, void* xp, int cap_rows, cudaStream_t st) {
   int blocks = sm_count() * 4;

@@ -81,7 +81,8 @@ class ExpertParallel:
         group: process group of the EP ranks (None = default group, or single GPU).
         placement: a ``Placement`` from ``spec_ep.parallel.placement`` (or raw
             ``(e2r, e2l, experts_per_rank)`` tables); default: contiguous experts.
-        capacity_factor: receive capacity in units of ``max_tokens * top_k`` rows.
+        capacity_factor: unused (kept for API compatibility): buffers are sized exactly per
+            call from the device-side row count.
         timeout_s: device-side wait limit before a peer is declared lost.
     """
 
@@ -115,9 +116,9 @@ class ExpertParallel:
             dist.all_gather_object(handles, self.comm.ipc_handle(), group=group)
             self.comm.open_peers(handles)
             dist.barrier(group=group)
-        rows = max_tokens * top_k
-        self.cap_rows = min(self.world * rows, int(math.ceil(capacity_factor * rows))) + self.G * 64
-        self.cap_rows = (self.cap_rows + 127) // 128 * 128
+        # worst case: every token of every source routes all k choices here
+        self.cap_rows = self.world * max_tokens * top_k + self.G * 64
+        self.rows_last = 0
         self.nchunks = self.world * ((max_tokens + 127) // 128)
         self.timeout_s = float(timeout_s)
         self.epoch = 0
@@ -153,19 +154,26 @@ class ExpertParallel:
         self.comm.route_plan(topk_e, self.e2r, slot, send_count)
         self.comm.dispatch(x, topk_e, topk_w, slot, self.e2r, self.e2l, self_tok, send_count, True, ep,
                            self.done[0:1], self.status, self.timeout_s)
-        G, R = self.G, self.cap_rows
+        G = self.G
         rows_from = torch.empty(W, dtype=torch.int32, device=dev)
         chunk_cnt = torch.empty(self.nchunks * G, dtype=torch.int32, device=dev)
         group_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
         group_cnt = torch.empty(G, dtype=torch.int32, device=dev)
         pad_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
+        self.comm.recv_count_scan(topk_e, topk_w, self_tok, self.e2r, self.e2l, send_count, G, T, self.cap_rows, ep,
+                                  rows_from, chunk_cnt, group_off, group_cnt, pad_off, self.done[0:1], self.status,
+                                  self.timeout_s)
+        # One small device->host read per layer sizes every buffer of this layer exactly
+        # (saved activations included); the receive capacity is the true worst case.
+        R = max(int(group_off[G].item()), 1)
+        self.rows_last = R
         xp = torch.empty(R, self.H, dtype=torch.bfloat16, device=dev)
         row_w = torch.empty(R, dtype=torch.float32, device=dev)
         row_src = torch.empty(R, dtype=torch.int32, device=dev)
         inv_rows = torch.empty(W, self.cap, k, dtype=torch.int32, device=dev)
-        self.comm.recv_plan(x, topk_e, topk_w, self_tok, self.e2r, self.e2l, send_count, G, ep, rows_from,
-                            chunk_cnt, group_off, group_cnt, pad_off, xp, row_w, row_src, inv_rows,
-                            self.done[0:1], self.status, self.timeout_s)
+        self.comm.recv_permute_gather(x, topk_e, topk_w, self_tok, self.e2r, self.e2l, send_count, G, ep, rows_from,
+                                      chunk_cnt, group_off, group_cnt, pad_off, xp, row_w, row_src, inv_rows,
+                                      self.done[0:1], self.status, self.timeout_s)
         return EPState(T, slot, send_count, self_tok, topk_e, topk_w, rows_from, group_off, group_cnt, xp, row_w,
                        row_src, inv_rows)
 
@@ -182,7 +190,7 @@ class ExpertParallel:
         ep = self.epoch
         self.comm.dispatch(dy, st.topk_e, st.topk_w, st.slot, self.e2r, self.e2l, st.self_tok, st.send_count,
                            False, ep, self.done[0:1], self.status, self.timeout_s)
-        dyp = torch.empty(self.cap_rows, self.H, dtype=torch.bfloat16, device=self.device)
+        dyp = torch.empty(st.xp.shape[0], self.H, dtype=torch.bfloat16, device=self.device)
         self.comm.recv_gather(dy, st.self_tok, st.row_src, st.group_off, st.send_count, dyp, ep, self.done[0:1],
                               self.status, self.timeout_s)
         return dyp
@@ -216,7 +224,7 @@ class _EPMoE(torch.autograd.Function):
         w_gu, w_d, gu = ctx.saved_tensors
         dout = dout.contiguous()
         dyp = ep.dispatch_bwd(dout, st)
-        row_dw = torch.zeros(ep.cap_rows, dtype=torch.float32, device=dout.device)
+        row_dw = torch.zeros(st.xp.shape[0], dtype=torch.float32, device=dout.device)
         dgu, hw, row_dw = gg.gg_swiglu_bwd(dyp, w_d, st.group_off, gu, st.row_w, row_dw=row_dw, status=ep.status)
         fused = getattr(sink, "fused_wgrad", None) if sink is not None else None
         g_gu = g_d = None
