@@ -211,6 +211,68 @@ class EpComm {
   sepx::EpArgs args_;
 };
 
+// Generic symmetric buffer: one cudaMalloc per rank, IPC-mapped on every peer. ``put``
+// copies a local tensor into a peer's buffer with one cudaMemcpyAsync (copy engine over
+// NVLink); used by the expert-weight transfer path (placement changes) and its benchmark.
+class SymmBuffer {
+ public:
+  SymmBuffer(int world, int rank, int64_t bytes, int device) : world_(world), rank_(rank), device_(device) {
+    TORCH_CHECK(world >= 1 && world <= 64 && rank >= 0 && rank < world, "bad world/rank");
+    c10::cuda::CUDAGuard g(device);
+    bytes_ = (size_t)bytes;
+    CUDA_OK(cudaMalloc(&base_, bytes_));
+    CUDA_OK(cudaMemset(base_, 0, bytes_));
+    peers_.assign(world, nullptr);
+    peers_[rank] = base_;
+  }
+  ~SymmBuffer() { close(); }
+  void close() {
+    if (!base_) return;
+    c10::cuda::CUDAGuard g(device_);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < world_; ++r)
+      if (r != rank_ && peers_[r]) cudaIpcCloseMemHandle(peers_[r]);
+    cudaFree(base_);
+    base_ = nullptr;
+  }
+  py::bytes ipc_handle() const {
+    cudaIpcMemHandle_t h;
+    CUDA_OK(cudaIpcGetMemHandle(&h, base_));
+    return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+  }
+  void open_peers(const std::vector<py::bytes>& handles) {
+    TORCH_CHECK((int)handles.size() == world_, "need one handle per rank");
+    c10::cuda::CUDAGuard g(device_);
+    for (int r = 0; r < world_; ++r) {
+      if (r == rank_) continue;
+      std::string s = handles[r];
+      cudaIpcMemHandle_t h;
+      memcpy(&h, s.data(), sizeof(h));
+      CUDA_OK(cudaIpcOpenMemHandle(&peers_[r], h, cudaIpcMemLazyEnablePeerAccess));
+    }
+  }
+  // local view as a uint8 tensor (no copy; lifetime tied to this object)
+  at::Tensor local() const {
+    return torch::from_blob(base_, {(int64_t)bytes_}, torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device_));
+  }
+  void put(const at::Tensor& src, int peer, int64_t byte_offset) {
+    TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "src must be a contiguous CUDA tensor");
+    TORCH_CHECK(peer >= 0 && peer < world_ && peers_[peer], "peer not mapped");
+    const size_t n = src.numel() * src.element_size();
+    TORCH_CHECK(byte_offset >= 0 && (size_t)byte_offset + n <= bytes_, "put out of bounds");
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    CUDA_OK(cudaMemcpyAsync(static_cast<char*>(peers_[peer]) + byte_offset, src.data_ptr(), n,
+                            cudaMemcpyDeviceToDevice, st));
+  }
+  int64_t size() const { return (int64_t)bytes_; }
+
+ private:
+  int world_, rank_, device_;
+  void* base_ = nullptr;
+  size_t bytes_ = 0;
+  std::vector<void*> peers_;
+};
+
 }  // namespace
 
 void register_ep_comm(pybind11::module& m) {
@@ -230,4 +292,12 @@ void register_ep_comm(pybind11::module& m) {
       .def("recv_gather", &EpComm::recv_gather)
       .def("combine", &EpComm::combine)
       .def("source_reduce", &EpComm::source_reduce);
+  py::class_<SymmBuffer>(m, "SymmBuffer")
+      .def(py::init<int, int, int64_t, int>(), py::arg("world"), py::arg("rank"), py::arg("bytes"), py::arg("device"))
+      .def("close", &SymmBuffer::close)
+      .def("ipc_handle", &SymmBuffer::ipc_handle)
+      .def("open_peers", &SymmBuffer::open_peers)
+      .def("local", &SymmBuffer::local)
+      .def("put", &SymmBuffer::put)
+      .def("size", &SymmBuffer::size);
 }

@@ -1,0 +1,100 @@
+"""transformers and DeepSpeed-config integrations."""
+import json
+import os
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_configs_parse():
+    from spec_ep.integrations.ds_moe import load_config
+
+    for name, size in (("qwen_ep4.json", 4), ("qwen_ep8.json", 8)):
+        cfg = load_config(os.path.join(ROOT, "configs", name))
+        assert cfg.autoep_size == size and cfg.enabled and cfg.preset_model == "qwen3_5_moe"
+        assert cfg.micro_batch == 16 and cfg.sepx.dispatch == "p2p"
+    cfg = load_config(os.path.join(ROOT, "configs", "qwen3_30b_a3b_ep8_sepx.json"))
+    assert cfg.sepx.timeout_us == 10_000_000 and cfg.optimizer["type"] == "AdamW"
+
+
+def test_config_validation():
+    from spec_ep.integrations.ds_moe import load_config
+
+    with pytest.raises(ValueError):
+        load_config({"expert_parallel": {"preset_model": "llama"}})
+    with pytest.raises(ValueError):
+        load_config({"expert_parallel": {"sepx": {"dispatch": "smoke-signals"}}})
+
+
+def test_hf_config_conversion():
+    from spec_ep.integrations.hf_qwen import config_from_hf, random_hf_model
+
+    m = random_hf_model()
+    c = config_from_hf(m.config)
+    assert (c.num_experts, c.top_k, c.hidden_size, c.head_dim) == (8, 2, 512, 128)
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
+
+
+@pytest.mark.gpu
+def test_swapped_hf_blocks_match_hf():
+    from spec_ep.integrations.hf_qwen import random_hf_model, swap_moe_blocks
+    from spec_ep.parallel.ep import ExpertParallel
+
+    m = random_hf_model().cuda().eval()
+    ids = torch.randint(0, 4096, (1, 256), device="cuda")
+    with torch.no_grad():
+        ref = m(input_ids=ids).logits.float()
+        ep = ExpertParallel(8, 2, 512, max_tokens=256)
+        assert swap_moe_blocks(m, ep) == 2
+        out = m(input_ids=ids).logits.float()
+    torch.cuda.synchronize()
+    ep.check()
+    assert _rel(out, ref) < 3e-2
+    ep.close()
+
+
+@pytest.mark.gpu
+def test_spec_ep_model_from_hf_matches_hf_logits():
+    from spec_ep.integrations.hf_qwen import config_from_hf, from_hf, random_hf_model, to_hf_state_dict
+    from spec_ep.models.qwen3_moe import Qwen3MoeForCausalLM
+    from spec_ep.parallel.ep import ExpertParallel
+
+    hf = random_hf_model().cuda().eval()
+    cfg = config_from_hf(hf.config)
+    ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=256)
+    model = Qwen3MoeForCausalLM(cfg, ep)
+    from_hf(hf, model)
+    ids = torch.randint(0, cfg.vocab_size, (1, 256), device="cuda")
+    with torch.no_grad():
+        ref = hf(input_ids=ids).logits.float()[0]
+        out = model(ids).float()
+    torch.cuda.synchronize()
+    ep.check()
+    assert _rel(out, ref) < 3e-2
+    sd = to_hf_state_dict(model)
+    hsd = hf.state_dict()
+    for k, v in sd.items():
+        assert torch.equal(v, hsd[k].to(v.dtype)), k
+    ep.close()
+
+
+@pytest.mark.gpu
+def test_ds_style_initialize_on_hf_model():
+    from spec_ep.integrations.ds_moe import initialize
+    from spec_ep.integrations.hf_qwen import random_hf_model
+
+    m = random_hf_model()
+    cfg = json.load(open(os.path.join(ROOT, "configs", "qwen3_30b_a3b_ep8_sepx.json")))
+    cfg["expert_parallel"]["autoep_size"] = 1
+    engine, opt, _, _ = initialize(model=m, config=cfg, max_tokens=128)
+    engine.eval()
+    with torch.no_grad():
+        out = engine(input_ids=torch.randint(0, 4096, (1, 128), device="cuda"), use_cache=False)
+    assert out.logits.shape == (1, 128, 4096)
+    engine.ep.check()
+    engine.ep.close()

@@ -1,0 +1,58 @@
+"""Routing dump format, visualiser (headless) and host-side utilities (CPU)."""
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_routing_recorder_dump_and_visualiser(tmp_path):
+    sys.path.insert(0, os.path.join(ROOT, "visualization"))
+    import visualize_expert_routing as viz
+
+    from spec_ep.utils.profile import RoutingRecorder, load_routing
+
+    for r in range(2):
+        rec = RoutingRecorder()
+        for l in range(3):
+            rec.record(l, torch.randint(0, 16, (32, 4)))
+        p = rec.save(tmp_path, rank=r)
+        t = torch.load(p)
+        assert t.dtype == torch.int16 and t.shape == (3, 32, 4)
+    files = sorted(tmp_path.glob("experts_rank*.pt"))
+    route = load_routing(files)
+    assert route.shape == (3, 64, 4)
+    out = viz.main([str(f) for f in files] + ["--num_experts", "16", "--num_gpus", "4"])
+    assert out.exists() and out.stat().st_size > 0
+    assert out.with_suffix(".csv").exists()
+
+
+def test_flop_counter_matches_hand_count():
+    from spec_ep.models.config import get_config
+    from spec_ep.utils.profile import FlopCounter
+
+    cfg = get_config("qwen3-30b-a3b")
+    f = FlopCounter(cfg, 4096, 4096).forward_flops()
+    # experts: 2 * T * k * 3 * H * I per layer
+    assert f["experts_per_layer"] == 2 * 4096 * 8 * 3 * 2048 * 768
+    assert f["total"] > 48 * f["experts_per_layer"]
+
+
+def test_env_mapping_from_slurm(monkeypatch):
+    from spec_ep.utils.dist import get_rank_and_world_size
+
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
+        monkeypatch.delenv(k, raising=False)
+    monkeypatch.setenv("SLURM_PROCID", "3")
+    monkeypatch.setenv("SLURM_NTASKS", "8")
+    monkeypatch.setenv("SLURM_LOCALID", "3")
+    assert get_rank_and_world_size() == (3, 8)
+    assert os.environ["LOCAL_RANK"] == "3"
+
+
+def test_imbalance_metric():
+    from spec_ep.utils.metrics import imbalance
+
+    assert abs(imbalance(torch.tensor([10, 10, 10, 10])) - 1.0) < 1e-6
+    assert abs(imbalance(torch.tensor([40, 0, 0, 0])) - 4.0) < 1e-6
