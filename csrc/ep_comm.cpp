@@ -55,6 +55,10 @@ class EpComm {
     args_.off_ret_w = take(sizeof(float) * (size_t)world * cap * k);
     args_.off_recv_x = take((size_t)2 * world * cap * hidden);
     args_.off_ret_x = take((size_t)2 * world * cap * hidden);
+    if (hidden % 128 == 0) {  // e4m3 payload slabs for fp8 dispatch
+      args_.off_recv_q = take((size_t)world * cap * hidden);
+      args_.off_recv_s = take(sizeof(float) * (size_t)world * cap * (hidden / 128));
+    }
     bytes_ = off;
     CUDA_OK(cudaMalloc(&heap_, bytes_));
     CUDA_OK(cudaMemset(heap_, 0, bytes_));
@@ -121,14 +125,14 @@ class EpComm {
 
   void dispatch(const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w, const at::Tensor& slot,
                 const at::Tensor& e2r, const at::Tensor& e2l, at::Tensor& self_tok, const at::Tensor& send_count,
-                bool with_meta, int64_t epoch, at::Tensor& done, at::Tensor& status, double timeout_s) {
+                bool with_meta, int64_t epoch, at::Tensor& done, at::Tensor& status, double timeout_s, bool fp8) {
     TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x must be contiguous bf16");
     TORCH_CHECK(x.size(1) == args_.H, "hidden size mismatch");
     auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
     sepx::ep_dispatch(a, x.data_ptr(), topk_e.data_ptr<int>(), topk_w.data_ptr<float>(), slot.data_ptr<int>(),
                       e2r.data_ptr<int>(), e2l.data_ptr<int>(), self_tok.data_ptr<int>(),
-                      send_count.data_ptr<int>(), with_meta, st);
+                      send_count.data_ptr<int>(), with_meta, st, fp8);
   }
 
   void recv_plan(const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w, const at::Tensor& self_tok,
@@ -163,7 +167,7 @@ class EpComm {
                            const at::Tensor& send_count, int G, int64_t epoch, const at::Tensor& rows_from,
                            const at::Tensor& chunk_cnt, const at::Tensor& group_off, const at::Tensor& group_cnt,
                            const at::Tensor& pad_off, at::Tensor& xp, at::Tensor& row_w, at::Tensor& row_src,
-                           at::Tensor& inv_rows, at::Tensor& done, at::Tensor& status, double timeout_s) {
+                           at::Tensor& inv_rows, at::Tensor& done, at::Tensor& status, double timeout_s, bool fp8) {
     TORCH_CHECK(xp.size(1) == args_.H && xp.is_contiguous(), "xp must be [rows, H]");
     auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
@@ -172,7 +176,7 @@ class EpComm {
                                  send_count.data_ptr<int>(), G, rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(),
                                  group_off.data_ptr<int>(), group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(),
                                  xp.data_ptr(), row_w.data_ptr<float>(), row_src.data_ptr<int>(),
-                                 inv_rows.data_ptr<int>(), st);
+                                 inv_rows.data_ptr<int>(), st, fp8);
   }
 
   void recv_gather(const at::Tensor& x, const at::Tensor& self_tok, const at::Tensor& row_src,

@@ -18,6 +18,7 @@ struct EpArgs {
   void* peer_base[64];  // base of every rank's symmetric region (this rank's included)
   size_t off_recv_x = 0, off_recv_e = 0, off_recv_w = 0;
   size_t off_ret_x = 0, off_ret_w = 0, off_hdr = 0;
+  size_t off_recv_q = 0, off_recv_s = 0;  // e4m3 rows [W][cap][H] and 1x128 scales [W][cap][H/128]
   int W = 1, rank = 0;
   int cap = 0;  // slots per source (max tokens per rank per call)
   int k = 1;
@@ -34,7 +35,7 @@ void ep_route_plan(const int* topk_e, int T, int k, const int* e2r, int W, int* 
                    int* send_count, cudaStream_t st);
 void ep_dispatch(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
                  const int* slot, const int* e2r, const int* e2l, int* self_tok,
-                 const int* send_count, bool with_meta, cudaStream_t st);
+                 const int* send_count, bool with_meta, cudaStream_t st, bool fp8 = false);
 void ep_recv_plan(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
                   const int* self_tok, const int* e2r, const int* e2l, const int* send_count,
                   int G, int cap_rows, int* rows_from, int* chunk_cnt, int* group_off,
@@ -49,7 +50,7 @@ void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* topk_e, c
                             const int* self_tok, const int* e2r, const int* e2l, const int* send_count, int G,
                             const int* rows_from, const int* chunk_cnt, const int* group_off, const int* group_cnt,
                             const int* pad_off, void* xp, float* row_w, int* row_src, int* inv_rows,
-                            cudaStream_t st);
+                            cudaStream_t st, bool fp8 = false);
 void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const int* row_src,
                     const int* total_rows, const int* send_count, void* xp, int cap_rows,
                     cudaStream_t st);

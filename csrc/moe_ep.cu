@@ -22,6 +22,7 @@
 //
 // Rows a rank sends to itself never cross the slab: the permute reads x directly and
 // the slot->token map for self rows is kept locally.
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <stdexcept>
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
                                                        const int* __restrict__ e2l,
                                                        int* __restrict__ self_tok,
                                                        const int* __restrict__ send_count,
-                                                       int with_meta) {
+                                                       int with_meta, int fp8) {
   const int lane = threadIdx.x & 31;
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -168,6 +169,54 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
       for (int i = 0; i < 8; ++i) {
         int c = c0 + i * 32 + lane;
         if (c < vec) r[i] = __ldg(src + c);
+      }
+      if (fp8) {
+        // e4m3 payload, one fp32 scale per 128 values (= 16 lanes x 8 values)
+        uint2 q[8];
+        float sc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = c0 + i * 32 + lane;
+          float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          if (c < vec) {
+            float2 a0 = unpack_bf16x2(r[i].x), a1 = unpack_bf16x2(r[i].y), a2 = unpack_bf16x2(r[i].z),
+                   a3 = unpack_bf16x2(r[i].w);
+            f[0] = a0.x; f[1] = a0.y; f[2] = a1.x; f[3] = a1.y; f[4] = a2.x; f[5] = a2.y; f[6] = a3.x; f[7] = a3.y;
+          }
+          float amax = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+#pragma unroll
+          for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, o));
+          sc[i] = amax > 0.f ? amax / 448.f : 1.f;
+          const float inv = 1.f / sc[i];
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_fp8x2_storage_t p2 =
+                __nv_cvt_float2_to_fp8x2(make_float2(f[2 * e] * inv, f[2 * e + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+            w[e] = (uint32_t)p2;
+          }
+          q[i] = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
+        }
+        unsigned long long rm = remote;
+        while (rm) {
+          int d = __ffsll(rm) - 1;
+          rm &= rm - 1;
+          int s = __ldg(slot + (size_t)t * a.W + d);
+          char* base = reinterpret_cast<char*>(a.peer_base[d]);
+          uint2* dq = reinterpret_cast<uint2*>(base + a.off_recv_q) + ((size_t)a.rank * a.cap + s) * vec;
+          float* ds = reinterpret_cast<float*>(base + a.off_recv_s) + ((size_t)a.rank * a.cap + s) * (a.H / 128);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            int c = c0 + i * 32 + lane;
+            if (c < vec) {
+              dq[c] = q[i];
+              if ((lane & 15) == 0) ds[c / 16] = sc[i];
+            }
+          }
+        }
+        continue;
       }
       unsigned long long rm = remote;
       while (rm) {
@@ -401,7 +450,7 @@ __global__ void __launch_bounds__(256) recv_gather_kernel(EpArgs a, const __nv_b
                                                           const int* __restrict__ row_src,
                                                           const int* __restrict__ total_rows,
                                                           const int* __restrict__ send_count,
-                                                          __nv_bfloat16* __restrict__ xp) {
+                                                          __nv_bfloat16* __restrict__ xp, int fp8 = 0) {
   // every block first waits for all peers' headers of this phase
   if (threadIdx.x < a.W) {
     const int src = threadIdx.x;
@@ -427,6 +476,28 @@ __global__ void __launch_bounds__(256) recv_gather_kernel(EpArgs a, const __nv_b
       continue;
     }
     const int src = code / a.cap, s = code % a.cap;
+    if (fp8 && src != a.rank) {
+      const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+      const uint2* q = reinterpret_cast<const uint2*>(base + a.off_recv_q) + ((size_t)src * a.cap + s) * vec;
+      const float* sc = reinterpret_cast<const float*>(base + a.off_recv_s) + ((size_t)src * a.cap + s) * (a.H / 128);
+      for (int c = lane; c < vec; c += 32) {
+        const uint2 w = q[c];
+        const float scale = sc[c / 16];
+        const uint32_t ww[2] = {w.x, w.y};
+        uint32_t o[4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)((ww[h] >> (16 * e)) & 0xFFFF), __NV_E4M3);
+            float2 f = __half22float2(*reinterpret_cast<__half2*>(&hr));
+            o[2 * h + e] = pack_bf16x2(f.x * scale, f.y * scale);
+          }
+        }
+        dst[c] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      continue;
+    }
     const uint4* srow;
     if (src == a.rank) {
       srow = reinterpret_cast<const uint4*>(x + (size_t)self_tok[s] * a.H);
@@ -586,12 +657,14 @@ void ep_route_plan(const int* topk_e, int T, int k, const int* e2r, int W, int* 
 
 void ep_dispatch(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w, const int* slot,
                  const int* e2r, const int* e2l, int* self_tok, const int* send_count, bool with_meta,
-                 cudaStream_t st) {
+                 cudaStream_t st, bool fp8) {
+  if (fp8 && (a.H % 128 || a.off_recv_q == 0)) throw std::runtime_error("fp8 dispatch needs H % 128 == 0 and fp8 slabs");
   if (a.H % 8) throw std::runtime_error("hidden size must be a multiple of 8");
   if (a.k > 32) throw std::runtime_error("top-k above 32 is not supported");
   int blocks = sm_count() * 2;
   dispatch_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w,
-                                          slot, e2r, e2l, self_tok, send_count, with_meta ? 1 : 0);
+                                          slot, e2r, e2l, self_tok, send_count, with_meta ? 1 : 0,
+                                          fp8 ? 1 : 0);
   check_launch("dispatch");
 }
 
@@ -635,7 +708,7 @@ void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* topk_e, c
                             const int* self_tok, const int* e2r, const int* e2l, const int* send_count, int G,
                             const int* rows_from, const int* chunk_cnt, const int* group_off, const int* group_cnt,
                             const int* pad_off, void* xp, float* row_w, int* row_src, int* inv_rows,
-                            cudaStream_t st) {
+                            cudaStream_t st, bool fp8) {
   const int nchunks = ((a.cap + kChunk - 1) / kChunk) * a.W;
   recv_permute_kernel<<<nchunks, kChunk, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w,
                                                   self_tok, e2r, e2l, rows_from, chunk_cnt, G, group_off, group_cnt,
@@ -643,7 +716,8 @@ void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* topk_e, c
                                                   inv_rows);
   check_launch("recv_permute");
   recv_gather_kernel<<<sm_count() * 4, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), self_tok, row_src,
-                                                     group_off + G, send_count, reinterpret_cast<__nv_bfloat16*>(xp));
+                                                     group_off + G, send_count, reinterpret_cast<__nv_bfloat16*>(xp),
+                                                     fp8 ? 1 : 0);
   check_launch("recv_gather");
 }
 

@@ -169,3 +169,50 @@ def test_ep_moe_balanced_placement_with_replicas():
     errq = ctx.SimpleQueue()
     mp.spawn(_placement_worker, args=(world, _free_port(), errq), nprocs=world, join=True)
     assert errq.empty()
+
+
+def _fp8_worker(rank, world, port, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        from spec_ep.parallel.ep import ExpertParallel, ep_moe
+
+        T, E, k, H, I = 1024, 16, 4, 1024, 256
+        g = torch.Generator().manual_seed(0)
+        epr = E // world
+        w_gu = (torch.randn(E, 2 * I, H, generator=g) / H**0.5).bfloat16().to(dev)[rank * epr:(rank + 1) * epr]
+        w_d = (torch.randn(E, H, I, generator=g) / I**0.5).bfloat16().to(dev)[rank * epr:(rank + 1) * epr]
+        torch.manual_seed(30 + rank)
+        x = torch.randn(T, H, device=dev).bfloat16()
+        tw, te = torch.softmax(torch.randn(T, E, device=dev), -1).topk(k, -1)
+        ep16 = ExpertParallel(E, k, H, max_tokens=T, device=dev)
+        ep8 = ExpertParallel(E, k, H, max_tokens=T, device=dev, fp8_dispatch=True)
+        with torch.no_grad():
+            ref = ep_moe(x, te.int(), tw, w_gu.contiguous(), w_d.contiguous(), ep16)
+            out = ep_moe(x, te.int(), tw, w_gu.contiguous(), w_d.contiguous(), ep8)
+        torch.cuda.synchronize()
+        ep16.check()
+        ep8.check()
+        err = _rel(out, ref)
+        assert 0 < err < 0.08, err  # e4m3 payload: small but non-zero error
+        dist.barrier()
+        ep16.close()
+        ep8.close()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+def test_ep_moe_fp8_dispatch():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.spawn(_fp8_worker, args=(min(n, 4), _free_port(), errq), nprocs=min(n, 4), join=True)
+    assert errq.empty()

@@ -40,6 +40,37 @@ def _rel(a, b):
     return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
 
 
+def _token_agreement(out, ref, tol=3e-2):
+    """Fraction of tokens whose logits match within ``tol`` (relative to the token's max).
+
+    Near-tied router probabilities can pick a different expert for a few tokens when two
+    softmax implementations round differently; those tokens then legitimately differ.
+    """
+    err = (out.float() - ref.float()).abs().amax(-1) / ref.float().abs().amax(-1).clamp_min(1e-6)
+    return float((err < tol).float().mean())
+
+
+@pytest.mark.gpu
+def test_swapped_block_matches_hf_experts_with_same_routing():
+    """Same routing decisions in, same expert output out (isolates numerics from top-k ties)."""
+    from spec_ep.integrations.hf_qwen import SepxQwen3MoeBlock, random_hf_model
+    from spec_ep.parallel.ep import ExpertParallel, ep_moe
+
+    m = random_hf_model().cuda().eval()
+    block = m.model.layers[0].mlp
+    x = torch.randn(256, 512, device="cuda").bfloat16()
+    with torch.no_grad():
+        _, w, e = block.gate(x)
+        ref = block.experts(x, e, w).float()
+        ep = ExpertParallel(8, 2, 512, max_tokens=256)
+        sb = SepxQwen3MoeBlock.from_hf_block(block, ep)
+        out = ep_moe(x, e.int(), w.float(), sb.gate_up_proj, sb.down_proj, ep).float()
+    torch.cuda.synchronize()
+    ep.check()
+    assert _rel(out, ref) < 2e-2
+    ep.close()
+
+
 @pytest.mark.gpu
 def test_swapped_hf_blocks_match_hf():
     from spec_ep.integrations.hf_qwen import random_hf_model, swap_moe_blocks
@@ -48,13 +79,13 @@ def test_swapped_hf_blocks_match_hf():
     m = random_hf_model().cuda().eval()
     ids = torch.randint(0, 4096, (1, 256), device="cuda")
     with torch.no_grad():
-        ref = m(input_ids=ids).logits.float()
+        ref = m(input_ids=ids).logits.float()[0]
         ep = ExpertParallel(8, 2, 512, max_tokens=256)
         assert swap_moe_blocks(m, ep) == 2
-        out = m(input_ids=ids).logits.float()
+        out = m(input_ids=ids).logits.float()[0]
     torch.cuda.synchronize()
     ep.check()
-    assert _rel(out, ref) < 3e-2
+    assert _token_agreement(out, ref) > 0.95
     ep.close()
 
 
@@ -75,7 +106,7 @@ def test_spec_ep_model_from_hf_matches_hf_logits():
         out = model(ids).float()
     torch.cuda.synchronize()
     ep.check()
-    assert _rel(out, ref) < 3e-2
+    assert _token_agreement(out, ref) > 0.95
     sd = to_hf_state_dict(model)
     hsd = hf.state_dict()
     for k, v in sd.items():
