@@ -117,66 +117,52 @@ class EpComm {
     return a;
   }
 
-  void route_plan(const at::Tensor& topk_e, const at::Tensor& e2r, at::Tensor& slot, at::Tensor& send_count) {
+  void route_plan(const at::Tensor& dst_tk, at::Tensor& slot, at::Tensor& send_count) {
+    TORCH_CHECK(dst_tk.scalar_type() == at::kInt && dst_tk.is_contiguous() && dst_tk.dim() == 2, "dst_tk [T, k] int32");
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
-    sepx::ep_route_plan(topk_e.data_ptr<int>(), topk_e.size(0), topk_e.size(1), e2r.data_ptr<int>(), world_,
-                        slot.data_ptr<int>(), send_count.data_ptr<int>(), st);
+    sepx::ep_route_plan(dst_tk.data_ptr<int>(), dst_tk.size(0), dst_tk.size(1), world_, slot.data_ptr<int>(),
+                        send_count.data_ptr<int>(), st);
   }
 
-  void dispatch(const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w, const at::Tensor& slot,
-                const at::Tensor& e2r, const at::Tensor& e2l, at::Tensor& self_tok, const at::Tensor& send_count,
-                bool with_meta, int64_t epoch, at::Tensor& done, at::Tensor& status, double timeout_s, bool fp8) {
+  void dispatch(const at::Tensor& x, const at::Tensor& dst_tk, const at::Tensor& meta_tk, const at::Tensor& topk_w,
+                const at::Tensor& slot, at::Tensor& self_tok, const at::Tensor& send_count, bool with_meta,
+                int64_t epoch, at::Tensor& done, at::Tensor& status, double timeout_s, bool fp8) {
     TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x must be contiguous bf16");
     TORCH_CHECK(x.size(1) == args_.H, "hidden size mismatch");
+    TORCH_CHECK(dst_tk.size(0) == x.size(0) && meta_tk.size(0) == x.size(0), "routing rows must match tokens");
     auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
-    sepx::ep_dispatch(a, x.data_ptr(), topk_e.data_ptr<int>(), topk_w.data_ptr<float>(), slot.data_ptr<int>(),
-                      e2r.data_ptr<int>(), e2l.data_ptr<int>(), self_tok.data_ptr<int>(),
-                      send_count.data_ptr<int>(), with_meta, st, fp8);
+    sepx::ep_dispatch(a, x.data_ptr(), dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), topk_w.data_ptr<float>(),
+                      slot.data_ptr<int>(), self_tok.data_ptr<int>(), send_count.data_ptr<int>(), with_meta, st, fp8);
   }
 
-  void recv_plan(const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w, const at::Tensor& self_tok,
-                 const at::Tensor& e2r, const at::Tensor& e2l, const at::Tensor& send_count, int G, int64_t epoch,
-                 at::Tensor& rows_from, at::Tensor& chunk_cnt, at::Tensor& group_off, at::Tensor& group_cnt,
-                 at::Tensor& pad_off, at::Tensor& xp, at::Tensor& row_w, at::Tensor& row_src, at::Tensor& inv_rows,
-                 at::Tensor& done, at::Tensor& status, double timeout_s) {
-    auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
-    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
-    sepx::ep_recv_plan(a, x.data_ptr(), topk_e.data_ptr<int>(), topk_w.data_ptr<float>(), self_tok.data_ptr<int>(),
-                       e2r.data_ptr<int>(), e2l.data_ptr<int>(), send_count.data_ptr<int>(), G, (int)xp.size(0),
-                       rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(), group_off.data_ptr<int>(),
-                       group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(), xp.data_ptr(), row_w.data_ptr<float>(),
-                       row_src.data_ptr<int>(), inv_rows.data_ptr<int>(), st);
-  }
-
-  void recv_count_scan(const at::Tensor& topk_e, const at::Tensor& topk_w, const at::Tensor& self_tok,
-                       const at::Tensor& e2r, const at::Tensor& e2l, const at::Tensor& send_count, int G, int T,
-                       int cap_rows, int64_t epoch, at::Tensor& rows_from, at::Tensor& chunk_cnt,
-                       at::Tensor& group_off, at::Tensor& group_cnt, at::Tensor& pad_off, at::Tensor& done,
-                       at::Tensor& status, double timeout_s) {
+  void recv_count_scan(const at::Tensor& dst_tk, const at::Tensor& meta_tk, const at::Tensor& topk_w,
+                       const at::Tensor& self_tok, const at::Tensor& send_count, int G, int T, int cap_rows,
+                       int64_t epoch, at::Tensor& rows_from, at::Tensor& chunk_cnt, at::Tensor& group_off,
+                       at::Tensor& group_cnt, at::Tensor& pad_off, at::Tensor& done, at::Tensor& status,
+                       double timeout_s) {
     auto a = call_args(T, 0, epoch, done, status, timeout_s);
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
-    sepx::ep_recv_count_scan(a, topk_e.data_ptr<int>(), topk_w.data_ptr<float>(), self_tok.data_ptr<int>(),
-                             e2r.data_ptr<int>(), e2l.data_ptr<int>(), send_count.data_ptr<int>(), G, cap_rows,
+    sepx::ep_recv_count_scan(a, dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), topk_w.data_ptr<float>(),
+                             self_tok.data_ptr<int>(), send_count.data_ptr<int>(), G, cap_rows,
                              rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(), group_off.data_ptr<int>(),
                              group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(), st);
   }
 
-  void recv_permute_gather(const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w,
-                           const at::Tensor& self_tok, const at::Tensor& e2r, const at::Tensor& e2l,
-                           const at::Tensor& send_count, int G, int64_t epoch, const at::Tensor& rows_from,
-                           const at::Tensor& chunk_cnt, const at::Tensor& group_off, const at::Tensor& group_cnt,
-                           const at::Tensor& pad_off, at::Tensor& xp, at::Tensor& row_w, at::Tensor& row_src,
-                           at::Tensor& inv_rows, at::Tensor& done, at::Tensor& status, double timeout_s, bool fp8) {
+  void recv_permute_gather(const at::Tensor& x, const at::Tensor& dst_tk, const at::Tensor& meta_tk,
+                           const at::Tensor& topk_w, const at::Tensor& self_tok, const at::Tensor& send_count, int G,
+                           int64_t epoch, const at::Tensor& rows_from, const at::Tensor& chunk_cnt,
+                           const at::Tensor& group_off, const at::Tensor& group_cnt, const at::Tensor& pad_off,
+                           at::Tensor& xp, at::Tensor& row_w, at::Tensor& row_src, at::Tensor& inv_rows,
+                           at::Tensor& done, at::Tensor& status, double timeout_s, bool fp8) {
     TORCH_CHECK(xp.size(1) == args_.H && xp.is_contiguous(), "xp must be [rows, H]");
     auto a = call_args(x.size(0), 0, epoch, done, status, timeout_s);
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
-    sepx::ep_recv_permute_gather(a, x.data_ptr(), topk_e.data_ptr<int>(), topk_w.data_ptr<float>(),
-                                 self_tok.data_ptr<int>(), e2r.data_ptr<int>(), e2l.data_ptr<int>(),
-                                 send_count.data_ptr<int>(), G, rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(),
-                                 group_off.data_ptr<int>(), group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(),
-                                 xp.data_ptr(), row_w.data_ptr<float>(), row_src.data_ptr<int>(),
-                                 inv_rows.data_ptr<int>(), st, fp8);
+    sepx::ep_recv_permute_gather(a, x.data_ptr(), dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(),
+                                 topk_w.data_ptr<float>(), self_tok.data_ptr<int>(), send_count.data_ptr<int>(), G,
+                                 rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(), group_off.data_ptr<int>(),
+                                 group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(), xp.data_ptr(),
+                                 row_w.data_ptr<float>(), row_src.data_ptr<int>(), inv_rows.data_ptr<int>(), st, fp8);
   }
 
   void recv_gather(const at::Tensor& x, const at::Tensor& self_tok, const at::Tensor& row_src,
@@ -189,6 +175,24 @@ class EpComm {
                          group_off.data_ptr<int>() + G, send_count.data_ptr<int>(), xp.data_ptr(), (int)xp.size(0), st);
   }
 
+  void wait_rows(const at::Tensor& send_count, at::Tensor& rows_from, int T, int phase, int64_t epoch,
+                 at::Tensor& done, at::Tensor& status, double timeout_s) {
+    auto a = call_args(T, phase, epoch, done, status, timeout_s);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_wait_rows(a, send_count.data_ptr<int>(), rows_from.data_ptr<int>(), st);
+  }
+
+  // Views of this rank's receive slabs (no copy): rows [W, cap, H] bf16, choice metadata
+  // [W, cap, k] int16, gate weights [W, cap, k] fp32.
+  std::vector<at::Tensor> slabs() const {
+    auto opt = torch::TensorOptions().device(torch::kCUDA, device_);
+    char* b = static_cast<char*>(heap_);
+    const int64_t W = world_, cap = args_.cap, H = args_.H, k = args_.k;
+    return {torch::from_blob(b + args_.off_recv_x, {W, cap, H}, opt.dtype(torch::kBFloat16)),
+            torch::from_blob(b + args_.off_recv_e, {W, cap, k}, opt.dtype(torch::kShort)),
+            torch::from_blob(b + args_.off_recv_w, {W, cap, k}, opt.dtype(torch::kFloat))};
+  }
+
   void combine(const at::Tensor& y, const at::Tensor& inv_rows, const at::Tensor& row_w, const at::Tensor& rows_from,
                bool weighted, const c10::optional<at::Tensor>& row_val, int T, int64_t epoch, at::Tensor& done,
                at::Tensor& status, double timeout_s) {
@@ -198,12 +202,12 @@ class EpComm {
                      weighted, row_val.has_value() ? row_val->data_ptr<float>() : nullptr, st);
   }
 
-  void source_reduce(const at::Tensor& slot, const at::Tensor& topk_e, const at::Tensor& e2r,
-                     const c10::optional<at::Tensor>& residual, at::Tensor& out, const c10::optional<at::Tensor>& val,
-                     int64_t epoch, at::Tensor& done, at::Tensor& status, double timeout_s) {
+  void source_reduce(const at::Tensor& slot, const at::Tensor& dst_tk, const c10::optional<at::Tensor>& residual,
+                     at::Tensor& out, const c10::optional<at::Tensor>& val, int64_t epoch, at::Tensor& done,
+                     at::Tensor& status, double timeout_s) {
     auto a = call_args(out.size(0), 1, epoch, done, status, timeout_s);
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
-    sepx::ep_source_reduce(a, slot.data_ptr<int>(), topk_e.data_ptr<int>(), e2r.data_ptr<int>(),
+    sepx::ep_source_reduce(a, slot.data_ptr<int>(), dst_tk.data_ptr<int>(),
                            residual.has_value() ? residual->data_ptr() : nullptr, out.data_ptr(),
                            val.has_value() ? val->data_ptr<float>() : nullptr, st);
   }
@@ -290,10 +294,11 @@ void register_ep_comm(pybind11::module& m) {
       .def("peer_base", &EpComm::peer_base)
       .def("route_plan", &EpComm::route_plan)
       .def("dispatch", &EpComm::dispatch)
-      .def("recv_plan", &EpComm::recv_plan)
       .def("recv_count_scan", &EpComm::recv_count_scan)
       .def("recv_permute_gather", &EpComm::recv_permute_gather)
       .def("recv_gather", &EpComm::recv_gather)
+      .def("wait_rows", &EpComm::wait_rows)
+      .def("slabs", &EpComm::slabs)
       .def("combine", &EpComm::combine)
       .def("source_reduce", &EpComm::source_reduce);
   py::class_<SymmBuffer>(m, "SymmBuffer")

@@ -31,32 +31,30 @@ struct EpArgs {
   unsigned long long timeout_ns = 5000000000ull;
 };
 
-void ep_route_plan(const int* topk_e, int T, int k, const int* e2r, int W, int* slot,
-                   int* send_count, cudaStream_t st);
-void ep_dispatch(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
-                 const int* slot, const int* e2r, const int* e2l, int* self_tok,
-                 const int* send_count, bool with_meta, cudaStream_t st, bool fp8 = false);
-void ep_recv_plan(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
-                  const int* self_tok, const int* e2r, const int* e2l, const int* send_count,
-                  int G, int cap_rows, int* rows_from, int* chunk_cnt, int* group_off,
-                  int* group_cnt, int* pad_off, void* xp, float* row_w, int* row_src,
-                  int* inv_rows, cudaStream_t st);
+// Routing of choice j of token t: dst_tk[t][j] = destination rank (-1: not sent),
+// meta_tk[t][j] = value delivered with the row (local expert slot on that rank).
+void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_count, cudaStream_t st);
+void ep_dispatch(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk, const float* topk_w,
+                 const int* slot, int* self_tok, const int* send_count, bool with_meta, cudaStream_t st,
+                 bool fp8 = false);
 // Receive plan in two halves so the caller can size buffers between them: count+scan
 // produce group_off (group_off[G] = rows needed), permute+gather fill them.
-void ep_recv_count_scan(const EpArgs& a, const int* topk_e, const float* topk_w, const int* self_tok,
-                        const int* e2r, const int* e2l, const int* send_count, int G, int cap_rows, int* rows_from,
+void ep_recv_count_scan(const EpArgs& a, const int* dst_tk, const int* meta_tk, const float* topk_w,
+                        const int* self_tok, const int* send_count, int G, int cap_rows, int* rows_from,
                         int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, cudaStream_t st);
-void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
-                            const int* self_tok, const int* e2r, const int* e2l, const int* send_count, int G,
+void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk,
+                            const float* topk_w, const int* self_tok, const int* send_count, int G,
                             const int* rows_from, const int* chunk_cnt, const int* group_off, const int* group_cnt,
                             const int* pad_off, void* xp, float* row_w, int* row_src, int* inv_rows,
                             cudaStream_t st, bool fp8 = false);
 void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const int* row_src,
                     const int* total_rows, const int* send_count, void* xp, int cap_rows,
                     cudaStream_t st);
+// Wait for every source's header of a.phase; rows_from[src] = rows it sent.
+void ep_wait_rows(const EpArgs& a, const int* send_count, int* rows_from, cudaStream_t st);
 void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float* row_w,
                 const int* rows_from, bool weighted, const float* row_val, cudaStream_t st);
-void ep_source_reduce(const EpArgs& a, const int* slot, const int* topk_e, const int* e2r,
-                      const void* residual, void* out, float* val, cudaStream_t st);
+void ep_source_reduce(const EpArgs& a, const int* slot, const int* dst_tk, const void* residual, void* out,
+                      float* val, cudaStream_t st);
 
 }  // namespace sepx

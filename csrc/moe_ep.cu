@@ -59,11 +59,11 @@ __device__ __forceinline__ bool wait_header(const uint64_t* hdr, uint32_t epoch,
 
 // ------------------------------------------------------------------------------------
 // K1: route plan. slot[t][d] = ordinal of token t among tokens sent to rank d (-1 if
-// none of t's experts is on d). Single block; T up to a few 10^4 tokens.
+// none of t's choices goes to d). dst_tk[t][j] is the destination rank of choice j (-1:
+// not sent). Single block; T up to a few 10^4 tokens.
 // ------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict__ topk_e, int T,
-                                                          int k, const int* __restrict__ e2r,
-                                                          int W, int* __restrict__ slot,
+__global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict__ dst_tk, int T,
+                                                          int k, int W, int* __restrict__ slot,
                                                           int* __restrict__ send_count) {
   __shared__ int s_part[1024 / 32][kMaxW];  // per-warp totals per destination
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -75,7 +75,10 @@ __global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict_
   for (int d = 0; d < W; ++d) cnt[d] = 0;
   for (int t = t_begin; t < t_end; ++t) {
     unsigned long long m = 0;
-    for (int j = 0; j < k; ++j) m |= 1ull << e2r[topk_e[t * k + j]];
+    for (int j = 0; j < k; ++j) {
+      const int d = dst_tk[t * k + j];
+      if (d >= 0) m |= 1ull << d;
+    }
     for (int d = 0; d < W; ++d) cnt[d] += (m >> d) & 1;
   }
   // exclusive scan of cnt[d] across threads (warp shuffle + per-warp totals)
@@ -105,7 +108,10 @@ __global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict_
   // pass 2: write slots
   for (int t = t_begin; t < t_end; ++t) {
     unsigned long long m = 0;
-    for (int j = 0; j < k; ++j) m |= 1ull << e2r[topk_e[t * k + j]];
+    for (int j = 0; j < k; ++j) {
+      const int d = dst_tk[t * k + j];
+      if (d >= 0) m |= 1ull << d;
+    }
     for (int d = 0; d < W; ++d) {
       if ((m >> d) & 1) slot[(size_t)t * W + d] = cnt[d]++;
       else slot[(size_t)t * W + d] = -1;
@@ -141,11 +147,10 @@ __device__ __forceinline__ void publish_last_cta(unsigned int* done_counter, con
 // destination's recv_x[rank][slot], with the k (local expert, weight) entries.
 // ------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bfloat16* __restrict__ x,
-                                                       const int* __restrict__ topk_e,
+                                                       const int* __restrict__ dst_tk,
+                                                       const int* __restrict__ meta_tk,
                                                        const float* __restrict__ topk_w,
                                                        const int* __restrict__ slot,
-                                                       const int* __restrict__ e2r,
-                                                       const int* __restrict__ e2l,
                                                        int* __restrict__ self_tok,
                                                        const int* __restrict__ send_count,
                                                        int with_meta, int fp8) {
@@ -157,7 +162,10 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * a.H);
     // destinations of this token
     unsigned long long m = 0;
-    for (int j = 0; j < a.k; ++j) m |= 1ull << __ldg(e2r + __ldg(topk_e + t * a.k + j));
+    for (int j = 0; j < a.k; ++j) {
+      const int d = __ldg(dst_tk + t * a.k + j);
+      if (d >= 0) m |= 1ull << d;
+    }
     if ((m >> a.rank) & 1) {
       if (lane == 0) self_tok[__ldg(slot + (size_t)t * a.W + a.rank)] = t;
     }
@@ -235,8 +243,8 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
     }
     if (with_meta && lane < a.k) {
       const int j = lane;
-      const int e = __ldg(topk_e + t * a.k + j);
-      const int owner = __ldg(e2r + e);
+      const int owner = __ldg(dst_tk + t * a.k + j);
+      const int meta = __ldg(meta_tk + t * a.k + j);
       const float w = __ldg(topk_w + t * a.k + j);
       unsigned long long rm = remote;
       while (rm) {
@@ -246,7 +254,7 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
         char* base = reinterpret_cast<char*>(a.peer_base[d]);
         int16_t* re = reinterpret_cast<int16_t*>(base + a.off_recv_e) + ((size_t)a.rank * a.cap + s) * a.k;
         float* rw = reinterpret_cast<float*>(base + a.off_recv_w) + ((size_t)a.rank * a.cap + s) * a.k;
-        re[j] = (owner == d) ? (int16_t)__ldg(e2l + e) : (int16_t)-1;
+        re[j] = (owner == d) ? (int16_t)meta : (int16_t)-1;
         rw[j] = w;
       }
     }
@@ -258,13 +266,12 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
 // Receive side. Rows are enumerated src-major: (src, slot) for slot < rows_from[src].
 // K4a count: per chunk of 128 rows, rows per local expert -> chunk_cnt[chunk][G].
 // ------------------------------------------------------------------------------------
-__device__ __forceinline__ void row_meta(const EpArgs& a, const int* topk_e, const float* topk_w,
-                                         const int* self_tok, const int* e2r, const int* e2l,
+__device__ __forceinline__ void row_meta(const EpArgs& a, const int* dst_tk, const float* topk_w,
+                                         const int* self_tok, const int* meta_tk,
                                          int src, int s, int j, int* le, float* w) {
   if (src == a.rank) {
     const int t = self_tok[s];
-    const int e = __ldg(topk_e + t * a.k + j);
-    *le = (__ldg(e2r + e) == a.rank) ? __ldg(e2l + e) : -1;
+    *le = (__ldg(dst_tk + t * a.k + j) == a.rank) ? __ldg(meta_tk + t * a.k + j) : -1;
     *w = __ldg(topk_w + t * a.k + j);
   } else {
     const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
@@ -277,11 +284,10 @@ __device__ __forceinline__ void row_meta(const EpArgs& a, const int* topk_e, con
 
 constexpr int kChunk = 128;
 
-__global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int* __restrict__ topk_e,
+__global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int* __restrict__ dst_tk,
                                                             const float* __restrict__ topk_w,
                                                             const int* __restrict__ self_tok,
-                                                            const int* __restrict__ e2r,
-                                                            const int* __restrict__ e2l,
+                                                            const int* __restrict__ meta_tk,
                                                             const int* __restrict__ send_count,
                                                             int* __restrict__ rows_from,
                                                             int* __restrict__ chunk_cnt, int G) {
@@ -314,8 +320,8 @@ __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int*
     for (int j = 0; j < a.k; ++j) {
       int le;
       float w;
-      row_meta(a, topk_e, topk_w, self_tok, e2r, e2l, src, s, j, &le, &w);
-      if (le >= 0) atomicAdd(&s_cnt[le], 1);
+      row_meta(a, dst_tk, topk_w, self_tok, meta_tk, src, s, j, &le, &w);
+      if (le >= 0 && le < G) atomicAdd(&s_cnt[le], 1);
     }
   }
   __syncthreads();
@@ -383,9 +389,9 @@ __global__ void __launch_bounds__(1024) recv_scan_kernel(EpArgs a, int* __restri
 // expert group, copy the row (from the slab or, for self rows, from x), record maps.
 // Also zero-fills the group padding rows.
 __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
-    EpArgs a, const __nv_bfloat16* __restrict__ x, const int* __restrict__ topk_e,
-    const float* __restrict__ topk_w, const int* __restrict__ self_tok, const int* __restrict__ e2r,
-    const int* __restrict__ e2l, const int* __restrict__ rows_from, const int* __restrict__ chunk_base,
+    EpArgs a, const __nv_bfloat16* __restrict__ x, const int* __restrict__ dst_tk,
+    const float* __restrict__ topk_w, const int* __restrict__ self_tok, const int* __restrict__ meta_tk,
+    const int* __restrict__ rows_from, const int* __restrict__ chunk_base,
     int G, const int* __restrict__ group_off, const int* __restrict__ group_cnt,
     const int* __restrict__ pad_off, __nv_bfloat16* __restrict__ xp, float* __restrict__ row_w,
     int* __restrict__ row_src, int* __restrict__ inv_rows) {
@@ -403,7 +409,7 @@ __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
   for (int j = 0; j < a.k; ++j) {
     int le = -1;
     float w = 0.f;
-    if (s < rows) row_meta(a, topk_e, topk_w, self_tok, e2r, e2l, src, s, j, &le, &w);
+    if (s < rows) row_meta(a, dst_tk, topk_w, self_tok, meta_tk, src, s, j, &le, &w);
     if (le >= G) le = -1;
     s_le[threadIdx.x] = le;
     __syncthreads();
@@ -576,8 +582,7 @@ __global__ void __launch_bounds__(256) combine_kernel(EpArgs a, const __nv_bfloa
 // back into val[t][j] from the rank that owns choice j.
 // ------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) source_reduce_kernel(EpArgs a, const int* __restrict__ slot,
-                                                            const int* __restrict__ topk_e,
-                                                            const int* __restrict__ e2r,
+                                                            const int* __restrict__ dst_tk,
                                                             const __nv_bfloat16* __restrict__ residual,
                                                             __nv_bfloat16* __restrict__ out,
                                                             float* __restrict__ val) {
@@ -601,8 +606,8 @@ __global__ void __launch_bounds__(256) source_reduce_kernel(EpArgs a, const int*
     for (int d = 0; d < a.W; ++d) sl[d] = __ldg(slot + (size_t)t * a.W + d);
     if (val && lane < a.k) {
       const int j = lane;
-      const int d = __ldg(e2r + __ldg(topk_e + t * a.k + j));
-      val[t * a.k + j] = retw[((size_t)d * a.cap + sl[d]) * a.k + j];
+      const int d = __ldg(dst_tk + t * a.k + j);
+      val[t * a.k + j] = d >= 0 ? retw[((size_t)d * a.cap + sl[d]) * a.k + j] : 0.f;
     }
     for (int c = lane; c < vec; c += 32) {
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -648,70 +653,44 @@ static int sm_count() {
   return n;
 }
 
-void ep_route_plan(const int* topk_e, int T, int k, const int* e2r, int W, int* slot, int* send_count,
-                   cudaStream_t st) {
+void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_count, cudaStream_t st) {
   if (W > kMaxW) throw std::runtime_error("EP world size above 64 is not supported");
-  route_plan_kernel<<<1, 1024, 0, st>>>(topk_e, T, k, e2r, W, slot, send_count);
+  route_plan_kernel<<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count);
   check_launch("route_plan");
 }
 
-void ep_dispatch(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w, const int* slot,
-                 const int* e2r, const int* e2l, int* self_tok, const int* send_count, bool with_meta,
-                 cudaStream_t st, bool fp8) {
+void ep_dispatch(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk, const float* topk_w,
+                 const int* slot, int* self_tok, const int* send_count, bool with_meta, cudaStream_t st, bool fp8) {
   if (fp8 && (a.H % 128 || a.off_recv_q == 0)) throw std::runtime_error("fp8 dispatch needs H % 128 == 0 and fp8 slabs");
   if (a.H % 8) throw std::runtime_error("hidden size must be a multiple of 8");
   if (a.k > 32) throw std::runtime_error("top-k above 32 is not supported");
   int blocks = sm_count() * 2;
-  dispatch_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w,
-                                          slot, e2r, e2l, self_tok, send_count, with_meta ? 1 : 0,
-                                          fp8 ? 1 : 0);
+  dispatch_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), dst_tk, meta_tk, topk_w,
+                                          slot, self_tok, send_count, with_meta ? 1 : 0, fp8 ? 1 : 0);
   check_launch("dispatch");
 }
 
-void ep_recv_plan(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w, const int* self_tok,
-                  const int* e2r, const int* e2l, const int* send_count, int G, int cap_rows,
-                  int* rows_from, int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, void* xp,
-                  float* row_w, int* row_src, int* inv_rows, cudaStream_t st) {
-  if (G > 1024) throw std::runtime_error("at most 1024 local experts");
-  if (a.k > 8) throw std::runtime_error("top-k above 8 is not supported by the permute kernel");
-  const int chunks_per_src = (a.cap + kChunk - 1) / kChunk;
-  const int nchunks = chunks_per_src * a.W;
-  recv_count_kernel<<<nchunks, kChunk, 0, st>>>(a, topk_e, topk_w, self_tok, e2r, e2l, send_count, rows_from,
-                                                chunk_cnt, G);
-  check_launch("recv_count");
-  recv_scan_kernel<<<1, 1024, 0, st>>>(a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows);
-  check_launch("recv_scan");
-  recv_permute_kernel<<<nchunks, kChunk, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w,
-                                                  self_tok, e2r, e2l, rows_from, chunk_cnt, G, group_off,
-                                                  group_cnt, pad_off, reinterpret_cast<__nv_bfloat16*>(xp), row_w,
-                                                  row_src, inv_rows);
-  check_launch("recv_permute");
-  recv_gather_kernel<<<sm_count() * 4, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), self_tok, row_src,
-                                                     group_off + G, send_count, reinterpret_cast<__nv_bfloat16*>(xp));
-  check_launch("recv_gather");
-}
-
-void ep_recv_count_scan(const EpArgs& a, const int* topk_e, const float* topk_w, const int* self_tok,
-                        const int* e2r, const int* e2l, const int* send_count, int G, int cap_rows, int* rows_from,
+void ep_recv_count_scan(const EpArgs& a, const int* dst_tk, const int* meta_tk, const float* topk_w,
+                        const int* self_tok, const int* send_count, int G, int cap_rows, int* rows_from,
                         int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, cudaStream_t st) {
   if (G > 1024) throw std::runtime_error("at most 1024 local experts");
   if (a.k > 8) throw std::runtime_error("top-k above 8 is not supported by the permute kernel");
   const int nchunks = ((a.cap + kChunk - 1) / kChunk) * a.W;
-  recv_count_kernel<<<nchunks, kChunk, 0, st>>>(a, topk_e, topk_w, self_tok, e2r, e2l, send_count, rows_from,
+  recv_count_kernel<<<nchunks, kChunk, 0, st>>>(a, dst_tk, topk_w, self_tok, meta_tk, send_count, rows_from,
                                                 chunk_cnt, G);
   check_launch("recv_count");
   recv_scan_kernel<<<1, 1024, 0, st>>>(a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows);
   check_launch("recv_scan");
 }
 
-void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* topk_e, const float* topk_w,
-                            const int* self_tok, const int* e2r, const int* e2l, const int* send_count, int G,
+void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk,
+                            const float* topk_w, const int* self_tok, const int* send_count, int G,
                             const int* rows_from, const int* chunk_cnt, const int* group_off, const int* group_cnt,
                             const int* pad_off, void* xp, float* row_w, int* row_src, int* inv_rows,
                             cudaStream_t st, bool fp8) {
   const int nchunks = ((a.cap + kChunk - 1) / kChunk) * a.W;
-  recv_permute_kernel<<<nchunks, kChunk, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w,
-                                                  self_tok, e2r, e2l, rows_from, chunk_cnt, G, group_off, group_cnt,
+  recv_permute_kernel<<<nchunks, kChunk, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), dst_tk, topk_w,
+                                                  self_tok, meta_tk, rows_from, chunk_cnt, G, group_off, group_cnt,
                                                   pad_off, reinterpret_cast<__nv_bfloat16*>(xp), row_w, row_src,
                                                   inv_rows);
   check_launch("recv_permute");
@@ -730,6 +709,26 @@ void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const i
   check_launch("recv_gather");
 }
 
+// Waits for every source's header of this phase; rows_from[src] = rows it sent.
+__global__ void wait_rows_kernel(EpArgs a, const int* __restrict__ send_count, int* __restrict__ rows_from) {
+  const int src = threadIdx.x;
+  if (src >= a.W) return;
+  uint32_t rows = 0;
+  if (src == a.rank) {
+    rows = (uint32_t)send_count[a.rank];
+  } else {
+    const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+    const uint64_t* hdr = reinterpret_cast<const uint64_t*>(base + a.off_hdr) + (size_t)a.phase * a.W + src;
+    if (!wait_header(hdr, a.epoch, &rows, a.status, a.timeout_ns)) rows = 0;
+  }
+  rows_from[src] = (int)min(rows, (uint32_t)a.cap);
+}
+
+void ep_wait_rows(const EpArgs& a, const int* send_count, int* rows_from, cudaStream_t st) {
+  wait_rows_kernel<<<1, 64, 0, st>>>(a, send_count, rows_from);
+  check_launch("wait_rows");
+}
+
 void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float* row_w, const int* rows_from,
                 bool weighted, const float* row_val, cudaStream_t st) {
   int blocks = sm_count() * 2;
@@ -738,11 +737,10 @@ void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float
   check_launch("combine");
 }
 
-void ep_source_reduce(const EpArgs& a, const int* slot, const int* topk_e, const int* e2r, const void* residual,
-                      void* out, float* val, cudaStream_t st) {
+void ep_source_reduce(const EpArgs& a, const int* slot, const int* dst_tk, const void* residual, void* out,
+                      float* val, cudaStream_t st) {
   int blocks = sm_count() * 2;
-  source_reduce_kernel<<<blocks, 256, 0, st>>>(a, slot, topk_e, e2r,
-                                               reinterpret_cast<const __nv_bfloat16*>(residual),
+  source_reduce_kernel<<<blocks, 256, 0, st>>>(a, slot, dst_tk, reinterpret_cast<const __nv_bfloat16*>(residual),
                                                reinterpret_cast<__nv_bfloat16*>(out), val);
   check_launch("source_reduce");
 }
@@ -771,10 +769,9 @@ constexpr int kNaSendCount = kNaSelfTok + kNaMaxT;      // [1]
 constexpr int kNaRowsFrom = kNaSendCount + 64;          // [1]
 constexpr int kNaGroupCnt = kNaRowsFrom + 64;           // [E]
 constexpr int kNaPadOff = kNaGroupCnt + kNaMaxE;        // [E + 1]
-constexpr int kNaE2R = kNaPadOff + kNaMaxE + 64;        // [E]   expert -> rank (all 0)
-constexpr int kNaE2L = kNaE2R + kNaMaxE;                // [E]   expert -> local slot (identity)
-constexpr int kNaChunkCnt = kNaE2L + kNaMaxE;           // [chunks * E]
-constexpr int kNaWords = kNaChunkCnt + kNaMaxChunks * kNaMaxE;  // 34,176 words = 136,704 bytes
+constexpr int kNaDst = kNaPadOff + kNaMaxE + 64;        // [T * 8] destination of each choice (all 0)
+constexpr int kNaChunkCnt = kNaDst + kNaMaxT * 8;       // [chunks * E]
+constexpr int kNaWords = kNaChunkCnt + kNaMaxChunks * kNaMaxE;  // 98,944 words = 395,776 bytes
 
 }  // namespace
 
@@ -782,13 +779,10 @@ static __device__ __align__(256) int g_sepx_noalloc_scratch[kNaWords];
 
 namespace {
 
-__global__ void noalloc_init_kernel(int* scratch, int T, int E) {
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kNaMaxT; i += gridDim.x * blockDim.x) {
+__global__ void noalloc_init_kernel(int* scratch, int T, int k) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kNaMaxT * 8; i += gridDim.x * blockDim.x) {
     if (i < T) scratch[kNaSelfTok + i] = i;  // world size 1: token t has slot t
-    if (i < E) {
-      scratch[kNaE2R + i] = 0;
-      scratch[kNaE2L + i] = i;
-    }
+    if (i < T * k) scratch[kNaDst + i] = 0;   // every choice stays on this GPU
   }
 }
 
@@ -844,14 +838,15 @@ extern "C" int sepx_moe_permute_noalloc(const void* x, const int* topk_e, const 
   a.status = status;
 
   cudaMemsetAsync(status, 0, sizeof(int), stream);
-  noalloc_init_kernel<<<(kNaMaxT + 255) / 256, 256, 0, stream>>>(s, T, E);
-  route_plan_kernel<<<1, 1024, 0, stream>>>(topk_e, T, k, s + kNaE2R, 1, s + kNaSlot, s + kNaSendCount);
-  recv_count_kernel<<<nchunks, kChunk, 0, stream>>>(a, topk_e, topk_w, s + kNaSelfTok, s + kNaE2R, s + kNaE2L,
+  noalloc_init_kernel<<<(kNaMaxT * 8 + 255) / 256, 256, 0, stream>>>(s, T, k);
+  route_plan_kernel<<<1, 1024, 0, stream>>>(s + kNaDst, T, k, 1, s + kNaSlot, s + kNaSendCount);
+  // local slot of each choice = its expert id (all experts on this GPU)
+  recv_count_kernel<<<nchunks, kChunk, 0, stream>>>(a, s + kNaDst, topk_w, s + kNaSelfTok, topk_e,
                                                     s + kNaSendCount, s + kNaRowsFrom, s + kNaChunkCnt, E);
   recv_scan_kernel<<<1, 1024, 0, stream>>>(a, s + kNaChunkCnt, nchunks, E, group_off, s + kNaGroupCnt,
                                            s + kNaPadOff, cap_rows);
   recv_permute_kernel<<<nchunks, kChunk, 0, stream>>>(
-      a, reinterpret_cast<const __nv_bfloat16*>(x), topk_e, topk_w, s + kNaSelfTok, s + kNaE2R, s + kNaE2L,
+      a, reinterpret_cast<const __nv_bfloat16*>(x), s + kNaDst, topk_w, s + kNaSelfTok, topk_e,
       s + kNaRowsFrom, s + kNaChunkCnt, E, group_off, s + kNaGroupCnt, s + kNaPadOff,
       reinterpret_cast<__nv_bfloat16*>(xp), row_w, row_src, inv_rows);
   int sms = 0;

@@ -59,7 +59,8 @@ class EPState:
     slot: torch.Tensor
     send_count: torch.Tensor
     self_tok: torch.Tensor
-    topk_e: torch.Tensor
+    dst_tk: torch.Tensor   # destination rank of each (token, choice); -1 = not sent
+    meta_tk: torch.Tensor  # local expert slot on that rank
     topk_w: torch.Tensor
     rows_from: torch.Tensor
     group_off: torch.Tensor
@@ -145,7 +146,18 @@ class ExpertParallel:
     def _args(self):
         return self.done, self.status, self.timeout_s
 
-    def dispatch_fwd(self, x, topk_e, topk_w) -> EPState:
+    def route_tables(self, topk_e):
+        """(dst_tk, meta_tk) for expert ids ``topk_e`` ([T, k]; negative ids are not sent)."""
+        e = topk_e.long()
+        valid = e >= 0
+        ec = e.clamp_min(0)
+        dst = torch.where(valid, self.e2r[ec], -1).int().contiguous()
+        meta = torch.where(valid, self.e2l[ec], -1).int().contiguous()
+        return dst, meta
+
+    def dispatch_fwd(self, x, topk_e, topk_w, tables=None) -> EPState:
+        """Send rows, build the expert-grouped receive layout. ``tables`` optionally gives
+        precomputed ``(dst_tk, meta_tk)`` (e.g. the hierarchical path's pilot routing)."""
         T, dev, W, k = x.shape[0], self.device, self.world, self.k
         if T > self.cap:
             raise ValueError(f"{T} tokens exceed the communicator capacity {self.cap}")
@@ -154,10 +166,10 @@ class ExpertParallel:
         slot = torch.empty(T, W, dtype=torch.int32, device=dev)
         send_count = torch.empty(W, dtype=torch.int32, device=dev)
         self_tok = torch.empty(self.cap, dtype=torch.int32, device=dev)
-        topk_e = topk_e.int().contiguous()
+        dst_tk, meta_tk = tables if tables is not None else self.route_tables(topk_e)
         topk_w = topk_w.float().contiguous()
-        self.comm.route_plan(topk_e, self.e2r, slot, send_count)
-        self.comm.dispatch(x, topk_e, topk_w, slot, self.e2r, self.e2l, self_tok, send_count, True, ep,
+        self.comm.route_plan(dst_tk, slot, send_count)
+        self.comm.dispatch(x, dst_tk, meta_tk, topk_w, slot, self_tok, send_count, True, ep,
                            self.done[0:1], self.status, self.timeout_s, self.fp8_dispatch)
         G = self.G
         rows_from = torch.empty(W, dtype=torch.int32, device=dev)
@@ -165,7 +177,7 @@ class ExpertParallel:
         group_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
         group_cnt = torch.empty(G, dtype=torch.int32, device=dev)
         pad_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
-        self.comm.recv_count_scan(topk_e, topk_w, self_tok, self.e2r, self.e2l, send_count, G, T, self.cap_rows, ep,
+        self.comm.recv_count_scan(dst_tk, meta_tk, topk_w, self_tok, send_count, G, T, self.cap_rows, ep,
                                   rows_from, chunk_cnt, group_off, group_cnt, pad_off, self.done[0:1], self.status,
                                   self.timeout_s)
         # One small device->host read per layer sizes every buffer of this layer exactly
@@ -176,24 +188,24 @@ class ExpertParallel:
         row_w = torch.empty(R, dtype=torch.float32, device=dev)
         row_src = torch.empty(R, dtype=torch.int32, device=dev)
         inv_rows = torch.empty(W, self.cap, k, dtype=torch.int32, device=dev)
-        self.comm.recv_permute_gather(x, topk_e, topk_w, self_tok, self.e2r, self.e2l, send_count, G, ep, rows_from,
+        self.comm.recv_permute_gather(x, dst_tk, meta_tk, topk_w, self_tok, send_count, G, ep, rows_from,
                                       chunk_cnt, group_off, group_cnt, pad_off, xp, row_w, row_src, inv_rows,
                                       self.done[0:1], self.status, self.timeout_s, self.fp8_dispatch)
-        return EPState(T, slot, send_count, self_tok, topk_e, topk_w, rows_from, group_off, group_cnt, xp, row_w,
-                       row_src, inv_rows)
+        return EPState(T, slot, send_count, self_tok, dst_tk, meta_tk, topk_w, rows_from, group_off, group_cnt, xp,
+                       row_w, row_src, inv_rows)
 
     def combine_fwd(self, y, st: EPState, residual=None):
         out = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
         self.comm.combine(y, st.inv_rows, st.row_w, st.rows_from, True, None, st.T, self.epoch, self.done[1:2],
                           self.status, self.timeout_s)
-        self.comm.source_reduce(st.slot, st.topk_e, self.e2r, residual, out, None, self.epoch, self.done[1:2],
+        self.comm.source_reduce(st.slot, st.dst_tk, residual, out, None, self.epoch, self.done[1:2],
                                 self.status, self.timeout_s)
         return out
 
     def dispatch_bwd(self, dy, st: EPState):
         self.epoch += 1
         ep = self.epoch
-        self.comm.dispatch(dy, st.topk_e, st.topk_w, st.slot, self.e2r, self.e2l, st.self_tok, st.send_count,
+        self.comm.dispatch(dy, st.dst_tk, st.meta_tk, st.topk_w, st.slot, st.self_tok, st.send_count,
                            False, ep, self.done[0:1], self.status, self.timeout_s, False)
         dyp = torch.empty(st.xp.shape[0], self.H, dtype=torch.bfloat16, device=self.device)
         self.comm.recv_gather(dy, st.self_tok, st.row_src, st.group_off, st.send_count, dyp, ep, self.done[0:1],
@@ -205,7 +217,7 @@ class ExpertParallel:
         dw = torch.empty(st.T, self.k, dtype=torch.float32, device=self.device)
         self.comm.combine(dxp, st.inv_rows, st.row_w, st.rows_from, False, row_dw, st.T, self.epoch,
                           self.done[1:2], self.status, self.timeout_s)
-        self.comm.source_reduce(st.slot, st.topk_e, self.e2r, None, dx, dw, self.epoch, self.done[1:2],
+        self.comm.source_reduce(st.slot, st.dst_tk, None, dx, dw, self.epoch, self.done[1:2],
                                 self.status, self.timeout_s)
         return dx, dw
 
