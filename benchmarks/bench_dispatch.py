@@ -69,6 +69,8 @@ def main():
     ap.add_argument("--scenario", nargs="+", default=["layer", "fp8", "hier"])
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--group-size", type=int, default=4)
+    ap.add_argument("--profile", action="store_true",
+                    help="per-kernel device times of the fused layer path (torch profiler, every rank)")
     args = ap.parse_args()
     from spec_ep.parallel.ep import ExpertParallel
     from spec_ep.parallel.hierarchical import HierarchicalEP
@@ -104,6 +106,31 @@ def main():
         ep.check()
         ep.close()
         out["layer"] = res
+
+    if args.profile:
+        from torch.profiler import ProfilerActivity, profile
+
+        ep = ExpertParallel(128, 8, 2048, max_tokens=4096, device=dev)
+        x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=0, rank=rank, device=dev)
+
+        def p2p():
+            st = ep.dispatch_fwd(x, te, tw)
+            ep.combine_fwd(st.xp, st)
+
+        for _ in range(3):
+            p2p()
+        torch.cuda.synchronize()
+        dist.barrier()
+        with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
+            for _ in range(5):
+                p2p()
+            torch.cuda.synchronize()
+        ep.check()
+        ep.close()
+        if rank in (0, world - 1):
+            print(f"--- rank {rank} ---")
+            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=18), flush=True)
+        dist.barrier()
 
     if "fp8" in args.scenario:
         res = []

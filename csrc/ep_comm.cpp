@@ -117,6 +117,14 @@ class EpComm {
     return a;
   }
 
+  void route_tables(const at::Tensor& topk_e, const at::Tensor& e2r, const at::Tensor& e2l, at::Tensor& dst,
+                    at::Tensor& meta) {
+    TORCH_CHECK(topk_e.scalar_type() == at::kInt && topk_e.is_contiguous(), "topk_e must be contiguous int32");
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_route_tables(topk_e.data_ptr<int>(), e2r.data_ptr<int>(), e2l.data_ptr<int>(), (int)topk_e.numel(),
+                          dst.data_ptr<int>(), meta.data_ptr<int>(), st);
+  }
+
   void route_plan(const at::Tensor& dst_tk, at::Tensor& slot, at::Tensor& send_count) {
     TORCH_CHECK(dst_tk.scalar_type() == at::kInt && dst_tk.is_contiguous() && dst_tk.dim() == 2, "dst_tk [T, k] int32");
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
@@ -292,6 +300,7 @@ void register_ep_comm(pybind11::module& m) {
       .def("ipc_handle", &EpComm::ipc_handle)
       .def("open_peers", &EpComm::open_peers)
       .def("peer_base", &EpComm::peer_base)
+      .def("route_tables", &EpComm::route_tables)
       .def("route_plan", &EpComm::route_plan)
       .def("dispatch", &EpComm::dispatch)
       .def("recv_count_scan", &EpComm::recv_count_scan)

@@ -33,6 +33,8 @@ struct EpArgs {
 
 // Routing of choice j of token t: dst_tk[t][j] = destination rank (-1: not sent),
 // meta_tk[t][j] = value delivered with the row (local expert slot on that rank).
+void ep_route_tables(const int* topk_e, const int* e2r, const int* e2l, int n, int* dst, int* meta,
+                     cudaStream_t st);
 void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_count, cudaStream_t st);
 void ep_dispatch(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk, const float* topk_w,
                  const int* slot, int* self_tok, const int* send_count, bool with_meta, cudaStream_t st,

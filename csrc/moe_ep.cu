@@ -65,57 +65,56 @@ __device__ __forceinline__ bool wait_header(const uint64_t* hdr, uint32_t epoch,
 __global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict__ dst_tk, int T,
                                                           int k, int W, int* __restrict__ slot,
                                                           int* __restrict__ send_count) {
-  __shared__ int s_part[1024 / 32][kMaxW];  // per-warp totals per destination
+  // One token per thread per round of 1024 tokens; per destination, a warp ballot gives
+  // each token its rank among the warp's senders, per-warp totals are scanned in shared
+  // memory, and a running base per destination carries across rounds. Slots follow
+  // token order (deterministic).
+  __shared__ int s_warp[32][kMaxW];
+  __shared__ int s_base[kMaxW];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (T + blockDim.x - 1) / blockDim.x;
-  const int t_begin = tid * per, t_end = min(T, t_begin + per);
-  // pass 1: mask per token, thread-local counts per destination (W <= 64: 64-bit mask)
-  int cnt[kMaxW];
-#pragma unroll 1
-  for (int d = 0; d < W; ++d) cnt[d] = 0;
-  for (int t = t_begin; t < t_end; ++t) {
-    unsigned long long m = 0;
-    for (int j = 0; j < k; ++j) {
-      const int d = dst_tk[t * k + j];
-      if (d >= 0) m |= 1ull << d;
-    }
-    for (int d = 0; d < W; ++d) cnt[d] += (m >> d) & 1;
-  }
-  // exclusive scan of cnt[d] across threads (warp shuffle + per-warp totals)
-  for (int d = 0; d < W; ++d) {
-    int v = cnt[d];
-    int incl = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int n = __shfl_up_sync(0xffffffff, incl, o);
-      if (lane >= o) incl += n;
-    }
-    if (lane == 31) s_part[warp][d] = incl;
-    cnt[d] = incl - v;  // exclusive within warp
-  }
+  if (tid < W) s_base[tid] = 0;
   __syncthreads();
-  if (tid < W) {
-    int acc = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-      int v = s_part[w][tid];
-      s_part[w][tid] = acc;
-      acc += v;
-    }
-    send_count[tid] = acc;
-  }
-  __syncthreads();
-  for (int d = 0; d < W; ++d) cnt[d] += s_part[warp][d];
-  // pass 2: write slots
-  for (int t = t_begin; t < t_end; ++t) {
+  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+    const int t = t0 + tid;
     unsigned long long m = 0;
-    for (int j = 0; j < k; ++j) {
-      const int d = dst_tk[t * k + j];
-      if (d >= 0) m |= 1ull << d;
+    if (t < T) {
+      for (int j = 0; j < k; ++j) {
+        const int d = __ldg(dst_tk + (size_t)t * k + j);
+        if (d >= 0) m |= 1ull << d;
+      }
     }
     for (int d = 0; d < W; ++d) {
-      if ((m >> d) & 1) slot[(size_t)t * W + d] = cnt[d]++;
-      else slot[(size_t)t * W + d] = -1;
+      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1ull);
+      if (lane == 0) s_warp[warp][d] = __popc(b);
     }
+    __syncthreads();
+    if (tid < W) {  // exclusive scan of the 32 warp totals of destination tid
+      int acc = s_base[tid];
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+        const int v = s_warp[w][tid];
+        s_warp[w][tid] = acc;
+        acc += v;
+      }
+      s_base[tid] = acc;
+    }
+    __syncthreads();
+    for (int d = 0; d < W; ++d) {  // every lane takes part in the ballot; only real tokens store
+      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1ull);
+      const int before = __popc(b & ((1u << lane) - 1u));
+      if (t < T) slot[(size_t)t * W + d] = ((m >> d) & 1ull) ? s_warp[warp][d] + before : -1;
+    }
+    __syncthreads();
+  }
+  if (tid < W) send_count[tid] = s_base[tid];
+}
+
+// Per-(token, choice) routing tables from expert ids: dst = e2r[e], meta = e2l[e] (-1 for e < 0).
+__global__ void route_tables_kernel(const int* __restrict__ topk_e, const int* __restrict__ e2r,
+                                    const int* __restrict__ e2l, int n, int* __restrict__ dst, int* __restrict__ meta) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int e = topk_e[i];
+    dst[i] = e >= 0 ? __ldg(e2r + e) : -1;
+    meta[i] = e >= 0 ? __ldg(e2l + e) : -1;
   }
 }
 
@@ -553,12 +552,19 @@ __global__ void __launch_bounds__(256) combine_kernel(EpArgs a, const __nv_bfloa
         float* rw = reinterpret_cast<float*>(dbase + a.off_ret_w) + ((size_t)a.rank * a.cap + s) * a.k;
         rw[lane] = p >= 0 ? row_val[p] : 0.f;
       }
+      // all of a slot's expert rows are loaded before any accumulation (up to 8 x 16 B in
+      // flight per lane per chunk)
       for (int c = lane; c < vec; c += 32) {
+        uint4 v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q < np) v[q] = reinterpret_cast<const uint4*>(y + (size_t)plist[q] * a.H)[c];
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int q = 0; q < np; ++q) {
-          uint4 v = reinterpret_cast<const uint4*>(y + (size_t)plist[q] * a.H)[c];
-          float2 f0 = unpack_bf16x2(v.x), f1 = unpack_bf16x2(v.y), f2 = unpack_bf16x2(v.z),
-                 f3 = unpack_bf16x2(v.w);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (q >= np) break;
+          float2 f0 = unpack_bf16x2(v[q].x), f1 = unpack_bf16x2(v[q].y), f2 = unpack_bf16x2(v[q].z),
+                 f3 = unpack_bf16x2(v[q].w);
           const float w = wl[q];
           acc[0] += w * f0.x; acc[1] += w * f0.y; acc[2] += w * f1.x; acc[3] += w * f1.y;
           acc[4] += w * f2.x; acc[5] += w * f2.y; acc[6] += w * f3.x; acc[7] += w * f3.y;
@@ -657,6 +663,11 @@ void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_
   if (W > kMaxW) throw std::runtime_error("EP world size above 64 is not supported");
   route_plan_kernel<<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count);
   check_launch("route_plan");
+}
+
+void ep_route_tables(const int* topk_e, const int* e2r, const int* e2l, int n, int* dst, int* meta, cudaStream_t st) {
+  route_tables_kernel<<<std::min((n + 255) / 256, 1024), 256, 0, st>>>(topk_e, e2r, e2l, n, dst, meta);
+  check_launch("route_tables");
 }
 
 void ep_dispatch(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk, const float* topk_w,

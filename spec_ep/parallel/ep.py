@@ -148,11 +148,10 @@ class ExpertParallel:
 
     def route_tables(self, topk_e):
         """(dst_tk, meta_tk) for expert ids ``topk_e`` ([T, k]; negative ids are not sent)."""
-        e = topk_e.long()
-        valid = e >= 0
-        ec = e.clamp_min(0)
-        dst = torch.where(valid, self.e2r[ec], -1).int().contiguous()
-        meta = torch.where(valid, self.e2l[ec], -1).int().contiguous()
+        e = topk_e.int().contiguous()
+        dst = torch.empty_like(e)
+        meta = torch.empty_like(e)
+        self.comm.route_tables(e, self.e2r, self.e2l, dst, meta)
         return dst, meta
 
     def dispatch_fwd(self, x, topk_e, topk_w, tables=None) -> EPState:
