@@ -1,0 +1,70 @@
+"""Small, self-contained cases of the hot kernels for Nsight Compute captures (one GPU).
+
+Each case runs its kernel a few times on inputs larger than L2 (126 MB) but a few GB at
+most, so a ``--set full`` capture of one launch ends in seconds:
+
+  gemm      tcgen05 grouped SwiGLU GEMM, 16 experts x 2048 rows, hidden 2048, inter 768
+  wgrad     tcgen05 grouped weight gradient (gate_up), same shapes
+  dispatch  fused EP receive + combine at world size 1: route plan, count/scan/permute,
+            gather of 32,768 expert rows (4096 tokens x top-8, hidden 2048), combine,
+            source reduce
+  adamw     block-wise 8-bit AdamW on 302M parameters (fp32 gradient)
+
+    python benchmarks/ncu_cases.py --case gemm
+    ncu --set full --clock-control none -k regex:grouped_gemm -s 2 -c 1 -o out python benchmarks/ncu_cases.py --case gemm
+"""
+import argparse
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", required=True, choices=["gemm", "wgrad", "dispatch", "adamw"])
+    ap.add_argument("--reps", type=int, default=4)
+    args = ap.parse_args()
+    from spec_ep.ops import grouped_gemm as gg
+
+    torch.manual_seed(0)
+    dev = "cuda"
+    if args.case in ("gemm", "wgrad"):
+        G, R, H, I = 16, 2048, 2048, 768
+        x = torch.randn(G * R, H, device=dev).bfloat16()
+        w = (torch.randn(G, 2 * I, H, device=dev) / H**0.5).bfloat16()
+        off = torch.arange(0, G + 1, device=dev, dtype=torch.int32) * R
+        h, gu = gg.gg_swiglu_fwd(x, w, off)
+        out = torch.empty(G, 2 * I, H, device=dev)
+        for _ in range(args.reps):
+            if args.case == "gemm":
+                gg.gg_swiglu_fwd(x, w, off, h, gu)
+            else:
+                gg.gg_wgrad(gu, x, off, G, out)
+    elif args.case == "dispatch":
+        from spec_ep.parallel.ep import ExpertParallel
+        from spec_ep.utils.routing import synthetic_routing
+
+        ep = ExpertParallel(128, 8, 2048, max_tokens=4096)
+        x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, device=dev)
+        for _ in range(args.reps):
+            st = ep.dispatch_fwd(x, te, tw)
+            ep.combine_fwd(st.xp, st)
+        ep.check()
+    else:
+        from spec_ep.ops.optim import FusedAdamW
+
+        p = torch.nn.Parameter((torch.randn(16, 1536, 2048 * 6, device=dev) * 0.02).bfloat16())
+        p._sepx_state_precision = "8bit"
+        opt = FusedAdamW([p], lr=1e-4)
+        g = torch.randn(p.shape, device=dev) * 1e-3
+        for _ in range(args.reps):
+            opt.apply_now(p, g)
+    torch.cuda.synchronize()
+    print(f"case {args.case} ok")
+
+
+if __name__ == "__main__":
+    main()

@@ -328,8 +328,18 @@ __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int*
     chunk_cnt[(size_t)blockIdx.x * G + g] = s_cnt[g];
 }
 
-// K4b scan (one block): chunk_base[chunk][g] = group_off[g] + rows of g in earlier chunks.
-// group_off is 64-row aligned; pad_off[g] lists the padding rows after each group.
+// K4b scan (one block of 1024 threads): chunk_base[chunk][g] = group_off[g] + rows of g in
+// earlier chunks. One warp per expert group scans its chunk counts 32 at a time; the group
+// totals are then scanned block-wide into 64-row-aligned group offsets.
+__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
+
 __global__ void __launch_bounds__(1024) recv_scan_kernel(EpArgs a, int* __restrict__ chunk_cnt,
                                                          int nchunks, int G,
                                                          int* __restrict__ group_off,
@@ -337,51 +347,77 @@ __global__ void __launch_bounds__(1024) recv_scan_kernel(EpArgs a, int* __restri
                                                          int* __restrict__ pad_off,
                                                          int cap_rows) {
   __shared__ int s_tot[1024];
+  __shared__ int s_off[1024];
+  __shared__ int s_pad[1024];
+  __shared__ int s_wsum[2][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  // 1) per group: exclusive scan over chunks (in place), total rows of the group
+  for (int g = warp; g < G; g += nw) {
+    int carry = 0;
+    for (int c0 = 0; c0 < nchunks; c0 += 32) {
+      const int c = c0 + lane;
+      const int v = c < nchunks ? chunk_cnt[(size_t)c * G + g] : 0;
+      const int incl = warp_incl_scan(v, lane);
+      if (c < nchunks) chunk_cnt[(size_t)c * G + g] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_tot[g] = carry;
+  }
+  __syncthreads();
+  // 2) block-wide exclusive scan of padded totals and of padding counts
   const int g = threadIdx.x;
-  int tot = 0;
-  if (g < G) {
-    for (int c = 0; c < nchunks; ++c) {
-      int v = chunk_cnt[(size_t)c * G + g];
-      chunk_cnt[(size_t)c * G + g] = tot;  // exclusive within group
-      tot += v;
-    }
-    s_tot[g] = tot;
+  const int tot = g < G ? s_tot[g] : 0;
+  const int padded = (tot + 63) & ~63;
+  const int pad = padded - tot;
+  int ip = warp_incl_scan(padded, lane), iq = warp_incl_scan(pad, lane);
+  if (lane == 31) {
+    s_wsum[0][warp] = ip;
+    s_wsum[1][warp] = iq;
   }
   __syncthreads();
+  if (warp == 0) {
+    int vp = lane < nw ? s_wsum[0][lane] : 0, vq = lane < nw ? s_wsum[1][lane] : 0;
+    int sp = warp_incl_scan(vp, lane), sq = warp_incl_scan(vq, lane);
+    if (lane < nw) {
+      s_wsum[0][lane] = sp - vp;
+      s_wsum[1][lane] = sq - vq;
+    }
+  }
+  __syncthreads();
+  const int off = s_wsum[0][warp] + ip - padded;
+  const int poff = s_wsum[1][warp] + iq - pad;
+  if (g < G) {
+    s_off[g] = off;
+    s_pad[g] = poff;
+  }
+  __syncthreads();
+  const int total = G > 0 ? s_off[G - 1] + ((s_tot[G - 1] + 63) & ~63) : 0;
+  const int ptotal = G > 0 ? s_pad[G - 1] + (((s_tot[G - 1] + 63) & ~63) - s_tot[G - 1]) : 0;
+  if (total > cap_rows) {
+    // cannot happen with the worst-case capacity; kept as a guard
+    if (threadIdx.x == 0) record_error(a.status, kErrOverflow);
+    if (g < G) {
+      group_off[g] = 0;
+      group_cnt[g] = 0;
+      pad_off[g] = 0;
+    }
+    if (threadIdx.x == 0) {
+      group_off[G] = 0;
+      pad_off[G] = 0;
+    }
+    return;
+  }
+  if (g < G) {
+    group_off[g] = s_off[g];
+    group_cnt[g] = s_tot[g];
+    pad_off[g] = s_pad[g];
+  }
   if (threadIdx.x == 0) {
-    int acc = 0, pacc = 0;
-    for (int i = 0; i < G; ++i) {
-      group_off[i] = acc;
-      group_cnt[i] = s_tot[i];
-      int padded = (s_tot[i] + 63) & ~63;
-      pad_off[i] = pacc;
-      pacc += padded - s_tot[i];
-      acc += padded;
-    }
-    if (acc > cap_rows) {
-      record_error(a.status, kErrOverflow);
-      // clamp: groups past the capacity become empty
-      int run = 0;
-      for (int i = 0; i < G; ++i) {
-        int padded = (group_cnt[i] + 63) & ~63;
-        if (run + padded > cap_rows) { group_cnt[i] = 0; padded = 0; }
-        group_off[i] = run;
-        run += padded;
-      }
-      acc = run;
-      pacc = 0;
-      for (int i = 0; i < G; ++i) {
-        pad_off[i] = pacc;
-        pacc += ((group_cnt[i] + 63) & ~63) - group_cnt[i];
-      }
-    }
-    group_off[G] = acc;
-    pad_off[G] = pacc;
+    group_off[G] = total;
+    pad_off[G] = ptotal;
   }
-  __syncthreads();
-  if (g < G) {
-    for (int c = 0; c < nchunks; ++c) chunk_cnt[(size_t)c * G + g] += group_off[g];
-  }
+  // 3) chunk bases become absolute row offsets
+  for (int i = threadIdx.x; i < nchunks * G; i += blockDim.x) chunk_cnt[i] += s_off[i % G];
 }
 
 // K4c permute: place every (row, local choice) at its deterministic position inside its
