@@ -143,6 +143,10 @@ def plan_balanced(load: torch.Tensor, world: int, replicate_top: int = 0) -> Pla
 
 def loads_from_routing(route: torch.Tensor, num_experts: int) -> torch.Tensor:
     """Per-layer expert loads from a ``[L, T, K]`` routing dump -> ``[L, E]``."""
+    if route.dim() != 3:
+        raise ValueError(f"routing dump must be [L, T, K], got shape {tuple(route.shape)}")
+    if route.numel() and (int(route.min()) < 0 or int(route.max()) >= num_experts):
+        raise ValueError("routing dump holds expert ids outside [0, num_experts)")
     L = route.shape[0]
     return torch.stack([torch.bincount(route[l].reshape(-1).long(), minlength=num_experts) for l in range(L)])
 

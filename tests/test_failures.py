@@ -1,0 +1,112 @@
+"""Failure detection without faulting a GPU.
+
+* Host side (gloo ranks on CPU): a rank that never joins makes the others fail with a
+  timeout error instead of hanging; bad configurations are rejected before any launch.
+* GPU side (2 GPUs, NVLS off): a peer that never publishes its dispatch header makes the
+  waiting kernel give up after its deadline, record an error code and return; the host
+  raises EPError and the CUDA context stays usable.
+"""
+import datetime
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rendezvous_worker(rank, port, q):
+    if rank == 1:
+        return  # this rank never joins
+    t0 = time.time()
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                                timeout=datetime.timedelta(seconds=3))
+        q.put(("joined", time.time() - t0))
+    except Exception as e:  # expected: timeout
+        q.put((type(e).__name__, time.time() - t0))
+
+
+def test_missing_rank_times_out_on_host():
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.spawn(_rendezvous_worker, args=(_free_port(), q), nprocs=2, join=True)
+    kind, dt = q.get()
+    assert kind != "joined" and dt < 60
+
+
+def test_bad_configurations_rejected():
+    from spec_ep.integrations.ds_moe import load_config
+    from spec_ep.parallel.placement import contiguous, plan_balanced
+
+    with pytest.raises(ValueError):
+        contiguous(10, 4)  # experts do not split over ranks
+    with pytest.raises(ValueError):
+        plan_balanced(torch.ones(10), 4)
+    with pytest.raises(ValueError):
+        load_config({"expert_parallel": {"use_grouped_mm": False}})
+
+
+def test_corrupt_routing_dump_rejected(tmp_path):
+    from spec_ep.parallel.placement import loads_from_routing
+
+    with pytest.raises(ValueError):
+        loads_from_routing(torch.randint(0, 8, (4, 3)), 8)  # [T, K] instead of [L, T, K]
+    with pytest.raises(ValueError):
+        loads_from_routing(torch.full((2, 4, 3), 9), 8)  # expert id out of range
+
+
+def _peer_timeout_worker(rank, port, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        from spec_ep.parallel.ep import EPError, ExpertParallel
+
+        ep = ExpertParallel(8, 2, 256, max_tokens=64, device=dev, timeout_s=1.0)
+        x = torch.randn(64, 256, device=dev).bfloat16()
+        te = torch.stack([torch.arange(64) % 8, (torch.arange(64) + 4) % 8], 1).int().to(dev)
+        tw = torch.full((64, 2), 0.5, device=dev)
+        if rank == 0:
+            # rank 1 never dispatches: the receive kernel must give up after ~1 s
+            t0 = time.time()
+            st = ep.dispatch_fwd(x, te, tw)
+            torch.cuda.synchronize()
+            dt = time.time() - t0
+            with pytest.raises(EPError):
+                ep.check()
+            assert dt < 30
+            # the context is still healthy
+            y = (x.float() @ x.float().t()).sum()
+            assert torch.isfinite(y)
+            del st
+        dist.barrier()  # between steps, with nothing in flight
+        ep.close()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+@pytest.mark.gpu
+def test_peer_never_signals_times_out_on_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.spawn(_peer_timeout_worker, args=(_free_port(), errq), nprocs=2, join=True)
+    assert errq.empty()
