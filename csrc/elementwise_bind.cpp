@@ -3,6 +3,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "attention.h"
 #include "elementwise.h"
 #include "opt_bind.h"
 
@@ -125,6 +126,46 @@ void xent_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, double scale, at
                      loss.data_ptr<float>(), cs());
 }
 
+void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+                   double scale, const c10::optional<at::Tensor>& status) {
+  req(q, at::kBFloat16, "q");
+  req(k, at::kBFloat16, "k");
+  req(v, at::kBFloat16, "v");
+  req(o, at::kBFloat16, "o");
+  req(lse, at::kFloat, "lse");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k.size(2) == 128, "q/k/v must be [T, heads, 128]");
+  const int T = q.size(0), Hq = q.size(1), Hkv = k.size(1);
+  sepx::attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), T, Hq, Hkv,
+                      (float)scale, status.has_value() ? status->data_ptr<int>() : nullptr, cs());
+}
+
+// Returns (dq, dk, dv), each shaped like its input.
+std::vector<at::Tensor> attention_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                      const at::Tensor& o, const at::Tensor& dout, const at::Tensor& lse, double scale,
+                                      const c10::optional<at::Tensor>& status) {
+  req(q, at::kBFloat16, "q");
+  req(k, at::kBFloat16, "k");
+  req(v, at::kBFloat16, "v");
+  req(o, at::kBFloat16, "o");
+  req(dout, at::kBFloat16, "dout");
+  req(lse, at::kFloat, "lse");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k.size(2) == 128, "q/k/v must be [T, heads, 128]");
+  const int T = q.size(0), Hq = q.size(1), Hkv = k.size(1);
+  TORCH_CHECK(o.numel() == q.numel() && dout.numel() == q.numel() && lse.numel() == (int64_t)T * Hq,
+              "o/dout/lse shapes do not match q");
+  auto f32 = q.options().dtype(at::kFloat);
+  at::Tensor dsum = at::empty({Hq, T}, f32);
+  at::Tensor dq_acc = at::empty({T, Hq, 128}, f32);
+  at::Tensor dk_acc = at::empty({T, Hkv, 128}, f32);
+  at::Tensor dv_acc = at::empty({T, Hkv, 128}, f32);
+  at::Tensor dq = at::empty_like(q), dk = at::empty_like(k), dv = at::empty_like(v);
+  sepx::attention_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(), lse.data_ptr<float>(),
+                      dsum.data_ptr<float>(), dq_acc.data_ptr<float>(), dk_acc.data_ptr<float>(),
+                      dv_acc.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), T, Hq, Hkv, (float)scale,
+                      status.has_value() ? status->data_ptr<int>() : nullptr, cs());
+  return {dq, dk, dv};
+}
+
 }  // namespace
 
 void register_elementwise(pybind11::module& m) {
@@ -138,4 +179,6 @@ void register_elementwise(pybind11::module& m) {
   m.def("router_bwd", &router_bwd);
   m.def("adamw_update", &adamw_update);
   m.def("xent_fwd_bwd", &xent_fwd_bwd);
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
 }
