@@ -1,6 +1,6 @@
-// AdamW update of 32-element blocks (one warp, one element per lane), shared by the standalone optimizer kernels
-// (elementwise.cu) and the fused weight-gradient + optimizer GEMM epilogue
-// (grouped_gemm.cu), so both paths produce the same parameters.
+// AdamW element math shared by the standalone optimizer kernels (elementwise.cu) and the
+// fused weight-gradient + optimizer GEMM epilogue (grouped_gemm.cu), so both paths produce
+// the same parameters bit for bit.
 //
 // State kinds:
 //   kOptFp32: fp32 master weight, fp32 first/second moments; bf16 weight = round(master).
@@ -8,6 +8,10 @@
 //             fp32 absmax scale per moment (block-wise quantisation, Dettmers et al.,
 //             ICLR 2022): m as int8 (linear, +-127), v as uint8 of sqrt(v) (0..255).
 //             No master copy: the bf16 weight is updated with stochastic rounding.
+//
+// Every operation is an explicitly rounded intrinsic or a fixed hardware approximation
+// (sqrt.approx / rcp.approx), never left to compiler contraction, so any kernel that
+// applies the update gets the same bits.
 #pragma once
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -27,45 +31,92 @@ __device__ __forceinline__ uint32_t opt_hash32(uint32_t x) {
   return x;
 }
 
-// Stochastic rounding to bf16: add uniform random bits below the kept mantissa, truncate.
-__device__ __forceinline__ uint32_t bf16_bits_stochastic(float x, uint32_t rnd) {
-  uint32_t u = __float_as_uint(x);
-  u += (rnd & 0xFFFFu);
-  return u >> 16;
+// Stochastic rounding to bf16: add 16 uniform random bits below the kept mantissa, truncate.
+__device__ __forceinline__ uint32_t bf16_bits_stochastic(float x, uint32_t rnd16) {
+  return (__float_as_uint(x) + rnd16) >> 16;
 }
 
-// sqrt through the hardware reciprocal square root (rsqrtf); exact 0 for x <= 0.
-__device__ __forceinline__ float opt_sqrt(float x) { return x > 0.f ? __fmul_rn(x, rsqrtf(x)) : 0.f; }
-
-// All arithmetic below uses explicitly rounded operations and fixed intrinsics (never
-// contracted into FMAs), so every kernel that applies this update gives bit-identical
-// results. h.bc2 holds sqrt(1 / (1 - beta2^step)).
-__device__ __forceinline__ float adamw_step_elem(float w, float g, float& m, float& v, float& sq, const OptHyper& h) {
-  m = __fadd_rn(__fmul_rn(h.beta1, m), __fmul_rn(1.f - h.beta1, g));
-  v = __fadd_rn(__fmul_rn(h.beta2, v), __fmul_rn(__fmul_rn(1.f - h.beta2, g), g));
-  sq = opt_sqrt(v);
-  const float denom = __fadd_rn(__fmul_rn(sq, h.bc2), h.eps);
-  const float upd = __fdividef(__fmul_rn(m, h.bc1), denom);
-  return __fsub_rn(__fmul_rn(w, 1.f - h.lr * h.weight_decay), __fmul_rn(h.lr, upd));
+// One 32-bit hash per element pair (2p, 2p + 1): the even element takes the low 16 bits,
+// the odd element the high 16 bits.
+__device__ __forceinline__ uint32_t opt_rand_pair(uint64_t pair, const OptHyper& h) {
+  return opt_hash32((uint32_t)pair ^ ((uint32_t)(pair >> 32) * 0x27d4eb2du) ^ (h.step * 0x9E3779B9u) ^ h.seed);
+}
+__device__ __forceinline__ uint32_t opt_rand16(uint64_t gi, const OptHyper& h) {
+  const uint32_t r = opt_rand_pair(gi >> 1, h);
+  return (gi & 1) ? (r >> 16) : (r & 0xFFFFu);
 }
 
-__device__ __forceinline__ uint32_t opt_rand(uint64_t gi, const OptHyper& h) {
-  return opt_hash32((uint32_t)gi ^ ((uint32_t)(gi >> 32) * 0x27d4eb2du) ^ (h.step * 0x9E3779B9u) ^ h.seed);
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// 8-bit block codec: m in [-127, 127] * mmax / 127, sqrt(v) in [0, 255] * vmax / 255.
-__device__ __forceinline__ float dec_m(int q, float scale) { return __fmul_rn((float)q, __fdividef(scale, 127.f)); }
-__device__ __forceinline__ float dec_v(int q, float scale) {
-  const float s = __fmul_rn((float)q, __fdividef(scale, 255.f));
+// Per-launch constants of one AdamW step. bc1 = 1 / (1 - beta1^t),
+// bc2 = sqrt(1 / (1 - beta2^t)); grad_scale is folded into the moment coefficients.
+struct AdamCoef {
+  float b1, c1, b2, c2, bc2, eps, lr_bc1, decay;
+};
+
+__device__ __forceinline__ AdamCoef adam_coef(const OptHyper& h) {
+  AdamCoef k;
+  k.b1 = h.beta1;
+  k.c1 = __fmul_rn(__fsub_rn(1.f, h.beta1), h.grad_scale);
+  k.b2 = h.beta2;
+  k.c2 = __fmul_rn(__fmul_rn(__fsub_rn(1.f, h.beta2), h.grad_scale), h.grad_scale);
+  k.bc2 = h.bc2;
+  k.eps = h.eps;
+  k.lr_bc1 = __fmul_rn(h.lr, h.bc1);
+  k.decay = __fsub_rn(1.f, __fmul_rn(h.lr, h.weight_decay));
+  return k;
+}
+
+// w <- w (1 - lr wd) - lr m_hat / (sqrt(v_hat) + eps), with m, v updated in place and
+// sq = sqrt(v) returned for the 8-bit encoder.
+__device__ __forceinline__ float adamw_step_elem(float w, float g, float& m, float& v, float& sq, const AdamCoef& k) {
+  m = __fmaf_rn(k.b1, m, __fmul_rn(k.c1, g));
+  v = __fmaf_rn(k.b2, v, __fmul_rn(__fmul_rn(k.c2, g), g));
+  sq = sqrt_approx(v);
+  const float r = rcp_approx(__fmaf_rn(sq, k.bc2, k.eps));
+  return __fmaf_rn(-k.lr_bc1, __fmul_rn(m, r), __fmul_rn(w, k.decay));
+}
+
+// ---------------------------------------------------------------------------------------
+// 8-bit block codec: m = q_m * mmax / 127, sqrt(v) = q_v * vmax / 255. Integer <-> float
+// conversions use the exponent-bias trick (2^23 + n has integer n in its low mantissa
+// bits), which keeps them on the FMA/ALU pipes; results equal (float)n and
+// __float2int_rn / __float2int_ru exactly.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ float dec_scale_m(float mmax) { return __fdividef(mmax, 127.f); }
+__device__ __forceinline__ float dec_scale_v(float vmax) { return __fdividef(vmax, 255.f); }
+// byte e of a word of int8 codes, pre-flipped by 0x80808080 (so the byte is q + 128)
+__device__ __forceinline__ float m_code_to_float(uint32_t word_x80, int e) {
+  return __fsub_rn(__uint_as_float(__byte_perm(word_x80, 0x4Bu, 0x4550 | e)), 8388736.f);  // 2^23 + 128
+}
+__device__ __forceinline__ float v_code_to_float(uint32_t word, int e) {
+  return __fsub_rn(__uint_as_float(__byte_perm(word, 0x4Bu, 0x4550 | e)), 8388608.f);  // 2^23
+}
+__device__ __forceinline__ float dec_m(float code, float dm) { return __fmul_rn(code, dm); }
+__device__ __forceinline__ float dec_v(float code, float dv) {
+  const float s = __fmul_rn(code, dv);
   return __fmul_rn(s, s);
 }
-// sqrt(v) is rounded up: a non-zero second moment never decodes to 0 (which would turn
-// the next update into m / eps); the error only ever shrinks the step.
-__device__ __forceinline__ int enc_m(float m, float mmax) {
-  return mmax > 0.f ? __float2int_rn(__fmul_rn(m, __fdividef(127.f, mmax))) : 0;
+// Encoder factors: 0 for an all-zero block (every code is then 0).
+__device__ __forceinline__ float enc_scale_m(float mmax) { return mmax > 0.f ? __fdividef(127.f, mmax) : 0.f; }
+__device__ __forceinline__ float enc_scale_v(float vmax) { return vmax > 0.f ? __fdividef(255.f, vmax) : 0.f; }
+// round-to-nearest-even int8 code in the low byte (two's complement)
+__device__ __forceinline__ uint32_t enc_m_bits(float m, float em) {
+  return __float_as_uint(__fadd_rn(__fmul_rn(m, em), 12582912.f));  // 1.5 * 2^23
 }
-__device__ __forceinline__ int enc_v(float sq, float vmax) {
-  return vmax > 0.f ? min(255, __float2int_ru(__fmul_rn(sq, __fdividef(255.f, vmax)))) : 0;
+// sqrt(v) is rounded up, so a non-zero second moment never decodes to 0 (which would turn
+// the next update into m / eps); the error only ever shrinks the step. Code in low byte.
+__device__ __forceinline__ uint32_t enc_v_bits(float sq, float ev) {
+  return __float_as_uint(__fadd_ru(fminf(__fmul_rn(sq, ev), 255.f), 8388608.f));
 }
 
 __device__ __forceinline__ float opt_warp_max(float v) {
@@ -74,98 +125,61 @@ __device__ __forceinline__ float opt_warp_max(float v) {
   return v;
 }
 
-// One thread updates one block of 32 consecutive elements [idx, idx + 32), idx % 32 == 0.
-__device__ __forceinline__ void adamw_block32(const float (&g)[32], size_t idx, const OptHyper& h) {
-  __nv_bfloat16* p = h.param + idx;
-  if (h.kind == kOptFp32) {
-    float* ms = h.master + idx;
-    float* mm = reinterpret_cast<float*>(h.m) + idx;
-    float* vv = reinterpret_cast<float*>(h.v) + idx;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      float4 w4 = reinterpret_cast<const float4*>(ms)[q];
-      float4 m4 = reinterpret_cast<const float4*>(mm)[q];
-      float4 v4 = reinterpret_cast<const float4*>(vv)[q];
-      float w[4] = {w4.x, w4.y, w4.z, w4.w}, m[4] = {m4.x, m4.y, m4.z, m4.w}, v[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float sq;
-        w[e] = adamw_step_elem(w[e], __fmul_rn(g[4 * q + e], h.grad_scale), m[e], v[e], sq, h);
-      }
-      reinterpret_cast<float4*>(ms)[q] = make_float4(w[0], w[1], w[2], w[3]);
-      reinterpret_cast<float4*>(mm)[q] = make_float4(m[0], m[1], m[2], m[3]);
-      reinterpret_cast<float4*>(vv)[q] = make_float4(v[0], v[1], v[2], v[3]);
-      reinterpret_cast<uint2*>(p)[q] = make_uint2(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]));
-    }
-    return;
-  }
-  int8_t* mq = reinterpret_cast<int8_t*>(h.m) + idx;
-  uint8_t* vq = reinterpret_cast<uint8_t*>(h.v) + idx;
-  const size_t blk = idx >> 5;
-  // issue every load of the block before any arithmetic
-  const float msc = h.m_scale[blk], vsc = h.v_scale[blk];
-  uint4 mraw[2] = {reinterpret_cast<const uint4*>(mq)[0], reinterpret_cast<const uint4*>(mq)[1]};
-  uint4 vraw[2] = {reinterpret_cast<const uint4*>(vq)[0], reinterpret_cast<const uint4*>(vq)[1]};
-  uint4 praw[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) praw[q] = reinterpret_cast<const uint4*>(p)[q];
-  const int8_t* mb = reinterpret_cast<const int8_t*>(mraw);
-  const uint8_t* vb = reinterpret_cast<const uint8_t*>(vraw);
+// One thread updates one whole 8-bit block of 32 consecutive elements (8 units of 4),
+// held in registers: register slot q holds unit u = (q + rot) & 7 (elements 4u .. 4u+3 of
+// the block), so callers can read shared memory in a lane-rotated order without
+// dynamic register indexing. g: gradients; w: bf16 pairs; mq / vq: 4 codes per word;
+// msc / vsc: the block's scales. Updated in place; i0 = index of the block's element 0.
+__device__ __forceinline__ void adamw_8bit_block(const float (&g)[32], uint2 (&w)[8], uint32_t (&mq)[8],
+                                                 uint32_t (&vq)[8], float& msc, float& vsc, uint64_t i0, int rot,
+                                                 const AdamCoef& k, const OptHyper& h) {
+  const float dm = dec_scale_m(msc), dv = dec_scale_v(vsc);
   float m[32], sq[32];
   float mmax = 0.f, vmax = 0.f;
-  uint32_t pbits[16];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint32_t pw4[4] = {praw[q].x, praw[q].y, praw[q].z, praw[q].w};
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t u = (uint32_t)(q + rot) & 7u;
+    const uint32_t mx = mq[q] ^ 0x80808080u;
+    const uint64_t pair = (i0 >> 1) + 2 * u;
+    const uint32_t r0 = opt_rand_pair(pair, h), r1 = opt_rand_pair(pair + 1, h);
+    const uint32_t rnd[4] = {r0 & 0xFFFFu, r0 >> 16, r1 & 0xFFFFu, r1 >> 16};
+    const uint32_t wb[2] = {w[q].x, w[q].y};
+    uint32_t ob[4];
 #pragma unroll
-    for (int e2 = 0; e2 < 4; ++e2) {
-      float2 w2 = unpack_bf16x2(pw4[e2]);
-      const float wv[2] = {w2.x, w2.y};
-      uint32_t outb[2];
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        const int e = 8 * q + 2 * e2 + s;
-        m[e] = dec_m(mb[e], msc);
-        float v = dec_v(vb[e], vsc);
-        const float w = adamw_step_elem(wv[s], __fmul_rn(g[e], h.grad_scale), m[e], v, sq[e], h);
-        outb[s] = bf16_bits_stochastic(w, opt_rand(idx + e, h));
-        mmax = fmaxf(mmax, fabsf(m[e]));
-        vmax = fmaxf(vmax, sq[e]);
-      }
-      pbits[4 * q + e2] = (outb[0] & 0xFFFFu) | (outb[1] << 16);
+    for (int e = 0; e < 4; ++e) {
+      const int j = 4 * q + e;
+      const float wv = __uint_as_float((e & 1) ? (wb[e >> 1] & 0xFFFF0000u) : (wb[e >> 1] << 16));
+      m[j] = dec_m(m_code_to_float(mx, e), dm);
+      float v = dec_v(v_code_to_float(vq[q], e), dv);
+      const float nw = adamw_step_elem(wv, g[j], m[j], v, sq[j], k);
+      ob[e] = bf16_bits_stochastic(nw, rnd[e]);
+      mmax = fmaxf(mmax, fabsf(m[j]));
+      vmax = fmaxf(vmax, sq[j]);
     }
+    w[q] = make_uint2(__byte_perm(ob[0], ob[1], 0x5410), __byte_perm(ob[2], ob[3], 0x5410));
   }
+  const float em = enc_scale_m(mmax), ev = enc_scale_v(vmax);
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
-    reinterpret_cast<uint4*>(p)[q] = make_uint4(pbits[4 * q], pbits[4 * q + 1], pbits[4 * q + 2], pbits[4 * q + 3]);
-  uint32_t mo[8], vo[8];
-#pragma unroll
-  for (int w4 = 0; w4 < 8; ++w4) {
-    uint32_t a = 0, b = 0;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const int e = 4 * w4 + s;
-      a |= ((uint32_t)(enc_m(m[e], mmax) & 0xFF)) << (8 * s);
-      b |= ((uint32_t)enc_v(sq[e], vmax)) << (8 * s);
-    }
-    mo[w4] = a;
-    vo[w4] = b;
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t a = __byte_perm(enc_m_bits(m[4 * q], em), enc_m_bits(m[4 * q + 1], em), 0x0040);
+    const uint32_t b = __byte_perm(enc_m_bits(m[4 * q + 2], em), enc_m_bits(m[4 * q + 3], em), 0x0040);
+    mq[q] = __byte_perm(a, b, 0x5410);
+    const uint32_t c = __byte_perm(enc_v_bits(sq[4 * q], ev), enc_v_bits(sq[4 * q + 1], ev), 0x0040);
+    const uint32_t d = __byte_perm(enc_v_bits(sq[4 * q + 2], ev), enc_v_bits(sq[4 * q + 3], ev), 0x0040);
+    vq[q] = __byte_perm(c, d, 0x5410);
   }
-  reinterpret_cast<uint4*>(mq)[0] = make_uint4(mo[0], mo[1], mo[2], mo[3]);
-  reinterpret_cast<uint4*>(mq)[1] = make_uint4(mo[4], mo[5], mo[6], mo[7]);
-  reinterpret_cast<uint4*>(vq)[0] = make_uint4(vo[0], vo[1], vo[2], vo[3]);
-  reinterpret_cast<uint4*>(vq)[1] = make_uint4(vo[4], vo[5], vo[6], vo[7]);
-  h.m_scale[blk] = mmax;
-  h.v_scale[blk] = vmax;
+  msc = mmax;
+  vsc = vmax;
 }
 
 // One warp updates U blocks of 32 consecutive elements; lane l owns element idx[u], and
 // the 32 lanes of one u cover one whole quantisation block (idx[u] - lane is a multiple
 // of 32). Every lane of the warp must call this (it uses warp shuffles). Same results as
-// adamw_block32.
+// adamw_8bit_block and the fp32 kernel in elementwise.cu.
 template <int U>
 __device__ __forceinline__ void adamw_warp_blocks(const float (&g)[U], const size_t (&idx)[U], const OptHyper& h) {
   const int lane = threadIdx.x & 31;
+  const AdamCoef k = adam_coef(h);
   if (h.kind == kOptFp32) {
     float* mm = reinterpret_cast<float*>(h.m);
     float* vv = reinterpret_cast<float*>(h.v);
@@ -179,7 +193,7 @@ __device__ __forceinline__ void adamw_warp_blocks(const float (&g)[U], const siz
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       float sq;
-      w[u] = adamw_step_elem(w[u], __fmul_rn(g[u], h.grad_scale), m[u], v[u], sq, h);
+      w[u] = adamw_step_elem(w[u], g[u], m[u], v[u], sq, k);
       h.master[idx[u]] = w[u];
       mm[idx[u]] = m[u];
       vv[idx[u]] = v[u];
@@ -187,10 +201,10 @@ __device__ __forceinline__ void adamw_warp_blocks(const float (&g)[U], const siz
     }
     return;
   }
-  int8_t* mq = reinterpret_cast<int8_t*>(h.m);
+  uint8_t* mq = reinterpret_cast<uint8_t*>(h.m);
   uint8_t* vq = reinterpret_cast<uint8_t*>(h.v);
   float msc[U], vsc[U], wv[U];
-  int mi[U], vi[U];
+  uint32_t mi[U], vi[U];
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const size_t blk = idx[u] >> 5;
@@ -202,15 +216,15 @@ __device__ __forceinline__ void adamw_warp_blocks(const float (&g)[U], const siz
   }
 #pragma unroll
   for (int u = 0; u < U; ++u) {
-    float m = dec_m(mi[u], msc[u]);
-    float v = dec_v(vi[u], vsc[u]);
+    float m = dec_m(m_code_to_float(mi[u] ^ 0x80u, 0), dec_scale_m(msc[u]));
+    float v = dec_v(v_code_to_float(vi[u], 0), dec_scale_v(vsc[u]));
     float sq;
-    const float w = adamw_step_elem(wv[u], __fmul_rn(g[u], h.grad_scale), m, v, sq, h);
-    h.param[idx[u]] = __ushort_as_bfloat16((unsigned short)bf16_bits_stochastic(w, opt_rand(idx[u], h)));
+    const float w = adamw_step_elem(wv[u], g[u], m, v, sq, k);
+    h.param[idx[u]] = __ushort_as_bfloat16((unsigned short)bf16_bits_stochastic(w, opt_rand16(idx[u], h)));
     const float mmax = opt_warp_max(fabsf(m));
     const float vmax = opt_warp_max(sq);
-    mq[idx[u]] = (int8_t)enc_m(m, mmax);
-    vq[idx[u]] = (uint8_t)enc_v(sq, vmax);
+    mq[idx[u]] = (uint8_t)(enc_m_bits(m, enc_scale_m(mmax)) & 0xFFu);
+    vq[idx[u]] = (uint8_t)(enc_v_bits(sq, enc_scale_v(vmax)) & 0xFFu);
     if (lane == 0) {
       h.m_scale[idx[u] >> 5] = mmax;
       h.v_scale[idx[u] >> 5] = vmax;

@@ -526,10 +526,18 @@ void router_bwd(const float* probs, const int* topk_e, const float* dw, int T, i
 }
 
 // =====================================================================================
-// Fused AdamW (standalone). The per-block math is adamw_block32 (adamw_math.cuh), shared
-// with the weight-gradient GEMM epilogue that applies the same update in place.
-//  * fp32 state: one thread per 4 elements (vectorised), any size; grads fp32 or bf16.
-//  * 8-bit state: one thread per 32-element quantisation block; size % 32 == 0.
+// Fused AdamW (standalone). The per-element math is adamw_math.cuh, shared with the
+// weight-gradient GEMM epilogue that applies the same update in place, so both give the
+// same bits.
+//  * fp32 state: 4 consecutive elements per thread and step (16-byte accesses, coalesced
+//    across the warp), any size (scalar tail). Streams at the HBM limit.
+//  * 8-bit state (size % 32 == 0): persistent, one CTA of 8 independent warps per SM.
+//    Each warp streams 1024-element chunks (32 quantisation blocks) through a 3-stage
+//    shared-memory ring with bulk copies (cp.async.bulk, completion on an mbarrier),
+//    two chunks ahead of the one it computes; lane b updates block b from shared memory
+//    in a lane-rotated unit order (conflict-free for 4/8/16-byte accesses) and the new
+//    weights and codes go back with bulk stores. The arithmetic (~35 instructions per
+//    element) then overlaps the streaming instead of waiting for it.
 // =====================================================================================
 template <typename G>
 __device__ __forceinline__ float grad_at(const G* g, size_t i);
@@ -541,59 +549,198 @@ __device__ __forceinline__ float grad_at<__nv_bfloat16>(const __nv_bfloat16* g, 
 }
 
 template <typename G>
-__device__ __forceinline__ void load_grad32(const G* g, size_t base, float (&out)[32]) {
+__device__ __forceinline__ void load_grad4(const G* g, size_t i, float (&out)[4]) {
   if constexpr (sizeof(G) == 4) {
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      float4 g4 = reinterpret_cast<const float4*>(g + base)[q];
-      out[4 * q] = g4.x; out[4 * q + 1] = g4.y; out[4 * q + 2] = g4.z; out[4 * q + 3] = g4.w;
-    }
+    const float4 g4 = *reinterpret_cast<const float4*>(g + i);
+    out[0] = g4.x; out[1] = g4.y; out[2] = g4.z; out[3] = g4.w;
   } else {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 g8 = reinterpret_cast<const uint4*>(g + base)[q];
-      uint32_t w4[4] = {g8.x, g8.y, g8.z, g8.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float2 f = unpack_bf16x2(w4[e]);
-        out[8 * q + 2 * e] = f.x;
-        out[8 * q + 2 * e + 1] = f.y;
-      }
-    }
+    const uint2 r = *reinterpret_cast<const uint2*>(g + i);
+    const float2 a = unpack_bf16x2(r.x), b = unpack_bf16x2(r.y);
+    out[0] = a.x; out[1] = a.y; out[2] = b.x; out[3] = b.y;
   }
 }
 
-// One thread per 32-element block (fp32 or 8-bit state); scalar tail for fp32 state.
 template <typename G>
-__global__ void __launch_bounds__(256) adamw_kernel(const G* __restrict__ g, size_t n, OptHyper h) {
-  const size_t nb = n / 32;
-  for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < nb; b += (size_t)gridDim.x * blockDim.x) {
-    float gg[32];
-    load_grad32(g, b * 32, gg);
-    adamw_block32(gg, b * 32, h);
-  }
-  if (h.kind == kOptFp32) {
-    float* mm = reinterpret_cast<float*>(h.m);
-    float* vv = reinterpret_cast<float*>(h.v);
-    for (size_t i = nb * 32 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-         i += (size_t)gridDim.x * blockDim.x) {
-      float m = mm[i], v = vv[i], sq;
-      const float w = adamw_step_elem(h.master[i], __fmul_rn(grad_at(g, i), h.grad_scale), m, v, sq, h);
-      h.master[i] = w;
-      mm[i] = m;
-      vv[i] = v;
-      h.param[i] = __float2bfloat16(w);
+__global__ void __launch_bounds__(256) adamw_fp32_kernel(const G* __restrict__ g, size_t n, OptHyper h) {
+  const AdamCoef k = adam_coef(h);
+  const size_t n4 = n / 4, stride = (size_t)gridDim.x * blockDim.x;
+  float4* ms = reinterpret_cast<float4*>(h.master);
+  float4* mm = reinterpret_cast<float4*>(h.m);
+  float4* vv = reinterpret_cast<float4*>(h.v);
+  uint2* pp = reinterpret_cast<uint2*>(h.param);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float gg[4];
+    load_grad4(g, i * 4, gg);
+    const float4 w4 = ms[i], m4 = mm[i], v4 = vv[i];
+    float w[4] = {w4.x, w4.y, w4.z, w4.w}, m[4] = {m4.x, m4.y, m4.z, m4.w}, v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float sq;
+      w[e] = adamw_step_elem(w[e], gg[e], m[e], v[e], sq, k);
     }
+    ms[i] = make_float4(w[0], w[1], w[2], w[3]);
+    mm[i] = make_float4(m[0], m[1], m[2], m[3]);
+    vv[i] = make_float4(v[0], v[1], v[2], v[3]);
+    pp[i] = make_uint2(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]));
   }
+  float* mms = reinterpret_cast<float*>(h.m);
+  float* vvs = reinterpret_cast<float*>(h.v);
+  for (size_t i = n4 * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    float m = mms[i], v = vvs[i], sq;
+    const float w = adamw_step_elem(h.master[i], grad_at(g, i), m, v, sq, k);
+    h.master[i] = w;
+    mms[i] = m;
+    vvs[i] = v;
+    h.param[i] = __float2bfloat16(w);
+  }
+}
+
+namespace opt8 {
+constexpr int kWarps = 8, kStages = 3, kChunk = 1024;
+template <typename G>
+struct Lay {  // one stage of one warp (bytes)
+  static constexpr int OFF_W = kChunk * (int)sizeof(G);
+  static constexpr int OFF_M = OFF_W + kChunk * 2;
+  static constexpr int OFF_V = OFF_M + kChunk;
+  static constexpr int BYTES = OFF_V + kChunk;
+  static constexpr int SMEM = kWarps * kStages * BYTES + kWarps * kStages * 8;
+};
+}  // namespace opt8
+
+template <typename G>
+__global__ void __launch_bounds__(opt8::kWarps * 32, 1)
+    adamw_8bit_kernel(const G* __restrict__ g, size_t n, OptHyper h, int* status, uint64_t timeout_ns) {
+  using namespace opt8;
+  using L = Lay<G>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = smem + warp * kStages * L::BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kStages * L::BYTES) + warp * kStages;
+  uint8_t* mq8 = reinterpret_cast<uint8_t*>(h.m);
+  uint8_t* vq8 = reinterpret_cast<uint8_t*>(h.v);
+  const AdamCoef k = adam_coef(h);
+  const size_t nchunks = (n + kChunk - 1) / kChunk;
+  const size_t nw = (size_t)gridDim.x * kWarps;
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  auto issue = [&](int s, size_t c) {  // lane 0
+    const size_t e0 = c * kChunk;
+    const uint32_t ne = (uint32_t)(n - e0 < (size_t)kChunk ? n - e0 : (size_t)kChunk);
+    uint8_t* b = ring + s * L::BYTES;
+    mbar_arrive_expect_tx(&bars[s], ne * (uint32_t)(sizeof(G) + 4));
+    bulk_load(b, g + e0, ne * (uint32_t)sizeof(G), &bars[s]);
+    bulk_load(b + L::OFF_W, h.param + e0, ne * 2, &bars[s]);
+    bulk_load(b + L::OFF_M, mq8 + e0, ne, &bars[s]);
+    bulk_load(b + L::OFF_V, vq8 + e0, ne, &bars[s]);
+  };
+  size_t c = (size_t)blockIdx.x * kWarps + warp;
+  if (lane == 0) {
+    if (c < nchunks) issue(0, c);
+    if (c + nw < nchunks) issue(1, c + nw);
+  }
+  volatile int abort_flag = 0;
+  const int rot = lane + (lane >> 3);  // unit rotation: conflict-free 4/8/16-byte accesses
+  for (int it = 0; c < nchunks; ++it, c += nw) {
+    const int s = it % kStages;
+    const size_t e0 = c * kChunk;
+    const size_t blk = e0 / 32 + lane;
+    const bool valid = e0 + (size_t)lane * 32 < n;
+    float msc = valid ? h.m_scale[blk] : 0.f, vsc = valid ? h.v_scale[blk] : 0.f;
+    if (!mbar_wait_bounded(&bars[s], (uint32_t)(it / kStages) & 1u, &abort_flag, status, timeout_ns)) break;
+    uint8_t* b = ring + s * L::BYTES;
+    if (valid) {
+      float gg[32];
+      uint2 w[8];
+      uint32_t mq[8], vq[8];
+      const uint8_t* grow = b + lane * 32 * (int)sizeof(G);
+      uint8_t* wrow = b + L::OFF_W + lane * 64;
+      uint8_t* mrow = b + L::OFF_M + lane * 32;
+      uint8_t* vrow = b + L::OFF_V + lane * 32;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int u = (q + rot) & 7;
+        if constexpr (sizeof(G) == 4) {
+          const float4 g4 = *reinterpret_cast<const float4*>(grow + 16 * u);
+          gg[4 * q] = g4.x; gg[4 * q + 1] = g4.y; gg[4 * q + 2] = g4.z; gg[4 * q + 3] = g4.w;
+        } else {
+          const uint2 r = *reinterpret_cast<const uint2*>(grow + 8 * u);
+          const float2 a = unpack_bf16x2(r.x), bb = unpack_bf16x2(r.y);
+          gg[4 * q] = a.x; gg[4 * q + 1] = a.y; gg[4 * q + 2] = bb.x; gg[4 * q + 3] = bb.y;
+        }
+        w[q] = *reinterpret_cast<const uint2*>(wrow + 8 * u);
+        mq[q] = *reinterpret_cast<const uint32_t*>(mrow + 4 * u);
+        vq[q] = *reinterpret_cast<const uint32_t*>(vrow + 4 * u);
+      }
+      adamw_8bit_block(gg, w, mq, vq, msc, vsc, e0 + (size_t)lane * 32, rot, k, h);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int u = (q + rot) & 7;
+        *reinterpret_cast<uint2*>(wrow + 8 * u) = w[q];
+        *reinterpret_cast<uint32_t*>(mrow + 4 * u) = mq[q];
+        *reinterpret_cast<uint32_t*>(vrow + 4 * u) = vq[q];
+      }
+      h.m_scale[blk] = msc;
+      h.v_scale[blk] = vsc;
+    }
+    fence_proxy_async_smem();  // this thread's shared-memory writes -> the bulk stores
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t ne = (uint32_t)(n - e0 < (size_t)kChunk ? n - e0 : (size_t)kChunk);
+      bulk_store(h.param + e0, b + L::OFF_W, ne * 2);
+      bulk_store(mq8 + e0, b + L::OFF_M, ne);
+      bulk_store(vq8 + e0, b + L::OFF_V, ne);
+      bulk_commit();
+      // refill the stage of iteration it-1 (its stores are the older pending group)
+      if (c + 2 * nw < nchunks) {
+        bulk_wait_read<1>();
+        issue((it + 2) % kStages, c + 2 * nw);
+      }
+    }
+    __syncwarp();
+  }
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
 }
 
 void adamw_update(const OptHyper& h, const void* g, bool g_bf16, size_t n, int num_sms, cudaStream_t st) {
   if (h.kind != kOptFp32 && h.kind != kOpt8bit) throw std::runtime_error("unknown optimizer state kind");
-  if (h.kind == kOpt8bit && n % 32) throw std::runtime_error("8-bit AdamW needs a multiple of 32 elements");
-  const size_t blocks_needed = (n / 32 + 255) / 256 + 1;
-  const int grid = (int)std::min<size_t>(blocks_needed, (size_t)num_sms * 16);
-  if (g_bf16) adamw_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(g), n, h);
-  else adamw_kernel<float><<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(g), n, h);
+  if (h.kind == kOpt8bit) {
+    if (n % 32) throw std::runtime_error("8-bit AdamW needs a multiple of 32 elements");
+    const uintptr_t al = reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(h.param) |
+                         reinterpret_cast<uintptr_t>(h.m) | reinterpret_cast<uintptr_t>(h.v);
+    if (al & 15) throw std::runtime_error("8-bit AdamW needs 16-byte aligned gradient, weight and state");
+    const size_t chunks = (n + opt8::kChunk - 1) / opt8::kChunk;
+    const int grid = (int)std::max<size_t>(1, std::min<size_t>((chunks + opt8::kWarps - 1) / opt8::kWarps, num_sms));
+    if (g_bf16) {
+      using L = opt8::Lay<__nv_bfloat16>;
+      static bool set = false;
+      if (!set) {
+        cudaFuncSetAttribute(adamw_8bit_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+        set = true;
+      }
+      adamw_8bit_kernel<__nv_bfloat16><<<grid, opt8::kWarps * 32, L::SMEM, st>>>(
+          reinterpret_cast<const __nv_bfloat16*>(g), n, h, nullptr, 2000000000ull);
+    } else {
+      using L = opt8::Lay<float>;
+      static bool set = false;
+      if (!set) {
+        cudaFuncSetAttribute(adamw_8bit_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+        set = true;
+      }
+      adamw_8bit_kernel<float><<<grid, opt8::kWarps * 32, L::SMEM, st>>>(reinterpret_cast<const float*>(g), n, h,
+                                                                         nullptr, 2000000000ull);
+    }
+  } else {
+    if ((reinterpret_cast<uintptr_t>(h.master) | reinterpret_cast<uintptr_t>(h.m) | reinterpret_cast<uintptr_t>(h.v) |
+         reinterpret_cast<uintptr_t>(h.param) | reinterpret_cast<uintptr_t>(g)) & 15)
+      throw std::runtime_error("AdamW needs 16-byte aligned gradient, weight and state");
+    const int grid = (int)std::max<size_t>(1, std::min<size_t>(((n + 3) / 4 + 255) / 256, (size_t)num_sms * 8));
+    if (g_bf16) adamw_fp32_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(g), n, h);
+    else adamw_fp32_kernel<float><<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(g), n, h);
+  }
   check("adamw");
 }
 

@@ -101,19 +101,20 @@ def test_xent():
     assert _rel(w.grad, wr.grad) < 3e-2
 
 
-@pytest.mark.parametrize("prec", ["fp32", "8bit"])
-def test_fused_adamw(prec):
+@pytest.mark.parametrize("prec,n", [("fp32", 10240), ("8bit", 10240), ("fp32", 10243), ("8bit", 10336)])
+def test_fused_adamw(prec, n):
+    """n = 10243 / 10336 exercise the fp32 scalar tail and a partial 1024-element 8-bit chunk."""
     from spec_ep.ops.optim import FusedAdamW, adamw_reference
 
     torch.manual_seed(0)
-    p = torch.nn.Parameter(torch.randn(10240, device="cuda").bfloat16())
+    p = torch.nn.Parameter(torch.randn(n, device="cuda").bfloat16())
     p0 = p.detach().float().clone()
     opt = FusedAdamW([p], lr=1e-2, weight_decay=0.1, state_precision=prec)
     m = torch.zeros_like(p0)
     v = torch.zeros_like(p0)
     ref = p0.clone()
     for step in range(1, 4):
-        g = torch.randn(10240, device="cuda")
+        g = torch.randn(n, device="cuda")
         p.grad = g.bfloat16()
         opt.step()
         ref, m, v = adamw_reference(ref, g.bfloat16().float(), m, v, 1e-2, 0.9, 0.95, 1e-8, 0.1, step)
