@@ -10,7 +10,7 @@
 //             No master copy: the bf16 weight is updated with stochastic rounding.
 //
 // Every operation is an explicitly rounded intrinsic or a fixed hardware approximation
-// (sqrt.approx / rcp.approx), never left to compiler contraction, so any kernel that
+// (sqrt.approx.ftz / rcp.approx.ftz), never left to compiler contraction, so any kernel that
 // applies the update gets the same bits.
 #pragma once
 #include <cuda_bf16.h>
@@ -48,12 +48,12 @@ __device__ __forceinline__ uint32_t opt_rand16(uint64_t gi, const OptHyper& h) {
 
 __device__ __forceinline__ float sqrt_approx(float x) {
   float y;
-  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
-  asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -125,23 +125,25 @@ __device__ __forceinline__ float opt_warp_max(float v) {
   return v;
 }
 
-// One thread updates one whole 8-bit block of 32 consecutive elements (8 units of 4),
-// held in registers: register slot q holds unit u = (q + rot) & 7 (elements 4u .. 4u+3 of
-// the block), so callers can read shared memory in a lane-rotated order without
-// dynamic register indexing. g: gradients; w: bf16 pairs; mq / vq: 4 codes per word;
-// msc / vsc: the block's scales. Updated in place; i0 = index of the block's element 0.
-__device__ __forceinline__ void adamw_8bit_block(const float (&g)[32], uint2 (&w)[8], uint32_t (&mq)[8],
-                                                 uint32_t (&vq)[8], float& msc, float& vsc, uint64_t i0, int rot,
-                                                 const AdamCoef& k, const OptHyper& h) {
+// Two lanes update one 8-bit block of 32 consecutive elements: lane pair (2b, 2b + 1)
+// holds block b, each lane 16 consecutive elements (4 units of 4) in registers; register
+// slot q holds unit u = (q + rot) & 3 (elements 4u .. 4u+3 of the lane's half), so callers
+// can read shared memory in a lane-rotated order without dynamic register indexing.
+// g: gradients; w: bf16 pairs; mq / vq: 4 codes per word; msc / vsc: the block's scales
+// (the same value on both lanes). Updated in place (new scales on both lanes);
+// i0 = index of the lane's first element. Every lane of the warp must call this.
+__device__ __forceinline__ void adamw_8bit_half(const float (&g)[16], uint2 (&w)[4], uint32_t (&mq)[4],
+                                                uint32_t (&vq)[4], float& msc, float& vsc, uint64_t i0, int rot,
+                                                const AdamCoef& k, const OptHyper& h) {
   const float dm = dec_scale_m(msc), dv = dec_scale_v(vsc);
-  float m[32], sq[32];
+  const uint64_t pair0 = i0 >> 1;
+  float m[16], sq[16];
   float mmax = 0.f, vmax = 0.f;
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const uint32_t u = (uint32_t)(q + rot) & 7u;
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t u = (uint32_t)(q + rot) & 3u;
     const uint32_t mx = mq[q] ^ 0x80808080u;
-    const uint64_t pair = (i0 >> 1) + 2 * u;
-    const uint32_t r0 = opt_rand_pair(pair, h), r1 = opt_rand_pair(pair + 1, h);
+    const uint32_t r0 = opt_rand_pair(pair0 + 2 * u, h), r1 = opt_rand_pair(pair0 + 2 * u + 1, h);
     const uint32_t rnd[4] = {r0 & 0xFFFFu, r0 >> 16, r1 & 0xFFFFu, r1 >> 16};
     const uint32_t wb[2] = {w[q].x, w[q].y};
     uint32_t ob[4];
@@ -158,9 +160,11 @@ __device__ __forceinline__ void adamw_8bit_block(const float (&g)[32], uint2 (&w
     }
     w[q] = make_uint2(__byte_perm(ob[0], ob[1], 0x5410), __byte_perm(ob[2], ob[3], 0x5410));
   }
+  mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, 1));
+  vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
   const float em = enc_scale_m(mmax), ev = enc_scale_v(vmax);
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
+  for (int q = 0; q < 4; ++q) {
     const uint32_t a = __byte_perm(enc_m_bits(m[4 * q], em), enc_m_bits(m[4 * q + 1], em), 0x0040);
     const uint32_t b = __byte_perm(enc_m_bits(m[4 * q + 2], em), enc_m_bits(m[4 * q + 3], em), 0x0040);
     mq[q] = __byte_perm(a, b, 0x5410);
@@ -175,7 +179,7 @@ __device__ __forceinline__ void adamw_8bit_block(const float (&g)[32], uint2 (&w
 // One warp updates U blocks of 32 consecutive elements; lane l owns element idx[u], and
 // the 32 lanes of one u cover one whole quantisation block (idx[u] - lane is a multiple
 // of 32). Every lane of the warp must call this (it uses warp shuffles). Same results as
-// adamw_8bit_block and the fp32 kernel in elementwise.cu.
+// adamw_8bit_half and the fp32 kernel in elementwise.cu.
 template <int U>
 __device__ __forceinline__ void adamw_warp_blocks(const float (&g)[U], const size_t (&idx)[U], const OptHyper& h) {
   const int lane = threadIdx.x & 31;

@@ -531,13 +531,13 @@ void router_bwd(const float* probs, const int* topk_e, const float* dw, int T, i
 // same bits.
 //  * fp32 state: 4 consecutive elements per thread and step (16-byte accesses, coalesced
 //    across the warp), any size (scalar tail). Streams at the HBM limit.
-//  * 8-bit state (size % 32 == 0): persistent, one CTA of 8 independent warps per SM.
-//    Each warp streams 1024-element chunks (32 quantisation blocks) through a 3-stage
+//  * 8-bit state (size % 32 == 0): persistent, one CTA of 16 independent warps per SM.
+//    Each warp streams 512-element chunks (16 quantisation blocks) through a 3-stage
 //    shared-memory ring with bulk copies (cp.async.bulk, completion on an mbarrier),
-//    two chunks ahead of the one it computes; lane b updates block b from shared memory
-//    in a lane-rotated unit order (conflict-free for 4/8/16-byte accesses) and the new
-//    weights and codes go back with bulk stores. The arithmetic (~35 instructions per
-//    element) then overlaps the streaming instead of waiting for it.
+//    two chunks ahead of the one it computes; a lane pair updates one block from shared
+//    memory in a lane-rotated unit order (conflict-free for 4/8/16-byte accesses), the
+//    block scales are prefetched a chunk ahead, and the new weights and codes go back
+//    with bulk stores, so the arithmetic overlaps the streaming instead of waiting for it.
 // =====================================================================================
 template <typename G>
 __device__ __forceinline__ float grad_at(const G* g, size_t i);
@@ -596,7 +596,7 @@ __global__ void __launch_bounds__(256) adamw_fp32_kernel(const G* __restrict__ g
 }
 
 namespace opt8 {
-constexpr int kWarps = 8, kStages = 3, kChunk = 1024;
+constexpr int kWarps = 16, kStages = 3, kChunk = 512;  // 16 quantisation blocks per chunk
 template <typename G>
 struct Lay {  // one stage of one warp (bytes)
   static constexpr int OFF_W = kChunk * (int)sizeof(G);
@@ -642,26 +642,37 @@ __global__ void __launch_bounds__(opt8::kWarps * 32, 1)
     if (c + nw < nchunks) issue(1, c + nw);
   }
   volatile int abort_flag = 0;
-  const int rot = lane + (lane >> 3);  // unit rotation: conflict-free 4/8/16-byte accesses
+  // lane l holds elements [16 l, 16 l + 16) of the chunk (block l / 2); unit rotation
+  // (l >> 1) + (l >> 3) keeps 16-, 8- and 4-byte shared-memory accesses conflict-free
+  const int rot = (lane >> 1) + (lane >> 3);
+  auto scales = [&](size_t cc, float& ms, float& vs) {
+    const size_t e = cc * kChunk + (size_t)lane * 16;
+    const bool ok = cc < nchunks && e < n;
+    ms = ok ? h.m_scale[e / 32] : 0.f;
+    vs = ok ? h.v_scale[e / 32] : 0.f;
+  };
+  float msc, vsc;
+  scales(c, msc, vsc);
   for (int it = 0; c < nchunks; ++it, c += nw) {
     const int s = it % kStages;
     const size_t e0 = c * kChunk;
-    const size_t blk = e0 / 32 + lane;
-    const bool valid = e0 + (size_t)lane * 32 < n;
-    float msc = valid ? h.m_scale[blk] : 0.f, vsc = valid ? h.v_scale[blk] : 0.f;
+    const size_t i0 = e0 + (size_t)lane * 16;
+    const bool valid = i0 < n;
+    float nmsc, nvsc;  // next chunk's scales, in flight during this chunk's arithmetic
+    scales(c + nw, nmsc, nvsc);
     if (!mbar_wait_bounded(&bars[s], (uint32_t)(it / kStages) & 1u, &abort_flag, status, timeout_ns)) break;
     uint8_t* b = ring + s * L::BYTES;
-    if (valid) {
-      float gg[32];
-      uint2 w[8];
-      uint32_t mq[8], vq[8];
-      const uint8_t* grow = b + lane * 32 * (int)sizeof(G);
-      uint8_t* wrow = b + L::OFF_W + lane * 64;
-      uint8_t* mrow = b + L::OFF_M + lane * 32;
-      uint8_t* vrow = b + L::OFF_V + lane * 32;
+    float gg[16];
+    uint2 w[4];
+    uint32_t mq[4], vq[4];
+    const uint8_t* grow = b + lane * 16 * (int)sizeof(G);
+    uint8_t* wrow = b + L::OFF_W + lane * 32;
+    uint8_t* mrow = b + L::OFF_M + lane * 16;
+    uint8_t* vrow = b + L::OFF_V + lane * 16;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int u = (q + rot) & 7;
+    for (int q = 0; q < 4; ++q) {
+      const int u = (q + rot) & 3;
+      if (valid) {
         if constexpr (sizeof(G) == 4) {
           const float4 g4 = *reinterpret_cast<const float4*>(grow + 16 * u);
           gg[4 * q] = g4.x; gg[4 * q + 1] = g4.y; gg[4 * q + 2] = g4.z; gg[4 * q + 3] = g4.w;
@@ -673,17 +684,25 @@ __global__ void __launch_bounds__(opt8::kWarps * 32, 1)
         w[q] = *reinterpret_cast<const uint2*>(wrow + 8 * u);
         mq[q] = *reinterpret_cast<const uint32_t*>(mrow + 4 * u);
         vq[q] = *reinterpret_cast<const uint32_t*>(vrow + 4 * u);
+      } else {
+        gg[4 * q] = gg[4 * q + 1] = gg[4 * q + 2] = gg[4 * q + 3] = 0.f;
+        w[q] = make_uint2(0u, 0u);
+        mq[q] = vq[q] = 0u;
       }
-      adamw_8bit_block(gg, w, mq, vq, msc, vsc, e0 + (size_t)lane * 32, rot, k, h);
+    }
+    adamw_8bit_half(gg, w, mq, vq, msc, vsc, i0, rot, k, h);
+    if (valid) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int u = (q + rot) & 7;
+      for (int q = 0; q < 4; ++q) {
+        const int u = (q + rot) & 3;
         *reinterpret_cast<uint2*>(wrow + 8 * u) = w[q];
         *reinterpret_cast<uint32_t*>(mrow + 4 * u) = mq[q];
         *reinterpret_cast<uint32_t*>(vrow + 4 * u) = vq[q];
       }
-      h.m_scale[blk] = msc;
-      h.v_scale[blk] = vsc;
+      if ((lane & 1) == 0) {
+        h.m_scale[i0 / 32] = msc;
+        h.v_scale[i0 / 32] = vsc;
+      }
     }
     fence_proxy_async_smem();  // this thread's shared-memory writes -> the bulk stores
     __syncwarp();
@@ -700,6 +719,8 @@ __global__ void __launch_bounds__(opt8::kWarps * 32, 1)
       }
     }
     __syncwarp();
+    msc = nmsc;
+    vsc = nvsc;
   }
   if (lane == 0) bulk_wait_all();
   __syncwarp();
