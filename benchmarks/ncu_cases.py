@@ -9,6 +9,8 @@ most, so a ``--set full`` capture of one launch ends in seconds:
             gather of 32,768 expert rows (4096 tokens x top-8, hidden 2048), combine,
             source reduce
   adamw     block-wise 8-bit AdamW on 302M parameters (fp32 gradient)
+  wgrad_adamw8  expert gate_up weight gradient with the 8-bit AdamW epilogue (128 experts
+            x 256 rows, W [128, 1536, 2048])
 
     python benchmarks/ncu_cases.py --case gemm
     ncu --set full --clock-control none -k regex:grouped_gemm -s 2 -c 1 -o out python benchmarks/ncu_cases.py --case gemm
@@ -24,7 +26,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", required=True, choices=["gemm", "wgrad", "dispatch", "adamw"])
+    ap.add_argument("--case", required=True, choices=["gemm", "wgrad", "dispatch", "adamw", "wgrad_adamw8"])
     ap.add_argument("--reps", type=int, default=4)
     args = ap.parse_args()
     from spec_ep.ops import grouped_gemm as gg
@@ -53,6 +55,18 @@ def main():
             st = ep.dispatch_fwd(x, te, tw)
             ep.combine_fwd(st.xp, st)
         ep.check()
+    elif args.case == "wgrad_adamw8":
+        from spec_ep.ops.optim import FusedAdamW
+
+        G, rows, M, N = 128, 256, 1536, 2048
+        a = (torch.randn(G * rows, M, device=dev) * 0.1).bfloat16()
+        b = (torch.randn(G * rows, N, device=dev) * 0.1).bfloat16()
+        off = torch.arange(0, G + 1, device=dev, dtype=torch.int32) * rows
+        p = torch.nn.Parameter((torch.randn(G, M, N, device=dev) * 0.02).bfloat16())
+        p._sepx_state_precision = "8bit"
+        opt = FusedAdamW([p], lr=1e-4)
+        for _ in range(args.reps):
+            opt.fused_wgrad(p, a, b, off)
     else:
         from spec_ep.ops.optim import FusedAdamW
 

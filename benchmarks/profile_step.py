@@ -4,6 +4,7 @@ Meant for ``ncu --profile-from-start off ...`` (launch list / kernel captures) o
 plain timing of one step. Single GPU.
 
     python benchmarks/profile_step.py --layers 8 [--warmup 2]
+    python benchmarks/profile_step.py --layers 48 --table   # per-kernel device time (torch profiler)
 """
 import argparse
 import os
@@ -21,6 +22,7 @@ def main():
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--expert-state", default="8bit")
+    ap.add_argument("--table", action="store_true", help="print per-kernel CUDA time of one step (torch profiler)")
     args = ap.parse_args()
     from spec_ep.models.config import get_config
     from spec_ep.models.qwen3_moe import Qwen3MoeForCausalLM
@@ -48,6 +50,13 @@ def main():
     torch.cuda.synchronize()
     ep.check()
     print(f"layers={args.layers} step_ms={s.elapsed_time(e):.2f} loss={loss.item():.4f}")
+    if args.table:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            tr.train_step(ids, lab, args.seq - 1)
+            torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70))
 
 
 if __name__ == "__main__":

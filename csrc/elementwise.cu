@@ -690,7 +690,7 @@ __global__ void __launch_bounds__(opt8::kWarps * 32, 1)
         mq[q] = vq[q] = 0u;
       }
     }
-    adamw_8bit_half(gg, w, mq, vq, msc, vsc, i0, rot, k, h);
+    adamw_8bit_units<4>(gg, w, mq, vq, msc, vsc, i0, rot, k, h);
     if (valid) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {

@@ -43,6 +43,15 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kEpiWarps = 8;                 // two warps per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
+// fused 8-bit optimizer epilogue: one job = 32 rows x 32 columns of W (bf16, 64B-swizzled)
+// + m codes + v codes (uint8, 32B-swizzled), streamed by TMA three jobs deep per warp
+constexpr int kOptJob = 4096;  // w 2048 B @0, m 1024 B @2048, v 1024 B @3072
+// ring depth per epilogue warp: what fits next to two mainloop stages
+__host__ __device__ constexpr int opt_ring(int bn) { return bn == 256 ? 3 : 5; }
+
+struct OptMaps {  // kEpiAdamW8 state tensor maps over [G * M, N]
+  CUtensorMap w, m, v;
+};
 
 template <int BN, int STAGES, int EPI>
 struct GemmSmem {
@@ -51,7 +60,12 @@ struct GemmSmem {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // epilogues that transpose 32x32 accumulator blocks through shared memory
   static constexpr int EPI_STAGE_OFF = STAGES * STAGE_BYTES;
-  static constexpr int EPI_STAGE_BYTES = (EPI == kEpiAdamW || EPI == kEpiF32) ? kEpiWarps * 32 * 33 * 4 : 0;
+  // kEpiAdamW8: per epilogue warp, a ring of kOptRing jobs (32x32 weights + m + v codes)
+  // followed by one mbarrier per ring slot
+  static constexpr int EPI_STAGE_BYTES =
+      (EPI == kEpiAdamW || EPI == kEpiF32)
+          ? kEpiWarps * 32 * 33 * 4
+          : (EPI == kEpiAdamW8 ? kEpiWarps * opt_ring(BN) * (kOptJob + 8) : 0);
   static constexpr int BAR_OFF = EPI_STAGE_OFF + EPI_STAGE_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
@@ -113,7 +127,8 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x))
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmB, const GemmParams p,
+                        const __grid_constant__ OptMaps om) {
   using L = GemmSmem<BN, STAGES, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -154,6 +169,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty_bar[a], kEpiWarps);
     }
     mbar_init(drain_bar, 1);
+    if (EPI == kEpiAdamW8) {
+      uint64_t* obars = reinterpret_cast<uint64_t*>(smem + L::EPI_STAGE_OFF + kEpiWarps * opt_ring(BN) * kOptJob);
+      for (int i = 0; i < kEpiWarps * opt_ring(BN); ++i) mbar_init(&obars[i], 1);
+    }
     *s_abort = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -161,6 +180,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (EPI == kEpiAdamW8) {
+      tma_prefetch_desc(&om.w);
+      tma_prefetch_desc(&om.m);
+      tma_prefetch_desc(&om.v);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 2 * BN);
@@ -270,6 +294,146 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+  } else if (EPI == kEpiAdamW8) {
+    // -------------------- epilogue: weight gradient -> 8-bit AdamW --------------------
+    // Thread = one accumulator row (TMEM lane); one 32-column TMEM load = one 8-bit
+    // quantisation block of W, so the update needs no shuffles. W, m and v of each
+    // 32x32 job arrive by TMA (swizzled, so the per-row 16-byte reads are bank-conflict
+    // free) several jobs ahead of the one being computed, the block scales a job ahead, and
+    // the updated W / m / v leave by TMA stores. The gradient never reaches HBM.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int kCStep = kEpiWarps / 4;
+    constexpr int J = BN / 32 / kCStep;  // jobs per tile for this warp
+    constexpr int kOptRing = opt_ring(BN);
+    const int ew = warp - 2;
+    uint8_t* ring = smem + L::EPI_STAGE_OFF + ew * kOptRing * kOptJob;
+    uint64_t* obar =
+        reinterpret_cast<uint64_t*>(smem + L::EPI_STAGE_OFF + kEpiWarps * kOptRing * kOptJob) + ew * kOptRing;
+    const int my_tiles = total_tiles > (int)blockIdx.x ? (total_tiles - (int)blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const int njobs = my_tiles * J;
+    const AdamCoef kc = adam_coef(p.opt);
+    const int nb_row = p.N / 32;
+    auto job_pos = [&](int j, int& grow, int& col0, TileInfo& ti) {
+      ti = decode_tile<RAGGED_K, BN>((int)blockIdx.x + (j / J) * (int)gridDim.x, p, s_prefix);
+      grow = ti.g * p.M + ti.row0 + q * 32;
+      col0 = ti.n0 + (half + (j % J) * kCStep) * 32;
+    };
+    auto issue = [&](int j) {  // lane 0
+      int grow, col0;
+      TileInfo ti;
+      job_pos(j, grow, col0, ti);
+      const int s = j % kOptRing;
+      uint8_t* b = ring + s * kOptJob;
+      mbar_arrive_expect_tx(&obar[s], kOptJob);
+      tma_load_2d(b, &om.w, &obar[s], col0, grow);
+      tma_load_2d(b + 2048, &om.m, &obar[s], col0, grow);
+      tma_load_2d(b + 3072, &om.v, &obar[s], col0, grow);
+    };
+    auto load_scales = [&](int j, float& ms, float& vs) {
+      ms = vs = 0.f;
+      if (j >= njobs) return;
+      int grow, col0;
+      TileInfo ti;
+      job_pos(j, grow, col0, ti);
+      const size_t bi = (size_t)(grow + lane) * nb_row + col0 / 32;
+      ms = p.opt.m_scale[bi];
+      vs = p.opt.v_scale[bi];
+    };
+    int issued = 0, consumed = 0;
+    if (lane == 0)
+      for (; issued < kOptRing - 1 && issued < njobs; ++issued) issue(issued);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    float msc, vsc;
+    load_scales(0, msc, vsc);
+    const int sw = (lane >> 1) & 3, sc = (lane >> 2) & 1;  // swizzled 16-byte chunk of this row
+    for (int j = 0; j < njobs; ++j) {
+      int grow, col0;
+      TileInfo ti;
+      job_pos(j, grow, col0, ti);
+      const int ci = j % J;
+      float nms, nvs;
+      load_scales(j + 1, nms, nvs);
+      if (ci == 0) {
+        if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, s_abort, p.status, p.timeout_ns)) break;
+        tc_fence_after();
+      }
+      const int s = j % kOptRing;
+      if (!mbar_wait_bounded(&obar[s], (uint32_t)(j / kOptRing) & 1u, s_abort, p.status, p.timeout_ns)) break;
+      ++consumed;
+      uint8_t* b = ring + s * kOptJob;
+      float g[32];
+      tmem_ld32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + (half + ci * kCStep) * 32, g);
+      if (ti.num_kb == 0) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) g[e] = 0.f;
+      }
+      uint8_t* wrow = b + lane * 64;
+      uint8_t* mrow = b + 2048 + lane * 32;
+      uint8_t* vrow = b + 3072 + lane * 32;
+      uint2 w[8];
+      uint32_t mq[8], vq[8];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const uint4 x = *reinterpret_cast<const uint4*>(wrow + ((cc ^ sw) << 4));
+        w[2 * cc] = make_uint2(x.x, x.y);
+        w[2 * cc + 1] = make_uint2(x.z, x.w);
+      }
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const uint4 x = *reinterpret_cast<const uint4*>(mrow + ((cc ^ sc) << 4));
+        const uint4 y = *reinterpret_cast<const uint4*>(vrow + ((cc ^ sc) << 4));
+        mq[4 * cc] = x.x; mq[4 * cc + 1] = x.y; mq[4 * cc + 2] = x.z; mq[4 * cc + 3] = x.w;
+        vq[4 * cc] = y.x; vq[4 * cc + 1] = y.y; vq[4 * cc + 2] = y.z; vq[4 * cc + 3] = y.w;
+      }
+      adamw_8bit_units<8>(g, w, mq, vq, msc, vsc, (uint64_t)(grow + lane) * p.N + col0, 0, kc, p.opt);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        *reinterpret_cast<uint4*>(wrow + ((cc ^ sw) << 4)) = make_uint4(w[2 * cc].x, w[2 * cc].y, w[2 * cc + 1].x, w[2 * cc + 1].y);
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        *reinterpret_cast<uint4*>(mrow + ((cc ^ sc) << 4)) = make_uint4(mq[4 * cc], mq[4 * cc + 1], mq[4 * cc + 2], mq[4 * cc + 3]);
+        *reinterpret_cast<uint4*>(vrow + ((cc ^ sc) << 4)) = make_uint4(vq[4 * cc], vq[4 * cc + 1], vq[4 * cc + 2], vq[4 * cc + 3]);
+      }
+      const size_t bi = (size_t)(grow + lane) * nb_row + col0 / 32;
+      p.opt.m_scale[bi] = msc;
+      p.opt.v_scale[bi] = vsc;
+      fence_proxy_async_smem();  // shared-memory writes -> the TMA stores
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&om.w, b, col0, grow);
+        tma_store_2d(&om.m, b + 2048, col0, grow);
+        tma_store_2d(&om.v, b + 3072, col0, grow);
+        bulk_commit();
+        if (issued < njobs) {  // refill the slot of job j - 1 (its stores are the older group)
+          bulk_wait_read<1>();
+          issue(issued);
+          ++issued;
+        }
+      }
+      __syncwarp();
+      if (ci == J - 1) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      msc = nms;
+      vsc = nvs;
+    }
+    if (lane == 0) {
+      // after an abort: let every issued load land (bounded) before the CTA exits
+      for (int j = consumed; j < issued; ++j) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&obar[j % kOptRing], (uint32_t)(j / kOptRing) & 1u) &&
+               globaltimer_ns() - t0 < p.timeout_ns) {
+        }
+      }
+      bulk_wait_all();
+    }
+    __syncwarp();
   } else {
     // --------------------------------- epilogue --------------------------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -405,10 +569,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (valid && p.row_dw) atomicAdd(p.row_dw + r, dw_part);
       } else if (EPI == kEpiAdamW) {
-        // The weight gradient never leaves the SM. Each 32x32 fp32 block (32 rows of this
-        // warp's lane quarter x 32 columns) is transposed through shared memory so that
-        // the warp then updates one row's 32 contiguous weights per step, one per lane
-        // (coalesced; the 8-bit quantisation block is exactly those 32 elements).
+        // fp32 state. The weight gradient never leaves the SM. Each 32x32 fp32 block (32
+        // rows of this warp's lane quarter x 32 columns) is transposed through shared
+        // memory so that the warp then updates one row's 32 contiguous weights per step,
+        // one per lane (coalesced).
         float* tile = reinterpret_cast<float*>(smem + L::EPI_STAGE_OFF) + (warp - 2) * 32 * 33;
         const size_t row_base = ((size_t)ti.g * p.M + ti.row0 + q * 32) * (size_t)p.N;
 #pragma unroll 1
@@ -428,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               g4[u] = tile[(i + u) * 33 + lane];
               idx[u] = row_base + (size_t)(i + u) * p.N + col;
             }
-            adamw_warp_blocks<4>(g4, idx, p.opt);
+            adamw_fp32_lanes<4>(g4, idx, p.opt);
           }
           __syncwarp();
         }
@@ -505,7 +669,7 @@ static int num_sms() {
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                   int max_tiles, cudaStream_t stream) {
+                   int max_tiles, cudaStream_t stream, const OptMaps& om = OptMaps{}) {
   using L = GemmSmem<BN, STAGES, EPI>;
   auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, RAGGED_K, EPI>;
   size_t smem = L::bytes(p.G);
@@ -517,7 +681,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
   int grid = num_sms();
   if (max_tiles > 0 && max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, p, om);
   note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("grouped_gemm launch: ") + cudaGetErrorString(e));
@@ -603,12 +767,46 @@ void grouped_gemm_ragged_k(const GemmCall& c, cudaStream_t stream) {
 // Weight gradient + AdamW: W[g] <- AdamW(W[g], sum_{r in group g} A[r, :]^T B[r, :]).
 // The fp32 gradient tile goes from TMEM straight into the optimizer update.
 // ---------------------------------------------------------------------------------
+static CUtensorMap make_tmap_state(const void* base, CUtensorMapDataType dt, int esize, int64_t rows, int64_t cols,
+                                   CUtensorMapSwizzle sw) {
+  CUtensorMap tm;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * esize)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((cols * esize) & 15))
+    throw std::runtime_error("optimizer state must be 16-byte aligned with 16-byte row stride");
+  CUresult r = get_encode_fn()(&tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return tm;
+}
+
 void grouped_gemm_wgrad_adamw(const GemmCall& c, cudaStream_t stream) {
   GemmParams p = c.p;
   if (p.M % 128) throw std::runtime_error("M must be a multiple of 128");
   if (p.opt.kind != kOptFp32 && p.opt.kind != kOpt8bit) throw std::runtime_error("bad optimizer kind");
   CUtensorMap ta = make_tmap_bf16(c.A, c.a_rows, p.M, c.lda, 64);
   CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
+  if (p.opt.kind == kOpt8bit) {
+    if (p.N % 32) throw std::runtime_error("8-bit fused optimizer needs N % 32 == 0");
+    const int64_t rows = (int64_t)p.G * p.M;
+    OptMaps om;
+    om.w = make_tmap_state(p.opt.param, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, p.N, CU_TENSOR_MAP_SWIZZLE_64B);
+    om.m = make_tmap_state(p.opt.m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, p.N, CU_TENSOR_MAP_SWIZZLE_32B);
+    om.v = make_tmap_state(p.opt.v, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, p.N, CU_TENSOR_MAP_SWIZZLE_32B);
+    if (p.N % 256 == 0) {
+      p.n_tiles = p.N / 256;
+      launch<256, 2, true, true, true, kEpiAdamW8>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream, om);
+    } else if (p.N % 128 == 0) {
+      p.n_tiles = p.N / 128;
+      launch<128, 2, true, true, true, kEpiAdamW8>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream, om);
+    } else {
+      throw std::runtime_error("N must be a multiple of 128");
+    }
+    return;
+  }
   if (p.N % 256 == 0) {
     p.n_tiles = p.N / 256;
     launch<256, 3, true, true, true, kEpiAdamW>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream);

@@ -12,7 +12,8 @@ enum : int {
   kEpiSwigluFwd = 1,  // D = [gate | up] -> h = silu(g) * u (out), pre-activation gu (aux)
   kEpiSwigluBwd = 2,  // D = dh (unweighted) -> dgu (out), w*h (aux2), dw += <dh, h> (row_dw)
   kEpiF32 = 3,        // D -> fp32 [G, M, ldo] (weight gradients)
-  kEpiAdamW = 4,      // D = weight gradient -> AdamW update of W[G, M, N] in place
+  kEpiAdamW = 4,      // D = weight gradient -> AdamW update of W[G, M, N] in place (fp32 state)
+  kEpiAdamW8 = 5,     // same, 8-bit state, with the state streamed through a TMA ring
 };
 
 struct GemmParams {

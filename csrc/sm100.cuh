@@ -136,6 +136,15 @@ __device__ __forceinline__ void bulk_wait_read() {
 // Wait until every bulk group of this thread has completed (writes included).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Tiled 2-D store shared -> global (tracked by the issuing thread's bulk async-groups).
+// Coordinates must be non-negative; c0 * elem_size a multiple of 16 bytes.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
 // ----------------------------------------------------------------------------------
 // tcgen05 / TMEM
 // ----------------------------------------------------------------------------------

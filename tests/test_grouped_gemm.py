@@ -148,16 +148,21 @@ def test_large_fwd_perf_sanity():
     assert _rel_err(gu, ref) < 1e-2
 
 
-@pytest.mark.parametrize("kind", ["fp32", "8bit"])
-def test_wgrad_adamw_fused_matches_unfused(kind):
-    """AdamW applied in the wgrad epilogue == wgrad to HBM followed by the standalone update."""
+@pytest.mark.parametrize("kind,M,N,G", [("fp32", 256, 384, 4), ("8bit", 256, 384, 4), ("8bit", 256, 512, 4),
+                                         ("8bit", 512, 768, 40)])
+def test_wgrad_adamw_fused_matches_unfused(kind, M, N, G):
+    """AdamW applied in the wgrad epilogue == wgrad to HBM followed by the standalone update.
+
+    N = 384 takes 128-column tiles, 512 / 768 take 256-column tiles; G = 40 gives every
+    CTA several tiles (the 8-bit epilogue's TMA ring wraps many times).
+    """
     from spec_ep.ops.grouped_gemm import gg_wgrad
     from spec_ep.ops.optim import FusedAdamW
 
     torch.manual_seed(6)
-    sizes = [128, 0, 64, 300]
+    sizes = ([128, 0, 64, 300] * ((G + 3) // 4))[:G]
     off = _offsets(sizes, 64)
-    R, M, N, G = off[-1], 256, 384, len(sizes)
+    R = off[-1]
     a = torch.zeros(R, M, device="cuda")
     b = torch.zeros(R, N, device="cuda")
     for g, s in enumerate(sizes):
