@@ -1,10 +1,12 @@
 """Run warm-up training steps, then exactly one step between cudaProfilerStart/Stop.
 
-Meant for ``ncu --profile-from-start off ...`` (launch list / kernel captures) or for a
-plain timing of one step. Single GPU.
+Meant for ``ncu --profile-from-start off ...`` (launch list / kernel captures, one GPU) or
+for a plain timing of one step; under torchrun it runs expert-parallel over all ranks and
+rank 0 prints its per-kernel table.
 
     python benchmarks/profile_step.py --layers 8 [--warmup 2]
     python benchmarks/profile_step.py --layers 48 --table   # per-kernel device time (torch profiler)
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/profile_step.py --layers 48 --table --expert-state fp32
 """
 import argparse
 import os
@@ -29,8 +31,13 @@ def main():
     from spec_ep.parallel.ep import ExpertParallel
     from spec_ep.train import Trainer
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    from spec_ep.utils.dist import init_distributed
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        rank, world, dev = init_distributed()
+    else:
+        rank, world, dev = 0, 1, torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
     cfg = get_config(args.model, num_layers=args.layers)
     ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=args.seq, device=dev)
     torch.manual_seed(0)
@@ -49,14 +56,21 @@ def main():
     torch.cuda.profiler.stop()
     torch.cuda.synchronize()
     ep.check()
-    print(f"layers={args.layers} step_ms={s.elapsed_time(e):.2f} loss={loss.item():.4f}")
+    if rank == 0:
+        print(f"world={world} layers={args.layers} step_ms={s.elapsed_time(e):.2f} loss={loss.item():.4f}")
     if args.table:
         from torch.profiler import ProfilerActivity, profile
 
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
             tr.train_step(ids, lab, args.seq - 1)
             torch.cuda.synchronize()
-        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70))
+        if rank == 0:
+            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
