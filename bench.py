@@ -16,7 +16,10 @@ back to the host.
 
 ``dispatch_combine_us_per_layer`` is measured separately on the MoE-layer shape
 (hidden 2048, 4096 tokens/rank, 128 experts, top-8, Zipf s=1.0 routing) with identity
-experts, so it is the pure dispatch+combine cost.
+experts, so it is the pure dispatch+combine cost, on the contiguous expert layout the
+reference uses. ``dispatch_combine_us_per_layer_planned`` repeats it with the
+speculative placement: experts packed by the load of a *previous* batch's routing (seed
+1) and the 16 hottest replicated on every rank, measured on the seed-0 batch.
 """
 from __future__ import annotations
 
@@ -126,6 +129,32 @@ def dispatch_combine_us(ep, dev, rank, world, iters, seed=0):
     return ms * 1000.0, b
 
 
+def dispatch_combine_planned_us(dev, rank, world, iters):
+    """Same layer with the placement planned from the previous batch's expert loads."""
+    from spec_ep.parallel.ep import ExpertParallel
+    from spec_ep.parallel.placement import plan_balanced
+    from spec_ep.utils.routing import synthetic_routing
+
+    _, te_prev, _ = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=1, rank=rank, device=dev)
+    load = torch.bincount(te_prev.flatten().long(), minlength=128).float()
+    if dist.is_initialized():
+        dist.all_reduce(load)
+    placement = plan_balanced(load.cpu(), world, replicate_top=16 if world > 1 else 0)
+    ep = ExpertParallel(128, 8, 2048, max_tokens=4096, device=dev, placement=placement)
+    x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=0, rank=rank, device=dev)
+
+    def once():
+        st = ep.dispatch_fwd(x, te, tw)
+        ep.combine_fwd(st.xp, st)
+
+    for _ in range(3):
+        once()
+    ms = timed(once, iters, dev)
+    ep.check()
+    ep.close()
+    return ms * 1000.0
+
+
 def run_spec_ep(args):
     world, rank, dev = init_dist()
     from spec_ep.models.config import get_config
@@ -188,6 +217,7 @@ def run_spec_ep(args):
                "last_loss": losses[-1] if losses else None}
 
     dc_us, bound = dispatch_combine_us(ep, dev, rank, world, args.dc_iters)
+    dc_planned_us = dispatch_combine_planned_us(dev, rank, world, args.dc_iters)
     peak = torch.cuda.max_memory_allocated(dev) / 2**30
     peak = max_over_ranks(peak, dev)
     if rank == 0:
@@ -206,6 +236,8 @@ def run_spec_ep(args):
             "impl": "spec_ep",
             "dispatch_combine_us_per_layer": dc_us,
             "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0, identity experts",
+            "dispatch_combine_us_per_layer_planned": dc_planned_us,
+            "planned_placement": "LPT packing of the previous batch's loads + top-16 experts replicated on every rank",
             "rows_per_token": bound,
             "loss": loss_dev, "peak_mem_gib": peak,
             "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
@@ -262,6 +294,8 @@ def run_reference(args):
             "impl": "reference", "metric": METRIC, "unavailable": reason, "n_gpus": world,
             "dispatch_combine_us_per_layer": ms * 1000.0,
             "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0, identity experts",
+            "dispatch_combine_us_per_layer_planned": dc_planned_us,
+            "planned_placement": "LPT packing of the previous batch's loads + top-16 experts replicated on every rank",
             "api": "spec_ep.rbd.RBD_combine_dispatch (reference, unmodified, NCCL)",
         }), flush=True)
     dist.barrier()

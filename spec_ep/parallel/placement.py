@@ -104,7 +104,8 @@ def plan_balanced(load: torch.Tensor, world: int, replicate_top: int = 0) -> Pla
     plus a replica of the ``replicate_top`` most loaded experts on every rank.
 
     Replicated experts' load is spread evenly across ranks before packing the rest, since
-    each source serves them locally.
+    each source serves them locally; their primary copies are dealt round-robin so every
+    rank keeps primary slots for the non-replicated experts.
     """
     E = load.numel()
     if E % world:
@@ -116,11 +117,17 @@ def plan_balanced(load: torch.Tensor, world: int, replicate_top: int = 0) -> Pla
     base = torch.zeros(world, dtype=torch.float64)
     for e in replicated:
         base += load[e] / world
-    heap = [(float(base[r]), r) for r in range(world)]
-    heapq.heapify(heap)
     owner = [-1] * E
     slots = [[] for _ in range(world)]
-    for e in order:
+    for i, e in enumerate(order[:replicate_top]):
+        r = i % world
+        while len(slots[r]) >= cap:  # more replicas than primary slots on this rank
+            r = (r + 1) % world
+        slots[r].append(e)
+        owner[e] = r
+    heap = [(float(base[r]), r) for r in range(world)]
+    heapq.heapify(heap)
+    for e in order[replicate_top:]:
         full = []
         while True:
             cur, r = heapq.heappop(heap)
