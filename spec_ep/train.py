@@ -50,33 +50,17 @@ class Trainer:
             fuse_expert_optimizer = expert_state == "8bit"
         self.fuse_expert_optimizer = fuse_expert_optimizer
         model.set_grad_sink(_ExpertUpdater(self))
+        self.buckets = _GradBuckets(self.dense, self.dp_group, self.bucket_bytes) if self.world > 1 else None
 
     def _sync_dense_grads(self):
-        if self.world <= 1:
-            return
-        grads = [p.grad for p in self.dense if p.grad is not None]
-        bucket, size = [], 0
-        for g in grads:
-            bucket.append(g)
-            size += g.numel() * g.element_size()
-            if size >= self.bucket_bytes:
-                self._reduce_bucket(bucket)
-                bucket, size = [], 0
-        if bucket:
-            self._reduce_bucket(bucket)
-
-    def _reduce_bucket(self, bucket):
-        flat = torch.cat([g.reshape(-1) for g in bucket])
-        dist.all_reduce(flat, group=self.dp_group)
-        flat.mul_(1.0 / self.world)
-        off = 0
-        for g in bucket:
-            n = g.numel()
-            g.copy_(flat[off:off + n].view_as(g))
-            off += n
+        """Wait for the bucketed all-reduces started during backward (ranks > 1)."""
+        if self.buckets is not None:
+            self.buckets.finish()
 
     def train_step(self, input_ids, labels, num_valid=None):
         """One optimizer step on a device-resident batch; returns the (device) loss."""
+        if self.buckets is not None:
+            self.buckets.begin()
         loss = self.model(input_ids, labels, num_valid)
         loss.backward()
         self._sync_dense_grads()
@@ -90,6 +74,93 @@ class Trainer:
         lab = labels_cpu.to(dev, non_blocking=True)
         loss = self.train_step(ids, lab, num_valid)
         return float(loss.to("cpu"))
+
+
+class _GradBuckets:
+    """Dense-gradient averaging overlapped with the backward pass.
+
+    Dense parameters are packed, in reverse registration order (roughly the order their
+    gradients become ready), into flat buckets of about ``bucket_bytes``; each slot starts
+    on a 16-byte boundary so the optimizer kernels can read it with vector loads. A
+    post-accumulate-grad hook copies each gradient into its slot and frees it; when a
+    bucket's last gradient lands, an asynchronous NCCL all-reduce (average) of the bucket
+    starts on NCCL's stream while backward continues. ``finish`` makes the compute stream
+    wait for every bucket and hands the reduced slots to the optimizer as ``.grad`` views.
+    A parameter that got no gradient in a step contributes zeros. Every rank runs the same
+    model, so buckets complete in the same order on every rank.
+    """
+
+    def __init__(self, params, group, bucket_bytes):
+        self.group = group
+        self.active = False
+        # NCCL averages in the collective; other backends sum and scale afterwards
+        self.avg = dist.get_backend(group) == "nccl"
+        self.world = dist.get_world_size(group)
+        self.buckets = []  # (flat buffer, [(param, offset)])
+        self.where = {}
+        cur, size = [], 0
+        for p in reversed(params):
+            cur.append(p)
+            size += p.numel() * p.element_size()
+            if size >= bucket_bytes:
+                self._add(cur)
+                cur, size = [], 0
+        if cur:
+            self._add(cur)
+        for p in params:
+            p.register_post_accumulate_grad_hook(self._hook)
+
+    def _add(self, ps):
+        dtype, dev = ps[0].dtype, ps[0].device
+        align = max(1, 16 // ps[0].element_size())
+        off, slots = 0, []
+        for p in ps:
+            if p.dtype != dtype:
+                raise TypeError("a gradient bucket holds one dtype")
+            slots.append((p, off))
+            off += (p.numel() + align - 1) // align * align
+        b = len(self.buckets)
+        self.buckets.append((torch.zeros(off, dtype=dtype, device=dev), slots))
+        for i, (p, _) in enumerate(slots):
+            self.where[id(p)] = (b, i)
+
+    def begin(self):
+        self.active = True
+        self.pending = [len(slots) for _, slots in self.buckets]
+        self.seen = [[False] * len(slots) for _, slots in self.buckets]
+        self.works = [None] * len(self.buckets)
+
+    def _hook(self, p):
+        if not self.active:  # backward outside a training step: leave .grad alone
+            return
+        b, i = self.where[id(p)]
+        flat, slots = self.buckets[b]
+        off = slots[i][1]
+        flat[off:off + p.numel()].copy_(p.grad.reshape(-1))
+        p.grad = None
+        self.seen[b][i] = True
+        self.pending[b] -= 1
+        if self.pending[b] == 0:
+            self._launch(b)
+
+    def _launch(self, b):
+        op = dist.ReduceOp.AVG if self.avg else dist.ReduceOp.SUM
+        self.works[b] = dist.all_reduce(self.buckets[b][0], op=op, group=self.group, async_op=True)
+
+    def finish(self):
+        for b, (flat, slots) in enumerate(self.buckets):
+            if self.works[b] is None:  # some parameter got no gradient this step
+                for i, (p, off) in enumerate(slots):
+                    if not self.seen[b][i]:
+                        flat[off:off + p.numel()].zero_()
+                self._launch(b)
+        for b, (flat, slots) in enumerate(self.buckets):
+            self.works[b].wait()
+            if not self.avg:
+                flat.mul_(1.0 / self.world)
+            for p, off in slots:
+                p.grad = flat[off:off + p.numel()].view_as(p)
+        self.active = False
 
 
 class _ExpertUpdater:
