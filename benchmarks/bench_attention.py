@@ -52,12 +52,16 @@ def main():
     o, lse = attention_fwd(q, k, v)
     out = {"T": T, "Hq": Hq, "Hkv": Hkv}
     out["tc_fwd_us"] = timed(lambda: attention_fwd(q, k, v), args.iters)
+    out["tc2_fwd_us"] = timed(lambda: attention_fwd(q, k, v, two_tile=True), args.iters)
+    o2, _ = attention_fwd(q, k, v, two_tile=True)
+    out["tc2_fwd_maxdiff_vs_tc"] = (o2.float() - o.float()).abs().max().item()
     out["tc_bwd_us"] = timed(lambda: attention_bwd(q, k, v, o, lse, do), args.iters)
 
     qs, ks, vs = (t.clone().requires_grad_() for t in (q, k, v))
     out["sdpa_fwd_us"] = timed(lambda: causal_gqa_attention(qs, ks, vs), args.iters)
     os_ = causal_gqa_attention(qs, ks, vs)
     out["sdpa_bwd_us"] = timed(lambda: torch.autograd.grad(os_, (qs, ks, vs), do, retain_graph=True), args.iters)
+    out["tc2_fwd_tflops"] = fwd_flops / out["tc2_fwd_us"] / 1e6
     for name in ("tc", "sdpa"):
         out[f"{name}_fwd_tflops"] = fwd_flops / out[f"{name}_fwd_us"] / 1e6
         out[f"{name}_bwd_tflops"] = bwd_flops / out[f"{name}_bwd_us"] / 1e6

@@ -9,7 +9,8 @@ most, so a ``--set full`` capture of one launch ends in seconds:
             gather of 32,768 expert rows (4096 tokens x top-8, hidden 2048), combine,
             source reduce
   adamw     block-wise 8-bit AdamW on 302M parameters (fp32 gradient)
-  attn_fwd / attn_bwd  tcgen05 causal GQA attention, 4096 tokens, 32 query / 4 kv heads
+  attn_fwd / attn_fwd2 / attn_bwd  tcgen05 causal GQA attention (one- and two-tile forward,
+            backward), 4096 tokens, 32 query / 4 kv heads
   wgrad_adamw8  expert gate_up weight gradient with the 8-bit AdamW epilogue (128 experts
             x 256 rows, W [128, 1536, 2048])
 
@@ -27,7 +28,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", required=True, choices=["gemm", "wgrad", "dispatch", "adamw", "wgrad_adamw8", "attn_fwd", "attn_bwd"])
+    ap.add_argument("--case", required=True, choices=["gemm", "wgrad", "dispatch", "adamw", "wgrad_adamw8", "attn_fwd", "attn_fwd2", "attn_bwd"])
     ap.add_argument("--reps", type=int, default=4)
     args = ap.parse_args()
     from spec_ep.ops import grouped_gemm as gg
@@ -56,7 +57,7 @@ def main():
             st = ep.dispatch_fwd(x, te, tw)
             ep.combine_fwd(st.xp, st)
         ep.check()
-    elif args.case in ("attn_fwd", "attn_bwd"):
+    elif args.case in ("attn_fwd", "attn_fwd2", "attn_bwd"):
         from spec_ep.ops.attention import attention_bwd, attention_fwd
 
         T, Hq, Hkv = 4096, 32, 4
@@ -66,8 +67,8 @@ def main():
         do = torch.randn(T, Hq * 128, device=dev).bfloat16()
         o, lse = attention_fwd(q, k, v)
         for _ in range(args.reps):
-            if args.case == "attn_fwd":
-                attention_fwd(q, k, v)
+            if args.case in ("attn_fwd", "attn_fwd2"):
+                attention_fwd(q, k, v, two_tile=args.case == "attn_fwd2")
             else:
                 attention_bwd(q, k, v, o, lse, do)
     elif args.case == "wgrad_adamw8":

@@ -273,6 +273,350 @@ __global__ void __launch_bounds__(attn::kThreads, 1)
 }
 
 // =====================================================================================
+// Forward, two query tiles per CTA ("ping-pong"). One CTA per (pair of 128-query tiles
+// A = 2m, B = 2m + 1, query head); both tiles share every K/V block load. Warp roles
+// (320 threads):
+//   warp 0      TMA: Q_A and Q_B once, then K/V blocks through a 2-stage ring
+//   warp 1      TMEM allocation (512 columns) + tcgen05.mma issue (one thread):
+//                 S_t = Q_t K_j^T into S_t (128 fp32 columns per tile t in {A, B});
+//                 O_t += P_t V_j with P_t read from TMEM (the A operand in TMEM)
+//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B (one row per thread):
+//               P packed to bf16 and stored back over S_t's first 64 columns.
+// S_t of block j + 1 overwrites P_t of block j, so it is issued once P_t V_j completed;
+// the MMA warp issues whichever tile's next step is ready, so one tile's P V and next S
+// run while the other tile's softmax works.
+// =====================================================================================
+namespace attn2 {
+constexpr int BQ = 128, BKV = 128, D = 128;
+constexpr int kThreads = 320;
+constexpr int TILE = BQ * D * 2;
+constexpr int OFF_Q = 0;                 // Q_A, Q_B
+constexpr int OFF_K = OFF_Q + 2 * TILE;  // 2 stages
+constexpr int OFF_V = OFF_K + 2 * TILE;  // 2 stages
+constexpr int OFF_BAR = OFF_V + 2 * TILE;
+// q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], pv_done[2], drain
+constexpr int NBAR = 12;
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr int SMEM = 1024 + OFF_MISC + 16;
+}  // namespace attn2
+
+// 2^x with the hardware approximation (one MUFU.EX2; denormal results flush to 0,
+// which softmax probabilities can afford).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// One 128-key block of one row: P = 2^(s c - mref) packed to bf16 pairs in pk, row sum
+// in rs; with TRACK also the raw row max; DIAG masks keys > r.
+template <bool DIAG, bool TRACK>
+__device__ __forceinline__ void attn_exp_pass(uint32_t taddr, float c, float mref, int r, uint32_t (&pk)[64],
+                                              float& rs, float& mraw) {
+  const float nm = -mref;
+  float acc = 0.f, mx = mraw;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    uint32_t u[64];
+    tmem_ld64(taddr + hh * 64, u);
+#pragma unroll
+    for (int e2 = 0; e2 < 32; ++e2) {
+      float s0 = __uint_as_float(u[2 * e2]), s1 = __uint_as_float(u[2 * e2 + 1]);
+      if (DIAG) {
+        const int e = hh * 64 + 2 * e2;
+        s0 = e <= r ? s0 : -INFINITY;
+        s1 = e + 1 <= r ? s1 : -INFINITY;
+      }
+      if (TRACK) mx = fmaxf(mx, fmaxf(s0, s1));
+      const float p0 = ex2_ftz(fmaf(s0, c, nm)), p1 = ex2_ftz(fmaf(s1, c, nm));
+      acc += p0 + p1;
+      pk[hh * 32 + e2] = pack_bf16x2(p0, p1);
+    }
+  }
+  rs = acc;
+  mraw = mx;
+}
+
+// Raw row max of one 128-key block (keys > r masked when DIAG).
+template <bool DIAG>
+__device__ __forceinline__ float attn_row_max(uint32_t taddr, int r) {
+  float mx = -INFINITY;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    uint32_t u[64];
+    tmem_ld64(taddr + hh * 64, u);
+#pragma unroll
+    for (int e = 0; e < 64; ++e)
+      if (!DIAG || hh * 64 + e <= r) mx = fmaxf(mx, __uint_as_float(u[e]));
+  }
+  return mx;
+}
+
+__global__ void __launch_bounds__(attn2::kThreads, 1)
+    attention_fwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  using namespace attn2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [tile]
+  uint64_t* p_full = bars + 7;    // [tile]
+  uint64_t* pv_done = bars + 9;   // [tile]
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = p.T / BQ;
+  const int npairs = (nqb + 1) / 2;
+  const int m = npairs - 1 - (int)(blockIdx.x / p.Hq);  // heavy (late) pairs first
+  const int h = blockIdx.x % p.Hq;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int qbA = 2 * m, qbB = 2 * m + 1;
+  const bool hasB = qbB < nqb;
+  const int nkvA = qbA + 1, nkvB = hasB ? qbB + 1 : 0;  // causal: key blocks 0..qb
+  const int nkv_all = hasB ? nkvB : nkvA;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_t = S_t's first 64
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, hasB ? 2 * TILE : TILE);
+      tma_load_2d(smem + OFF_Q, &tmQ, q_full, h * D, qbA * BQ);
+      tma_load_2d(smem + OFF_Q + TILE / 2, &tmQ, q_full, h * D + 64, qbA * BQ);
+      if (hasB) {
+        tma_load_2d(smem + OFF_Q + TILE, &tmQ, q_full, h * D, qbB * BQ);
+        tma_load_2d(smem + OFF_Q + TILE + TILE / 2, &tmQ, q_full, h * D + 64, qbB * BQ);
+      }
+      for (int j = 0; j < nkv_all; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait_bounded(&kv_empty[st], ((j >> 1) & 1) ^ 1, s_abort, p.status, p.timeout_ns)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
+        uint8_t* sk = smem + OFF_K + st * TILE;
+        uint8_t* sv = smem + OFF_V + st * TILE;
+        tma_load_2d(sk, &tmK, &kv_full[st], hk * D, j * BKV);
+        tma_load_2d(sk + TILE / 2, &tmK, &kv_full[st], hk * D + 64, j * BKV);
+        // V as the MN-major B operand: boxes {64 dims, 64 keys}; key half kc, dim half dc
+#pragma unroll
+        for (int kc = 0; kc < 2; ++kc)
+#pragma unroll
+          for (int dc = 0; dc < 2; ++dc)
+            tma_load_2d(sv + kc * (TILE / 2) + dc * 8192, &tmV, &kv_full[st], hk * D + dc * 64, j * BKV + kc * 64);
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc_s = make_idesc_bf16(BQ, BKV, false, false);
+    constexpr uint32_t idesc_o = make_idesc_bf16(BQ, D, false, true);
+    const int nkv[2] = {nkvA, nkvB};
+    auto issue_s = [&](int t, int j) {  // S_t = Q_t K_j^T
+      const uint32_t sq = smem_u32(smem + OFF_Q + t * TILE);
+      const uint32_t sk = smem_u32(smem + OFF_K + (j & 1) * TILE);
+      if (lane == 0) {
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + t * 128, make_smem_desc_sw128(sq + kb * (TILE / 2) + kk * 32, 16, 1024),
+                      make_smem_desc_sw128(sk + kb * (TILE / 2) + kk * 32, 16, 1024), idesc_s,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&s_full[t]);
+      }
+      __syncwarp();
+    };
+    auto issue_pv = [&](int t, int j) {  // O_t += P_t V_j, P_t read from TMEM
+      const uint32_t sv = smem_u32(smem + OFF_V + (j & 1) * TILE);
+      if (lane == 0) {
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + (uint32_t)((kb * 4 + kk) * 8),
+                         make_smem_desc_sw128(sv + kb * (TILE / 2) + kk * 2048, 8192, 1024), idesc_o,
+                         (j > 0 || kb > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[t]);
+      }
+      __syncwarp();
+    };
+    bool ok = mbar_wait_bounded(q_full, 0, s_abort, p.status, p.timeout_ns) &&
+              mbar_wait_bounded(&kv_full[0], 0, s_abort, p.status, p.timeout_ns);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0, 0);
+      if (hasB) issue_s(1, 0);
+    }
+    // Issue whichever step is ready: P_t V_j once the softmax wrote P_t(j); S_t(j+1) once
+    // P_t V_j has completed (S overwrites P) and K_{j+1} has landed. Polling uses the
+    // non-suspending probe and backs off, so this warp leaves issue slots to the softmax.
+    int jp[2] = {0, 0};  // next block whose P V is due, per tile
+    int js[2] = {1, 1};  // next block whose S is due, per tile
+    int jc = 0;          // next block whose K/V stage is released
+    uint64_t t_idle = 0;
+    while (ok) {
+      bool progressed = false;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (jp[t] < nkv[t] && jp[t] < js[t] && mbar_test_wait(&p_full[t], jp[t] & 1)) {
+          tc_fence_after();
+          issue_pv(t, jp[t]);
+          ++jp[t];
+          progressed = true;
+        }
+        if (js[t] < nkv[t] && js[t] == jp[t] && mbar_test_wait(&pv_done[t], (js[t] - 1) & 1) &&
+            mbar_test_wait(&kv_full[js[t] & 1], (js[t] >> 1) & 1)) {
+          tc_fence_after();
+          issue_s(t, js[t]);
+          ++js[t];
+          progressed = true;
+        }
+      }
+      while (jc < nkv_all && (jc < jp[0] || jc >= nkv[0]) && (jc < jp[1] || jc >= nkv[1])) {
+        if (lane == 0) umma_commit(&kv_empty[jc & 1]);  // K_jc / V_jc free once these MMAs finish
+        __syncwarp();
+        ++jc;
+      }
+      if (jp[0] >= nkv[0] && jp[1] >= nkv[1]) break;
+      if (progressed) {
+        t_idle = 0;
+      } else {
+        __nanosleep(64);
+        const uint64_t now = globaltimer_ns();
+        if (t_idle == 0) t_idle = now;
+        if (*s_abort) break;
+        if (now - t_idle > p.timeout_ns) {
+          *s_abort = 1;
+          record_error(p.status, kErrTimeoutMbar);
+          break;
+        }
+      }
+    }
+  } else {
+    const int t = (warp - 2) >> 2;  // tile
+    const int q4 = warp & 3;        // TMEM lane quarter
+    const int r = q4 * 32 + lane;   // row within the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t ts = tmem + t * 128 + lane_off, to = tmem + 256 + t * 128 + lane_off;
+    const float c = p.scale_log2;  // softmax scale * log2(e)
+    const int qb = t ? qbB : qbA;
+    const int nk = t ? nkvB : nkvA;
+    float mrow = -INFINITY, l = 0.f;
+    bool ok = nk > 0;
+    for (int j = 0; j < nk && ok; ++j) {
+      if (!mbar_wait_bounded(&s_full[t], j & 1, s_abort, p.status, p.timeout_ns)) { ok = false; break; }
+      tc_fence_after();
+      // One pass: P = 2^(s c - m_ref) against the running max, tracking the block max on
+      // the way. Only when some row's max grows by more than 2^8 (lazy rescaling) does the
+      // warp rescale O and recompute P from S, still intact until P is stored over it.
+      const bool diag = (j == qb);
+      uint32_t pk[64];
+      float rs = 0.f, mraw = -INFINITY;
+      if (j == 0) {  // first block: the row max comes first
+        mraw = diag ? attn_row_max<true>(ts, r) : attn_row_max<false>(ts, r);
+        mrow = mraw * c;
+        if (diag) attn_exp_pass<true, false>(ts, c, mrow, r, pk, rs, mraw);
+        else attn_exp_pass<false, false>(ts, c, mrow, r, pk, rs, mraw);
+      } else {
+        if (diag) attn_exp_pass<true, true>(ts, c, mrow, r, pk, rs, mraw);
+        else attn_exp_pass<false, true>(ts, c, mrow, r, pk, rs, mraw);
+        const float mb = mraw * c;
+        if (__any_sync(0xffffffffu, mb > mrow + 8.f)) {
+          const float m_new = fmaxf(mrow, mb);
+          const float alpha = exp2f(mrow - m_new);
+          l *= alpha;
+          // O_t is idle here: P_t V_{j-1} completed before S_t of block j was issued
+#pragma unroll 1
+          for (int cc = 0; cc < 4; ++cc) {
+            float v[32];
+            tmem_ld32(to + cc * 32, v);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= alpha;
+            tmem_st32(to + cc * 32, v);
+          }
+          mrow = m_new;
+          if (diag) attn_exp_pass<true, false>(ts, c, mrow, r, pk, rs, mraw);
+          else attn_exp_pass<false, false>(ts, c, mrow, r, pk, rs, mraw);
+        }
+      }
+      {
+        uint32_t lo[32], hi[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          lo[e] = pk[e];
+          hi[e] = pk[32 + e];
+        }
+        tmem_st32_u(ts, lo);
+        tmem_st32_u(ts + 32, hi);
+      }
+      l += rs;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && mbar_wait_bounded(&pv_done[t], (nk - 1) & 1, s_abort, p.status, p.timeout_ns)) {
+      tc_fence_after();
+      const int qrow = qb * BQ + r;
+      const float inv = 1.f / l;
+      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.o) + (size_t)qrow * p.Hq * D + h * D;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float v[32];
+        tmem_ld32(to + cc * 32, v);
+        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(pack_bf16x2(v[8 * q] * inv, v[8 * q + 1] * inv),
+                              pack_bf16x2(v[8 * q + 2] * inv, v[8 * q + 3] * inv),
+                              pack_bf16x2(v[8 * q + 4] * inv, v[8 * q + 5] * inv),
+                              pack_bf16x2(v[8 * q + 6] * inv, v[8 * q + 7] * inv));
+      }
+      // natural-log LSE of the scaled logits: mrow is in log2 units
+      p.lse[(size_t)h * p.T + qrow] = (mrow + log2f(l)) * 0.69314718055994531f;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    if (*s_abort) {
+      if (lane == 0) umma_commit(drain);
+      __syncwarp();
+      uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < p.timeout_ns) {
+      }
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// =====================================================================================
 // Backward. One CTA per (128-key block j, query head h); it walks the query blocks
 // i = j .. T/128-1 (causal). Per query block:
 //   MMA:      S = Q_i K_j^T,  dP = dO_i V_j^T                        (TMEM)
@@ -598,6 +942,33 @@ void attention_fwd(const void* q, const void* k, const void* v, void* o, float* 
   note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("attention_fwd launch: ") + cudaGetErrorString(e));
+}
+
+void attention_fwd_pp(const void* q, const void* k, const void* v, void* o, float* lse, int T, int Hq, int Hkv,
+                      float scale, int* status, cudaStream_t st) {
+  using namespace attn2;
+  if (T % BQ) throw std::runtime_error("attention: sequence length must be a multiple of 128");
+  if (Hq % Hkv) throw std::runtime_error("attention: query heads must be a multiple of kv heads");
+  CUtensorMap tq = tmap_2d(q, T, (int64_t)Hq * D, BQ);
+  CUtensorMap tk = tmap_2d(k, T, (int64_t)Hkv * D, BKV);
+  CUtensorMap tv = tmap_2d(v, T, (int64_t)Hkv * D, 64);
+  AttnParams p;
+  p.T = T;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = o;
+  p.lse = lse;
+  p.status = status;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attention_fwd_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    configured = true;
+  }
+  attention_fwd_pp_kernel<<<((T / BQ + 1) / 2) * Hq, kThreads, SMEM, st>>>(tq, tk, tv, p);
+  note_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("attention_fwd_pp launch: ") + cudaGetErrorString(e));
 }
 
 void attention_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,

@@ -30,6 +30,10 @@ struct AttnBwdParams {
 void attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int T, int Hq, int Hkv,
                    float scale, int* status, cudaStream_t st);
 
+// Same result, two query tiles per CTA sharing K/V loads (P kept in TMEM).
+void attention_fwd_pp(const void* q, const void* k, const void* v, void* o, float* lse, int T, int Hq, int Hkv,
+                      float scale, int* status, cudaStream_t st);
+
 // Backward: dq/dk/dv (bf16) from dout, using the forward's o and lse. dsum, dq_acc,
 // dk_acc, dv_acc are fp32 scratch ([Hq*T], [T*Hq*128], [T*Hkv*128] x2).
 void attention_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,

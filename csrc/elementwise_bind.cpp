@@ -127,7 +127,7 @@ void xent_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, double scale, at
 }
 
 void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
-                   double scale, const c10::optional<at::Tensor>& status) {
+                   double scale, const c10::optional<at::Tensor>& status, bool two_tile) {
   req(q, at::kBFloat16, "q");
   req(k, at::kBFloat16, "k");
   req(v, at::kBFloat16, "v");
@@ -135,8 +135,13 @@ void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   req(lse, at::kFloat, "lse");
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k.size(2) == 128, "q/k/v must be [T, heads, 128]");
   const int T = q.size(0), Hq = q.size(1), Hkv = k.size(1);
-  sepx::attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), T, Hq, Hkv,
-                      (float)scale, status.has_value() ? status->data_ptr<int>() : nullptr, cs());
+  int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
+  if (two_tile)
+    sepx::attention_fwd_pp(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), T, Hq,
+                           Hkv, (float)scale, st, cs());
+  else
+    sepx::attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), T, Hq, Hkv,
+                        (float)scale, st, cs());
 }
 
 // Returns (dq, dk, dv), each shaped like its input.

@@ -9,8 +9,9 @@ def _rel(a, b):
     return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6)).item()
 
 
+@pytest.mark.parametrize("two_tile", [False, True])
 @pytest.mark.parametrize("T,Hq,Hkv", [(128, 2, 1), (512, 4, 2), (1024, 8, 1), (384, 4, 4)])
-def test_attention_fwd(T, Hq, Hkv):
+def test_attention_fwd(T, Hq, Hkv, two_tile):
     from spec_ep.ops.attention import attention_fwd, causal_gqa_attention_reference
 
     torch.manual_seed(0)
@@ -18,7 +19,7 @@ def test_attention_fwd(T, Hq, Hkv):
     k = torch.randn(T, Hkv, 128, device="cuda").bfloat16()
     v = torch.randn(T, Hkv, 128, device="cuda").bfloat16()
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
-    o, lse = attention_fwd(q, k, v, status=st)
+    o, lse = attention_fwd(q, k, v, status=st, two_tile=two_tile)
     torch.cuda.synchronize()
     assert st.item() == 0
     ref, ref_lse = causal_gqa_attention_reference(q, k, v, return_lse=True)
@@ -26,7 +27,8 @@ def test_attention_fwd(T, Hq, Hkv):
     assert (lse - ref_lse).abs().max().item() < 2e-2
 
 
-def test_attention_fwd_large_logits_lazy_rescale():
+@pytest.mark.parametrize("two_tile", [False, True])
+def test_attention_fwd_large_logits_lazy_rescale(two_tile):
     """Rows whose max keeps growing across key blocks exercise the O rescaling path."""
     from spec_ep.ops.attention import attention_fwd, causal_gqa_attention_reference
 
@@ -36,7 +38,7 @@ def test_attention_fwd_large_logits_lazy_rescale():
     k = (torch.randn(T, 1, 128, device="cuda") * 3).bfloat16()
     k += torch.linspace(0, 4, T, device="cuda").view(T, 1, 1).bfloat16()  # later keys score higher
     v = torch.randn(T, 1, 128, device="cuda").bfloat16()
-    o, lse = attention_fwd(q, k, v)
+    o, lse = attention_fwd(q, k, v, two_tile=two_tile)
     ref, ref_lse = causal_gqa_attention_reference(q, k, v, return_lse=True)
     torch.cuda.synchronize()
     assert _rel(o, ref) < 3e-2
