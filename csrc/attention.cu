@@ -283,8 +283,8 @@ __global__ void __launch_bounds__(attn::kThreads, 1)
 //   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B (one row per thread):
 //               P packed to bf16 and stored back over S_t's first 64 columns.
 // S_t of block j + 1 overwrites P_t of block j, so it is issued once P_t V_j completed;
-// the MMA warp issues whichever tile's next step is ready, so one tile's P V and next S
-// run while the other tile's softmax works.
+// the MMA warp issues, per block, tile A's P V and next S, then tile B's, so one tile's
+// P V and next S run while the other tile's softmax works.
 // =====================================================================================
 namespace attn2 {
 constexpr int BQ = 128, BKV = 128, D = 128;
@@ -472,50 +472,29 @@ __global__ void __launch_bounds__(attn2::kThreads, 1)
       issue_s(0, 0);
       if (hasB) issue_s(1, 0);
     }
-    // Issue whichever step is ready: P_t V_j once the softmax wrote P_t(j); S_t(j+1) once
-    // P_t V_j has completed (S overwrites P) and K_{j+1} has landed. Polling uses the
-    // non-suspending probe and backs off, so this warp leaves issue slots to the softmax.
-    int jp[2] = {0, 0};  // next block whose P V is due, per tile
-    int js[2] = {1, 1};  // next block whose S is due, per tile
-    int jc = 0;          // next block whose K/V stage is released
-    uint64_t t_idle = 0;
-    while (ok) {
-      bool progressed = false;
+    // Fixed issue order with blocking waits: for each block j, tile A's P V then its next
+    // S (which overwrites P_A, so it waits for that P V to complete), then tile B's.
+    for (int j = 0; j < nkv_all && ok; ++j) {
+      const int nx = j + 1;
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
-        if (jp[t] < nkv[t] && jp[t] < js[t] && mbar_test_wait(&p_full[t], jp[t] & 1)) {
+        if (!ok || j >= nkv[t]) continue;
+        if (!mbar_wait_bounded(&p_full[t], j & 1, s_abort, p.status, p.timeout_ns)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(t, j);
+        if (nx < nkv[t]) {
+          if (!mbar_wait_bounded(&kv_full[nx & 1], (nx >> 1) & 1, s_abort, p.status, p.timeout_ns) ||
+              !mbar_wait_bounded(&pv_done[t], j & 1, s_abort, p.status, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          issue_pv(t, jp[t]);
-          ++jp[t];
-          progressed = true;
-        }
-        if (js[t] < nkv[t] && js[t] == jp[t] && mbar_test_wait(&pv_done[t], (js[t] - 1) & 1) &&
-            mbar_test_wait(&kv_full[js[t] & 1], (js[t] >> 1) & 1)) {
-          tc_fence_after();
-          issue_s(t, js[t]);
-          ++js[t];
-          progressed = true;
+          issue_s(t, nx);
         }
       }
-      while (jc < nkv_all && (jc < jp[0] || jc >= nkv[0]) && (jc < jp[1] || jc >= nkv[1])) {
-        if (lane == 0) umma_commit(&kv_empty[jc & 1]);  // K_jc / V_jc free once these MMAs finish
-        __syncwarp();
-        ++jc;
-      }
-      if (jp[0] >= nkv[0] && jp[1] >= nkv[1]) break;
-      if (progressed) {
-        t_idle = 0;
-      } else {
-        __nanosleep(64);
-        const uint64_t now = globaltimer_ns();
-        if (t_idle == 0) t_idle = now;
-        if (*s_abort) break;
-        if (now - t_idle > p.timeout_ns) {
-          *s_abort = 1;
-          record_error(p.status, kErrTimeoutMbar);
-          break;
-        }
-      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&kv_empty[j & 1]);  // K_j / V_j free once these MMAs finish
+      __syncwarp();
     }
   } else {
     const int t = (warp - 2) >> 2;  // tile
