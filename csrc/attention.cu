@@ -402,6 +402,10 @@ __global__ void __launch_bounds__(attn2::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  long long* const trace = (blockIdx.x == 0) ? p.trace : nullptr;
+  auto stamp = [&](int role, int j, int ev) {
+    if (trace && lane == 0 && j < 64) trace[(role * 64 + j) * 4 + ev] = clock64();
+  };
   // TMEM columns: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_t = S_t's first 64
 
   if (warp == 0) {
@@ -480,16 +484,20 @@ __global__ void __launch_bounds__(attn2::kThreads, 1)
       for (int t = 0; t < 2; ++t) {
         if (!ok || j >= nkv[t]) continue;
         if (!mbar_wait_bounded(&p_full[t], j & 1, s_abort, p.status, p.timeout_ns)) { ok = false; break; }
+        stamp(t, j, 0);
         tc_fence_after();
         issue_pv(t, j);
+        stamp(t, j, 1);
         if (nx < nkv[t]) {
           if (!mbar_wait_bounded(&kv_full[nx & 1], (nx >> 1) & 1, s_abort, p.status, p.timeout_ns) ||
               !mbar_wait_bounded(&pv_done[t], j & 1, s_abort, p.status, p.timeout_ns)) {
             ok = false;
             break;
           }
+          stamp(t, j, 2);
           tc_fence_after();
           issue_s(t, nx);
+          stamp(t, j, 3);
         }
       }
       if (!ok) break;
@@ -509,6 +517,7 @@ __global__ void __launch_bounds__(attn2::kThreads, 1)
     bool ok = nk > 0;
     for (int j = 0; j < nk && ok; ++j) {
       if (!mbar_wait_bounded(&s_full[t], j & 1, s_abort, p.status, p.timeout_ns)) { ok = false; break; }
+      if (q4 == 2) stamp(2 + t, j, 0);
       tc_fence_after();
       // One pass: P = 2^(s c - m_ref) against the running max, tracking the block max on
       // the way. Only when some row's max grows by more than 2^8 (lazy rescaling) does the
@@ -550,6 +559,7 @@ __global__ void __launch_bounds__(attn2::kThreads, 1)
           lo[e] = pk[e];
           hi[e] = pk[32 + e];
         }
+        if (q4 == 2) stamp(2 + t, j, 1);
         tmem_st32_u(ts, lo);
         tmem_st32_u(ts + 32, hi);
       }
@@ -558,6 +568,7 @@ __global__ void __launch_bounds__(attn2::kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
+      if (q4 == 2) stamp(2 + t, j, 2);
     }
     if (ok && mbar_wait_bounded(&pv_done[t], (nk - 1) & 1, s_abort, p.status, p.timeout_ns)) {
       tc_fence_after();
@@ -924,7 +935,7 @@ void attention_fwd(const void* q, const void* k, const void* v, void* o, float* 
 }
 
 void attention_fwd_pp(const void* q, const void* k, const void* v, void* o, float* lse, int T, int Hq, int Hkv,
-                      float scale, int* status, cudaStream_t st) {
+                      float scale, int* status, cudaStream_t st, long long* trace) {
   using namespace attn2;
   if (T % BQ) throw std::runtime_error("attention: sequence length must be a multiple of 128");
   if (Hq % Hkv) throw std::runtime_error("attention: query heads must be a multiple of kv heads");
@@ -939,6 +950,7 @@ void attention_fwd_pp(const void* q, const void* k, const void* v, void* o, floa
   p.o = o;
   p.lse = lse;
   p.status = status;
+  p.trace = trace;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(attention_fwd_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);

@@ -12,6 +12,11 @@ struct AttnParams {
   float* lse = nullptr;    // [Hq, T] natural-log log-sum-exp of the scaled logits
   int* status = nullptr;
   unsigned long long timeout_ns = 2000000000ull;
+  // Optional trace (two-tile forward, CTA 0 only): SM-clock stamps per 128-key block j,
+  // [role][j][event] with roles 0/1 = MMA issue for tile A/B (P ready, P V issued, P V
+  // done, next S issued) and 2/3 = a softmax warp of tile A/B (S ready, P computed,
+  // P published, -). Laid out as int64 [4][64][4]; null disables it.
+  long long* trace = nullptr;
 };
 
 struct AttnBwdParams {
@@ -32,7 +37,7 @@ void attention_fwd(const void* q, const void* k, const void* v, void* o, float* 
 
 // Same result, two query tiles per CTA sharing K/V loads (P kept in TMEM).
 void attention_fwd_pp(const void* q, const void* k, const void* v, void* o, float* lse, int T, int Hq, int Hkv,
-                      float scale, int* status, cudaStream_t st);
+                      float scale, int* status, cudaStream_t st, long long* trace = nullptr);
 
 // Backward: dq/dk/dv (bf16) from dout, using the forward's o and lse. dsum, dq_acc,
 // dk_acc, dv_acc are fp32 scratch ([Hq*T], [T*Hq*128], [T*Hkv*128] x2).

@@ -127,7 +127,8 @@ void xent_fwd_bwd(at::Tensor& logits, const at::Tensor& labels, double scale, at
 }
 
 void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
-                   double scale, const c10::optional<at::Tensor>& status, bool two_tile) {
+                   double scale, const c10::optional<at::Tensor>& status, bool two_tile,
+                   const c10::optional<at::Tensor>& trace) {
   req(q, at::kBFloat16, "q");
   req(k, at::kBFloat16, "k");
   req(v, at::kBFloat16, "v");
@@ -138,7 +139,8 @@ void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   int* st = status.has_value() ? status->data_ptr<int>() : nullptr;
   if (two_tile)
     sepx::attention_fwd_pp(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), T, Hq,
-                           Hkv, (float)scale, st, cs());
+                           Hkv, (float)scale, st, cs(),
+                           trace.has_value() ? reinterpret_cast<long long*>(trace->data_ptr<int64_t>()) : nullptr);
   else
     sepx::attention_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), T, Hq, Hkv,
                         (float)scale, st, cs());

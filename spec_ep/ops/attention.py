@@ -19,17 +19,19 @@ import torch.nn.functional as F
 from ._ext import load
 
 
-def attention_fwd(q, k, v, scale=None, status=None, two_tile=False):
+def attention_fwd(q, k, v, scale=None, status=None, two_tile=False, trace=None):
     """tcgen05 forward: returns (o [T, Hq*128] bf16, lse [Hq, T] fp32, natural log).
 
-    ``two_tile`` selects the kernel that runs two query tiles per CTA with P kept in TMEM.
+    ``two_tile`` selects the kernel that runs two query tiles per CTA with P kept in TMEM;
+    ``trace`` (int64 [4, 64, 4], two-tile only) receives SM-clock stamps of CTA 0's
+    pipeline events (see csrc/attention.h).
     """
     T, Hq, D = q.shape
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     o = torch.empty(T, Hq * D, device=q.device, dtype=torch.bfloat16)
     lse = torch.empty(Hq, T, device=q.device, dtype=torch.float32)
-    load().attention_fwd(q.contiguous(), k.contiguous(), v.contiguous(), o, lse, scale, status, bool(two_tile))
+    load().attention_fwd(q.contiguous(), k.contiguous(), v.contiguous(), o, lse, scale, status, bool(two_tile), trace)
     return o, lse
 
 
