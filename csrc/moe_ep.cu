@@ -320,7 +320,11 @@ __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int*
       int le;
       float w;
       row_meta(a, dst_tk, topk_w, self_tok, meta_tk, src, s, j, &le, &w);
-      if (le >= 0 && le < G) atomicAdd(&s_cnt[le], 1);
+      if (le >= G || le < -1) {
+        record_error(a.status, kErrCorrupt);  // corrupted metadata: the entry is dropped
+      } else if (le >= 0) {
+        atomicAdd(&s_cnt[le], 1);
+      }
     }
   }
   __syncthreads();
@@ -445,7 +449,7 @@ __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
     int le = -1;
     float w = 0.f;
     if (s < rows) row_meta(a, dst_tk, topk_w, self_tok, meta_tk, src, s, j, &le, &w);
-    if (le >= G) le = -1;
+    if (le >= G || le < -1) le = -1;  // corrupted entry (recorded by the count kernel)
     s_le[threadIdx.x] = le;
     __syncthreads();
     int pos = -1, before = 0, total = 0;

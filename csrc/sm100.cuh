@@ -19,6 +19,7 @@ enum : int {
   kErrTimeoutPeer = 2,     // a peer rank never published its header/flag
   kErrOverflow = 3,        // received rows exceed the receive capacity
   kErrBadArg = 4,
+  kErrCorrupt = 5,         // a received row names a local expert outside [0, G)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -33,9 +33,10 @@ import torch.distributed as dist
 
 from ..ops import grouped_gemm as gg
 from ..ops._ext import load
+from ..utils.profile import stage
 
 ERRORS = {1: "pipeline barrier timeout", 2: "peer rank never signalled (timeout)", 3: "receive capacity overflow",
-          4: "bad argument"}
+          4: "bad argument", 5: "received row names an out-of-range local expert (corrupted metadata)"}
 
 
 class EPError(RuntimeError):
@@ -224,11 +225,14 @@ class ExpertParallel:
 class _EPMoE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, topk_w, w_gu, w_d, topk_e, ep: ExpertParallel, grad_sink, residual):
-        st = ep.dispatch_fwd(x.contiguous(), topk_e, topk_w)
-        h, gu = gg.gg_swiglu_fwd(st.xp, w_gu, st.group_off, status=ep.status)
-        y = gg.gg_fwd(h, w_d, st.group_off, status=ep.status)
+        with stage("ep.dispatch"):
+            st = ep.dispatch_fwd(x.contiguous(), topk_e, topk_w)
+        with stage("ep.experts"):
+            h, gu = gg.gg_swiglu_fwd(st.xp, w_gu, st.group_off, status=ep.status)
+            y = gg.gg_fwd(h, w_d, st.group_off, status=ep.status)
         del h
-        out = ep.combine_fwd(y, st, residual)
+        with stage("ep.combine"):
+            out = ep.combine_fwd(y, st, residual)
         ctx.ep, ctx.st, ctx.sink = ep, st, grad_sink
         ctx.has_residual = residual is not None
         ctx.save_for_backward(w_gu, w_d, gu)
@@ -239,7 +243,8 @@ class _EPMoE(torch.autograd.Function):
         ep, st, sink = ctx.ep, ctx.st, ctx.sink
         w_gu, w_d, gu = ctx.saved_tensors
         dout = dout.contiguous()
-        dyp = ep.dispatch_bwd(dout, st)
+        with stage("ep.dispatch_bwd"):
+            dyp = ep.dispatch_bwd(dout, st)
         row_dw = torch.zeros(st.xp.shape[0], dtype=torch.float32, device=dout.device)
         dgu, hw, row_dw = gg.gg_swiglu_bwd(dyp, w_d, st.group_off, gu, st.row_w, row_dw=row_dw, status=ep.status)
         fused = getattr(sink, "fused_wgrad", None) if sink is not None else None
@@ -255,7 +260,8 @@ class _EPMoE(torch.autograd.Function):
         else:
             dwgu = gg.gg_wgrad(dgu, st.xp, st.group_off, ep.G, status=ep.status)
         del dgu
-        dx, dtopk_w = ep.combine_bwd(dxp, row_dw, st)
+        with stage("ep.combine_bwd"):
+            dx, dtopk_w = ep.combine_bwd(dxp, row_dw, st)
         if fused is None:
             if sink is not None:
                 sink(w_d, dwd)

@@ -9,9 +9,14 @@
   shapes, memory and FLOPs; Chrome trace per rank plus a key-averages table.
 * ``FlopCounter`` - analytic FLOPs of one step of the MoE model (replaces DeepSpeed's
   FlopsProfiler, which is not available here) and achieved TFLOP/s.
+* ``stage`` / ``enable_stage_ranges`` - NVTX ranges (also visible as labels in
+  torch.profiler traces) around the expert-parallel stages; off by default, or with
+  ``SEPX_NVTX=1`` in the environment, so a normal step pays nothing for them.
 """
 from __future__ import annotations
 
+import contextlib
+import os
 from pathlib import Path
 
 import torch
@@ -171,3 +176,26 @@ class CommLogger:
                          "avg_us": 1000 * total_ms / max(len(evs), 1),
                          "algbw_GBps": nbytes / (total_ms * 1e-3) / 1e9 if total_ms > 0 else 0.0}
         return out
+
+
+_STAGE_RANGES = os.environ.get("SEPX_NVTX", "0") == "1"
+
+
+def enable_stage_ranges(on: bool = True):
+    """Turn the NVTX / profiler ranges of :func:`stage` on or off."""
+    global _STAGE_RANGES
+    _STAGE_RANGES = bool(on)
+
+
+@contextlib.contextmanager
+def stage(name: str):
+    """NVTX range + torch.profiler label around one stage (no-op unless enabled)."""
+    if not _STAGE_RANGES:
+        yield
+        return
+    torch.cuda.nvtx.range_push(name)
+    try:
+        with record_function(name):
+            yield
+    finally:
+        torch.cuda.nvtx.range_pop()

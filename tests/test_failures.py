@@ -110,3 +110,29 @@ def test_peer_never_signals_times_out_on_gpu():
     errq = ctx.SimpleQueue()
     mp.spawn(_peer_timeout_worker, args=(_free_port(), errq), nprocs=2, join=True)
     assert errq.empty()
+
+
+@pytest.mark.gpu
+def test_corrupted_expert_ids_are_reported_not_followed():
+    """A receive-side expert id outside [0, G) is dropped with an error code: no
+    out-of-range write happens and ExpertParallel.check() raises."""
+    from spec_ep.parallel.ep import EPError, ExpertParallel
+
+    E, k, H, T = 8, 2, 256, 64
+    ep = ExpertParallel(E, k, H, max_tokens=T)
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    te = torch.randint(0, E, (T, k), device="cuda", dtype=torch.int32)
+    tw = torch.rand(T, k, device="cuda")
+    dst, meta = ep.route_tables(te)
+    meta = meta.clone()
+    meta[5, 1] = E + 7  # corrupted local expert id
+    st = ep.dispatch_fwd(x, te, tw, tables=(dst, meta))
+    ep.combine_fwd(st.xp, st)
+    torch.cuda.synchronize()
+    with pytest.raises(EPError, match="out-of-range local expert"):
+        ep.check()
+    # the communicator stays usable: a clean layer afterwards reports no error
+    st = ep.dispatch_fwd(x, te, tw)
+    ep.combine_fwd(st.xp, st)
+    ep.check()
+    ep.close()
