@@ -213,10 +213,19 @@ class ExpertParallel:
         return dyp
 
     def combine_bwd(self, dxp, row_dw, st: EPState):
-        dx = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
-        dw = torch.empty(st.T, self.k, dtype=torch.float32, device=self.device)
+        self.combine_bwd_send(dxp, row_dw, st)
+        return self.combine_bwd_finish(st)
+
+    def combine_bwd_send(self, dxp, row_dw, st: EPState):
+        """Store this rank's input-gradient partials (and router-weight gradients) into the
+        source ranks' return slabs; independent local work can run before the finish."""
         self.comm.combine(dxp, st.inv_rows, st.row_w, st.rows_from, False, row_dw, st.T, self.epoch,
                           self.done[1:2], self.status, self.timeout_s)
+
+    def combine_bwd_finish(self, st: EPState):
+        """Wait for every rank's partials of this layer and sum them per token."""
+        dx = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
+        dw = torch.empty(st.T, self.k, dtype=torch.float32, device=self.device)
         self.comm.source_reduce(st.slot, st.dst_tk, None, dx, dw, self.epoch, self.done[1:2],
                                 self.status, self.timeout_s)
         return dx, dw
@@ -247,28 +256,30 @@ class _EPMoE(torch.autograd.Function):
             dyp = ep.dispatch_bwd(dout, st)
         row_dw = torch.zeros(st.xp.shape[0], dtype=torch.float32, device=dout.device)
         dgu, hw, row_dw = gg.gg_swiglu_bwd(dyp, w_d, st.group_off, gu, st.row_w, row_dw=row_dw, status=ep.status)
+        dxp = gg.gg_dgrad(dgu, w_gu, st.group_off, status=ep.status)
+        with stage("ep.combine_bwd"):
+            ep.combine_bwd_send(dxp, row_dw, st)
+        del dxp
+        # The expert weight gradients (and their optimizer updates) feed nothing downstream,
+        # so they run while the other ranks' partials of this layer are still in flight.
         fused = getattr(sink, "fused_wgrad", None) if sink is not None else None
         g_gu = g_d = None
-        if fused is not None:  # optimizer applied inside the wgrad GEMM epilogue
-            fused(w_d, dyp, hw, st.group_off, ep.status)
-        else:
-            dwd = gg.gg_wgrad(dyp, hw, st.group_off, ep.G, status=ep.status)
-        del hw, dyp
-        dxp = gg.gg_dgrad(dgu, w_gu, st.group_off, status=ep.status)
-        if fused is not None:
-            fused(w_gu, dgu, st.xp, st.group_off, ep.status)
-        else:
-            dwgu = gg.gg_wgrad(dgu, st.xp, st.group_off, ep.G, status=ep.status)
-        del dgu
-        with stage("ep.combine_bwd"):
-            dx, dtopk_w = ep.combine_bwd(dxp, row_dw, st)
-        if fused is None:
-            if sink is not None:
-                sink(w_d, dwd)
-                sink(w_gu, dwgu)
+        with stage("ep.expert_wgrad"):
+            if fused is not None:  # optimizer applied inside the wgrad GEMM epilogue
+                fused(w_d, dyp, hw, st.group_off, ep.status)
+                fused(w_gu, dgu, st.xp, st.group_off, ep.status)
             else:
-                g_d = dwd.to(w_d.dtype) if ctx.needs_input_grad[3] else None
-                g_gu = dwgu.to(w_gu.dtype) if ctx.needs_input_grad[2] else None
+                dwd = gg.gg_wgrad(dyp, hw, st.group_off, ep.G, status=ep.status)
+                dwgu = gg.gg_wgrad(dgu, st.xp, st.group_off, ep.G, status=ep.status)
+                if sink is not None:
+                    sink(w_d, dwd)
+                    sink(w_gu, dwgu)
+                else:
+                    g_d = dwd.to(w_d.dtype) if ctx.needs_input_grad[3] else None
+                    g_gu = dwgu.to(w_gu.dtype) if ctx.needs_input_grad[2] else None
+        del hw, dyp, dgu
+        with stage("ep.combine_bwd"):
+            dx, dtopk_w = ep.combine_bwd_finish(st)
         ctx.st = None
         dres = dout if ctx.has_residual else None
         return dx, dtopk_w, g_gu, g_d, None, None, None, dres
