@@ -9,6 +9,9 @@ Zipf bias of exponent s; max over ranks of CUDA-event time):
   fp8      inference dispatch with e4m3 1x128 payload: prefill 8192 and decode 128
            tokens/rank, Zipf s=1.0, with and without replicating the 16 hottest experts
            on every rank.
+  graph    decode: 128 tokens/rank, fp8 payload, 16 hottest experts replicated, identity
+           experts; eager layers vs the same 8 layers replayed from one CUDA graph
+           (device-side epochs, no host sync), time per layer.
   hier     Qwen3-235B-A22B MoE layer (hidden 4096, 128 experts, top-8, 4096 tokens/rank)
            on logical groups of --group-size: two-stage path vs flat P2P vs naive NCCL,
            Zipf s in {0, 0.5, 1.0, 1.5}.
@@ -66,7 +69,7 @@ def rows_per_token(te, e2r, rank, world):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--scenario", nargs="+", default=["layer", "fp8", "hier"])
+    ap.add_argument("--scenario", nargs="+", default=["layer", "fp8", "graph", "hier"])
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--group-size", type=int, default=4)
     ap.add_argument("--profile", action="store_true",
@@ -80,6 +83,10 @@ def main():
     from spec_ep.utils.routing import synthetic_routing
 
     rank, world, dev = init_distributed()
+    if not dist.is_initialized():  # a single rank still uses the collectives below
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29560")
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
     out = {"world": world}
     ident = lambda rows, ids: rows  # noqa: E731
     ref = reference_rbd()
@@ -155,6 +162,36 @@ def main():
                 row["bytes_per_row"] = {"bf16": 2048 * 2, "fp8": 2048 + 16 * 4}
                 res.append(row)
         out["fp8"] = res
+
+    if "graph" in args.scenario:
+        from spec_ep.parallel.ep import EPGraph
+
+        T, L = 128, 8
+        res = []
+        for fp8 in (False, True):
+            x, te, tw = synthetic_routing(T, 2048, 128, 8, s=1.0, seed=0, rank=rank, device=dev)
+            load = torch.bincount(te.flatten().long(), minlength=128).float()
+            dist.all_reduce(load)
+            placement = plan_balanced(load.cpu(), world, replicate_top=16)
+            ep = ExpertParallel(128, 8, 2048, max_tokens=T, device=dev, fp8_dispatch=fp8, placement=placement)
+
+            def layers(static):
+                y = x
+                for _ in range(L):
+                    st = ep.dispatch_fwd(y, te, tw, static_rows=static)
+                    y = ep.combine_fwd(st.xp, st)
+                return y
+
+            row = {"tokens": T, "fp8": fp8, "replicate_top": 16}
+            row["eager_us_per_layer"] = timed(lambda: layers(False), args.iters) / L
+            g = EPGraph(ep, lambda: layers(True))
+            row["graph_us_per_layer"] = timed(g.replay, args.iters) / L
+            ep.check()
+            del g
+            ep.graph_epochs(False)
+            ep.close()
+            res.append(row)
+        out["graph"] = res
 
     if "hier" in args.scenario and world % args.group_size == 0:
         res = []

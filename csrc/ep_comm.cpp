@@ -103,6 +103,18 @@ class EpComm {
 
   int64_t peer_base(int r) const { return reinterpret_cast<int64_t>(args_.peer_base[r]); }
 
+  // Graph replay: kernels add this device counter (int32, bumped once per layer call by
+  // the captured sequence) to the host epoch. None restores host-only epochs.
+  void set_device_epoch(const c10::optional<at::Tensor>& counter) {
+    if (counter.has_value()) {
+      TORCH_CHECK(counter->is_cuda() && counter->scalar_type() == at::kInt && counter->numel() == 1,
+                  "device epoch counter must be one int32 on the GPU");
+      epoch_dev_ = reinterpret_cast<const uint32_t*>(counter->data_ptr<int>());
+    } else {
+      epoch_dev_ = nullptr;
+    }
+  }
+
   // -------------------------------------------------------------------------------
   sepx::EpArgs call_args(int T, int phase, int64_t epoch, at::Tensor& done, at::Tensor& status,
                          double timeout_s) const {
@@ -111,6 +123,7 @@ class EpComm {
     a.T = T;
     a.phase = phase;
     a.epoch = (uint32_t)epoch;
+    a.epoch_dev = epoch_dev_;
     a.done_counter = reinterpret_cast<unsigned int*>(done.data_ptr<int>());
     a.status = status.data_ptr<int>();
     a.timeout_ns = (unsigned long long)(timeout_s * 1e9);
@@ -225,6 +238,7 @@ class EpComm {
   void* heap_ = nullptr;
   size_t bytes_ = 0;
   sepx::EpArgs args_;
+  const uint32_t* epoch_dev_ = nullptr;
 };
 
 // Generic symmetric buffer: one cudaMalloc per rank, IPC-mapped on every peer. ``put``
@@ -300,6 +314,7 @@ void register_ep_comm(pybind11::module& m) {
       .def("ipc_handle", &EpComm::ipc_handle)
       .def("open_peers", &EpComm::open_peers)
       .def("peer_base", &EpComm::peer_base)
+      .def("set_device_epoch", &EpComm::set_device_epoch)
       .def("route_tables", &EpComm::route_tables)
       .def("route_plan", &EpComm::route_plan)
       .def("dispatch", &EpComm::dispatch)

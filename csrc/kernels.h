@@ -26,6 +26,9 @@ struct EpArgs {
   int T = 0;      // tokens of this rank in this call
   int phase = 0;  // header row used by this call
   uint32_t epoch = 0;
+  // Optional device counter added to epoch (graph replay: a kernel in the captured
+  // sequence bumps it, so every replay runs under a new epoch); null: epoch alone.
+  const uint32_t* epoch_dev = nullptr;
   unsigned int* done_counter = nullptr;
   int* status = nullptr;
   unsigned long long timeout_ns = 5000000000ull;

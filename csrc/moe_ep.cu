@@ -118,6 +118,11 @@ __global__ void route_tables_kernel(const int* __restrict__ topk_e, const int* _
   }
 }
 
+// Epoch of this call: the host value plus the device counter when one is given.
+__device__ __forceinline__ uint32_t ep_epoch(const EpArgs& a) {
+  return a.epoch_dev ? a.epoch + *a.epoch_dev : a.epoch;
+}
+
 // Publish helper: the last CTA to finish writes the headers (release, system scope).
 __device__ __forceinline__ void publish_last_cta(unsigned int* done_counter, const EpArgs& a,
                                                  int phase, const int* counts_per_dst,
@@ -137,7 +142,7 @@ __device__ __forceinline__ void publish_last_cta(unsigned int* done_counter, con
     uint64_t* hdr = reinterpret_cast<uint64_t*>(base + a.off_hdr) + (size_t)phase * a.W + a.rank;
     uint32_t rows = (uint32_t)counts_per_dst[d];
     (void)counts_are_per_src;
-    st_release_sys_u64(hdr, ((uint64_t)a.epoch << 32) | rows);
+    st_release_sys_u64(hdr, ((uint64_t)ep_epoch(a) << 32) | rows);
   }
 }
 
@@ -304,7 +309,7 @@ __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int*
     } else {
       const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
       const uint64_t* hdr = reinterpret_cast<const uint64_t*>(base + a.off_hdr) + (size_t)a.phase * a.W + src;
-      if (!wait_header(hdr, a.epoch, &rows, a.status, a.timeout_ns)) rows = 0;
+      if (!wait_header(hdr, ep_epoch(a), &rows, a.status, a.timeout_ns)) rows = 0;
     }
     if (rows > (uint32_t)a.cap) {
       record_error(a.status, kErrOverflow);
@@ -503,7 +508,7 @@ __global__ void __launch_bounds__(256) recv_gather_kernel(EpArgs a, const __nv_b
       const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
       const uint64_t* hdr = reinterpret_cast<const uint64_t*>(base + a.off_hdr) + (size_t)a.phase * a.W + src;
       uint32_t rows;
-      wait_header(hdr, a.epoch, &rows, a.status, a.timeout_ns);
+      wait_header(hdr, ep_epoch(a), &rows, a.status, a.timeout_ns);
     }
   }
   __syncthreads();
@@ -637,7 +642,7 @@ __global__ void __launch_bounds__(256) source_reduce_kernel(EpArgs a, const int*
     const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
     const uint64_t* hdr = reinterpret_cast<const uint64_t*>(base + a.off_hdr) + (size_t)a.phase * a.W + d;
     uint32_t rows;
-    wait_header(hdr, a.epoch, &rows, a.status, a.timeout_ns);
+    wait_header(hdr, ep_epoch(a), &rows, a.status, a.timeout_ns);
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -770,7 +775,7 @@ __global__ void wait_rows_kernel(EpArgs a, const int* __restrict__ send_count, i
   } else {
     const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
     const uint64_t* hdr = reinterpret_cast<const uint64_t*>(base + a.off_hdr) + (size_t)a.phase * a.W + src;
-    if (!wait_header(hdr, a.epoch, &rows, a.status, a.timeout_ns)) rows = 0;
+    if (!wait_header(hdr, ep_epoch(a), &rows, a.status, a.timeout_ns)) rows = 0;
   }
   rows_from[src] = (int)min(rows, (uint32_t)a.cap);
 }

@@ -35,6 +35,8 @@ from ..ops import grouped_gemm as gg
 from ..ops._ext import load
 from ..utils.profile import stage
 
+GRAPH_EPOCH_BASE = 1 << 31  # epochs of graph-replayed calls: base + device counter
+
 ERRORS = {1: "pipeline barrier timeout", 2: "peer rank never signalled (timeout)", 3: "receive capacity overflow",
           4: "bad argument", 5: "received row names an out-of-range local expert (corrupted metadata)"}
 
@@ -127,6 +129,8 @@ class ExpertParallel:
         self.nchunks = self.world * ((max_tokens + 127) // 128)
         self.timeout_s = float(timeout_s)
         self.epoch = 0
+        self.cur_epoch = 0
+        self.epoch_dev = None  # device epoch counter, set by graph_epochs(True)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.done = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.fp8_dispatch = bool(fp8_dispatch)
@@ -144,6 +148,32 @@ class ExpertParallel:
     def close(self):
         self.comm.close()
 
+    def graph_epochs(self, on: bool = True):
+        """Switch to (or from) a device-side epoch counter.
+
+        Kernels validate peer headers against the epoch of their call. A captured CUDA
+        graph replays its kernels with the arguments of the capture, so for capture each
+        layer call instead bumps a device counter that every kernel of the call adds to a
+        fixed base (2^31 and up, disjoint from the host-counted epochs). Every rank of the
+        group must switch at the same call.
+        """
+        if on:
+            if self.epoch_dev is None:
+                self.epoch_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.comm.set_device_epoch(self.epoch_dev)
+        else:
+            self.comm.set_device_epoch(None)
+        self._graph = bool(on)
+
+    def _next_epoch(self) -> int:
+        if getattr(self, "_graph", False):
+            self.epoch_dev.add_(1)
+            self.cur_epoch = GRAPH_EPOCH_BASE
+        else:
+            self.epoch += 1
+            self.cur_epoch = self.epoch
+        return self.cur_epoch
+
     def _args(self):
         return self.done, self.status, self.timeout_s
 
@@ -155,14 +185,18 @@ class ExpertParallel:
         self.comm.route_tables(e, self.e2r, self.e2l, dst, meta)
         return dst, meta
 
-    def dispatch_fwd(self, x, topk_e, topk_w, tables=None) -> EPState:
+    def dispatch_fwd(self, x, topk_e, topk_w, tables=None, static_rows=False) -> EPState:
         """Send rows, build the expert-grouped receive layout. ``tables`` optionally gives
-        precomputed ``(dst_tk, meta_tk)`` (e.g. the hierarchical path's pilot routing)."""
+        precomputed ``(dst_tk, meta_tk)`` (e.g. the hierarchical path's pilot routing).
+
+        ``static_rows`` sizes the receive buffers at their worst case instead of reading
+        the received row count back to the host: no host sync, so the layer can be
+        captured in a CUDA graph (inference; the expert GEMMs skip the unused rows).
+        """
         T, dev, W, k = x.shape[0], self.device, self.world, self.k
         if T > self.cap:
             raise ValueError(f"{T} tokens exceed the communicator capacity {self.cap}")
-        self.epoch += 1
-        ep = self.epoch
+        ep = self._next_epoch()
         slot = torch.empty(T, W, dtype=torch.int32, device=dev)
         send_count = torch.empty(W, dtype=torch.int32, device=dev)
         self_tok = torch.empty(self.cap, dtype=torch.int32, device=dev)
@@ -182,8 +216,11 @@ class ExpertParallel:
                                   self.timeout_s)
         # One small device->host read per layer sizes every buffer of this layer exactly
         # (saved activations included); the receive capacity is the true worst case.
-        R = max(int(group_off[G].item()), 1)
-        self.rows_last = R
+        if static_rows:
+            R = self.cap_rows
+        else:
+            R = max(int(group_off[G].item()), 1)
+            self.rows_last = R
         xp = torch.empty(R, self.H, dtype=torch.bfloat16, device=dev)
         row_w = torch.empty(R, dtype=torch.float32, device=dev)
         row_src = torch.empty(R, dtype=torch.int32, device=dev)
@@ -196,15 +233,14 @@ class ExpertParallel:
 
     def combine_fwd(self, y, st: EPState, residual=None):
         out = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
-        self.comm.combine(y, st.inv_rows, st.row_w, st.rows_from, True, None, st.T, self.epoch, self.done[1:2],
+        self.comm.combine(y, st.inv_rows, st.row_w, st.rows_from, True, None, st.T, self.cur_epoch, self.done[1:2],
                           self.status, self.timeout_s)
-        self.comm.source_reduce(st.slot, st.dst_tk, residual, out, None, self.epoch, self.done[1:2],
+        self.comm.source_reduce(st.slot, st.dst_tk, residual, out, None, self.cur_epoch, self.done[1:2],
                                 self.status, self.timeout_s)
         return out
 
     def dispatch_bwd(self, dy, st: EPState):
-        self.epoch += 1
-        ep = self.epoch
+        ep = self._next_epoch()
         self.comm.dispatch(dy, st.dst_tk, st.meta_tk, st.topk_w, st.slot, st.self_tok, st.send_count,
                            False, ep, self.done[0:1], self.status, self.timeout_s, False)
         dyp = torch.empty(st.xp.shape[0], self.H, dtype=torch.bfloat16, device=self.device)
@@ -219,16 +255,45 @@ class ExpertParallel:
     def combine_bwd_send(self, dxp, row_dw, st: EPState):
         """Store this rank's input-gradient partials (and router-weight gradients) into the
         source ranks' return slabs; independent local work can run before the finish."""
-        self.comm.combine(dxp, st.inv_rows, st.row_w, st.rows_from, False, row_dw, st.T, self.epoch,
+        self.comm.combine(dxp, st.inv_rows, st.row_w, st.rows_from, False, row_dw, st.T, self.cur_epoch,
                           self.done[1:2], self.status, self.timeout_s)
 
     def combine_bwd_finish(self, st: EPState):
         """Wait for every rank's partials of this layer and sum them per token."""
         dx = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
         dw = torch.empty(st.T, self.k, dtype=torch.float32, device=self.device)
-        self.comm.source_reduce(st.slot, st.dst_tk, None, dx, dw, self.epoch, self.done[1:2],
+        self.comm.source_reduce(st.slot, st.dst_tk, None, dx, dw, self.cur_epoch, self.done[1:2],
                                 self.status, self.timeout_s)
         return dx, dw
+
+
+class EPGraph:
+    """A callable that runs expert-parallel inference layers, captured as one CUDA graph.
+
+    ``fn`` must call ``dispatch_fwd(..., static_rows=True)`` (no host sync) and read its
+    inputs from tensors that stay allocated; copy new inputs into them and ``replay()``.
+    Capture switches ``ep`` to device-side epochs (each replayed layer call bumps the
+    counter on the device), runs ``warmup`` eager calls on a side stream, then captures
+    one call. Every rank of the group must build and replay its graph in the same order.
+    Errors recorded by the kernels surface through ``ep.check()`` as usual.
+    """
+
+    def __init__(self, ep: "ExpertParallel", fn, warmup: int = 2):
+        self.ep, self.fn = ep, fn
+        ep.graph_epochs(True)
+        side = torch.cuda.Stream(device=ep.device)
+        side.wait_stream(torch.cuda.current_stream(ep.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                fn()
+        torch.cuda.current_stream(ep.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = fn()
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
 
 
 class _EPMoE(torch.autograd.Function):
