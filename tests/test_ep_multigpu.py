@@ -275,3 +275,69 @@ def test_hierarchical_two_stage_dispatch():
     errq = ctx.SimpleQueue()
     mp.spawn(_hier_worker, args=(world, _free_port(), errq), nprocs=world, join=True)
     assert errq.empty()
+
+
+def _graph_worker(rank, world, port, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        from spec_ep.ops.grouped_gemm import gg_fwd, gg_swiglu_fwd
+        from spec_ep.parallel.ep import EPGraph, ExpertParallel
+
+        T, E, k, H, I = 128, 16, 4, 512, 256
+        g = torch.Generator().manual_seed(0)
+        epr = E // world
+        w_gu = (torch.randn(E, 2 * I, H, generator=g) / H**0.5).bfloat16()[rank * epr:(rank + 1) * epr].to(dev)
+        w_d = (torch.randn(E, H, I, generator=g) / I**0.5).bfloat16()[rank * epr:(rank + 1) * epr].to(dev)
+
+        def layers(ep, x, te, tw, static):
+            for _ in range(2):
+                st = ep.dispatch_fwd(x, te, tw, static_rows=static)
+                h, _ = gg_swiglu_fwd(st.xp, w_gu, st.group_off, status=ep.status)
+                x = ep.combine_fwd(gg_fwd(h, w_d, st.group_off, status=ep.status), st)
+            return x
+
+        def inputs(seed):
+            gg = torch.Generator(device=dev).manual_seed(1000 * seed + rank)
+            x = torch.randn(T, H, device=dev, generator=gg).bfloat16()
+            tw, te = torch.softmax(torch.randn(T, E, device=dev, generator=gg), -1).topk(k, -1)
+            return x, te.int(), tw
+
+        eager_ep = ExpertParallel(E, k, H, max_tokens=T, device=dev)
+        graph_ep = ExpertParallel(E, k, H, max_tokens=T, device=dev)
+        xs, tes, tws = inputs(0)
+        graph = EPGraph(graph_ep, lambda: layers(graph_ep, xs, tes, tws, True))
+        for seed in (1, 2, 3):  # every replay runs under a new device-side epoch
+            x, te, tw = inputs(seed)
+            xs.copy_(x)
+            tes.copy_(te)
+            tws.copy_(tw)
+            got = graph.replay().clone()
+            want = layers(eager_ep, x, te, tw, False)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), seed
+        graph_ep.check()
+        eager_ep.check()
+        dist.barrier()
+        del graph
+        graph_ep.close()
+        eager_ep.close()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+def test_ep_layers_cuda_graph_across_gpus():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(n, 4)
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.spawn(_graph_worker, args=(world, _free_port(), errq), nprocs=world, join=True)
+    assert errq.empty()
