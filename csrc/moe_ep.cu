@@ -447,22 +447,33 @@ __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
   __shared__ int s_base[1024];
   for (int g = threadIdx.x; g < G; g += blockDim.x) s_base[g] = chunk_base[(size_t)blockIdx.x * G + g];
   __syncthreads();
-  __shared__ int s_le[kChunk];
+  // per-warp entry counts of each group in the current pass (zero between passes)
+  constexpr int kWarpsPerChunk = kChunk / 32;
+  __shared__ int s_wcnt[kWarpsPerChunk * 1024];
+  for (int i = threadIdx.x; i < kWarpsPerChunk * G; i += blockDim.x) s_wcnt[i] = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned lanes_below = (1u << lane) - 1u;
   // Positions are deterministic: within an expert group, entries of this chunk are
-  // ordered by (choice j, slot). Each pass j ranks the block's threads sharing a group.
+  // ordered by (choice j, slot). Each pass j ranks the block's threads sharing a group:
+  // within a warp by __match_any_sync, across warps by per-warp group counts.
   for (int j = 0; j < a.k; ++j) {
     int le = -1;
     float w = 0.f;
     if (s < rows) row_meta(a, dst_tk, topk_w, self_tok, meta_tk, src, s, j, &le, &w);
     if (le >= G || le < -1) le = -1;  // corrupted entry (recorded by the count kernel)
-    s_le[threadIdx.x] = le;
+    const unsigned peers = __match_any_sync(0xffffffffu, le);
+    const bool leader = (__ffs(peers) - 1) == lane;
+    if (le >= 0 && leader) s_wcnt[warp * G + le] = __popc(peers);
     __syncthreads();
     int pos = -1, before = 0, total = 0;
     if (le >= 0) {
-      for (int i = 0; i < kChunk; ++i) {
-        const int same = (s_le[i] == le);
-        before += (i < (int)threadIdx.x) & same;
-        total += same;
+      before = __popc(peers & lanes_below);
+#pragma unroll
+      for (int w2 = 0; w2 < kWarpsPerChunk; ++w2) {
+        const int c = s_wcnt[w2 * G + le];
+        before += (w2 < warp) ? c : 0;
+        total += c;
       }
       pos = s_base[le] + before;
       if (pos - group_off[le] < group_cnt[le]) {
@@ -472,7 +483,8 @@ __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
         pos = -1;  // beyond capacity: dropped (overflow already recorded)
       }
     }
-    __syncthreads();  // every thread has read s_base for this pass
+    __syncthreads();  // every thread has read s_base and s_wcnt for this pass
+    if (le >= 0 && leader) s_wcnt[warp * G + le] = 0;
     if (le >= 0 && before == total - 1) s_base[le] += total;  // last of its group advances
     if (s < rows) inv_rows[((size_t)src * a.cap + s) * a.k + j] = pos;
     __syncthreads();
