@@ -25,6 +25,8 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include <stdexcept>
 #include <string>
 
@@ -245,7 +247,36 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
         }
       }
     }
-    if (with_meta && lane < a.k) {
+    if (with_meta && a.k == 8) {
+      // top-8: the 8 expert ids (16 B) and 8 weights (32 B) of each (token, destination)
+      // go out as three 16-byte stores gathered by warp shuffles (one NVLink write each)
+      const int j = lane < 8 ? lane : 0;
+      const int owner = __ldg(dst_tk + t * 8 + j);
+      const int meta = __ldg(meta_tk + t * 8 + j);
+      const float w = __ldg(topk_w + t * 8 + j);
+      float wf[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) wf[q] = __shfl_sync(0xffffffffu, w, q);
+      unsigned long long rm = remote;
+      while (rm) {
+        const int d = __ffsll(rm) - 1;
+        rm &= rm - 1;
+        const int e = (owner == d) ? meta : -1;
+        const uint32_t pair = ((uint32_t)e & 0xFFFFu) | ((uint32_t)__shfl_down_sync(0xffffffffu, e, 1) << 16);
+        const uint32_t p1 = __shfl_sync(0xffffffffu, pair, 2), p2 = __shfl_sync(0xffffffffu, pair, 4),
+                       p3 = __shfl_sync(0xffffffffu, pair, 6);
+        if (lane == 0) {
+          const int s = __ldg(slot + (size_t)t * a.W + d);
+          char* base = reinterpret_cast<char*>(a.peer_base[d]);
+          const size_t row = (size_t)a.rank * a.cap + s;
+          *reinterpret_cast<uint4*>(reinterpret_cast<int16_t*>(base + a.off_recv_e) + row * 8) =
+              make_uint4(pair, p1, p2, p3);
+          float4* rw = reinterpret_cast<float4*>(reinterpret_cast<float*>(base + a.off_recv_w) + row * 8);
+          rw[0] = make_float4(wf[0], wf[1], wf[2], wf[3]);
+          rw[1] = make_float4(wf[4], wf[5], wf[6], wf[7]);
+        }
+      }
+    } else if (with_meta && lane < a.k) {
       const int j = lane;
       const int owner = __ldg(dst_tk + t * a.k + j);
       const int meta = __ldg(meta_tk + t * a.k + j);
@@ -727,12 +758,21 @@ void ep_route_tables(const int* topk_e, const int* e2r, const int* e2l, int n, i
   check_launch("route_tables");
 }
 
+// Grid of the warp-per-token / warp-per-slot kernels: one warp per slot of the
+// communicator's capacity (8 per CTA), at most two CTAs per SM. It depends only on the
+// capacity, never on a call's token count, because the last-CTA publish counts
+// completions modulo the grid size on a counter that persists across calls.
+static int ep_grid(const EpArgs& a) {
+  const int want = (a.cap + 7) / 8;
+  return std::max(1, std::min(sm_count() * 2, want));
+}
+
 void ep_dispatch(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk, const float* topk_w,
                  const int* slot, int* self_tok, const int* send_count, bool with_meta, cudaStream_t st, bool fp8) {
   if (fp8 && (a.H % 128 || a.off_recv_q == 0)) throw std::runtime_error("fp8 dispatch needs H % 128 == 0 and fp8 slabs");
   if (a.H % 8) throw std::runtime_error("hidden size must be a multiple of 8");
   if (a.k > 32) throw std::runtime_error("top-k above 32 is not supported");
-  int blocks = sm_count() * 2;
+  const int blocks = ep_grid(a);
   dispatch_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(x), dst_tk, meta_tk, topk_w,
                                           slot, self_tok, send_count, with_meta ? 1 : 0, fp8 ? 1 : 0);
   check_launch("dispatch");
@@ -799,7 +839,7 @@ void ep_wait_rows(const EpArgs& a, const int* send_count, int* rows_from, cudaSt
 
 void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float* row_w, const int* rows_from,
                 bool weighted, const float* row_val, cudaStream_t st) {
-  int blocks = sm_count() * 2;
+  const int blocks = ep_grid(a);
   combine_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(y), inv_rows, row_w, rows_from,
                                          weighted ? 1 : 0, row_val, nullptr);
   check_launch("combine");
@@ -807,7 +847,7 @@ void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float
 
 void ep_source_reduce(const EpArgs& a, const int* slot, const int* dst_tk, const void* residual, void* out,
                       float* val, cudaStream_t st) {
-  int blocks = sm_count() * 2;
+  const int blocks = ep_grid(a);
   source_reduce_kernel<<<blocks, 256, 0, st>>>(a, slot, dst_tk, reinterpret_cast<const __nv_bfloat16*>(residual),
                                                reinterpret_cast<__nv_bfloat16*>(out), val);
   check_launch("source_reduce");

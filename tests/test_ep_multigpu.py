@@ -91,15 +91,16 @@ def _worker(rank, world, port, T, E, k, H, I, skew, errq):
         raise
 
 
-@pytest.mark.parametrize("skew", [False, True])
-def test_ep_moe_two_or_more_gpus(skew):
+@pytest.mark.parametrize("skew,k", [(False, 4), (True, 4), (False, 8)])
+def test_ep_moe_two_or_more_gpus(skew, k):
+    """k = 8 also covers the packed (vector-store) metadata of the dispatch."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs at least 2 GPUs")
     world = min(n, 4)
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    mp.spawn(_worker, args=(world, _free_port(), 1024, 16, 4, 512, 256, skew, errq), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), 1024, 16, k, 512, 256, skew, errq), nprocs=world, join=True)
     assert errq.empty()
 
 
