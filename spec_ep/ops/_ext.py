@@ -18,6 +18,8 @@ def load():
     if _C is not None:
         return _C
     try:
+        import torch  # noqa: F401  (loads libc10 / libtorch, which the extension links against)
+
         _C = importlib.import_module("spec_ep._C")
     except Exception as e:  # pragma: no cover - depends on the build
         _ERR = e
