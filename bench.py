@@ -210,8 +210,12 @@ def run_spec_ep(args):
     e2e = None
     if not args.no_e2e:
         losses = []
-        e2e_ms = timed(lambda: losses.append(trainer.train_step_from_host(ids_cpu, lab_cpu, num_valid)), args.steps, dev)
+        with ClockSampler(gpu_uuid(dev)) as clk_e2e:
+            e2e_ms = timed(lambda: losses.append(trainer.train_step_from_host(ids_cpu, lab_cpu, num_valid)),
+                           args.steps, dev)
+        e2e_clocks = gather_clocks(clk_e2e.summary())
         e2e = {"value": tokens / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": e2e_ms,
+               "clocks": e2e_clocks,
                "h2d_bytes_per_step": ids_cpu.numel() * ids_cpu.element_size() + lab_cpu.numel() * lab_cpu.element_size(),
                "d2h_bytes_per_step": 4, "api": "spec_ep.train.Trainer.train_step_from_host",
                "last_loss": losses[-1] if losses else None}
