@@ -923,11 +923,8 @@ void attention_fwd(const void* q, const void* k, const void* v, void* o, float* 
   p.o = o;
   p.lse = lse;
   p.status = status;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attention_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    configured = true;
-  }
+  static unsigned long long smem_devices = 0;
+  smem_optin_once(attention_fwd_kernel, SMEM, smem_devices);
   attention_fwd_kernel<<<(T / BQ) * Hq, kThreads, SMEM, st>>>(tq, tk, tv, p);
   note_launch();
   cudaError_t e = cudaGetLastError();
@@ -951,11 +948,8 @@ void attention_fwd_pp(const void* q, const void* k, const void* v, void* o, floa
   p.lse = lse;
   p.status = status;
   p.trace = trace;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attention_fwd_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    configured = true;
-  }
+  static unsigned long long smem_devices = 0;
+  smem_optin_once(attention_fwd_pp_kernel, SMEM, smem_devices);
   attention_fwd_pp_kernel<<<((T / BQ + 1) / 2) * Hq, kThreads, SMEM, st>>>(tq, tk, tv, p);
   note_launch();
   cudaError_t e = cudaGetLastError();
@@ -992,11 +986,8 @@ void attention_bwd(const void* q, const void* k, const void* v, const void* o, c
   p.dk_acc = dk_acc;
   p.dv_acc = dv_acc;
   p.status = status;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attention_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    configured = true;
-  }
+  static unsigned long long smem_devices = 0;
+  smem_optin_once(attention_bwd_kernel, SMEM, smem_devices);
   attention_bwd_kernel<<<(T / 128) * Hq, 192, SMEM, st>>>(tq, tk, tv, tdo, p);
   note_launch();
   f32_to_bf16_kernel<<<1184, 256, 0, st>>>(dq_acc, reinterpret_cast<__nv_bfloat16*>(dq), nq / 4);

@@ -737,20 +737,14 @@ void adamw_update(const OptHyper& h, const void* g, bool g_bf16, size_t n, int n
     const int grid = (int)std::max<size_t>(1, std::min<size_t>((chunks + opt8::kWarps - 1) / opt8::kWarps, num_sms));
     if (g_bf16) {
       using L = opt8::Lay<__nv_bfloat16>;
-      static bool set = false;
-      if (!set) {
-        cudaFuncSetAttribute(adamw_8bit_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
-        set = true;
-      }
+      static unsigned long long smem_devices = 0;
+      smem_optin_once(adamw_8bit_kernel<__nv_bfloat16>, L::SMEM, smem_devices);
       adamw_8bit_kernel<__nv_bfloat16><<<grid, opt8::kWarps * 32, L::SMEM, st>>>(
           reinterpret_cast<const __nv_bfloat16*>(g), n, h, nullptr, 2000000000ull);
     } else {
       using L = opt8::Lay<float>;
-      static bool set = false;
-      if (!set) {
-        cudaFuncSetAttribute(adamw_8bit_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
-        set = true;
-      }
+      static unsigned long long smem_devices = 0;
+      smem_optin_once(adamw_8bit_kernel<float>, L::SMEM, smem_devices);
       adamw_8bit_kernel<float><<<grid, opt8::kWarps * 32, L::SMEM, st>>>(reinterpret_cast<const float*>(g), n, h,
                                                                          nullptr, 2000000000ull);
     }

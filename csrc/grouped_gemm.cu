@@ -673,11 +673,8 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
   using L = GemmSmem<BN, STAGES, EPI>;
   auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, RAGGED_K, EPI>;
   size_t smem = L::bytes(p.G);
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-    configured = true;
-  }
+  static unsigned long long smem_devices = 0;
+  smem_optin_once(kern, 232448, smem_devices);
   int grid = num_sms();
   if (max_tiles > 0 && max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;

@@ -36,6 +36,19 @@ __device__ __forceinline__ void record_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// Host: opt a kernel into `bytes` of dynamic shared memory on the current device, once per
+// device (the attribute is per device; `done` is the call site's bitmask of devices).
+template <typename Kernel>
+inline void smem_optin_once(Kernel kernel, int bytes, unsigned long long& done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(done & bit)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done |= bit;
+  }
+}
+
 // ----------------------------------------------------------------------------------
 // mbarrier
 // ----------------------------------------------------------------------------------

@@ -1,5 +1,6 @@
 """Overlapped dense-gradient averaging (spec_ep.train._GradBuckets) on 2 gloo ranks (CPU)."""
 import os
+import socket
 
 import torch
 import torch.distributed as dist
@@ -46,8 +47,14 @@ def _worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
+def _free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
 def test_grad_buckets_average_two_ranks():
-    world, port = 2, 29631
+    world, port = 2, _free_port()
     out = mp.Manager().dict()
     mp.spawn(_worker, args=(world, port, out), nprocs=world, join=True)
     assert all(out.get(r) for r in range(world))
