@@ -148,3 +148,37 @@ def test_plan_traffic_counts_single_process():
     assert t["rbd_inter"] == 2
     # rbd_intra: same-node copies to rank 1: token0 expert 2, token2 expert 3 => 2
     assert t["rbd_intra"] == 2
+
+
+def _check_empty_and_skewed(rank, init_file, q):
+    from spec_ep.rbd import RBD_combine_dispatch, naive_combine_dispatch
+
+    local_group = _init(rank, 4, init_file, 2)
+    E, k, H = 8, 2, 4
+    T = 0 if rank == 3 else 12  # rank 3 sends nothing
+    torch.manual_seed(rank)
+    tokens = torch.randn(T, H)
+    weights = torch.rand(T, k)
+    # every copy goes to experts 0 and 1 (rank 0): ranks 1-3 receive nothing
+    route = torch.stack([torch.zeros(T, dtype=torch.long), torch.ones(T, dtype=torch.long)], -1)
+
+    def expert(x, ids):  # non-identity per-expert map x -> x * (e + 1) + e
+        return x * (ids.float() + 1).unsqueeze(-1) + ids.float().unsqueeze(-1)
+
+    ref = sum(weights[:, j:j + 1] * expert(tokens, route[:, j]) for j in range(k))
+    for concurrent in (False, True):
+        out = RBD_combine_dispatch(tokens, weights, expert, route, E=E, gpus_per_node=2,
+                                   local_group=local_group, concurrent=concurrent)
+        assert out.shape == (T, H)
+        torch.testing.assert_close(out, ref)
+    torch.testing.assert_close(naive_combine_dispatch(tokens, weights, expert, route, E), ref)
+    q.put(rank)
+    dist.destroy_process_group()
+
+
+def test_empty_and_skewed_ranks(tmp_path):
+    """A rank with no tokens and ranks that receive no rows still complete every stage."""
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.spawn(_check_empty_and_skewed, args=(tmp_path / "init", q), nprocs=4)
+    assert sorted(q.get() for _ in range(4)) == [0, 1, 2, 3]
