@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -296,6 +297,46 @@ class SymmBuffer {
   }
   int64_t size() const { return (int64_t)bytes_; }
 
+  // Speculative replication: copy the experts named by (fetch_rank[s], fetch_slot[s])
+  // from their primary rank's buffer into local cache slot P + s of every region
+  // (region r holds [slots][reg_stride[r] bytes] at byte reg_off[r]). One kernel with
+  // plain peer loads; the slot choice stays on the device.
+  void fetch_experts(int P, int src_limit, const std::vector<int64_t>& reg_off,
+                     const std::vector<int64_t>& reg_stride, const at::Tensor& fetch_rank,
+                     const at::Tensor& fetch_slot, int blocks_per_slot) {
+    TORCH_CHECK(reg_off.size() == reg_stride.size() && !reg_off.empty() && reg_off.size() <= 4,
+                "1 to 4 weight regions");
+    TORCH_CHECK(fetch_rank.is_cuda() && fetch_rank.scalar_type() == at::kInt && fetch_rank.is_contiguous(),
+                "fetch_rank must be a contiguous int32 CUDA tensor");
+    TORCH_CHECK(fetch_slot.is_cuda() && fetch_slot.scalar_type() == at::kInt && fetch_slot.is_contiguous() &&
+                    fetch_slot.numel() == fetch_rank.numel(),
+                "fetch_slot must match fetch_rank");
+    const int S = (int)fetch_rank.numel();
+    TORCH_CHECK(P >= 1 && S >= 1, "need primary and cache slots");
+    TORCH_CHECK(src_limit >= 1, "src_limit must be positive");
+    for (int r = 0; r < world_; ++r) TORCH_CHECK(peers_[r], "peer ", r, " not mapped");
+    sepx::SpecFetchArgs a;
+    for (int r = 0; r < 64; ++r) a.peer_base[r] = r < world_ ? peers_[r] : nullptr;
+    a.local_base = base_;
+    a.W = world_;
+    a.P = P;
+    a.S = S;
+    a.src_limit = src_limit;
+    a.nreg = (int)reg_off.size();
+    // every rank's buffer has the same size and layout, so bounds checked here hold on peers
+    const size_t slots = (size_t)std::max(P + S, src_limit);
+    for (int r = 0; r < a.nreg; ++r) {
+      TORCH_CHECK(reg_off[r] >= 0 && reg_stride[r] > 0 && (size_t)reg_off[r] + slots * (size_t)reg_stride[r] <= bytes_,
+                  "weight region ", r, " does not fit the buffer");
+      a.reg_off[r] = (size_t)reg_off[r];
+      a.reg_stride[r] = (size_t)reg_stride[r];
+    }
+    a.fetch_rank = fetch_rank.data_ptr<int>();
+    a.fetch_slot = fetch_slot.data_ptr<int>();
+    c10::cuda::CUDAGuard g(device_);
+    sepx::spec_fetch(a, blocks_per_slot, at::cuda::getCurrentCUDAStream().stream());
+  }
+
  private:
   int world_, rank_, device_;
   void* base_ = nullptr;
@@ -303,9 +344,68 @@ class SymmBuffer {
   std::vector<void*> peers_;
 };
 
+// Speculative replication policy: one block turns predicted expert ids into cache
+// updates, fetch orders and routing tables (speculative.cu).
+void spec_policy(const at::Tensor& pred_e, int rank, int P, int min_count, const at::Tensor& base_e2r,
+                 const at::Tensor& base_e2l, const at::Tensor& owner, const at::Tensor& owner_slot,
+                 at::Tensor& slot_expert, at::Tensor& slot_stamp, at::Tensor& step, at::Tensor& e2r, at::Tensor& e2l,
+                 at::Tensor& fetch_rank, at::Tensor& fetch_slot, const c10::optional<at::Tensor>& stats) {
+  auto ok = [](const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kInt && t.is_contiguous(), name,
+                " must be a contiguous int32 CUDA tensor");
+  };
+  ok(pred_e, "pred_e");
+  ok(base_e2r, "base_e2r");
+  ok(base_e2l, "base_e2l");
+  ok(owner, "owner");
+  ok(owner_slot, "owner_slot");
+  ok(slot_expert, "slot_expert");
+  ok(slot_stamp, "slot_stamp");
+  ok(step, "step");
+  ok(e2r, "e2r");
+  ok(e2l, "e2l");
+  ok(fetch_rank, "fetch_rank");
+  ok(fetch_slot, "fetch_slot");
+  TORCH_CHECK(pred_e.dim() == 2, "pred_e must be [T, k]");
+  const int E = (int)base_e2r.numel(), S = (int)slot_expert.numel();
+  TORCH_CHECK(base_e2l.numel() == E && owner.numel() == E && owner_slot.numel() == E && e2r.numel() == E &&
+                  e2l.numel() == E,
+              "expert tables must all have E entries");
+  TORCH_CHECK(slot_stamp.numel() == S && fetch_rank.numel() == S && fetch_slot.numel() == S && step.numel() == 1,
+              "cache tensors must all have S entries");
+  sepx::SpecPolicyArgs a;
+  a.pred_e = pred_e.data_ptr<int>();
+  a.T = (int)pred_e.size(0);
+  a.k = (int)pred_e.size(1);
+  a.E = E;
+  a.S = S;
+  a.P = P;
+  a.rank = rank;
+  a.min_count = min_count;
+  a.base_e2r = base_e2r.data_ptr<int>();
+  a.base_e2l = base_e2l.data_ptr<int>();
+  a.owner = owner.data_ptr<int>();
+  a.owner_slot = owner_slot.data_ptr<int>();
+  a.slot_expert = slot_expert.data_ptr<int>();
+  a.slot_stamp = slot_stamp.data_ptr<int>();
+  a.step = step.data_ptr<int>();
+  a.e2r = e2r.data_ptr<int>();
+  a.e2l = e2l.data_ptr<int>();
+  a.fetch_rank = fetch_rank.data_ptr<int>();
+  a.fetch_slot = fetch_slot.data_ptr<int>();
+  if (stats.has_value()) {
+    TORCH_CHECK(stats->is_cuda() && stats->scalar_type() == at::kLong && stats->numel() == 4,
+                "stats must be 4 int64 on the GPU");
+    a.stats = reinterpret_cast<long long*>(stats->data_ptr<int64_t>());
+  }
+  c10::cuda::CUDAGuard g(pred_e.device());
+  sepx::spec_policy(a, at::cuda::getCurrentCUDAStream().stream());
+}
+
 }  // namespace
 
 void register_ep_comm(pybind11::module& m) {
+  m.def("spec_policy", &spec_policy, "speculative replica cache update (LRU) + routing tables");
   py::class_<EpComm>(m, "EpComm")
       .def(py::init<int, int, int, int, int, int>(), py::arg("world"), py::arg("rank"), py::arg("cap"),
            py::arg("k"), py::arg("hidden"), py::arg("device"))
@@ -332,5 +432,6 @@ void register_ep_comm(pybind11::module& m) {
       .def("open_peers", &SymmBuffer::open_peers)
       .def("local", &SymmBuffer::local)
       .def("put", &SymmBuffer::put)
+      .def("fetch_experts", &SymmBuffer::fetch_experts)
       .def("size", &SymmBuffer::size);
 }

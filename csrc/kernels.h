@@ -62,4 +62,42 @@ void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float
 void ep_source_reduce(const EpArgs& a, const int* slot, const int* dst_tk, const void* residual, void* out,
                       float* val, cudaStream_t st);
 
+// ---------------------------------------------------------------------------------
+// Speculative expert replication (speculative.cu)
+// ---------------------------------------------------------------------------------
+struct SpecPolicyArgs {
+  const int* pred_e = nullptr;  // [T][k] predicted expert ids (negative: ignored)
+  int T = 0, k = 1, E = 0;
+  int S = 0;          // cache slots
+  int P = 0;          // local slots before the cache (primaries + static replicas)
+  int rank = 0;
+  int min_count = 1;  // fewest predicted rows that make an expert worth caching
+  const int* base_e2r = nullptr;  // [E] routing tables without the cache (as seen from this rank)
+  const int* base_e2l = nullptr;
+  const int* owner = nullptr;       // [E] primary rank of each expert
+  const int* owner_slot = nullptr;  // [E] its slot on that rank
+  int* slot_expert = nullptr;       // [S] cached expert per slot (-1: empty), updated
+  int* slot_stamp = nullptr;        // [S] step of last use (-1: never), updated
+  int* step = nullptr;              // [1] call counter, incremented
+  int* e2r = nullptr;               // [E] out: routing tables with the cache
+  int* e2l = nullptr;
+  int* fetch_rank = nullptr;        // [S] out: rank to copy slot s from (-1: no copy)
+  int* fetch_slot = nullptr;        // [S] out: slot on that rank
+  long long* stats = nullptr;       // [4] accumulated: hits, fetches, predicted remote rows, of them now local
+};
+void spec_policy(const SpecPolicyArgs& a, cudaStream_t st);
+
+struct SpecFetchArgs {
+  const void* peer_base[64];  // every rank's symmetric weight buffer
+  void* local_base = nullptr;
+  int W = 1, P = 0, S = 0;
+  int src_limit = 0;          // source slots must be below this (pinned slots of every rank)
+  int nreg = 0;               // weight arrays per expert (e.g. gate_up and down)
+  size_t reg_off[4];          // byte offset of each array in the buffer
+  size_t reg_stride[4];       // bytes per expert slot of each array
+  const int* fetch_rank = nullptr;
+  const int* fetch_slot = nullptr;
+};
+void spec_fetch(const SpecFetchArgs& a, int blocks_per_slot, cudaStream_t st);
+
 }  // namespace sepx

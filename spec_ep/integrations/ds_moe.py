@@ -8,12 +8,23 @@ reads the same JSON keys::
      "expert_parallel": {"enabled": true, "autoep_size": 8, "preset_model": "qwen3_5_moe",
                          "use_grouped_mm": true,
                          "sepx": {"dispatch": "p2p", "groups": 1, "fp8": false,
-                                  "replicate_top_k": 0, "timeout_us": 10000000}},
+                                  "replicate_top_k": 0, "routing_dump": null,
+                                  "speculative_slots": 0, "speculative_min_count": 1,
+                                  "timeout_us": 10000000}},
      "optimizer": {"type": "AdamW", "params": {...}}}
 
 and returns ``(engine, optimizer, None, None)``. ``autoep_size`` < world builds
 expert-parallel groups of that size (contiguous ranks) and expert-data-parallel groups
 across them; dense weights are data-parallel over every rank.
+
+``sepx`` keys: ``fp8`` sends forward rows as e4m3 with 1x128 scales; ``routing_dump``
+(a glob or list of ``experts_rank*.pt`` files) plans a load-balanced placement from
+recorded routing, with ``replicate_top_k`` hot experts on every rank; ``speculative_slots``
+> 0 turns on speculative replication (an LRU cache of that many predicted-hot experts
+per layer and rank; inference only). ``dispatch`` must be ``"p2p"`` for the model engine
+(``"rbd"`` names the torch reference, ``spec_ep.rbd.RBD_combine_dispatch``, which is an
+API rather than an engine), and ``groups`` > 1 (the two-stage path,
+``spec_ep.parallel.hierarchical.HierarchicalEP``) is a forward-only layer of its own.
 """
 from __future__ import annotations
 
@@ -31,7 +42,10 @@ class SepxOptions:
     dispatch: str = "p2p"          # "p2p" (fused NVLink kernels) | "rbd" (torch RBD over NCCL)
     groups: int = 1                # logical GPU groups for the two-stage path
     fp8: bool = False              # e4m3 1x128 dispatch payload (forward only)
-    replicate_top_k: int = 0       # hot experts replicated on every rank
+    replicate_top_k: int = 0       # hot experts replicated on every rank (needs routing_dump)
+    routing_dump: object = None    # glob / list of experts_rank*.pt files for the placement planner
+    speculative_slots: int = 0     # LRU replica cache slots per layer and rank (inference)
+    speculative_min_count: int = 1  # fewest predicted rows that make an expert worth fetching
     timeout_us: int = 10_000_000   # device-side wait limit
 
 
@@ -64,7 +78,41 @@ def load_config(cfg) -> EPConfig:
         raise ValueError("expert_parallel.sepx.dispatch must be 'p2p' or 'rbd'")
     if not out.use_grouped_mm:
         raise ValueError("use_grouped_mm=false is not supported: experts always run as grouped GEMMs")
+    sx = out.sepx
+    if int(sx.groups) < 1 or int(sx.replicate_top_k) < 0 or int(sx.speculative_slots) < 0 or \
+            int(sx.speculative_min_count) < 1 or int(sx.timeout_us) <= 0:
+        raise ValueError("expert_parallel.sepx: groups >= 1, replicate_top_k >= 0, speculative_slots >= 0, "
+                         "speculative_min_count >= 1 and timeout_us > 0 are required")
+    if sx.replicate_top_k and not sx.routing_dump:
+        raise ValueError("expert_parallel.sepx.replicate_top_k needs measured routing: set sepx.routing_dump")
     return out
+
+
+def plan_placement(cfg: EPConfig, num_experts: int, world: int):
+    """Placement for the EP group: planned from ``sepx.routing_dump`` (expert loads summed
+    over layers, ``replicate_top_k`` hot experts on every rank), else contiguous."""
+    import glob
+
+    from ..parallel.placement import contiguous, loads_from_routing, plan_balanced
+    from ..utils.profile import load_routing
+
+    dump = cfg.sepx.routing_dump
+    if not dump:
+        return contiguous(num_experts, world)
+    files = sorted(glob.glob(dump)) if isinstance(dump, str) else list(dump)
+    if not files:
+        raise FileNotFoundError(f"sepx.routing_dump matches no files: {dump!r}")
+    loads = loads_from_routing(load_routing(files), num_experts).sum(0)
+    return plan_balanced(loads, world, int(cfg.sepx.replicate_top_k))
+
+
+def _check_engine_options(cfg: EPConfig):
+    if cfg.sepx.dispatch != "p2p":
+        raise ValueError("the model engine dispatches with the fused p2p kernels (sepx.dispatch='p2p'); "
+                         "spec_ep.rbd.RBD_combine_dispatch is the torch reference API")
+    if int(cfg.sepx.groups) > 1:
+        raise ValueError("sepx.groups > 1: the two-stage path (spec_ep.parallel.hierarchical.HierarchicalEP) is a "
+                         "forward-only layer of its own; the model engine uses the flat path")
 
 
 def make_groups(autoep_size: int):
@@ -124,9 +172,9 @@ def initialize(model=None, config=None, max_tokens: int = 4096, device=None):
     Qwen3-MoE-shaped ``spec_ep`` model. Returns ``(engine, optimizer, None, None)``.
     """
     from ..parallel.ep import ExpertParallel
-    from ..parallel.placement import contiguous
 
     cfg = load_config(config if config is not None else {})
+    _check_engine_options(cfg)
     if device is None:
         device = torch.device("cuda", torch.cuda.current_device())
     ep_group, dp_group = make_groups(cfg.autoep_size) if cfg.enabled else (None, None)
@@ -139,10 +187,16 @@ def initialize(model=None, config=None, max_tokens: int = 4096, device=None):
         from ..train import Trainer
 
         mcfg = get_config(model or "qwen3-30b-a3b")
-        placement = contiguous(mcfg.num_experts, world)
+        placement = plan_placement(cfg, mcfg.num_experts, world)
         ep = ExpertParallel(mcfg.num_experts, mcfg.top_k, mcfg.hidden_size, max_tokens, group=ep_group,
-                            placement=placement, timeout_s=cfg.sepx.timeout_us * 1e-6, device=device)
+                            placement=placement, timeout_s=cfg.sepx.timeout_us * 1e-6, device=device,
+                            fp8_dispatch=bool(cfg.sepx.fp8))
         net = Qwen3MoeForCausalLM(mcfg, ep, device=device)
+        if cfg.sepx.speculative_slots:  # inference engine: no optimizer
+            from ..parallel.speculative import enable_speculation
+
+            enable_speculation(net, int(cfg.sepx.speculative_slots), int(cfg.sepx.speculative_min_count))
+            return SepxEngine(net, None, ep, cfg), None, None, None
         tr = Trainer(net, lr=opt_params.get("lr", 1e-4), betas=tuple(opt_params.get("betas", (0.9, 0.95))),
                      weight_decay=opt_params.get("weight_decay", 0.1), expert_dp_group=dp_group)
         return SepxEngine(net, tr, ep, cfg), tr.opt, None, None
@@ -150,9 +204,11 @@ def initialize(model=None, config=None, max_tokens: int = 4096, device=None):
     from .hf_qwen import swap_moe_blocks
 
     c = getattr(model.config, "text_config", model.config)
+    if cfg.sepx.speculative_slots:
+        raise ValueError("sepx.speculative_slots applies to spec_ep models (Qwen3MoeForCausalLM), not HF blocks")
     ep = ExpertParallel(c.num_experts, c.num_experts_per_tok, c.hidden_size, max_tokens, group=ep_group,
-                        placement=contiguous(c.num_experts, world), timeout_s=cfg.sepx.timeout_us * 1e-6,
-                        device=device)
+                        placement=plan_placement(cfg, c.num_experts, world), timeout_s=cfg.sepx.timeout_us * 1e-6,
+                        device=device, fp8_dispatch=bool(cfg.sepx.fp8))
     model.to(device=device, dtype=torch.bfloat16)
     n = swap_moe_blocks(model, ep)
     if n == 0:

@@ -59,9 +59,18 @@ class Qwen3MoeLayer(nn.Module):
         self.grad_sink = None
         self.router_bias = None  # optional selection bias (synthetic skew studies)
         self.routing_callback = None  # receives topk expert ids (routing capture)
+        self.spec = None  # SpeculativeExperts (speculative replication, inference only)
 
     def forward(self, x, pos=None):
         cfg = self.cfg
+        spec = self.spec
+        if spec is not None:
+            if torch.is_grad_enabled() and self.w_gu.requires_grad:
+                raise RuntimeError("speculative expert replication is inference-only: run under torch.no_grad()")
+            # predict this layer's experts from the incoming residual stream; the replica
+            # fetch runs on a side stream while the attention below executes
+            spec.speculate(x, self.post_norm, self.w_router, cfg.top_k, cfg.rms_norm_eps, cfg.norm_topk_prob,
+                           self.router_bias)
         h = rms_norm(x, self.input_norm, cfg.rms_norm_eps)
         qkv = F.linear(h, self.w_qkv)
         q, k, v = qk_norm_rope(qkv, self.q_norm, self.k_norm, cfg.num_heads, cfg.num_kv_heads, cfg.rms_norm_eps,
@@ -73,6 +82,8 @@ class Qwen3MoeLayer(nn.Module):
         topk_w, topk_e = router_topk(logits, cfg.top_k, cfg.norm_topk_prob, self.router_bias)
         if self.routing_callback is not None:
             self.routing_callback(topk_e)
+        if spec is not None:
+            return ep_moe(h, topk_e, topk_w, spec.w_gu, spec.w_d, self.ep, None, residual=x, route=spec.tables())
         return ep_moe(h, topk_e, topk_w, self.w_gu, self.w_d, self.ep, self.grad_sink, residual=x)
 
 

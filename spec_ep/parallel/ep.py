@@ -177,12 +177,19 @@ class ExpertParallel:
     def _args(self):
         return self.done, self.status, self.timeout_s
 
-    def route_tables(self, topk_e):
-        """(dst_tk, meta_tk) for expert ids ``topk_e`` ([T, k]; negative ids are not sent)."""
+    def set_local_slots(self, G: int):
+        """Number of local expert groups the receive side lays out (primaries plus, with
+        speculative replication, the replica cache slots)."""
+        self.G = int(G)
+        self.cap_rows = self.world * self.cap * self.k + self.G * 64
+
+    def route_tables(self, topk_e, e2r=None, e2l=None):
+        """(dst_tk, meta_tk) for expert ids ``topk_e`` ([T, k]; negative ids are not sent),
+        through this communicator's placement or the given ``(e2r, e2l)`` device tables."""
         e = topk_e.int().contiguous()
         dst = torch.empty_like(e)
         meta = torch.empty_like(e)
-        self.comm.route_tables(e, self.e2r, self.e2l, dst, meta)
+        self.comm.route_tables(e, self.e2r if e2r is None else e2r, self.e2l if e2l is None else e2l, dst, meta)
         return dst, meta
 
     def dispatch_fwd(self, x, topk_e, topk_w, tables=None, static_rows=False) -> EPState:
@@ -298,9 +305,10 @@ class EPGraph:
 
 class _EPMoE(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, topk_w, w_gu, w_d, topk_e, ep: ExpertParallel, grad_sink, residual):
+    def forward(ctx, x, topk_w, w_gu, w_d, topk_e, ep: ExpertParallel, grad_sink, residual, route):
         with stage("ep.dispatch"):
-            st = ep.dispatch_fwd(x.contiguous(), topk_e, topk_w)
+            tables = ep.route_tables(topk_e, *route) if route is not None else None
+            st = ep.dispatch_fwd(x.contiguous(), topk_e, topk_w, tables=tables)
         with stage("ep.experts"):
             h, gu = gg.gg_swiglu_fwd(st.xp, w_gu, st.group_off, status=ep.status)
             y = gg.gg_fwd(h, w_d, st.group_off, status=ep.status)
@@ -347,14 +355,16 @@ class _EPMoE(torch.autograd.Function):
             dx, dtopk_w = ep.combine_bwd_finish(st)
         ctx.st = None
         dres = dout if ctx.has_residual else None
-        return dx, dtopk_w, g_gu, g_d, None, None, None, dres
+        return dx, dtopk_w, g_gu, g_d, None, None, None, dres, None
 
 
-def ep_moe(x, topk_e, topk_w, w_gu, w_d, ep: ExpertParallel, grad_sink=None, residual=None):
+def ep_moe(x, topk_e, topk_w, w_gu, w_d, ep: ExpertParallel, grad_sink=None, residual=None, route=None):
     """Expert-parallel SwiGLU MoE: ``out[t] = residual[t] + sum_j w[t,j] * FFN_{e[t,j]}(x[t])``.
 
     ``w_gu [G, 2I, H]`` and ``w_d [G, H, I]`` hold this rank's ``G`` local experts.
     ``grad_sink(param, fp32_grad)``, when given, receives the expert weight gradients
-    (e.g. an optimizer applying them immediately) instead of autograd.
+    (e.g. an optimizer applying them immediately) instead of autograd. ``route``
+    optionally gives per-call ``(e2r, e2l)`` device tables (speculative replicas)
+    instead of the communicator's placement.
     """
-    return _EPMoE.apply(x, topk_w, w_gu, w_d, topk_e, ep, grad_sink, residual)
+    return _EPMoE.apply(x, topk_w, w_gu, w_d, topk_e, ep, grad_sink, residual, route)

@@ -362,16 +362,24 @@ def naive_combine_dispatch(tokens, weights, expert, route, E, group=None):
     return tokens.new_zeros(tokens.shape).index_add(0, tok[order], out * w)
 
 
-def dedup_combine_dispatch(tokens, weights, expert, route, E, group=None):
+def dedup_combine_dispatch(tokens, weights, expert, route, E, group=None, e2r=None):
     """Per-rank dedup: one row per (token, destination rank), weights applied at the
     expert rank and one partial per (token, rank) returned. This is the semantics of the
     fused sm_100a dispatch/combine kernels.
+
+    ``e2r`` ([E], optional) is this source rank's expert -> rank table (placement with
+    replicas, or a speculative replica cache: a replicated expert resolves to a local
+    copy); default: contiguous experts. ``expert(rows, ids)`` always receives global
+    expert ids, so any rank holding a copy computes the same function.
     """
     world = dist.get_world_size(group)
     epr = E // world
     T, k = route.shape
     dev = route.device
-    dst = torch.div(route, epr, rounding_mode="floor")  # [T, k]
+    if e2r is None:
+        dst = torch.div(route, epr, rounding_mode="floor")  # [T, k]
+    else:
+        dst = e2r.to(dev).long()[route]
     hot = torch.zeros(T, world, dtype=torch.bool, device=dev)
     hot.scatter_(1, dst, True)
     pairs = torch.nonzero(hot.T)  # (rank, token) sorted by rank then token
@@ -381,9 +389,10 @@ def dedup_combine_dispatch(tokens, weights, expert, route, E, group=None):
     s, r = send.tolist(), recv.tolist()
     rows = _all2all(tokens[d_tok], s, r, group)
     meta_e, _ = _a2a_raw(route[d_tok], s, r, group)  # [rows, k] experts of each row
+    meta_d, _ = _a2a_raw(dst[d_tok], s, r, group)    # [rows, k] rank the source chose for each
     meta_w = _all2all(weights[d_tok], s, r, group)
     me = dist.get_rank(group)
-    mine = torch.div(meta_e, epr, rounding_mode="floor") == me  # [rows, k]
+    mine = meta_d == me  # [rows, k]
     ri, rj = torch.nonzero(mine, as_tuple=True)
     y = expert(rows[ri], meta_e[ri, rj])
     part = rows.new_zeros(rows.shape).index_add(0, ri, y * meta_w[ri, rj].unsqueeze(-1).to(y.dtype))

@@ -129,3 +129,28 @@ def test_ds_style_initialize_on_hf_model():
     assert out.logits.shape == (1, 128, 4096)
     engine.ep.check()
     engine.ep.close()
+
+
+def test_sepx_placement_and_engine_options(tmp_path):
+    from spec_ep.integrations.ds_moe import _check_engine_options, load_config, plan_placement
+
+    with pytest.raises(ValueError, match="routing_dump"):
+        load_config({"expert_parallel": {"sepx": {"replicate_top_k": 4}}})
+    with pytest.raises(ValueError):
+        load_config({"expert_parallel": {"sepx": {"speculative_slots": -1}}})
+    for bad in ({"dispatch": "rbd"}, {"groups": 2}):
+        with pytest.raises(ValueError):
+            _check_engine_options(load_config({"expert_parallel": {"sepx": bad}}))
+    # a recorded routing dump ([L, T, K] int16 per rank) drives the placement planner
+    g = torch.Generator().manual_seed(0)
+    for r in range(2):
+        hot = torch.randint(0, 4, (3, 64, 2), generator=g)  # experts 0..3 dominate
+        cold = torch.randint(0, 16, (3, 16, 2), generator=g)
+        torch.save(torch.cat([hot, cold], 1).to(torch.int16), tmp_path / f"experts_rank{r}.pt")
+    cfg = load_config({"expert_parallel": {"sepx": {"routing_dump": str(tmp_path / "experts_rank*.pt"),
+                                                    "replicate_top_k": 2}}})
+    pl = plan_placement(cfg, 16, 4)
+    assert len(pl.replicated) == 2 and set(pl.replicated) <= {0, 1, 2, 3}
+    assert sorted(e for r in range(4) for e in pl.local_experts[r] if pl.owner[e] == r) == list(range(16))
+    flat = plan_placement(load_config({}), 16, 4)
+    assert flat.owner == [e // 4 for e in range(16)]

@@ -1,0 +1,224 @@
+"""Speculative expert replication (spec_ep.parallel.speculative): cache policy, routing.
+
+CPU tests check the LRU policy (the host reference) step by step and, on gloo ranks, that
+routing through a replica cache changes which rank computes an expert but not the MoE
+output, while sending fewer rows to other ranks. GPU tests compare the policy kernel with
+the host reference and check the replica fetch and the model plumbing.
+"""
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from spec_ep.parallel.placement import contiguous, plan_balanced
+from spec_ep.parallel.speculative import ReplicaCache, policy_reference
+
+
+def _cache(E=8, world=2, rank=0, S=2, min_count=1, placement=None):
+    return ReplicaCache(placement or contiguous(E, world), rank, S, min_count, device="cpu")
+
+
+def _pred(counts):
+    """[n, 1] expert ids with the given multiplicity per expert."""
+    ids = [e for e, c in counts.items() for _ in range(c)]
+    return torch.tensor(ids, dtype=torch.int32).view(-1, 1)
+
+
+def test_lru_policy_sequence():
+    c = _cache()  # rank 0 owns experts 0..3 (P = 4), two cache slots
+    c.plan_host(_pred({4: 5, 5: 3, 6: 1, 0: 9}))  # local expert 0 is never a candidate
+    assert c.slot_expert.tolist() == [4, 5]
+    assert c.fetch_rank.tolist() == [1, 1] and c.fetch_slot.tolist() == [0, 1]
+    assert c.e2r[4] == 0 and c.e2l[4] == 4 and c.e2r[5] == 0 and c.e2l[5] == 5
+    assert c.e2r[6] == 1 and c.e2l[6] == 2
+    c.plan_host(_pred({6: 4, 4: 2}))  # 4 hits, 5 is evicted for 6
+    assert c.slot_expert.tolist() == [4, 6]
+    assert c.fetch_rank.tolist() == [-1, 1] and c.fetch_slot.tolist() == [-1, 2]
+    assert c.e2r[5] == 1 and c.e2l[5] == 1  # evicted: back to its primary
+    c.plan_host(_pred({4: 3}))  # only 4 wanted; 6 stays cached and served locally
+    assert c.slot_expert.tolist() == [4, 6] and c.fetch_rank.tolist() == [-1, -1]
+    assert c.e2r[6] == 0 and c.e2l[6] == 5
+    assert c.slot_stamp.tolist() == [3, 2]
+    c.plan_host(_pred({7: 5, 5: 4}))  # no hits: the least recently used slot (6's) goes first
+    assert c.slot_expert.tolist() == [5, 7]
+    assert c.fetch_rank.tolist() == [1, 1] and c.fetch_slot.tolist() == [1, 3]
+    s = c.summary()
+    assert s["hits"] == 2 and s["fetches"] == 5
+
+
+def test_min_count_and_pinned_experts():
+    c = _cache(E=16, world=4, rank=1, S=4, min_count=3)  # rank 1 owns 4..7
+    c.plan_host(_pred({4: 50, 5: 50, 0: 2, 9: 3, 13: 7}))
+    cached = sorted(e for e in c.slot_expert.tolist() if e >= 0)
+    assert cached == [9, 13]  # 0 has too few rows; 4 and 5 are pinned here
+    for e in range(16):
+        if e in (9, 13):
+            assert int(c.e2r[e]) == 1 and int(c.e2l[e]) >= 4
+        else:
+            assert int(c.e2r[e]) == e // 4 and int(c.e2l[e]) == e % 4
+
+
+def test_static_replicas_are_pinned_and_not_cached():
+    load = torch.tensor([100., 90, 1, 1, 1, 1, 1, 1])
+    pl = plan_balanced(load, 2, replicate_top=2)  # experts 0 and 1 on both ranks
+    c = _cache(placement=pl, rank=1, S=2)
+    c.plan_host(_pred({0: 9, 1: 9, 2: 1, 3: 1}))
+    cached = [e for e in c.slot_expert.tolist() if e >= 0]
+    assert 0 not in cached and 1 not in cached
+    assert c.P == pl.slots(1)
+    # a fetched expert comes from its primary rank and the primary's slot
+    for s, e in enumerate(c.slot_expert.tolist()):
+        if e >= 0:
+            assert int(c.fetch_rank[s]) == pl.owner[e]
+            assert int(c.fetch_slot[s]) == pl.local_experts[pl.owner[e]].index(e)
+
+
+def test_policy_reference_is_deterministic_and_bounded():
+    g = torch.Generator().manual_seed(0)
+    pl = contiguous(64, 8)
+    base_r, base_l, _ = pl.tables(3)
+    owner = torch.tensor(pl.owner, dtype=torch.int32)
+    oslot = torch.tensor([pl.local_experts[pl.owner[e]].index(e) for e in range(64)], dtype=torch.int32)
+    se = torch.full((8,), -1, dtype=torch.int32)
+    ss = torch.full((8,), -1, dtype=torch.int32)
+    st = torch.zeros(1, dtype=torch.int32)
+    for _ in range(20):
+        pred = torch.randint(0, 64, (64, 4), generator=g, dtype=torch.int32)
+        e2r, e2l, fr, fs, stats = policy_reference(pred, 3, 8, 1, base_r, base_l, owner, oslot, se, ss, st)
+        live = [e for e in se.tolist() if e >= 0]
+        assert len(live) == len(set(live))  # an expert is cached at most once
+        assert all(pl.owner[e] != 3 for e in live)
+        assert stats[0] + stats[1] <= 8
+        for s in range(8):
+            if int(fr[s]) >= 0:
+                assert int(fr[s]) == pl.owner[int(se[s])] and int(fs[s]) == int(oslot[int(se[s])])
+        assert int((e2r == 3).sum()) == 8 + len(live)
+        assert stats[3] <= stats[2]
+
+
+# ---------------------------------------------------------------------------------------
+# gloo ranks: routing through each rank's cache preserves the MoE output
+# ---------------------------------------------------------------------------------------
+def _expert(rows, ids):
+    e = ids.to(rows.dtype).unsqueeze(-1)
+    return torch.tanh(rows * (e + 1) + e)
+
+
+def _spec_worker(rank, init_file, world):
+    from spec_ep.rbd import dedup_combine_dispatch, plan_traffic  # noqa: F401
+
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+    try:
+        E, k, T, H, S = 16, 4, 256, 8, 4
+        g = torch.Generator().manual_seed(100 + rank)
+        bias = -torch.arange(E, dtype=torch.float32) * 0.35  # Zipf-like skew toward low ids
+        logits = torch.randn(T, E, generator=g) + bias
+        w, route = torch.softmax(logits, -1).topk(k, -1)
+        w = w / w.sum(-1, keepdim=True)
+        x = torch.randn(T, H, generator=g)
+        # prediction: the true routing with a quarter of the choices replaced at random
+        pred = route.clone()
+        flip = torch.rand(route.shape, generator=g) < 0.25
+        pred[flip] = torch.randint(0, E, (int(flip.sum()),), generator=g)
+        cache = ReplicaCache(contiguous(E, world), rank, S, device="cpu")
+        cache.plan_host(pred.int())
+        base = dedup_combine_dispatch(x, w, _expert, route, E)
+        spec = dedup_combine_dispatch(x, w, _expert, route, E, e2r=cache.e2r)
+        torch.testing.assert_close(spec, base, rtol=1e-5, atol=1e-5)
+        epr = E // world
+        d_base = torch.div(route, epr, rounding_mode="floor")
+        d_spec = cache.e2r.long()[route]
+
+        def remote_rows(d):
+            hot = torch.zeros(T, world, dtype=torch.bool).scatter_(1, d, True)
+            return int(hot.sum() - hot[:, rank].sum())
+
+        assert remote_rows(d_spec) < remote_rows(d_base)
+        assert cache.summary()["local_share"] > 0.2
+    finally:
+        dist.destroy_process_group()
+
+
+def test_speculative_routing_preserves_output_gloo(tmp_path: Path):
+    mp.spawn(_spec_worker, args=(tmp_path / "init", 4), nprocs=4)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU
+# ---------------------------------------------------------------------------------------
+@pytest.mark.gpu
+def test_policy_kernel_matches_host_reference():
+    dev = torch.device("cuda", 0)
+    pl = plan_balanced(torch.rand(128, generator=torch.Generator().manual_seed(1)) * 100, 8, replicate_top=4)
+    gpu = ReplicaCache(pl, 3, 16, min_count=2, device=dev)
+    host = ReplicaCache(pl, 3, 16, min_count=2, device="cpu")
+    g = torch.Generator().manual_seed(2)
+    bias = torch.linspace(2.0, -2.0, 128)
+    for step in range(8):
+        logits = torch.randn(512, 128, generator=g) + bias[torch.randperm(128, generator=g)] * (step % 2)
+        pred = logits.topk(8, -1).indices.int()
+        gpu.update(pred.to(dev))
+        host.plan_host(pred)
+        torch.cuda.synchronize()
+        for name in ("slot_expert", "slot_stamp", "step", "e2r", "e2l", "fetch_rank", "fetch_slot", "stats"):
+            assert torch.equal(getattr(gpu, name).cpu(), getattr(host, name)), (step, name)
+
+
+@pytest.mark.gpu
+def test_fetch_kernel_copies_pinned_slots():
+    from spec_ep.ops._ext import load
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    P, S, a_bytes, b_bytes = 4, 3, 2 * 64 * 128 * 2, 128 * 64 * 2
+    off_b = (P + S) * a_bytes
+    buf = load().SymmBuffer(1, 0, off_b + (P + S) * b_bytes, 0)
+    raw = buf.local()
+    raw.copy_(torch.randint(0, 256, raw.shape, dtype=torch.uint8, device=dev))
+    before = raw.clone()
+    fr = torch.tensor([0, -1, 0], dtype=torch.int32, device=dev)
+    fs = torch.tensor([2, 1, 0], dtype=torch.int32, device=dev)
+    buf.fetch_experts(P, P, [0, off_b], [a_bytes, b_bytes], fr, fs, 2)
+    torch.cuda.synchronize()
+    A = raw[:off_b].view(P + S, a_bytes)
+    B = raw[off_b:].view(P + S, b_bytes)
+    A0 = before[:off_b].view(P + S, a_bytes)
+    B0 = before[off_b:].view(P + S, b_bytes)
+    assert torch.equal(A[P + 0], A0[2]) and torch.equal(B[P + 0], B0[2])
+    assert torch.equal(A[P + 1], A0[P + 1]) and torch.equal(B[P + 1], B0[P + 1])  # no fetch requested
+    assert torch.equal(A[P + 2], A0[0]) and torch.equal(B[P + 2], B0[0])
+    assert torch.equal(A[:P], A0[:P]) and torch.equal(B[:P], B0[:P])  # pinned slots untouched
+    buf.close()
+
+
+@pytest.mark.gpu
+@torch.no_grad()
+def test_model_with_speculation_matches_plain_forward_one_gpu():
+    """One GPU holds every expert, so the cache never fetches: the speculative path
+    (prediction on a side stream, per-call tables, widened receive layout) must give
+    exactly the plain forward's logits."""
+    from spec_ep.models.config import get_config
+    from spec_ep.models.qwen3_moe import Qwen3MoeForCausalLM
+    from spec_ep.parallel.ep import ExpertParallel
+    from spec_ep.parallel.speculative import enable_speculation, speculation_summary
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = get_config("tiny")
+    T = 256
+    ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=T, device=dev)
+    torch.manual_seed(0)
+    model = Qwen3MoeForCausalLM(cfg, ep, device=dev)
+    ids = torch.randint(0, cfg.vocab_size, (1, T), device=dev)
+    ref = model(ids).float()
+    specs = enable_speculation(model, num_slots=2)
+    out = model(ids).float()
+    torch.cuda.synchronize()
+    ep.check()
+    assert torch.equal(out, ref)
+    s = speculation_summary(model)
+    assert s["fetches"] == 0 and s["predicted_remote_rows"] == 0
+    for sp in specs:
+        sp.close()
