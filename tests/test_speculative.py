@@ -222,3 +222,79 @@ def test_model_with_speculation_matches_plain_forward_one_gpu():
     assert s["fetches"] == 0 and s["predicted_remote_rows"] == 0
     for sp in specs:
         sp.close()
+
+
+def _free_port():
+    import socket
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def _multi_gpu_worker(rank, world, port, errq):
+    import os
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        from spec_ep.models.config import get_config
+        from spec_ep.models.qwen3_moe import Qwen3MoeForCausalLM
+        from spec_ep.parallel.ep import ExpertParallel
+        from spec_ep.parallel.speculative import enable_speculation, speculation_summary
+
+        cfg = get_config("tiny", num_experts=16, top_k=4)
+        T, S = 512, 3
+        ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=T, device=dev)
+        torch.manual_seed(0)  # same dense weights on every rank
+        model = Qwen3MoeForCausalLM(cfg, ep, device=dev)
+        torch.manual_seed(100 + rank)  # different experts per rank
+        with torch.no_grad():
+            for layer in model.layers:
+                layer.w_gu.normal_(0.0, 0.02)
+                layer.w_d.normal_(0.0, 0.02)
+                layer.router_bias = torch.linspace(1.5, -1.5, cfg.num_experts, device=dev)  # skewed popularity
+        ids = torch.randint(0, cfg.vocab_size, (1, T), device=dev,
+                            generator=torch.Generator(device=dev).manual_seed(7 + rank))
+        with torch.no_grad():
+            ref = model.hidden_states(ids).float()
+            full_gu = [torch.empty_like(model.layers[0].w_gu) for _ in range(world)]
+            specs = enable_speculation(model, num_slots=S)
+            for _ in range(2):  # second call: cache hits
+                out = model.hidden_states(ids).float()
+            torch.cuda.synchronize()
+        ep.check()
+        rel = ((out - ref).abs().max() / ref.abs().max()).item()
+        assert rel < 2e-2, rel
+        summ = speculation_summary(model)
+        assert summ["fetches"] > 0 and summ["hits"] > 0, summ
+        # every cached replica holds its primary's weights, bit for bit
+        for layer, sp in zip(model.layers, specs):
+            dist.all_gather(full_gu, layer.w_gu.data.contiguous())
+            for s, e in enumerate(sp.cache.slot_expert.tolist()):
+                if e >= 0:
+                    owner = int(sp.cache.owner[e])
+                    assert torch.equal(sp.w_gu[sp.P + s], full_gu[owner][int(sp.cache.owner_slot[e])])
+        dist.barrier()
+        for sp in specs:
+            sp.close()
+        ep.close()
+        dist.destroy_process_group()
+    except Exception:  # report to the parent, never hang it
+        import traceback
+
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+@pytest.mark.gpu
+def test_speculative_model_two_gpus_fetches_replicas_and_matches_plain():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.spawn(_multi_gpu_worker, args=(2, _free_port(), errq), nprocs=2, join=True)
+    assert errq.empty()
