@@ -11,6 +11,10 @@ every rank a disjoint ``seq_len`` slice of token ids, and runs the requested mod
   comm      per-op device time / bytes of the EP dispatch+combine (max over ranks)
   train     timed training steps (forward + backward + AdamW)
 
+``--speculative-slots N`` turns on speculative expert replication (an LRU cache of N
+predicted-hot experts per layer and rank; inference modes only) and prints the cache
+statistics at the end.
+
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 examples/ds_moe.py \
         --config-pth configs/qwen3_30b_a3b_ep8_sepx.json --modes latency flops routing
 """
@@ -67,12 +71,17 @@ def main():
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--modes", nargs="+", default=["latency", "flops"])
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--speculative-slots", type=int, default=0)
     args, _ = ap.parse_known_args()  # launchers may inject --local_rank
     rank, world, dev = init_distributed()
     logs = Path(os.environ.get("LOGS", f"logs/{time.strftime('%Y-%m-%d_%H-%M-%S')}"))
     logs.mkdir(parents=True, exist_ok=True)
     cfg = json.load(open(args.config_pth))
     cfg["expert_parallel"]["autoep_size"] = min(cfg["expert_parallel"].get("autoep_size", world), world)
+    if args.speculative_slots:
+        cfg["expert_parallel"].setdefault("sepx", {})["speculative_slots"] = args.speculative_slots
+        if "train" in args.modes:
+            raise SystemExit("speculative replication is inference-only: drop the train mode")
     from spec_ep.models import config as mc
 
     if args.layers:
@@ -120,6 +129,10 @@ def main():
         ms, loss = timed(lambda: [engine.train_step(ids, labels, args.seq_len - 1) for _ in range(args.steps)][-1], dev)
         print0(f"train step {ms / args.steps:.1f} ms, {world * args.seq_len / (ms / args.steps / 1e3):.0f} tokens/s, "
                f"loss {float(loss):.3f}")
+    if args.speculative_slots:
+        from spec_ep.parallel.speculative import speculation_summary
+
+        print0(f"speculative replication: {speculation_summary(engine.module)}")
     report_peak_mem(dev)
     engine.ep.close()
     shutdown_comm()
