@@ -100,4 +100,7 @@ struct SpecFetchArgs {
 };
 void spec_fetch(const SpecFetchArgs& a, int blocks_per_slot, cudaStream_t st);
 
+// Device timeline (trace.cu): ring[2 i] = tag, ring[2 i + 1] = %globaltimer ns.
+void trace_stamp(unsigned long long* ring, unsigned int* counter, int cap, int tag, cudaStream_t st);
+
 }  // namespace sepx

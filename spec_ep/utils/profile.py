@@ -189,13 +189,26 @@ def enable_stage_ranges(on: bool = True):
 
 @contextlib.contextmanager
 def stage(name: str):
-    """NVTX range + torch.profiler label around one stage (no-op unless enabled)."""
-    if not _STAGE_RANGES:
+    """NVTX range + torch.profiler label around one stage, and device timestamps when a
+    :class:`spec_ep.utils.trace.DeviceTimeline` is enabled (no-op otherwise)."""
+    from .trace import active_timeline
+
+    tl = active_timeline()
+    if not _STAGE_RANGES and tl is None:
         yield
         return
-    torch.cuda.nvtx.range_push(name)
+    if tl is not None:
+        tl.mark(name + ":begin")
+    if _STAGE_RANGES:
+        torch.cuda.nvtx.range_push(name)
     try:
-        with record_function(name):
+        if _STAGE_RANGES:
+            with record_function(name):
+                yield
+        else:
             yield
     finally:
-        torch.cuda.nvtx.range_pop()
+        if _STAGE_RANGES:
+            torch.cuda.nvtx.range_pop()
+        if tl is not None:
+            tl.mark(name + ":end")
