@@ -56,3 +56,31 @@ def test_imbalance_metric():
 
     assert abs(imbalance(torch.tensor([10, 10, 10, 10])) - 1.0) < 1e-6
     assert abs(imbalance(torch.tensor([40, 0, 0, 0])) - 4.0) < 1e-6
+
+
+def test_expert_transfer_group_splits():
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("expert_transfer", os.path.join(root, "benchmarks",
+                                                                                  "expert_transfer.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    numel, world, gs = 6 * 64, 8, 4
+    for balance in ("even", "uneven_internode", "uneven_intranode"):
+        if balance == "uneven_internode":
+            gs_b = 2  # four groups
+        else:
+            gs_b = gs
+        sends, recvs = zip(*(mod.group_splits(numel, r, world, gs_b, balance, 0.5) for r in range(world)))
+        for r in range(world):
+            assert all(sends[r][d] == 0 for d in range(world) if d // gs_b == r // gs_b)  # nothing in-group
+            for d in range(world):
+                assert sends[r][d] == recvs[d][r]  # what r sends to d is what d expects from r
+        if balance == "even":
+            assert all(sum(s) == numel for s in sends)
+        else:
+            totals = sorted(sum(s) for s in sends)
+            assert totals[0] == numel * 0.5 and totals[-1] == numel * 1.5
+            assert sum(totals) == numel * world
