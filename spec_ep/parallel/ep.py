@@ -136,6 +136,36 @@ class ExpertParallel:
         self.fp8_dispatch = bool(fp8_dispatch)
         if self.fp8_dispatch and hidden % 128:
             raise ValueError("fp8 dispatch needs hidden % 128 == 0")
+        self.stats_on = False  # traffic statistics of forward dispatches (enable_stats)
+        self._reset_stats()
+
+    # -------------------------------------------------------------------------------
+    def _reset_stats(self):
+        self.stat_sent = torch.zeros(self.world, dtype=torch.int64, device=self.device)
+        self.stat_copies = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.stat_tokens = 0
+        self.stat_recv_rows: list[int] = []
+
+    def enable_stats(self, on: bool = True):
+        """Accumulate forward-dispatch traffic on the device (two small reductions per
+        layer call while on): rows sent per destination, remote (token, expert) copies,
+        tokens, and the received row counts the host already reads."""
+        self.stats_on = bool(on)
+
+    def take_stats(self) -> dict:
+        """Per-token traffic since the last call, then reset: ``remote_rows_per_token``
+        (one row per (token, other rank), what the kernels send), ``naive_rows_per_token``
+        (one row per remote (token, expert) copy, a plain all-to-all), and the mean
+        received rows per layer call on this rank."""
+        sent = self.stat_sent.tolist()
+        copies = int(self.stat_copies.item())
+        T = max(self.stat_tokens, 1)
+        remote = sum(sent) - sent[self.rank]
+        recv = self.stat_recv_rows
+        out = {"remote_rows_per_token": remote / T, "naive_rows_per_token": copies / T,
+               "recv_rows_per_call": (sum(recv) / len(recv)) if recv else 0.0, "tokens": self.stat_tokens}
+        self._reset_stats()
+        return out
 
     # -------------------------------------------------------------------------------
     def check(self):
@@ -228,6 +258,12 @@ class ExpertParallel:
         else:
             R = max(int(group_off[G].item()), 1)
             self.rows_last = R
+        if self.stats_on:
+            self.stat_sent += send_count
+            self.stat_copies += ((dst_tk >= 0) & (dst_tk != self.rank)).sum()
+            self.stat_tokens += T
+            if not static_rows:
+                self.stat_recv_rows.append(R)
         xp = torch.empty(R, self.H, dtype=torch.bfloat16, device=dev)
         row_w = torch.empty(R, dtype=torch.float32, device=dev)
         row_src = torch.empty(R, dtype=torch.int32, device=dev)
