@@ -18,10 +18,10 @@
 //     rank's symmetric buffer (plain 16-byte peer loads over NVLink, no TMA) into the
 //     cache slots.
 //
-// Everything stays on the device (no host sync), so a layer with speculation can be
-// captured in a CUDA graph; the only state is the cache map, its LRU stamps and a step
-// counter, all device tensors. Replica slots are only ever read by this rank, primaries
-// only ever written at load time, so a fetch needs no cross-rank synchronisation.
+// Everything stays on the device (no host sync); the only state is the cache map, its
+// LRU stamps and a step counter, all device tensors. Replica slots are only ever read by
+// this rank, primaries only ever written at load time, so a fetch needs no cross-rank
+// synchronisation.
 #include <cuda_runtime.h>
 
 #include <stdexcept>
