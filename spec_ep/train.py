@@ -6,6 +6,9 @@
 * Dense weights (attention, router, norms, embeddings) are replicated on every rank;
   their gradients are all-reduced (NCCL, bucketed) over the data-parallel group, which
   for pure EP is every rank.
+* Expert replicas inside the EP group (a planned placement that copies hot experts to
+  every rank) each see only the tokens routed to their copy; their gradients are summed
+  over the EP group before the update, so every copy takes the same step.
 * Expert replicas across DP groups (EP < world) are all-reduced over the replica group
   before their in-backward update.
 * Optimizer state precision is chosen per parameter group to fit the memory budget:
@@ -163,6 +166,27 @@ class _GradBuckets:
         self.active = False
 
 
+def replica_slots(placement, rank: int) -> list[int]:
+    """Local slots of the placement's replicated experts on ``rank``, in expert-id order
+    (every rank holds every replicated expert, primary or copy)."""
+    if placement is None or not placement.replicated:
+        return []
+    return [placement.slot_of(rank, e) for e in sorted(placement.replicated)]
+
+
+def sum_replica_grads(g: torch.Tensor, slots: list[int], group=None):
+    """Sum the gradient rows of replicated experts (``g`` is ``[local slots, ...]``) over
+    ``group`` in place: each copy's gradient covers only the tokens it served, the
+    expert's gradient is their sum."""
+    if not slots or not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
+        return g
+    idx = torch.tensor(slots, dtype=torch.long, device=g.device)
+    rows = g.index_select(0, idx)
+    dist.all_reduce(rows, group=group)
+    g.index_copy_(0, idx, rows)
+    return g
+
+
 class _ExpertUpdater:
     """Receives expert weight gradients inside the MoE backward.
 
@@ -176,11 +200,16 @@ class _ExpertUpdater:
 
     def __init__(self, trainer):
         self.t = trainer
-        use = trainer.fuse_expert_optimizer and trainer.expert_world == 1
+        ep = getattr(trainer.model, "ep", None)
+        self.rep_slots = replica_slots(getattr(ep, "placement", None), ep.rank) if ep is not None else []
+        self.ep_group = ep.group if ep is not None else None
+        use = trainer.fuse_expert_optimizer and trainer.expert_world == 1 and not self.rep_slots
         self.fused_wgrad = trainer.opt.fused_wgrad if use else None
 
     def __call__(self, p, g):
         t = self.t
+        if self.rep_slots:
+            sum_replica_grads(g, self.rep_slots, self.ep_group)
         if t.expert_world > 1:
             dist.all_reduce(g, group=t.expert_dp_group)
             g.mul_(1.0 / t.expert_world)

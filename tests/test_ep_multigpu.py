@@ -342,3 +342,69 @@ def test_ep_layers_cuda_graph_across_gpus():
     errq = ctx.SimpleQueue()
     mp.spawn(_graph_worker, args=(world, _free_port(), errq), nprocs=world, join=True)
     assert errq.empty()
+
+
+def _replica_train_worker(rank, world, port, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        from spec_ep.models.config import get_config
+        from spec_ep.models.qwen3_moe import Qwen3MoeForCausalLM
+        from spec_ep.parallel.ep import ExpertParallel
+        from spec_ep.parallel.placement import plan_balanced
+        from spec_ep.train import Trainer
+
+        cfg = get_config("tiny", num_experts=8, top_k=2)
+        T = 256
+        load = torch.tensor([40., 30, 5, 4, 3, 2, 1, 1])
+        pl = plan_balanced(load, world, replicate_top=2)
+        ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=T, device=dev, placement=pl)
+        torch.manual_seed(0)
+        model = Qwen3MoeForCausalLM(cfg, ep, device=dev)
+        g = torch.Generator().manual_seed(1)
+        I, H = cfg.moe_intermediate_size, cfg.hidden_size
+        full_gu = (torch.randn(cfg.num_experts, 2 * I, H, generator=g) * 0.02).bfloat16()
+        full_d = (torch.randn(cfg.num_experts, H, I, generator=g) * 0.02).bfloat16()
+        mine = pl.local_experts[rank]
+        with torch.no_grad():
+            for layer in model.layers:
+                layer.w_gu.copy_(full_gu[mine].to(dev))
+                layer.w_d.copy_(full_d[mine].to(dev))
+                layer.router_bias = torch.linspace(1.0, -1.0, cfg.num_experts, device=dev)
+        trainer = Trainer(model, lr=1e-2, expert_state="fp32")
+        ids = torch.randint(0, cfg.vocab_size, (1, T), device=dev,
+                            generator=torch.Generator(device=dev).manual_seed(10 + rank))
+        labels = torch.cat([ids[:, 1:], torch.full((1, 1), -1, device=dev)], 1).int()
+        for _ in range(2):
+            trainer.train_step(ids, labels, T - 1)
+        torch.cuda.synchronize()
+        ep.check()
+        reps = sorted(pl.replicated)
+        for layer in model.layers:
+            for p, full in ((layer.w_gu, full_gu), (layer.w_d, full_d)):
+                rows = torch.stack([p.detach()[pl.slot_of(rank, e)] for e in reps]).contiguous()
+                got = [torch.empty_like(rows) for _ in range(world)]
+                dist.all_gather(got, rows)
+                for other in got[1:]:
+                    assert torch.equal(other, got[0])  # every copy took the same step
+                assert not torch.equal(rows.cpu(), full[reps])  # and the step moved them
+        dist.barrier()
+        ep.close()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+def test_replicated_experts_stay_identical_through_training():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.spawn(_replica_train_worker, args=(2, _free_port(), errq), nprocs=2, join=True)
+    assert errq.empty()

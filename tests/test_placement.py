@@ -80,3 +80,43 @@ def _reshard_worker(rank, world, init_file):
 
 def test_reshard_moves_weights(tmp_path: Path):
     mp.spawn(_reshard_worker, args=(4, tmp_path / "init"), nprocs=4)
+
+
+def _replica_grad_worker(rank, port, out):
+    import torch.distributed as dist
+
+    from spec_ep.parallel.placement import plan_balanced
+    from spec_ep.train import replica_slots, sum_replica_grads
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2)
+    try:
+        load = torch.tensor([50., 40, 3, 3, 2, 2, 1, 1])
+        pl = plan_balanced(load, 2, replicate_top=2)
+        slots = replica_slots(pl, rank)
+        assert [pl.local_experts[rank][s] for s in slots] == sorted(pl.replicated)
+        g = torch.full((pl.slots(rank), 3), float(rank + 1))
+        for i, e in enumerate(pl.local_experts[rank]):
+            g[i] *= e + 1
+        before = g.clone()
+        sum_replica_grads(g, slots)
+        for i, e in enumerate(pl.local_experts[rank]):
+            if e in pl.replicated:  # (1 + 2) * (e + 1): both copies' rows summed
+                assert torch.equal(g[i], torch.full((3,), 3.0 * (e + 1)))
+            else:
+                assert torch.equal(g[i], before[i])
+        out[rank] = True
+    finally:
+        dist.destroy_process_group()
+
+
+def test_replicated_expert_gradients_are_summed_over_holders():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    out = mp.Manager().dict()
+    mp.spawn(_replica_grad_worker, args=(port, out), nprocs=2, join=True)
+    assert out.get(0) and out.get(1)
