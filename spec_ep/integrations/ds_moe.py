@@ -19,7 +19,8 @@ across them; dense weights are data-parallel over every rank.
 
 ``sepx`` keys: ``fp8`` sends forward rows as e4m3 with 1x128 scales; ``routing_dump``
 (a glob or list of ``experts_rank*.pt`` files) plans a load-balanced placement from
-recorded routing, with ``replicate_top_k`` hot experts on every rank; ``speculative_slots``
+recorded routing, with ``replicate_top_k`` hot experts copied to every rank, or to
+``replica_copies`` ranks each; ``speculative_slots``
 > 0 turns on speculative replication (an LRU cache of that many predicted-hot experts
 per layer and rank; inference only). ``dispatch`` must be ``"p2p"`` for the model engine
 (``"rbd"`` names the torch reference, ``spec_ep.rbd.RBD_combine_dispatch``, which is an
@@ -42,7 +43,8 @@ class SepxOptions:
     dispatch: str = "p2p"          # "p2p" (fused NVLink kernels) | "rbd" (torch RBD over NCCL)
     groups: int = 1                # logical GPU groups for the two-stage path
     fp8: bool = False              # e4m3 1x128 dispatch payload (forward only)
-    replicate_top_k: int = 0       # hot experts replicated on every rank (needs routing_dump)
+    replicate_top_k: int = 0       # hot experts replicated (needs routing_dump)
+    replica_copies: int = 0        # ranks holding each replicated expert (0: every rank)
     routing_dump: object = None    # glob / list of experts_rank*.pt files for the placement planner
     speculative_slots: int = 0     # LRU replica cache slots per layer and rank (inference)
     speculative_min_count: int = 1  # fewest predicted rows that make an expert worth fetching
@@ -79,7 +81,7 @@ def load_config(cfg) -> EPConfig:
     if not out.use_grouped_mm:
         raise ValueError("use_grouped_mm=false is not supported: experts always run as grouped GEMMs")
     sx = out.sepx
-    if int(sx.groups) < 1 or int(sx.replicate_top_k) < 0 or int(sx.speculative_slots) < 0 or \
+    if int(sx.groups) < 1 or int(sx.replicate_top_k) < 0 or int(sx.replica_copies) < 0 or int(sx.speculative_slots) < 0 or \
             int(sx.speculative_min_count) < 1 or int(sx.timeout_us) <= 0:
         raise ValueError("expert_parallel.sepx: groups >= 1, replicate_top_k >= 0, speculative_slots >= 0, "
                          "speculative_min_count >= 1 and timeout_us > 0 are required")
@@ -103,7 +105,8 @@ def plan_placement(cfg: EPConfig, num_experts: int, world: int):
     if not files:
         raise FileNotFoundError(f"sepx.routing_dump matches no files: {dump!r}")
     loads = loads_from_routing(load_routing(files), num_experts).sum(0)
-    return plan_balanced(loads, world, int(cfg.sepx.replicate_top_k))
+    copies = int(cfg.sepx.replica_copies) or None
+    return plan_balanced(loads, world, int(cfg.sepx.replicate_top_k), copies)
 
 
 def _check_engine_options(cfg: EPConfig):

@@ -7,8 +7,12 @@ host planner whose output drives the dispatch kernels directly:
 * Every expert has exactly one *primary* rank (so every expert exists somewhere).
 * ``plan_balanced`` assigns primaries by greedy longest-processing-time bin packing of
   the measured per-expert loads, ``E / world`` slots per rank.
-* ``replicate_top`` hot experts additionally get a *replica* slot on every rank; a token
-  routed to a replicated expert is served by its own rank's copy (no transfer at all).
+* ``replicate_top`` hot experts additionally get *replica* slots: on every rank by
+  default (a token routed to a replicated expert is then served by its own rank's copy,
+  no transfer at all), or with ``copies=c`` on ``c`` ranks only (the primary plus the
+  ``c - 1`` least-loaded ranks). A source without a copy sends to one holder; the
+  sources without a copy are dealt round-robin over the holders, so each holder serves
+  an equal share of them.
 * ``Placement.tables(rank)`` returns the per-rank ``(e2r, e2l)`` lookup tables the
   dispatch kernel uses: destination rank and local slot for each expert, as seen from
   that source rank.
@@ -29,9 +33,29 @@ class Placement:
     world: int
     owner: list[int]                      # primary rank of each expert
     local_experts: list[list[int]]        # per rank: global expert id of each local slot
-    replicated: list[int] = field(default_factory=list)  # experts with a copy on every rank
+    replicated: list[int] = field(default_factory=list)  # experts with more than one copy
+    holders: dict[int, list[int]] | None = None  # ranks holding each replicated expert (None: every rank)
 
     # -----------------------------------------------------------------------------
+    def holders_of(self, expert: int) -> list[int]:
+        """Ranks holding a copy of ``expert`` (ascending)."""
+        if expert not in self.replicated:
+            return [self.owner[expert]]
+        if self.holders is None or expert not in self.holders:
+            return list(range(self.world))
+        return sorted(self.holders[expert])
+
+    def serving_rank(self, source: int, expert: int) -> int:
+        """Rank whose copy of ``expert`` serves tokens of ``source``: its own copy if it
+        holds one, else the holders in turn over the sources without a copy."""
+        hs = self.holders_of(expert)
+        if source in hs:
+            return source
+        if len(hs) == 1:
+            return hs[0]
+        others = [r for r in range(self.world) if r not in hs]
+        return hs[others.index(source) % len(hs)]
+
     def slots(self, rank: int) -> int:
         return len(self.local_experts[rank])
 
@@ -44,19 +68,16 @@ class Placement:
     def tables(self, rank: int) -> tuple[torch.Tensor, torch.Tensor, list[int]]:
         """(e2r, e2l, experts_per_rank) seen from source ``rank``.
 
-        A replicated expert resolves to this rank's own copy; any other expert to its
-        primary rank and the primary's slot.
+        A replicated expert resolves to this rank's own copy when it holds one, else to
+        ``serving_rank``; any other expert to its primary rank and the primary's slot.
         """
         E = self.num_experts
         e2r = torch.empty(E, dtype=torch.int32)
         e2l = torch.empty(E, dtype=torch.int32)
-        mine = {e: i for i, e in enumerate(self.local_experts[rank])}
+        rep = set(self.replicated)
         for e in range(E):
-            if e in mine and (e in self.replicated or self.owner[e] == rank):
-                e2r[e], e2l[e] = rank, mine[e]
-            else:
-                o = self.owner[e]
-                e2r[e], e2l[e] = o, self.local_experts[o].index(e)
+            d = self.serving_rank(rank, e) if e in rep else self.owner[e]
+            e2r[e], e2l[e] = d, self.local_experts[d].index(e)
         return e2r, e2l, self.per_rank()
 
     def expected_rows(self, load: torch.Tensor, source_share: torch.Tensor | None = None) -> torch.Tensor:
@@ -69,9 +90,11 @@ class Placement:
         share = source_share.double() if source_share is not None else torch.full((self.world,), 1.0 / self.world,
                                                                                  dtype=torch.float64)
         rows = torch.zeros(self.world, dtype=torch.float64)
+        rep = set(self.replicated)
         for e in range(self.num_experts):
-            if e in self.replicated:
-                rows += load[e] * share
+            if e in rep:
+                for src in range(self.world):
+                    rows[self.serving_rank(src, e)] += load[e] * share[src]
             else:
                 rows[self.owner[e]] += load[e]
         return rows
@@ -81,13 +104,19 @@ class Placement:
         return float(rows.max() / rows.mean().clamp_min(1e-9))
 
     def to_dict(self) -> dict:
-        return {"num_experts": self.num_experts, "world": self.world, "owner": list(self.owner),
-                "local_experts": [list(x) for x in self.local_experts], "replicated": list(self.replicated)}
+        d = {"num_experts": self.num_experts, "world": self.world, "owner": list(self.owner),
+             "local_experts": [list(x) for x in self.local_experts], "replicated": list(self.replicated)}
+        if self.holders is not None:
+            d["holders"] = {str(e): list(h) for e, h in self.holders.items()}
+        return d
 
     @staticmethod
     def from_dict(d: dict) -> "Placement":
+        holders = d.get("holders")
+        if holders is not None:
+            holders = {int(e): list(h) for e, h in holders.items()}
         return Placement(d["num_experts"], d["world"], list(d["owner"]), [list(x) for x in d["local_experts"]],
-                         list(d.get("replicated", [])))
+                         list(d.get("replicated", [])), holders)
 
 
 def contiguous(num_experts: int, world: int) -> Placement:
@@ -99,9 +128,10 @@ def contiguous(num_experts: int, world: int) -> Placement:
     return Placement(num_experts, world, owner, [list(range(r * epr, (r + 1) * epr)) for r in range(world)])
 
 
-def plan_balanced(load: torch.Tensor, world: int, replicate_top: int = 0) -> Placement:
+def plan_balanced(load: torch.Tensor, world: int, replicate_top: int = 0, copies: int | None = None) -> Placement:
     """Greedy LPT packing of per-expert ``load`` onto ranks with E / world primary slots each,
-    plus a replica of the ``replicate_top`` most loaded experts on every rank.
+    plus replicas of the ``replicate_top`` most loaded experts: on every rank, or with
+    ``copies`` < world on that many ranks (see :func:`_partial_holders`).
 
     Replicated experts' load is spread evenly across ranks before packing the rest, since
     each source serves them locally; their primary copies are dealt round-robin so every
@@ -110,6 +140,10 @@ def plan_balanced(load: torch.Tensor, world: int, replicate_top: int = 0) -> Pla
     E = load.numel()
     if E % world:
         raise ValueError(f"{E} experts do not split over {world} ranks")
+    if copies is not None and copies < world:
+        if copies < 1:
+            raise ValueError("copies must be at least 1")
+        return _partial_holders(plan_balanced(load, world, 0), load, replicate_top, copies)
     cap = E // world
     load = load.double().cpu()
     order = torch.argsort(load, descending=True).tolist()
@@ -148,6 +182,29 @@ def plan_balanced(load: torch.Tensor, world: int, replicate_top: int = 0) -> Pla
     return Placement(E, world, owner, local, replicated)
 
 
+def _partial_holders(base: Placement, load: torch.Tensor, replicate_top: int, copies: int) -> Placement:
+    """Add ``copies - 1`` replicas of each of the ``replicate_top`` hottest experts to
+    ``base`` (primaries unchanged). Experts are taken hottest first; each replica goes to
+    the rank with the least expected rows at that point (ties: lowest rank), and the
+    expected rows are recomputed with the expert's load split over its holders."""
+    load = load.double().cpu()
+    order = torch.argsort(load, descending=True).tolist()[:replicate_top]
+    pl = Placement(base.num_experts, base.world, list(base.owner), [list(x) for x in base.local_experts], [], {})
+    for e in order:
+        hs = [pl.owner[e]]
+        pl.replicated.append(e)
+        pl.holders[e] = hs
+        for _ in range(copies - 1):
+            rows = pl.expected_rows(load)
+            cand = [r for r in range(pl.world) if r not in hs]
+            r = min(cand, key=lambda x: (float(rows[x]), x))
+            hs.append(r)
+            hs.sort()
+            pl.local_experts[r].append(e)
+    pl.replicated.sort()
+    return pl
+
+
 def loads_from_routing(route: torch.Tensor, num_experts: int) -> torch.Tensor:
     """Per-layer expert loads from a ``[L, T, K]`` routing dump -> ``[L, E]``."""
     if route.dim() != 3:
@@ -158,9 +215,10 @@ def loads_from_routing(route: torch.Tensor, num_experts: int) -> torch.Tensor:
     return torch.stack([torch.bincount(route[l].reshape(-1).long(), minlength=num_experts) for l in range(L)])
 
 
-def plan_from_routing(route: torch.Tensor, num_experts: int, world: int, replicate_top: int = 0) -> list[Placement]:
+def plan_from_routing(route: torch.Tensor, num_experts: int, world: int, replicate_top: int = 0,
+                      copies: int | None = None) -> list[Placement]:
     """One placement per layer from recorded routing (the experts_rank*.pt format)."""
-    return [plan_balanced(l, world, replicate_top) for l in loads_from_routing(route, num_experts)]
+    return [plan_balanced(l, world, replicate_top, copies) for l in loads_from_routing(route, num_experts)]
 
 
 # ---------------------------------------------------------------------------------------

@@ -167,23 +167,30 @@ class _GradBuckets:
 
 
 def replica_slots(placement, rank: int) -> list[int]:
-    """Local slots of the placement's replicated experts on ``rank``, in expert-id order
-    (every rank holds every replicated expert, primary or copy)."""
+    """For each replicated expert of the placement (expert-id order), its local slot on
+    ``rank``, or -1 where ``rank`` holds no copy (partial replication)."""
     if placement is None or not placement.replicated:
         return []
-    return [placement.slot_of(rank, e) for e in sorted(placement.replicated)]
+    return [placement.slot_of(rank, e) if rank in placement.holders_of(e) else -1
+            for e in sorted(placement.replicated)]
 
 
 def sum_replica_grads(g: torch.Tensor, slots: list[int], group=None):
     """Sum the gradient rows of replicated experts (``g`` is ``[local slots, ...]``) over
     ``group`` in place: each copy's gradient covers only the tokens it served, the
-    expert's gradient is their sum."""
+    expert's gradient is their sum. Every rank of ``group`` calls it with one entry per
+    replicated expert (-1: no copy here, contributes zeros)."""
     if not slots or not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
         return g
-    idx = torch.tensor(slots, dtype=torch.long, device=g.device)
-    rows = g.index_select(0, idx)
+    held = [i for i, s in enumerate(slots) if s >= 0]
+    rows = g.new_zeros((len(slots),) + tuple(g.shape[1:]))
+    if held:
+        at = torch.tensor(held, dtype=torch.long, device=g.device)
+        src = torch.tensor([slots[i] for i in held], dtype=torch.long, device=g.device)
+        rows.index_copy_(0, at, g.index_select(0, src))
     dist.all_reduce(rows, group=group)
-    g.index_copy_(0, idx, rows)
+    if held:
+        g.index_copy_(0, src, rows.index_select(0, at))
     return g
 
 

@@ -152,5 +152,8 @@ def test_sepx_placement_and_engine_options(tmp_path):
     pl = plan_placement(cfg, 16, 4)
     assert len(pl.replicated) == 2 and set(pl.replicated) <= {0, 1, 2, 3}
     assert sorted(e for r in range(4) for e in pl.local_experts[r] if pl.owner[e] == r) == list(range(16))
+    part = plan_placement(load_config({"expert_parallel": {"sepx": {
+        "routing_dump": str(tmp_path / "experts_rank*.pt"), "replicate_top_k": 2, "replica_copies": 2}}}), 16, 4)
+    assert all(len(part.holders_of(e)) == 2 for e in part.replicated)
     flat = plan_placement(load_config({}), 16, 4)
     assert flat.owner == [e // 4 for e in range(16)]

@@ -120,3 +120,79 @@ def test_replicated_expert_gradients_are_summed_over_holders():
     out = mp.Manager().dict()
     mp.spawn(_replica_grad_worker, args=(port, out), nprocs=2, join=True)
     assert out.get(0) and out.get(1)
+
+
+def test_partial_replication_holders_tables_and_balance():
+    g = torch.Generator().manual_seed(4)
+    load = (torch.rand(16, generator=g) * 10) + torch.tensor([80.0, 60, 40] + [0.0] * 13)
+    W = 4
+    pl = plan_balanced(load, W, replicate_top=3, copies=2)
+    assert sorted(pl.replicated) == [0, 1, 2]
+    for e in range(16):
+        hs = pl.holders_of(e)
+        assert pl.owner[e] in hs and len(hs) == (2 if e in pl.replicated else 1)
+        for r in hs:
+            assert e in pl.local_experts[r]
+    assert sorted(e for r in range(W) for e in pl.local_experts[r] if pl.owner[e] == r) == list(range(16))
+    for src in range(W):
+        e2r, e2l, _ = pl.tables(src)
+        for e in range(16):
+            d = int(e2r[e])
+            assert d in pl.holders_of(e)
+            if src in pl.holders_of(e):
+                assert d == src
+            assert pl.local_experts[d][int(e2l[e])] == e
+    for e in pl.replicated:  # the sources without a copy split evenly over the holders
+        hs = pl.holders_of(e)
+        served = [pl.serving_rank(s, e) for s in range(W) if s not in hs]
+        assert max(served.count(h) for h in hs) - min(served.count(h) for h in hs) <= 1
+    assert pl.imbalance(load) <= plan_balanced(load, W).imbalance(load) + 1e-9
+    back = Placement.from_dict(pl.to_dict())
+    assert back.holders == pl.holders and back.tables(1)[0].tolist() == pl.tables(1)[0].tolist()
+
+
+def _partial_worker(rank, port, out):
+    import torch.distributed as dist
+
+    from spec_ep.rbd import dedup_combine_dispatch
+    from spec_ep.train import replica_slots, sum_replica_grads
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=4)
+    try:
+        load = torch.tensor([90., 70, 50, 4, 3, 3, 2, 2, 2, 1, 1, 1, 1, 1, 1, 1])
+        pl = plan_balanced(load, 4, replicate_top=3, copies=2)
+        g = torch.Generator().manual_seed(50 + rank)
+        T, k, H = 128, 3, 8
+        logits = torch.randn(T, 16, generator=g) + torch.log(load)
+        w, route = torch.softmax(logits, -1).topk(k, -1)
+        x = torch.randn(T, H, generator=g)
+
+        def fn(rows, ids):
+            return torch.sin(rows * (ids.unsqueeze(-1) + 1.0))
+
+        base = dedup_combine_dispatch(x, w, fn, route, 16)
+        part = dedup_combine_dispatch(x, w, fn, route, 16, e2r=pl.tables(rank)[0])
+        torch.testing.assert_close(part, base, rtol=1e-5, atol=1e-5)
+        # gradients of partially replicated experts: summed over their holders only
+        slots = replica_slots(pl, rank)
+        grad = torch.full((pl.slots(rank), 2), float(rank + 1))
+        sum_replica_grads(grad, slots)
+        for i, e in enumerate(pl.local_experts[rank]):
+            want = float(sum(h + 1 for h in pl.holders_of(e))) if e in pl.replicated else float(rank + 1)
+            assert torch.equal(grad[i], torch.full((2,), want)), (rank, e, grad[i])
+        out[rank] = True
+    finally:
+        dist.destroy_process_group()
+
+
+def test_partial_replication_routing_and_gradients_gloo():
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    out = mp.Manager().dict()
+    mp.spawn(_partial_worker, args=(port, out), nprocs=4, join=True)
+    assert all(out.get(r) for r in range(4))
