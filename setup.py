@@ -6,7 +6,7 @@ nvcc flags makes torch.utils.cpp_extension skip its own architecture list.
 import glob
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -27,7 +27,9 @@ sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(
 setup(
     name="spec_ep",
     version="0.1.0",
-    packages=["spec_ep"],
+    packages=find_packages(include=["spec_ep", "spec_ep.*"]),
+    python_requires=">=3.10",
+    install_requires=["torch"],
     ext_modules=[
         CUDAExtension(
             name="spec_ep._C",
