@@ -84,3 +84,35 @@ def test_expert_transfer_group_splits():
             totals = sorted(sum(s) for s in sends)
             assert totals[0] == numel * 0.5 and totals[-1] == numel * 1.5
             assert sum(totals) == numel * world
+
+
+def test_visualiser_counts_gpu_load_through_a_placement_with_replicas(tmp_path):
+    import json
+
+    sys.path.insert(0, os.path.join(ROOT, "visualization"))
+    import visualize_expert_routing as viz
+
+    from spec_ep.parallel.placement import plan_balanced
+
+    E, W = 8, 2
+    g = torch.Generator().manual_seed(0)
+    dumps = [torch.randint(0, E, (2, 64, 2), generator=g) for _ in range(W)]
+    dumps[0][..., 0] = 0  # expert 0 is hot
+    load = torch.bincount(torch.cat(dumps, 1)[0].reshape(-1), minlength=E).float()
+    pl = plan_balanced(load, W, replicate_top=1)
+    files = []
+    for r, d in enumerate(dumps):
+        files.append(tmp_path / f"experts_rank{r}.pt")
+        torch.save(d.to(torch.int16), files[-1])
+    (tmp_path / "placement.json").write_text(json.dumps(pl.to_dict()))
+    viz.main([str(f) for f in files] + ["--num_experts", str(E), "--num_gpus", str(W),
+                                         "--placement", str(tmp_path / "placement.json")])
+    rows = [line.split(",") for line in open(files[0].with_suffix(".csv")).read().splitlines()[1:]]
+    gpu = {int(i): int(v) for l, kind, i, v in rows if kind == "gpu" and l == "0"}
+    # each source's copies go where its own tables send them (expert 0 served locally)
+    want = [0] * W
+    for r, d in enumerate(dumps):
+        for e in d[0].reshape(-1).tolist():
+            want[int(pl.tables(r)[0][e])] += 1
+    assert [gpu[i] for i in range(W)] == want
+    assert sum(want) == 2 * 64 * 2 * W // 2

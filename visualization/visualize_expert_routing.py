@@ -16,19 +16,39 @@ from __future__ import annotations
 
 import argparse
 import json
+import sys
 from pathlib import Path
 
 import torch
 
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
-def histograms(route: torch.Tensor, num_experts: int, num_gpus: int, owner=None):
-    """Per layer: (tokens per expert [E], tokens per GPU [G])."""
+
+def histograms(route: torch.Tensor, num_experts: int, num_gpus: int, owner=None, placement=None, sources=None):
+    """Per layer: (tokens per expert [E], tokens per GPU [G]).
+
+    GPU load follows ``placement`` (a ``spec_ep.parallel.placement.Placement``) when given:
+    with ``sources`` (the source rank of every token, e.g. one dump file per rank) each
+    token's copy goes where that source's routing tables send it, so replicated experts
+    count on the rank that serves them; without sources, replicated experts' rows split
+    evenly over the source ranks. Otherwise ``owner`` (expert -> rank) or contiguous
+    blocks of ``num_experts // num_gpus`` experts.
+    """
     out = []
     owner_t = torch.tensor(owner) if owner is not None else torch.arange(num_experts) // (num_experts // num_gpus)
+    tables = None
+    if placement is not None and sources is not None:
+        tables = torch.stack([placement.tables(r)[0].long() for r in range(placement.world)])  # [W, E]
     for l in range(route.shape[0]):
         ids = route[l].reshape(-1).long()
         e = torch.bincount(ids, minlength=num_experts)
-        g = torch.zeros(num_gpus, dtype=torch.long).index_add_(0, owner_t, e)
+        if tables is not None:
+            src = sources.long().repeat_interleave(route.shape[2])
+            g = torch.bincount(tables[src, ids], minlength=num_gpus)
+        elif placement is not None:
+            g = placement.expected_rows(e).round().long()
+        else:
+            g = torch.zeros(num_gpus, dtype=torch.long).index_add_(0, owner_t, e)
         out.append((e, g))
     return out
 
@@ -101,9 +121,16 @@ def main(argv=None):
     ap.add_argument("--num_gpus", type=int, default=8)
     ap.add_argument("--placement", type=Path, default=None, help="placement JSON (Placement.to_dict)")
     args = ap.parse_args(argv)
-    route = torch.cat([torch.load(f).long() for f in args.files], dim=1)
-    owner = json.loads(args.placement.read_text())["owner"] if args.placement else None
-    hists = histograms(route, args.num_experts, args.num_gpus, owner)
+    dumps = [torch.load(f).long() for f in args.files]
+    route = torch.cat(dumps, dim=1)
+    placement = sources = None
+    if args.placement:
+        from spec_ep.parallel.placement import Placement
+
+        placement = Placement.from_dict(json.loads(args.placement.read_text()))
+        if len(dumps) == placement.world:  # one dump per source rank: exact serving ranks
+            sources = torch.cat([torch.full((d.shape[1],), r) for r, d in enumerate(dumps)])
+    hists = histograms(route, args.num_experts, args.num_gpus, placement=placement, sources=sources)
     title = (f"Routing distribution ({len(args.files)} rank file(s), {route.shape[1]} tokens, "
              f"top-{route.shape[2]}); dashed = balanced level")
     out = args.files[0].with_suffix(".png")
