@@ -34,7 +34,8 @@ from spec_ep.integrations.ds_moe import initialize  # noqa: E402
 from spec_ep.utils.dist import init_distributed, print0, shutdown_comm  # noqa: E402
 from spec_ep.utils.metrics import max_over_ranks  # noqa: E402
 from spec_ep.utils.profile import (FlopCounter, RoutingRecorder, add_expert_statistics_hook, count_params,  # noqa: E402
-                                   record_function, report_peak_mem, save_torch_profile, torch_profile_ctx)
+                                   end_flops_profile, record_function, report_peak_mem, save_torch_profile,
+                                   start_flops_profile, torch_profile_ctx)
 
 
 def get_batch(vocab, rank, seq_len, device, text_ids=None):
@@ -114,7 +115,11 @@ def main():
         fc = FlopCounter(engine.module.cfg, args.seq_len, args.seq_len)
         with torch.no_grad():
             ms, _ = timed(lambda: engine(ids), dev)
-        print0(f"forward: {fc.step_flops(False) / 1e12:.1f} TFLOP/rank, {fc.tflops(ms, False):.0f} TFLOP/s per GPU")
+            prof = start_flops_profile(engine, args.seq_len, args.seq_len)
+            engine(ids)
+            path = end_flops_profile(prof, logs)
+        print0(f"forward: {fc.step_flops(False) / 1e12:.1f} TFLOP/rank, {fc.tflops(ms, False):.0f} TFLOP/s per GPU "
+               f"(breakdown: {path})")
     if "comm" in args.modes:
         ep = engine.ep
         x = torch.randn(args.seq_len, engine.module.cfg.hidden_size, device=dev).bfloat16()

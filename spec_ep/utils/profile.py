@@ -134,6 +134,81 @@ class FlopCounter:
         return self.step_flops(training) / (step_ms * 1e-3) / 1e12
 
 
+class FlopsProfile:
+    """Timed region with an analytic FLOP breakdown (the reference wraps DeepSpeed's
+    FlopsProfiler the same way, src/utils_profile.py:38-50).
+
+    ``prof = start_flops_profile(engine)``; run the forward (or training steps);
+    ``end_flops_profile(prof, outdir)`` writes ``flops_profile_{rank}.txt`` with the
+    per-component FLOPs, the device time and the achieved TFLOP/s of this rank.
+    """
+
+    def __init__(self, model, tokens_per_rank=None, seq_len=None, training=False, steps=1):
+        self.model = getattr(model, "module", model)
+        cfg = self.model.cfg
+        self.tokens = tokens_per_rank or 4096
+        self.counter = FlopCounter(cfg, self.tokens, seq_len or self.tokens)
+        self.training, self.steps = training, steps
+        self.ms = None
+        if torch.cuda.is_available():
+            self._s, self._e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            self._s.record()
+        else:
+            import time
+
+            self._t0 = time.perf_counter()
+
+    def stop(self) -> float:
+        if self.ms is None:
+            if torch.cuda.is_available():
+                self._e.record()
+                self._e.synchronize()
+                self.ms = self._s.elapsed_time(self._e)
+            else:
+                import time
+
+                self.ms = (time.perf_counter() - self._t0) * 1000.0
+        return self.ms
+
+    def report(self) -> str:
+        f = self.counter.forward_flops()
+        mult = 3 if self.training else 1
+        c = self.counter.cfg
+        total, expert = count_params(self.model)
+        ms = self.stop() / self.steps
+        lines = [f"flops profile, rank {_rank()}: {'training step' if self.training else 'forward'}, "
+                 f"{self.tokens} tokens, {c.num_layers} layers",
+                 f"local params: {total / 1e9:.3f} B ({expert / 1e9:.3f} B in experts)",
+                 f"{'component':<22}{'GFLOP':>14}{'share':>9}"]
+        parts = {"attention (QK^T, PV)": f["attention_per_layer"] * c.num_layers,
+                 "experts (SwiGLU)": f["experts_per_layer"] * c.num_layers,
+                 "qkv + o projections": (f["per_layer"] - f["attention_per_layer"] - f["experts_per_layer"]
+                                         - 2 * self.tokens * c.hidden_size * c.num_experts) * c.num_layers,
+                 "router": 2 * self.tokens * c.hidden_size * c.num_experts * c.num_layers,
+                 "lm head": f["lm_head"]}
+        tot = f["total"]
+        for k, v in parts.items():
+            lines.append(f"{k:<22}{mult * v / 1e9:>14.1f}{v / tot:>9.1%}")
+        lines.append(f"{'total':<22}{mult * tot / 1e9:>14.1f}")
+        lines.append(f"device time per {'step' if self.training else 'forward'}: {ms:.3f} ms; "
+                     f"achieved {mult * tot / (ms * 1e-3) / 1e12:.1f} TFLOP/s")
+        return "\n".join(lines) + "\n"
+
+
+def start_flops_profile(engine, tokens_per_rank=None, seq_len=None, training=False, steps=1) -> FlopsProfile:
+    """Start a FLOP-profiled region on the current stream (``engine`` or a model)."""
+    return FlopsProfile(engine, tokens_per_rank, seq_len, training, steps)
+
+
+def end_flops_profile(prof: FlopsProfile, outdir) -> Path:
+    """Stop the region and write ``flops_profile_{rank}.txt`` under ``outdir``."""
+    outdir = Path(outdir)
+    outdir.mkdir(parents=True, exist_ok=True)
+    path = outdir / f"flops_profile_{_rank()}.txt"
+    path.write_text(prof.report())
+    return path
+
+
 class CommLogger:
     """Per-operation count / bytes / device time of collectives and P2P transfers.
 

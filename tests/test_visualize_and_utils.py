@@ -116,3 +116,20 @@ def test_visualiser_counts_gpu_load_through_a_placement_with_replicas(tmp_path):
             want[int(pl.tables(r)[0][e])] += 1
     assert [gpu[i] for i in range(W)] == want
     assert sum(want) == 2 * 64 * 2 * W // 2
+
+
+def test_flops_profile_file(tmp_path):
+    from spec_ep.models.config import get_config
+    from spec_ep.utils.profile import end_flops_profile, start_flops_profile
+
+    class _M(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.cfg = get_config("tiny")
+            self.w = torch.nn.Parameter(torch.zeros(10))
+
+    prof = start_flops_profile(_M(), tokens_per_rank=256, seq_len=256, training=True)
+    path = end_flops_profile(prof, tmp_path)
+    text = path.read_text()
+    assert path.name == "flops_profile_0.txt"
+    assert "experts (SwiGLU)" in text and "TFLOP/s" in text and "total" in text
