@@ -32,6 +32,7 @@ def main():
     ap.add_argument("--fp8", action="store_true", help="e4m3 1x128 dispatch payload")
     ap.add_argument("--cases", nargs="+", default=["prefill", "decode"])
     ap.add_argument("--decode-steps", type=int, default=20)
+    ap.add_argument("--predictor", choices=["router", "mlp"], default="router")
     args = ap.parse_args()
 
     from spec_ep.models.config import get_config
@@ -113,8 +114,8 @@ def main():
 
         with torch.no_grad():
             res = [measure("plain")]
-            enable_speculation(model, args.slots)
-            r = measure(f"speculative_slots{args.slots}")
+            enable_speculation(model, args.slots, predictor=args.predictor)
+            r = measure(f"speculative_slots{args.slots}_{args.predictor}")
             st = torch.zeros(4, dtype=torch.int64, device=dev)
             for layer in model.layers:
                 st += layer.spec.cache.stats

@@ -64,6 +64,7 @@ class Qwen3MoeLayer(nn.Module):
     def forward(self, x, pos=None):
         cfg = self.cfg
         spec = self.spec
+        x_in = x
         if spec is not None:
             if torch.is_grad_enabled() and self.w_gu.requires_grad:
                 raise RuntimeError("speculative expert replication is inference-only: run under torch.no_grad()")
@@ -83,6 +84,7 @@ class Qwen3MoeLayer(nn.Module):
         if self.routing_callback is not None:
             self.routing_callback(topk_e)
         if spec is not None:
+            spec.observe(x_in, topk_e)
             return ep_moe(h, topk_e, topk_w, spec.w_gu, spec.w_d, self.ep, None, residual=x, route=spec.tables())
         return ep_moe(h, topk_e, topk_w, self.w_gu, self.w_d, self.ep, self.grad_sink, residual=x)
 

@@ -153,6 +153,44 @@ class ReplicaCache:
                 "predicted_rows_served_locally": local, "local_share": local / max(cand, 1)}
 
 
+class MLPPredictor(torch.nn.Module):
+    """The plan's second predictor (docs/plan.md:3-8): a small MLP on the residual stream
+    that enters the layer (before attention), trained online to reproduce the layer's
+    router choices. ``learn(x_in, topk_e)`` takes one Adam step of a multi-label loss
+    (binary cross-entropy against the multi-hot of the chosen experts); ``predict``
+    returns its top-k experts. Plain torch ops (GEMMs of [T, H] x [H, width]); the
+    default predictor, the layer's own router on the residual stream, needs no training.
+    """
+
+    def __init__(self, hidden: int, num_experts: int, width: int = 256, lr: float = 1e-3, device=None,
+                 dtype=torch.float32):
+        super().__init__()
+        self.net = torch.nn.Sequential(torch.nn.Linear(hidden, width), torch.nn.SiLU(),
+                                       torch.nn.Linear(width, num_experts)).to(device=device, dtype=dtype)
+        self.opt = torch.optim.Adam(self.net.parameters(), lr=lr)
+        self.E = num_experts
+        self.steps = 0
+
+    def _in(self, x):
+        x = x.to(self.net[0].weight.dtype)
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+
+    @torch.no_grad()
+    def predict(self, x_in: torch.Tensor, top_k: int) -> torch.Tensor:
+        return self.net(self._in(x_in)).topk(top_k, -1).indices.int()
+
+    def learn(self, x_in: torch.Tensor, topk_e: torch.Tensor) -> float:
+        with torch.enable_grad():
+            target = torch.zeros(x_in.shape[0], self.E, device=x_in.device, dtype=self.net[0].weight.dtype)
+            target.scatter_(1, topk_e.long(), 1.0)
+            loss = torch.nn.functional.binary_cross_entropy_with_logits(self.net(self._in(x_in.detach())), target)
+            self.opt.zero_grad(set_to_none=True)
+            loss.backward()
+            self.opt.step()
+        self.steps += 1
+        return loss.detach()
+
+
 class SpeculativeExperts:
     """One MoE layer's experts in a symmetric buffer with an LRU replica cache.
 
@@ -186,6 +224,18 @@ class SpeculativeExperts:
         self.stream = torch.cuda.Stream(device=self.device)
         self.ready = torch.cuda.Event()
         self.pending = False
+        self.predictor: MLPPredictor | None = None
+
+    def observe(self, x_prev, topk_e):
+        """Feed the layer's actual choices to its ``MLPPredictor`` (side stream)."""
+        if self.predictor is None:
+            return
+        cur = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(cur)
+        x_prev.record_stream(self.stream)
+        topk_e.record_stream(self.stream)
+        with torch.cuda.stream(self.stream):
+            self.predictor.learn(x_prev, topk_e)
 
     def load_primaries(self, w_gu: torch.Tensor, w_d: torch.Tensor):
         """Copy this rank's pinned experts in; collective (peers may read them afterwards)."""
@@ -196,14 +246,18 @@ class SpeculativeExperts:
         self.buf.barrier()
 
     def speculate(self, x_prev, post_norm, w_router, top_k, eps, renorm=True, bias=None):
-        """Predict this layer's experts from ``x_prev`` (``predict_topk``), update the cache
-        and fetch the new replicas, all on the side stream after the work already queued
-        on the current stream (so the fetch overlaps what the current stream runs next)."""
+        """Predict this layer's experts from ``x_prev`` (``predict_topk``, or the layer's
+        ``MLPPredictor`` when one is set), update the cache and fetch the new replicas, all
+        on the side stream after the work already queued on the current stream (so the
+        fetch overlaps what the current stream runs next)."""
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur)
         x_prev.record_stream(self.stream)  # read on the side stream: keep it allocated
         with torch.cuda.stream(self.stream):
-            pred_e = predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm, bias)
+            if self.predictor is not None:
+                pred_e = self.predictor.predict(x_prev, top_k)
+            else:
+                pred_e = predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm, bias)
             self.cache.update(pred_e)
             self.buf._b.fetch_experts(self.P, self.p_max, [0, self.off_d], [self.gu_stride, self.d_stride],
                                       self.cache.fetch_rank, self.cache.fetch_slot, self.blocks_per_slot)
@@ -233,13 +287,18 @@ def predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm=True, bias=None
     return e
 
 
-def enable_speculation(model, num_slots: int, min_count: int = 1, group=None, blocks_per_slot=None):
+def enable_speculation(model, num_slots: int, min_count: int = 1, group=None, blocks_per_slot=None,
+                       predictor: str = "router", predictor_width: int = 256):
     """Switch a ``Qwen3MoeForCausalLM`` to speculative expert replication (inference).
 
     Every layer's expert weights move into a ``SpeculativeExperts`` buffer (the layer's
     parameters become views of its pinned slots), and the shared ``ExpertParallel`` is
-    widened to ``P + num_slots`` local expert groups. Collective over the EP group.
+    widened to ``P + num_slots`` local expert groups. ``predictor`` is ``"router"`` (the
+    layer's router on its incoming residual stream) or ``"mlp"`` (an ``MLPPredictor`` per
+    layer, trained online from the routing it observes). Collective over the EP group.
     """
+    if predictor not in ("router", "mlp"):
+        raise ValueError("predictor must be 'router' or 'mlp'")
     ep = model.ep
     placement = ep.placement
     if placement is None:
@@ -255,6 +314,8 @@ def enable_speculation(model, num_slots: int, min_count: int = 1, group=None, bl
         sp.load_primaries(layer.w_gu.data, layer.w_d.data)
         layer.w_gu.data = sp.w_gu[:sp.P]
         layer.w_d.data = sp.w_d[:sp.P]
+        if predictor == "mlp":
+            sp.predictor = MLPPredictor(cfg.hidden_size, cfg.num_experts, predictor_width, device=ep.device)
         layer.spec = sp
         specs.append(sp)
     ep.set_local_slots(specs[0].P + num_slots)

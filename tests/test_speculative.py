@@ -298,3 +298,54 @@ def test_speculative_model_two_gpus_fetches_replicas_and_matches_plain():
     errq = ctx.SimpleQueue()
     mp.spawn(_multi_gpu_worker, args=(2, _free_port(), errq), nprocs=2, join=True)
     assert errq.empty()
+
+
+def test_mlp_predictor_learns_a_routing_rule():
+    from spec_ep.parallel.speculative import MLPPredictor
+
+    torch.manual_seed(0)
+    H, E, k, T = 32, 16, 2, 512
+    w = torch.randn(H, E)
+    bias = torch.linspace(1.0, -1.0, E)
+
+    def routing(x):  # stand-in for the layer's router: a fixed rule the predictor must learn
+        return (torch.tanh(x) @ w + bias).topk(k, -1).indices
+
+    pred = MLPPredictor(H, E, width=64, lr=3e-3)
+    x_test = torch.randn(T, H)
+    base = (pred.predict(x_test, k).long().unsqueeze(-1) == routing(x_test).unsqueeze(1)).any(-1).float().mean()
+    for _ in range(300):
+        x = torch.randn(T, H)
+        pred.learn(x, routing(x))
+    hit = (pred.predict(x_test, k).long().unsqueeze(-1) == routing(x_test).unsqueeze(1)).any(-1).float().mean()
+    assert hit > 0.7 and hit > base + 0.4, (float(base), float(hit))  # 0.14 -> 0.77 measured
+
+
+@pytest.mark.gpu
+@torch.no_grad()
+def test_model_with_mlp_predictor_one_gpu():
+    """The online MLP predictor trains on the side stream during inference; with every
+    expert on one GPU the output must still equal the plain forward exactly."""
+    from spec_ep.models.config import get_config
+    from spec_ep.models.qwen3_moe import Qwen3MoeForCausalLM
+    from spec_ep.parallel.ep import ExpertParallel
+    from spec_ep.parallel.speculative import enable_speculation
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = get_config("tiny")
+    T = 256
+    ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=T, device=dev)
+    torch.manual_seed(0)
+    model = Qwen3MoeForCausalLM(cfg, ep, device=dev)
+    ids = torch.randint(0, cfg.vocab_size, (1, T), device=dev)
+    ref = model(ids).float()
+    specs = enable_speculation(model, num_slots=2, predictor="mlp")
+    for _ in range(3):
+        out = model(ids).float()
+    torch.cuda.synchronize()
+    ep.check()
+    assert torch.equal(out, ref)
+    assert all(sp.predictor.steps == 3 for sp in specs)
+    for sp in specs:
+        sp.close()
