@@ -33,6 +33,7 @@ def main():
     ap.add_argument("--cases", nargs="+", default=["prefill", "decode"])
     ap.add_argument("--decode-steps", type=int, default=20)
     ap.add_argument("--predictor", choices=["router", "mlp"], default="router")
+    ap.add_argument("--interval", type=int, default=1, help="re-plan the caches every N calls")
     args = ap.parse_args()
 
     from spec_ep.models.config import get_config
@@ -61,7 +62,8 @@ def main():
         model = Qwen3MoeForCausalLM(cfg, ep, device=dev)
         model.eval()
         for l, layer in enumerate(model.layers):
-            layer.router_bias = zipf_bias(E, args.zipf, seed=l, device=dev)
+            # Zipf popularity in logit space, as the dispatch benchmarks' synthetic routing
+            layer.router_logit_bias = zipf_bias(E, args.zipf, seed=l, device=dev)
         return ep, model
 
     def run_case(name, T, calls):
@@ -114,8 +116,8 @@ def main():
 
         with torch.no_grad():
             res = [measure("plain")]
-            enable_speculation(model, args.slots, predictor=args.predictor)
-            r = measure(f"speculative_slots{args.slots}_{args.predictor}")
+            enable_speculation(model, args.slots, predictor=args.predictor, interval=args.interval)
+            r = measure(f"speculative_slots{args.slots}_{args.predictor}_every{args.interval}")
             st = torch.zeros(4, dtype=torch.int64, device=dev)
             for layer in model.layers:
                 st += layer.spec.cache.stats

@@ -57,7 +57,8 @@ class Qwen3MoeLayer(nn.Module):
         for p in (self.w_gu, self.w_d):
             p._sepx_expert = True
         self.grad_sink = None
-        self.router_bias = None  # optional selection bias (synthetic skew studies)
+        self.router_bias = None  # optional selection bias added to the probabilities
+        self.router_logit_bias = None  # optional fp32 [E] bias added to the router logits (skew studies)
         self.routing_callback = None  # receives topk expert ids (routing capture)
         self.spec = None  # SpeculativeExperts (speculative replication, inference only)
 
@@ -71,7 +72,7 @@ class Qwen3MoeLayer(nn.Module):
             # predict this layer's experts from the incoming residual stream; the replica
             # fetch runs on a side stream while the attention below executes
             spec.speculate(x, self.post_norm, self.w_router, cfg.top_k, cfg.rms_norm_eps, cfg.norm_topk_prob,
-                           self.router_bias)
+                           self.router_bias, self.router_logit_bias)
         h = rms_norm(x, self.input_norm, cfg.rms_norm_eps)
         qkv = F.linear(h, self.w_qkv)
         q, k, v = qk_norm_rope(qkv, self.q_norm, self.k_norm, cfg.num_heads, cfg.num_kv_heads, cfg.rms_norm_eps,
@@ -80,6 +81,8 @@ class Qwen3MoeLayer(nn.Module):
         x = x + F.linear(a, self.w_o)
         h = rms_norm(x, self.post_norm, cfg.rms_norm_eps)
         logits = F.linear(h, self.w_router).float()
+        if self.router_logit_bias is not None:
+            logits = logits + self.router_logit_bias
         topk_w, topk_e = router_topk(logits, cfg.top_k, cfg.norm_topk_prob, self.router_bias)
         if self.routing_callback is not None:
             self.routing_callback(topk_e)

@@ -225,10 +225,14 @@ class SpeculativeExperts:
         self.ready = torch.cuda.Event()
         self.pending = False
         self.predictor: MLPPredictor | None = None
+        self.interval = 1  # re-plan the cache every `interval` calls; reuse the tables between
+        self.calls = 0
+        self.planned = False  # this call re-planned the cache
 
     def observe(self, x_prev, topk_e):
-        """Feed the layer's actual choices to its ``MLPPredictor`` (side stream)."""
-        if self.predictor is None:
+        """Feed the layer's actual choices to its ``MLPPredictor`` (side stream), on the
+        calls that re-planned the cache."""
+        if self.predictor is None or not self.planned:
             return
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur)
@@ -245,11 +249,16 @@ class SpeculativeExperts:
         self.w_d[:self.P].copy_(w_d)
         self.buf.barrier()
 
-    def speculate(self, x_prev, post_norm, w_router, top_k, eps, renorm=True, bias=None):
+    def speculate(self, x_prev, post_norm, w_router, top_k, eps, renorm=True, bias=None, logit_bias=None):
         """Predict this layer's experts from ``x_prev`` (``predict_topk``, or the layer's
         ``MLPPredictor`` when one is set), update the cache and fetch the new replicas, all
         on the side stream after the work already queued on the current stream (so the
-        fetch overlaps what the current stream runs next)."""
+        fetch overlaps what the current stream runs next). Between re-plans (``interval``
+        > 1) the call only counts and the cached tables stay in force."""
+        self.planned = self.calls % self.interval == 0
+        self.calls += 1
+        if not self.planned:
+            return
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur)
         x_prev.record_stream(self.stream)  # read on the side stream: keep it allocated
@@ -257,7 +266,7 @@ class SpeculativeExperts:
             if self.predictor is not None:
                 pred_e = self.predictor.predict(x_prev, top_k)
             else:
-                pred_e = predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm, bias)
+                pred_e = predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm, bias, logit_bias)
             self.cache.update(pred_e)
             self.buf._b.fetch_experts(self.P, self.p_max, [0, self.off_d], [self.gu_stride, self.d_stride],
                                       self.cache.fetch_rank, self.cache.fetch_slot, self.blocks_per_slot)
@@ -275,7 +284,7 @@ class SpeculativeExperts:
         self.buf.close()
 
 
-def predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm=True, bias=None):
+def predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm=True, bias=None, logit_bias=None):
     """Predicted expert ids [T, k]: the layer's router on RMSNorm(x_prev; post_norm)."""
     import torch.nn.functional as F
 
@@ -283,20 +292,28 @@ def predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm=True, bias=None
     from ..ops.router import router_topk
 
     h = rms_norm(x_prev, post_norm, eps)
-    _, e = router_topk(F.linear(h, w_router).float(), top_k, renorm, bias)
+    logits = F.linear(h, w_router).float()
+    if logit_bias is not None:
+        logits = logits + logit_bias
+    _, e = router_topk(logits, top_k, renorm, bias)
     return e
 
 
 def enable_speculation(model, num_slots: int, min_count: int = 1, group=None, blocks_per_slot=None,
-                       predictor: str = "router", predictor_width: int = 256):
+                       predictor: str = "router", predictor_width: int = 256, interval: int = 1):
     """Switch a ``Qwen3MoeForCausalLM`` to speculative expert replication (inference).
 
     Every layer's expert weights move into a ``SpeculativeExperts`` buffer (the layer's
     parameters become views of its pinned slots), and the shared ``ExpertParallel`` is
     widened to ``P + num_slots`` local expert groups. ``predictor`` is ``"router"`` (the
     layer's router on its incoming residual stream) or ``"mlp"`` (an ``MLPPredictor`` per
-    layer, trained online from the routing it observes). Collective over the EP group.
+    layer, trained online from the routing it observes). ``interval`` > 1 re-plans each
+    layer's cache only every that many calls (decode steps see a stable hot set; the
+    prediction, policy and fetch launches then run once per ``interval`` steps).
+    Collective over the EP group.
     """
+    if interval < 1:
+        raise ValueError("interval must be at least 1")
     if predictor not in ("router", "mlp"):
         raise ValueError("predictor must be 'router' or 'mlp'")
     ep = model.ep
@@ -316,6 +333,7 @@ def enable_speculation(model, num_slots: int, min_count: int = 1, group=None, bl
         layer.w_d.data = sp.w_d[:sp.P]
         if predictor == "mlp":
             sp.predictor = MLPPredictor(cfg.hidden_size, cfg.num_experts, predictor_width, device=ep.device)
+        sp.interval = int(interval)
         layer.spec = sp
         specs.append(sp)
     ep.set_local_slots(specs[0].P + num_slots)

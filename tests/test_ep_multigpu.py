@@ -372,7 +372,7 @@ def _replica_train_worker(rank, world, port, errq):
             for layer in model.layers:
                 layer.w_gu.copy_(full_gu[mine].to(dev))
                 layer.w_d.copy_(full_d[mine].to(dev))
-                layer.router_bias = torch.linspace(1.0, -1.0, cfg.num_experts, device=dev)
+                layer.router_logit_bias = torch.linspace(1.0, -1.0, cfg.num_experts, device=dev)
         trainer = Trainer(model, lr=1e-2, expert_state="fp32")
         ids = torch.randint(0, cfg.vocab_size, (1, T), device=dev,
                             generator=torch.Generator(device=dev).manual_seed(10 + rank))

@@ -255,7 +255,9 @@ def _multi_gpu_worker(rank, world, port, errq):
             for layer in model.layers:
                 layer.w_gu.normal_(0.0, 0.02)
                 layer.w_d.normal_(0.0, 0.02)
-                layer.router_bias = torch.linspace(1.5, -1.5, cfg.num_experts, device=dev)  # skewed popularity
+                # skewed popularity in logit space: every rank still routes some tokens to
+                # every expert (a bias on the probabilities would fix the top-k outright)
+                layer.router_logit_bias = torch.linspace(0.6, -0.6, cfg.num_experts, device=dev)
         ids = torch.randint(0, cfg.vocab_size, (1, T), device=dev,
                             generator=torch.Generator(device=dev).manual_seed(7 + rank))
         with torch.no_grad():
@@ -349,3 +351,22 @@ def test_model_with_mlp_predictor_one_gpu():
     assert all(sp.predictor.steps == 3 for sp in specs)
     for sp in specs:
         sp.close()
+
+
+def test_replan_interval_counts_calls_without_a_gpu():
+    """Between re-plans ``speculate`` only counts calls (no stream work), so the interval
+    logic is checked with a stand-in object that has no GPU state."""
+    from spec_ep.parallel.speculative import SpeculativeExperts
+
+    class _Stub:
+        interval, calls, planned, predictor = 3, 0, False, None
+
+    stub = _Stub()
+    seen = []
+    for _ in range(7):
+        try:
+            SpeculativeExperts.speculate(stub, None, None, None, 2, 1e-6)
+        except AttributeError:  # a planning call reaches the CUDA streams the stub lacks
+            pass
+        seen.append(stub.planned)
+    assert seen == [True, False, False, True, False, False, True]
