@@ -10,6 +10,7 @@ reads the same JSON keys::
                          "sepx": {"dispatch": "p2p", "groups": 1, "fp8": false,
                                   "replicate_top_k": 0, "routing_dump": null,
                                   "speculative_slots": 0, "speculative_min_count": 1,
+                                  "speculative_predictor": "router", "speculative_interval": 1,
                                   "timeout_us": 10000000}},
      "optimizer": {"type": "AdamW", "params": {...}}}
 
@@ -48,6 +49,8 @@ class SepxOptions:
     routing_dump: object = None    # glob / list of experts_rank*.pt files for the placement planner
     speculative_slots: int = 0     # LRU replica cache slots per layer and rank (inference)
     speculative_min_count: int = 1  # fewest predicted rows that make an expert worth fetching
+    speculative_predictor: str = "router"  # "router" (router on the residual) | "mlp" (online MLP)
+    speculative_interval: int = 1  # re-plan each layer's cache every N calls
     timeout_us: int = 10_000_000   # device-side wait limit
 
 
@@ -85,6 +88,9 @@ def load_config(cfg) -> EPConfig:
             int(sx.speculative_min_count) < 1 or int(sx.timeout_us) <= 0:
         raise ValueError("expert_parallel.sepx: groups >= 1, replicate_top_k >= 0, speculative_slots >= 0, "
                          "speculative_min_count >= 1 and timeout_us > 0 are required")
+    if sx.speculative_predictor not in ("router", "mlp") or int(sx.speculative_interval) < 1:
+        raise ValueError("expert_parallel.sepx: speculative_predictor must be 'router' or 'mlp' and "
+                         "speculative_interval >= 1")
     if sx.replicate_top_k and not sx.routing_dump:
         raise ValueError("expert_parallel.sepx.replicate_top_k needs measured routing: set sepx.routing_dump")
     return out
@@ -198,7 +204,9 @@ def initialize(model=None, config=None, max_tokens: int = 4096, device=None):
         if cfg.sepx.speculative_slots:  # inference engine: no optimizer
             from ..parallel.speculative import enable_speculation
 
-            enable_speculation(net, int(cfg.sepx.speculative_slots), int(cfg.sepx.speculative_min_count))
+            enable_speculation(net, int(cfg.sepx.speculative_slots), int(cfg.sepx.speculative_min_count),
+                               predictor=cfg.sepx.speculative_predictor,
+                               interval=int(cfg.sepx.speculative_interval))
             return SepxEngine(net, None, ep, cfg), None, None, None
         tr = Trainer(net, lr=opt_params.get("lr", 1e-4), betas=tuple(opt_params.get("betas", (0.9, 0.95))),
                      weight_decay=opt_params.get("weight_decay", 0.1), expert_dp_group=dp_group)

@@ -138,6 +138,10 @@ def test_sepx_placement_and_engine_options(tmp_path):
         load_config({"expert_parallel": {"sepx": {"replicate_top_k": 4}}})
     with pytest.raises(ValueError):
         load_config({"expert_parallel": {"sepx": {"speculative_slots": -1}}})
+    with pytest.raises(ValueError):
+        load_config({"expert_parallel": {"sepx": {"speculative_predictor": "oracle"}}})
+    assert load_config({"expert_parallel": {"sepx": {"speculative_predictor": "mlp",
+                                                     "speculative_interval": 4}}}).sepx.speculative_interval == 4
     for bad in ({"dispatch": "rbd"}, {"groups": 2}):
         with pytest.raises(ValueError):
             _check_engine_options(load_config({"expert_parallel": {"sepx": bad}}))
