@@ -12,7 +12,9 @@ Input: one ``experts_rank{r}.pt`` dump per source rank (int16 ``[L, T, K]``, wri
                      from the step's own routing (oracle) or the previous step's
 
 with remote rows per token (per-rank dedup) against the naive per-copy count, the
-receive imbalance, and for the caches hits, fetches and fetched bytes.
+receive imbalance, and for the caches hits, fetches, the expert weight bytes fetched
+and the token bytes kept off NVLink (dispatch rows + combine partials) against the
+contiguous layout: the cache pays where the second exceeds the first.
 
     python benchmarks/replay_routing.py logs/run/experts_rank*.pt --world 8 --tokens-per-step 128
     python benchmarks/replay_routing.py --synthetic --world 8 --num-experts 128 --top-k 8
@@ -38,10 +40,16 @@ def main(argv=None):
     ap.add_argument("--copies", type=int, default=2)
     ap.add_argument("--slots", type=int, default=16)
     ap.add_argument("--tokens-per-step", type=int, default=128)
+    ap.add_argument("--min-count", type=int, default=1, help="cache experts predicted for >= this many tokens")
+    ap.add_argument("--interval", type=int, default=1, help="re-plan the caches every this many steps")
     ap.add_argument("--expert-bytes", type=int, default=3 * 2048 * 768 * 2)
+    ap.add_argument("--row-bytes", type=int, default=2048 * 2, help="bytes of one token row (bf16 hidden)")
     ap.add_argument("--synthetic", action="store_true", help="Zipf-routed dumps instead of files")
     ap.add_argument("--zipf", type=float, default=1.0)
     ap.add_argument("--tokens", type=int, default=1024, help="tokens per rank of a synthetic dump")
+    ap.add_argument("--hidden", type=int, default=2048,
+                    help="hidden size of a synthetic dump's router (the logit spread grows with it, so it sets "
+                         "how much the Zipf bias dominates; 2048 is the dispatch benchmarks' layer)")
     args = ap.parse_args(argv)
     from spec_ep.parallel.placement import contiguous, plan_balanced
     from spec_ep.parallel.simulate import placement_traffic, replay_cache, split_steps
@@ -51,7 +59,7 @@ def main(argv=None):
         W = args.world or 8
         dumps = []
         for r in range(W):
-            _, te, _ = synthetic_routing(args.tokens, 256, args.num_experts, args.top_k, s=args.zipf, seed=0, rank=r)
+            _, te, _ = synthetic_routing(args.tokens, args.hidden, args.num_experts, args.top_k, s=args.zipf, seed=0, rank=r)
             dumps.append(te.long().unsqueeze(0))
     else:
         if not args.files:
@@ -77,13 +85,15 @@ def main(argv=None):
             out.append(rec)
         steps = split_steps(dumps, l, args.tokens_per_step)
         for pred in ("oracle", "previous"):
-            res = replay_cache(steps, contiguous(E, W), args.slots, predict=pred, expert_bytes=args.expert_bytes)
+            res = replay_cache(steps, contiguous(E, W), args.slots, predict=pred, expert_bytes=args.expert_bytes,
+                               row_bytes=args.row_bytes, min_count=args.min_count, interval=args.interval)
             out.append({"layer": l, "scheme": f"cache{args.slots}_{pred}", "steps": len(steps),
                         "remote_rows_per_token": res["mean_remote_rows_per_token"],
                         "naive_rows_per_token": sum(s["naive_rows_per_token"] for s in res["steps"]) / len(steps),
                         "recv_imbalance": res["mean_recv_imbalance"], "hits": res["hits"],
                         "fetches": res["fetches"], "hit_rate": res["hit_rate"],
-                        "fetched_MiB": res["fetched_bytes"] / 2**20})
+                        "fetched_MiB": res["fetched_bytes"] / 2**20,
+                        "token_MiB_saved": res["saved_bytes"] / 2**20})
     for rec in out:
         print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in rec.items()}))
     return out

@@ -10,7 +10,8 @@ what a placement or a replica cache would do to the traffic, without a GPU:
   (``policy_reference``, the host twin of the policy kernel) over a sequence of steps:
   the prediction for a step is the step's own routing (``"oracle"``) or the previous
   step's (``"previous"``), and the traffic is measured on the step's actual routing
-  through the tables the cache produced. Reports hits, fetches and fetched bytes.
+  through the tables the cache produced. Reports hits, fetches, fetched weight bytes and
+  the token bytes the cache kept off NVLink.
 
 Reference parity: the reference feeds its recorded routing to an all-to-all timing
 benchmark (benchmark/all2all/even_vs_uneven.py:76-92) and sketches the caching idea in
@@ -47,8 +48,17 @@ def placement_traffic(routes: list[torch.Tensor], placement: Placement) -> dict:
 
 
 def replay_cache(steps: list[list[torch.Tensor]], placement: Placement, slots: int, min_count: int = 1,
-                 predict: str = "previous", expert_bytes: int = 0) -> dict:
-    """``steps[s][r]``: ``[T, K]`` routing of source rank r at step s (one layer)."""
+                 predict: str = "previous", expert_bytes: int = 0, row_bytes: int = 0, interval: int = 1) -> dict:
+    """``steps[s][r]``: ``[T, K]`` routing of source rank r at step s (one layer).
+
+    ``saved_bytes``: token rows the cache kept off NVLink against ``placement`` alone,
+    counted both ways (dispatch row out, combine partial back) at ``row_bytes`` each; set
+    it beside ``fetched_bytes`` (weights moved in) to see whether the cache pays.
+    ``interval``: re-plan the caches only every that many steps and keep their tables in
+    between (``enable_speculation(..., interval=N)``); ``min_count``: cache only experts
+    predicted for at least that many of a rank's tokens."""
+    if interval < 1:
+        raise ValueError("interval must be at least 1")
     if predict not in ("oracle", "previous"):
         raise ValueError("predict must be 'oracle' or 'previous'")
     W = placement.world
@@ -58,6 +68,9 @@ def replay_cache(steps: list[list[torch.Tensor]], placement: Placement, slots: i
         if predict == "previous" and s == 0:
             tables = [placement.tables(r)[0] for r in range(W)]  # nothing to predict from yet
             fetched = 0
+        elif (s - (predict == "previous")) % interval:
+            tables = [c.e2r for c in caches]  # between re-plans: the last tables stay in force
+            fetched = 0
         else:
             src = routes if predict == "oracle" else steps[s - 1]
             before = [int(c.stats[1]) for c in caches]
@@ -66,13 +79,17 @@ def replay_cache(steps: list[list[torch.Tensor]], placement: Placement, slots: i
             fetched = sum(int(c.stats[1]) - b for c, b in zip(caches, before))
             tables = [c.e2r for c in caches]
         t = traffic(routes, tables, W)
-        t.update(step=s, fetches=fetched, fetched_bytes=fetched * expert_bytes)
+        base = traffic(routes, [placement.tables(r)[0] for r in range(W)], W)
+        tokens = sum(int(r.shape[0]) for r in routes)
+        saved = (base["remote_rows_per_token"] - t["remote_rows_per_token"]) * tokens * 2 * row_bytes
+        t.update(step=s, fetches=fetched, fetched_bytes=fetched * expert_bytes,
+                 base_remote_rows_per_token=base["remote_rows_per_token"], saved_bytes=saved)
         per_step.append(t)
     hits = sum(int(c.stats[0]) for c in caches)
     fetches = sum(int(c.stats[1]) for c in caches)
     n = max(len(per_step), 1)
     return {"steps": per_step, "hits": hits, "fetches": fetches, "hit_rate": hits / max(hits + fetches, 1),
-            "fetched_bytes": fetches * expert_bytes,
+            "fetched_bytes": fetches * expert_bytes, "saved_bytes": sum(p["saved_bytes"] for p in per_step),
             "mean_remote_rows_per_token": sum(p["remote_rows_per_token"] for p in per_step) / n,
             "mean_recv_imbalance": sum(p["recv_imbalance"] for p in per_step) / n}
 

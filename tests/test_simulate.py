@@ -27,12 +27,22 @@ def test_cache_replay_cuts_remote_rows_and_counts_fetches():
              for _ in range(6)]
     base = sum(traffic(s, [contiguous(E, W).tables(r)[0] for r in range(W)], W)["remote_rows_per_token"]
                for s in steps) / len(steps)
-    oracle = replay_cache(steps, contiguous(E, W), slots=8, predict="oracle", expert_bytes=100)
+    oracle = replay_cache(steps, contiguous(E, W), slots=8, predict="oracle", expert_bytes=100, row_bytes=10)
     prev = replay_cache(steps, contiguous(E, W), slots=8, predict="previous", expert_bytes=100)
     assert oracle["mean_remote_rows_per_token"] < base and prev["mean_remote_rows_per_token"] < base
     assert oracle["fetched_bytes"] == 100 * oracle["fetches"] > 0
     assert prev["steps"][0]["fetches"] == 0  # nothing to predict the first step from
     assert 0.0 < prev["hit_rate"] <= 1.0
+    # saved token bytes: (base - cached) remote rows, both directions, at row_bytes each
+    want = sum((st["base_remote_rows_per_token"] - st["remote_rows_per_token"]) * W * 64 * 2 * 10
+               for st in oracle["steps"])
+    assert abs(oracle["saved_bytes"] - want) < 1e-6 and oracle["saved_bytes"] > 0
+    assert prev["saved_bytes"] == 0.0  # row_bytes defaults to 0
+    assert prev["steps"][0]["saved_bytes"] == 0.0
+    # re-planning every 3 steps: fetches only on planning steps (1, 4 for "previous")
+    sparse = replay_cache(steps, contiguous(E, W), slots=8, predict="previous", interval=3)
+    assert all(st["fetches"] == 0 for st in sparse["steps"] if st["step"] not in (1, 4))
+    assert sparse["fetches"] <= prev["fetches"]
 
 
 def test_replay_cli_on_dumps(tmp_path):
