@@ -90,11 +90,14 @@ def _reduce(values: list[float], op, device):
 
 
 def train_loop(trainer, batches: TokenBatches, steps: int, start_step: int = 0, log_dir=None, ckpt_every: int = 0,
-               save_fn=None, ep=None, print_fn=print, num_valid=None):
+               save_fn=None, ep=None, print_fn=print, num_valid=None, heartbeat=None):
     """Run steps ``start_step .. steps-1``; returns the per-step records of this rank.
 
     ``save_fn(path, step)`` is called (on every rank: it is collective) after every
-    ``ckpt_every`` steps with ``<log_dir>/step_<n>``.
+    ``ckpt_every`` steps with ``<log_dir>/step_<n>``. With a ``heartbeat``
+    (``spec_ep.utils.heartbeat.Heartbeat``), every step starts with a host-side arrival
+    that waits for all peers to arrive too (``PeerLostError`` names a lost rank before
+    this rank launches anything); steps count from ``start_step``.
     """
     rank = dist.get_rank() if (dist.is_available() and dist.is_initialized()) else 0
     world = dist.get_world_size() if (dist.is_available() and dist.is_initialized()) else 1
@@ -110,6 +113,8 @@ def train_loop(trainer, batches: TokenBatches, steps: int, start_step: int = 0, 
     tokens_per_step = batches.mb * batches.seq
     try:
         for step in range(start_step, steps):
+            if heartbeat is not None:
+                heartbeat.arrive(step - start_step)
             ids, labels = batches.get(step)
             stop = _timer()
             loss = trainer.train_step_from_host(ids, labels, num_valid)
@@ -160,6 +165,9 @@ def main(argv=None):
     ap.add_argument("--ckpt-every", type=int, default=0)
     ap.add_argument("--resume", default=None, help="checkpoint directory written by this launcher")
     ap.add_argument("--ep-stats", action="store_true")
+    ap.add_argument("--heartbeat-timeout", type=float, default=0.0,
+                    help="seconds without progress after which a peer counts as lost (host check before "
+                         "every step; set it above the longest step); 0 = off")
     args = ap.parse_args(argv)
 
     from . import checkpoint
@@ -195,8 +203,13 @@ def main(argv=None):
 
     # synthetic batches carry no label for their last position; file windows label every one
     valid = args.micro_batch * (args.seq if args.token_file else args.seq - 1)
+    heartbeat = None
+    if args.heartbeat_timeout > 0 and world > 1:
+        from .utils.heartbeat import Heartbeat
+
+        heartbeat = Heartbeat.from_default_group(timeout_s=args.heartbeat_timeout)
     train_loop(trainer, batches, args.steps, start, args.log_dir, args.ckpt_every, save_fn,
-               ep if args.ep_stats else None, num_valid=valid)
+               ep if args.ep_stats else None, num_valid=valid, heartbeat=heartbeat)
     ep.check()
     ep.close()
     shutdown_comm()

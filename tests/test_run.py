@@ -70,12 +70,18 @@ def _free_port():
 
 
 def _worker(rank, port, out):
+    from spec_ep.utils.heartbeat import Heartbeat
+
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2)
     try:
         printed = []
         recs = train_loop(_TinyTrainer(40), TokenBatches(40, 8, 2, rank, 2, seed=5), 3, 0, None,
                           print_fn=printed.append)
-        out[rank] = (len(recs), len(printed))
+        # resumed at step 3 with a heartbeat: arrivals count from the resume point
+        hb = Heartbeat.from_default_group(timeout_s=30.0)
+        more = train_loop(_TinyTrainer(40), TokenBatches(40, 8, 2, rank, 2, seed=5), 5, 3, None,
+                          print_fn=None, heartbeat=hb)
+        out[rank] = (len(recs), len(printed), [r["step"] for r in more], hb.arrived)
     finally:
         dist.destroy_process_group()
 
@@ -83,7 +89,7 @@ def _worker(rank, port, out):
 def test_train_loop_two_gloo_ranks():
     out = mp.Manager().dict()
     mp.spawn(_worker, args=(_free_port(), out), nprocs=2, join=True)
-    assert out[0] == (3, 3) and out[1] == (3, 0)  # only rank 0 prints the job line
+    assert out[0] == (3, 3, [3, 4], 2) and out[1] == (3, 0, [3, 4], 2)  # only rank 0 prints the job line
 
 
 @pytest.mark.gpu
