@@ -20,6 +20,10 @@ experts, so it is the pure dispatch+combine cost, on the contiguous expert layou
 reference uses. ``dispatch_combine_us_per_layer_planned`` repeats it with the
 speculative placement: experts packed by the load of a *previous* batch's routing (seed
 1) and the 16 hottest replicated on every rank, measured on the seed-0 batch.
+
+``roofline`` gives both measured times as fractions of their bounds (the slowest of
+compute at the measured bf16 peak, minimum HBM bytes at the measured copy bandwidth and
+NVLink bytes at the measured peer bandwidth; ``spec_ep.utils.roofline``).
 """
 from __future__ import annotations
 
@@ -246,6 +250,13 @@ def run_spec_ep(args):
             "loss": loss_dev, "peak_mem_gib": peak,
             "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
         }
+        try:  # fraction of roofline (CPU arithmetic after the timed regions)
+            from spec_ep.utils.roofline import bench_fields
+
+            out["roofline"] = bench_fields(cfg, T, args.seq, world, prec, ms, dc_us,
+                                           os.path.join(ROOT, "MEASURED_PEAKS.json"))
+        except Exception as e:  # the analysis must never cost the measured line
+            out["roofline"] = {"error": f"{type(e).__name__}: {e}"}
         print(json.dumps(out), flush=True)
     if dist.is_initialized():
         dist.barrier()

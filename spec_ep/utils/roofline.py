@@ -158,3 +158,23 @@ def synthetic_layer_rows(world: int, tokens: int = 4096, hidden: int = 2048, num
     worst = max(max(a, b) for a, b in zip(sent, recv)) / tokens
     return {"sent": sent, "received": recv, "worst_rows_per_token": worst,
             "mean_rows_per_token": sum(sent) / (world * tokens)}
+
+
+def bench_fields(cfg, tokens: int, seq_len: int, world: int, expert_state: str, step_ms: float,
+                 dispatch_combine_us: float | None, peaks_path=None) -> dict:
+    """Roofline block of the flagship benchmark's JSON line: the training step's bound and
+    fraction, and the dispatch + combine layer's (worst rank's rows on the benchmark's
+    Zipf s=1.0 routing, 4096 tokens/rank, hidden 2048, 128 experts, top-8)."""
+    peaks = Peaks.load(peaks_path)
+
+    def pick(r, measured_ms):
+        return {"bound_ms": r["bound_ms"], "bound_by": r["bound_by"], "fraction": fraction(r["bound_ms"], measured_ms),
+                "compute_ms": r["compute_ms"], "hbm_ms": r["hbm_ms"], "nvlink_ms": r["nvlink_ms"]}
+
+    out = {"peaks": peaks.source,
+           "training_step": pick(train_step_roofline(cfg, tokens, seq_len, world, expert_state, peaks), step_ms)}
+    if dispatch_combine_us is not None:
+        rows = synthetic_layer_rows(world)["worst_rows_per_token"]
+        dc = dispatch_combine_roofline(4096, 2048, 8, rows, peaks)
+        out["dispatch_combine"] = {**pick(dc, dispatch_combine_us / 1e3), "rows_per_token": rows}
+    return out

@@ -71,3 +71,16 @@ def test_cli_reads_bench_lines(tmp_path, capsys, monkeypatch):
     rows = [json.loads(x) for x in capsys.readouterr().out.splitlines()]
     assert [r["path"] for r in rows] == ["training step", "dispatch+combine"]
     assert all(0 < r["fraction"] < 1 for r in rows)
+
+
+def test_bench_fields_block():
+    from spec_ep.utils.roofline import bench_fields
+
+    cfg = get_config("qwen3-30b-a3b")
+    out = bench_fields(cfg, 4096, 4096, 8, "fp32", 212.6, 693.0, ROOT / "MEASURED_PEAKS.json")
+    assert out["training_step"]["bound_by"] in ("compute", "hbm", "nvlink")
+    assert 0.2 < out["training_step"]["fraction"] < 0.5
+    assert 0.3 < out["dispatch_combine"]["fraction"] < 0.6 and out["dispatch_combine"]["bound_by"] == "nvlink"
+    json.dumps(out)  # goes into the benchmark's JSON line
+    one = bench_fields(cfg, 4096, 4096, 1, "8bit", 202.1, None, None)
+    assert one["peaks"] == "fallback" and "dispatch_combine" not in one
