@@ -47,6 +47,9 @@ def main(argv=None):
     ap.add_argument("--synthetic", action="store_true", help="Zipf-routed dumps instead of files")
     ap.add_argument("--zipf", type=float, default=1.0)
     ap.add_argument("--tokens", type=int, default=1024, help="tokens per rank of a synthetic dump")
+    ap.add_argument("--drift-every", type=int, default=0,
+                    help="synthetic: re-draw which experts are hot every this many steps (0: stationary); "
+                         "static placements are then planned from the first step only")
     ap.add_argument("--hidden", type=int, default=2048,
                     help="hidden size of a synthetic dump's router (the logit spread grows with it, so it sets "
                          "how much the Zipf bias dominates; 2048 is the dispatch benchmarks' layer)")
@@ -59,7 +62,15 @@ def main(argv=None):
         W = args.world or 8
         dumps = []
         for r in range(W):
-            _, te, _ = synthetic_routing(args.tokens, args.hidden, args.num_experts, args.top_k, s=args.zipf, seed=0, rank=r)
+            if args.drift_every:
+                n_steps = max(args.tokens // args.tokens_per_step, 1)
+                parts = [synthetic_routing(args.tokens_per_step, args.hidden, args.num_experts, args.top_k,
+                                           s=args.zipf, seed=0, rank=r, bias_seed=i // args.drift_every,
+                                           token_seed=i)[1] for i in range(n_steps)]
+                te = torch.cat(parts)
+            else:
+                _, te, _ = synthetic_routing(args.tokens, args.hidden, args.num_experts, args.top_k, s=args.zipf,
+                                             seed=0, rank=r)
             dumps.append(te.long().unsqueeze(0))
     else:
         if not args.files:
@@ -73,7 +84,8 @@ def main(argv=None):
     out = []
     for l in (args.layers if args.layers is not None else range(L)):
         routes = [d[l] for d in dumps]
-        load = torch.bincount(torch.cat(routes).reshape(-1), minlength=E).float()
+        seen = [r[:args.tokens_per_step] for r in routes] if args.drift_every else routes  # what the planner knows
+        load = torch.bincount(torch.cat(seen).reshape(-1), minlength=E).float()
         schemes = {"contiguous": contiguous(E, W), "balanced": plan_balanced(load, W),
                    f"replicate_top{args.replicate_top}": plan_balanced(load, W, args.replicate_top)}
         if 1 < args.copies < W:

@@ -17,17 +17,21 @@ def zipf_bias(num_experts: int, s: float, seed: int = 0, device="cpu") -> torch.
 
 
 def synthetic_routing(T: int, hidden: int, num_experts: int, k: int, s: float = 1.0, seed: int = 0,
-                      rank: int = 0, device="cpu", renorm: bool = True):
+                      rank: int = 0, device="cpu", renorm: bool = True, bias_seed: int | None = None,
+                      token_seed: int | None = None):
     """(x [T, H] bf16, topk_e [T, k] int32, topk_w [T, k] fp32) for one rank.
 
     ``seed`` selects the routing distribution (shared by all ranks); ``rank`` selects the
     rank's tokens. Computed with plain torch so every implementation sees the same routes.
+    ``bias_seed`` (default ``seed``) draws the popularity order alone, with the router
+    weights kept: a new ``bias_seed`` moves which experts are hot (drifting popularity);
+    ``token_seed`` (default ``seed``) draws the tokens alone.
     """
-    g = torch.Generator().manual_seed(seed * 1000 + rank)
+    g = torch.Generator().manual_seed((seed if token_seed is None else token_seed) * 1000 + rank)
     x = torch.randn(T, hidden, generator=g)
     gw = torch.Generator().manual_seed(seed)
     w = torch.randn(hidden, num_experts, generator=gw) * 0.02
-    logits = x @ w + zipf_bias(num_experts, s, seed)
+    logits = x @ w + zipf_bias(num_experts, s, seed if bias_seed is None else bias_seed)
     p = torch.softmax(logits, -1)
     topk_w, topk_e = p.topk(k, -1)
     if renorm:

@@ -63,3 +63,22 @@ def test_replay_cli_on_dumps(tmp_path):
     assert all(o["remote_rows_per_token"] <= o["naive_rows_per_token"] + 1e-9 for o in out)
     assert split_steps([torch.zeros(2, 256, 2, dtype=torch.long)], 0, 64)[3][0].shape == (64, 2)
     assert plan_balanced(torch.ones(16), 4).imbalance(torch.ones(16)) == 1.0
+
+
+def test_synthetic_drift_moves_the_hot_set():
+    from spec_ep.utils.routing import synthetic_routing
+
+    E = 32
+    hot = []
+    for b in (0, 1):
+        _, te, _ = synthetic_routing(2048, 64, E, 4, s=1.5, seed=0, bias_seed=b)
+        hot.append(set(torch.bincount(te.reshape(-1).long(), minlength=E).topk(4).indices.tolist()))
+    assert hot[0] != hot[1]
+    sys.path.insert(0, os.path.join(ROOT, "benchmarks"))
+    import replay_routing
+
+    out = replay_routing.main(["--synthetic", "--world", "2", "--num-experts", "16", "--top-k", "2", "--tokens", "256",
+                               "--tokens-per-step", "64", "--drift-every", "2", "--hidden", "64", "--slots", "2",
+                               "--replicate-top", "2", "--copies", "1"])
+    cache = [o for o in out if o["scheme"] == "cache2_previous"]
+    assert len(cache) == 1 and cache[0]["steps"] == 4 and "token_MiB_saved" in cache[0]
