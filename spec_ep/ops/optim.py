@@ -17,7 +17,6 @@ HBM.
 """
 from __future__ import annotations
 
-import math
 
 import torch
 

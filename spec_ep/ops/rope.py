@@ -6,7 +6,6 @@ Rotary convention is rotate-half (pairs ``(i, i + 64)``), as in transformers' Qw
 """
 from __future__ import annotations
 
-import math
 
 import torch
 

@@ -25,7 +25,6 @@ the torch reference of the same semantics is ``spec_ep.rbd.dedup_combine_dispatc
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import torch
