@@ -90,15 +90,20 @@ def _reduce(values: list[float], op, device):
 
 
 def train_loop(trainer, batches: TokenBatches, steps: int, start_step: int = 0, log_dir=None, ckpt_every: int = 0,
-               save_fn=None, ep=None, print_fn=print, num_valid=None, heartbeat=None):
+               save_fn=None, ep=None, print_fn=print, num_valid=None, heartbeat=None, timeline=None):
     """Run steps ``start_step .. steps-1``; returns the per-step records of this rank.
 
     ``save_fn(path, step)`` is called (on every rank: it is collective) after every
     ``ckpt_every`` steps with ``<log_dir>/step_<n>``. With a ``heartbeat``
     (``spec_ep.utils.heartbeat.Heartbeat``), every step starts with a host-side arrival
     that waits for all peers to arrive too (``PeerLostError`` names a lost rank before
-    this rank launches anything); steps count from ``start_step``.
+    this rank launches anything); steps count from ``start_step``. With a ``timeline``
+    (``spec_ep.utils.trace.DeviceTimeline``), every EP stage of the step (dispatch,
+    experts, combine and their backward halves) is stamped on the device and the record
+    gets ``stage_us``: per stage, the mean device µs per layer call and the call count.
     """
+    from .utils.trace import enable_stage_timeline
+
     rank = dist.get_rank() if (dist.is_available() and dist.is_initialized()) else 0
     world = dist.get_world_size() if (dist.is_available() and dist.is_initialized()) else 1
     device = ep.device if ep is not None else (torch.device("cuda", torch.cuda.current_device())
@@ -116,11 +121,21 @@ def train_loop(trainer, batches: TokenBatches, steps: int, start_step: int = 0, 
             if heartbeat is not None:
                 heartbeat.arrive(step - start_step)
             ids, labels = batches.get(step)
+            if timeline is not None:
+                timeline.reset()
+                enable_stage_timeline(timeline)
             stop = _timer()
-            loss = trainer.train_step_from_host(ids, labels, num_valid)
+            try:
+                loss = trainer.train_step_from_host(ids, labels, num_valid)
+            finally:
+                if timeline is not None:
+                    enable_stage_timeline(None)
             ms = stop()
             rec = {"ts": time.time(), "rank": rank, "step": step, "loss": loss, "ms": ms,
                    "tokens_per_s_rank": tokens_per_step / (ms / 1000.0)}
+            if timeline is not None:
+                rec["stage_us"] = {k: {"mean_us": v["mean_us"], "count": v["count"]}
+                                   for k, v in timeline.durations().items()}
             if ep is not None:
                 rec.update(ep.take_stats())
             if f is not None:
@@ -165,6 +180,8 @@ def main(argv=None):
     ap.add_argument("--ckpt-every", type=int, default=0)
     ap.add_argument("--resume", default=None, help="checkpoint directory written by this launcher")
     ap.add_argument("--ep-stats", action="store_true")
+    ap.add_argument("--stage-times", action="store_true",
+                    help="stamp every EP stage on the device; per-stage µs per layer call in the metrics")
     ap.add_argument("--heartbeat-timeout", type=float, default=0.0,
                     help="seconds without progress after which a peer counts as lost (host check before "
                          "every step; set it above the longest step); 0 = off")
@@ -208,8 +225,13 @@ def main(argv=None):
         from .utils.heartbeat import Heartbeat
 
         heartbeat = Heartbeat.from_default_group(timeout_s=args.heartbeat_timeout)
+    timeline = None
+    if args.stage_times:
+        from .utils.trace import DeviceTimeline
+
+        timeline = DeviceTimeline(capacity=64 * cfg.num_layers * 8, device=dev)
     train_loop(trainer, batches, args.steps, start, args.log_dir, args.ckpt_every, save_fn,
-               ep if args.ep_stats else None, num_valid=valid, heartbeat=heartbeat)
+               ep if args.ep_stats else None, num_valid=valid, heartbeat=heartbeat, timeline=timeline)
     ep.check()
     ep.close()
     shutdown_comm()

@@ -110,3 +110,30 @@ def test_launcher_trains_checkpoints_and_resumes_tiny_model(tmp_path, capsys):
     # same weights, optimizer state and batches: the resumed steps repeat the original losses
     for a, b in zip(resumed, lines[2:]):
         assert abs(a["loss"] - b["loss"]) <= 1e-3 * abs(b["loss"]), (a["loss"], b["loss"])
+
+
+def test_train_loop_records_stage_times_from_a_timeline():
+    """The loop turns the stage timeline on around each step only and records its
+    per-stage means (a stand-in timeline: the device one is covered by the GPU tests)."""
+    from spec_ep.utils.trace import active_timeline
+
+    class _Timeline:
+        def __init__(self):
+            self.resets, self.seen = 0, []
+
+        def reset(self):
+            self.resets += 1
+
+        def durations(self):
+            return {"dispatch": {"count": 2, "total_us": 30.0, "mean_us": 15.0},
+                    "combine": {"count": 2, "total_us": 10.0, "mean_us": 5.0}}
+
+    class _Probe(_TinyTrainer):
+        def train_step_from_host(self, ids, labels, num_valid=None):
+            tl.seen.append(active_timeline())
+            return super().train_step_from_host(ids, labels, num_valid)
+
+    tl = _Timeline()
+    recs = train_loop(_Probe(30), TokenBatches(30, 8, 2, 0, 1, seed=2), 3, 0, None, print_fn=None, timeline=tl)
+    assert tl.resets == 3 and tl.seen == [tl, tl, tl] and active_timeline() is None
+    assert recs[0]["stage_us"] == {"dispatch": {"mean_us": 15.0, "count": 2}, "combine": {"mean_us": 5.0, "count": 2}}
