@@ -305,16 +305,20 @@ def run_reference(args):
         once()
     ms = timed(once, args.dc_iters, dev)
     if rank == 0:
-        print(json.dumps({
-            "impl": "reference", "metric": METRIC, "unavailable": reason, "n_gpus": world,
-            "dispatch_combine_us_per_layer": ms * 1000.0,
-            "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0, identity experts",
-            "dispatch_combine_us_per_layer_planned": dc_planned_us,
-            "planned_placement": "LPT packing of the previous batch's loads + top-16 experts replicated on every rank",
-            "api": "spec_ep.rbd.RBD_combine_dispatch (reference, unmodified, NCCL)",
-        }), flush=True)
+        print(json.dumps(reference_record(world, ms * 1000.0, reason)), flush=True)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def reference_record(world: int, dispatch_combine_us: float, reason: str) -> dict:
+    """The reference arm's JSON line: its dispatch+combine time on this framework's layer
+    shape; the training metric is unavailable for the given reason."""
+    return {
+        "impl": "reference", "metric": METRIC, "unavailable": reason, "n_gpus": world,
+        "dispatch_combine_us_per_layer": dispatch_combine_us,
+        "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0, identity experts",
+        "api": "spec_ep.rbd.RBD_combine_dispatch (reference, unmodified, NCCL)",
+    }
 
 
 if __name__ == "__main__":

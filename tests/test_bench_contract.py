@@ -1,0 +1,46 @@
+"""bench.py on the CPU: every name its functions read resolves (a typo or a variable
+from the other arm would only fail on the GPU box, after the timed region), and the
+reference arm's JSON line has the contract's keys."""
+import builtins
+import importlib.util
+import json
+import symtable
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _load_bench():
+    spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _unresolved(table, module_names):
+    bad = []
+    for child in table.get_children():
+        if child.get_type() == "function":
+            for sym in child.get_symbols():
+                if sym.is_global() and sym.is_referenced():
+                    name = sym.get_name()
+                    if name not in module_names and not hasattr(builtins, name):
+                        bad.append(f"{child.get_name()}: {name}")
+        bad += _unresolved(child, module_names)
+    return bad
+
+
+def test_every_name_in_bench_resolves():
+    src = (ROOT / "bench.py").read_text()
+    mod = _load_bench()
+    top = symtable.symtable(src, "bench.py", "exec")
+    assert _unresolved(top, set(vars(mod))) == []
+
+
+def test_reference_record_contract():
+    mod = _load_bench()
+    rec = mod.reference_record(8, 3609.0, "no training path")
+    json.dumps(rec)
+    assert rec["impl"] == "reference" and rec["metric"] == mod.METRIC and rec["n_gpus"] == 8
+    assert rec["dispatch_combine_us_per_layer"] == 3609.0 and rec["unavailable"] == "no training path"
+    assert not any("planned" in k for k in rec)  # the planned placement is this framework's, not the reference's
