@@ -44,3 +44,26 @@ def test_reference_record_contract():
     assert rec["impl"] == "reference" and rec["metric"] == mod.METRIC and rec["n_gpus"] == 8
     assert rec["dispatch_combine_us_per_layer"] == 3609.0 and rec["unavailable"] == "no training path"
     assert not any("planned" in k for k in rec)  # the planned placement is this framework's, not the reference's
+
+
+def _static_unresolved(path: Path):
+    """Names read inside functions that no module-level binding, global statement or
+    builtin provides (static: the file is not imported)."""
+    import ast
+
+    src = path.read_text()
+    top = symtable.symtable(src, str(path), "exec")
+    defined = {s.get_name() for s in top.get_symbols() if s.is_assigned() or s.is_imported() or s.is_namespace()}
+    for node in ast.walk(ast.parse(src)):
+        if isinstance(node, ast.Global):
+            defined |= set(node.names)
+    defined |= {"__file__", "__name__", "__doc__"}
+    return [f"{path.relative_to(ROOT)}: {bad}" for bad in _unresolved(top, defined)]
+
+
+def test_no_unresolved_names_in_gpu_only_code():
+    files = [ROOT / "bench.py", ROOT / "__graft_entry__.py", ROOT / "setup.py"]
+    for d in ("spec_ep", "benchmarks", "examples", "visualization"):
+        files += sorted((ROOT / d).rglob("*.py"))
+    bad = [b for f in files for b in _static_unresolved(f)]
+    assert bad == []
