@@ -21,6 +21,7 @@ class ClockSampler:
         self.path = None
 
     def __enter__(self):
+        self.out = None
         try:
             fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
             os.close(fd)
@@ -29,8 +30,10 @@ class ClockSampler:
                 cmd.insert(1, f"--id={self.uuid}")
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
+        except OSError:  # no nvidia-smi: the summary reports the region as unsampled
             self.proc = None
+            if self.out is not None:
+                self.out.close()
         return self
 
     def __exit__(self, *exc):
