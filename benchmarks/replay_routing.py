@@ -12,7 +12,8 @@ Input: one ``experts_rank{r}.pt`` dump per source rank (int16 ``[L, T, K]``, wri
                      from the step's own routing (oracle) or the previous step's
 
 with remote rows per token (per-rank dedup) against the naive per-copy count, the
-receive imbalance, and for the caches hits, fetches, the expert weight bytes fetched
+receive imbalance, the worst rank's max(sent, received) rows per token (what bounds the
+dispatch's link time), and for the caches hits, fetches, the expert weight bytes fetched
 and the token bytes kept off NVLink (dispatch rows + combine partials) against the
 contiguous layout: the cache pays where the second exceeds the first.
 
@@ -102,7 +103,9 @@ def main(argv=None):
             out.append({"layer": l, "scheme": f"cache{args.slots}_{pred}", "steps": len(steps),
                         "remote_rows_per_token": res["mean_remote_rows_per_token"],
                         "naive_rows_per_token": sum(s["naive_rows_per_token"] for s in res["steps"]) / len(steps),
-                        "recv_imbalance": res["mean_recv_imbalance"], "hits": res["hits"],
+                        "recv_imbalance": res["mean_recv_imbalance"],
+                        "worst_link_rows_per_token": sum(s["worst_link_rows_per_token"] for s in res["steps"])
+                        / len(steps), "hits": res["hits"],
                         "fetches": res["fetches"], "hit_rate": res["hit_rate"],
                         "fetched_MiB": res["fetched_bytes"] / 2**20,
                         "token_MiB_saved": res["saved_bytes"] / 2**20})

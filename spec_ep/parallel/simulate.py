@@ -4,8 +4,9 @@ Answers, for a routing dump (``experts_rank{r}.pt``, int16 ``[L, T, K]`` per sou
 what a placement or a replica cache would do to the traffic, without a GPU:
 
 * ``traffic(routes, tables)`` — rows each source sends (one per (token, other rank), the
-  fused kernels' dedup) and the naive per-copy count, rows each rank receives, and the
-  receive imbalance (max / mean).
+  fused kernels' dedup) and the naive per-copy count, rows each rank receives, the
+  receive imbalance (max / mean), and the worst rank's max(rows sent, rows received over
+  NVLink) per token, which bounds the dispatch's link time.
 * ``replay_cache(steps, placement, slots, ...)`` — runs each rank's speculative LRU cache
   (``policy_reference``, the host twin of the policy kernel) over a sequence of steps:
   the prediction for a step is the step's own routing (``"oracle"``) or the previous
@@ -29,18 +30,28 @@ def traffic(routes: list[torch.Tensor], tables: list[torch.Tensor], world: int) 
     """``routes[r]``: ``[T_r, K]`` expert ids of source rank r; ``tables[r]``: its ``[E]``
     expert -> rank table."""
     sent = naive = tokens = 0
-    recv = torch.zeros(world, dtype=torch.float64)
+    recv = torch.zeros(world, dtype=torch.float64)  # rows each rank receives, its own included
+    remote_in = torch.zeros(world, dtype=torch.float64)  # rows each rank receives from other ranks
+    out_rows = torch.zeros(world, dtype=torch.float64)  # rows each rank sends to other ranks
     for r, (route, e2r) in enumerate(zip(routes, tables)):
         T = route.shape[0]
         dst = e2r.long()[route.long()]
         hot = torch.zeros(T, world, dtype=torch.bool).scatter_(1, dst, True)
         per_rank = hot.sum(0).double()
         recv += per_rank
-        sent += int(per_rank.sum() - per_rank[r])
+        remote = per_rank.clone()
+        remote[r] = 0
+        remote_in += remote
+        out_rows[r] = remote.sum()
+        sent += int(remote.sum())
         naive += int((dst != r).sum())
         tokens += T
+    # the slowest link bounds a dispatch (and its combine): the rank that sends or
+    # receives the most rows over NVLink, per token of that rank's share
+    worst = float(torch.maximum(out_rows, remote_in).max()) * world / max(tokens, 1)
     return {"remote_rows_per_token": sent / max(tokens, 1), "naive_rows_per_token": naive / max(tokens, 1),
-            "recv_rows": recv.tolist(), "recv_imbalance": float(recv.max() / recv.mean().clamp_min(1e-9))}
+            "recv_rows": recv.tolist(), "recv_imbalance": float(recv.max() / recv.mean().clamp_min(1e-9)),
+            "worst_link_rows_per_token": worst}
 
 
 def placement_traffic(routes: list[torch.Tensor], placement: Placement) -> dict:

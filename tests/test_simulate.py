@@ -17,6 +17,8 @@ def test_traffic_counts_by_hand():
     # rank 0 sends token 1 and token 2 to rank 1 (2 rows; naive 3 copies); rank 1 sends token 1 to rank 0
     assert t["remote_rows_per_token"] == 3 / 5 and t["naive_rows_per_token"] == 4 / 5
     assert t["recv_rows"] == [3.0, 4.0]
+    # rank 0 sends 2 rows and receives 1, rank 1 the reverse: 2 rows per 2.5 tokens
+    assert t["worst_link_rows_per_token"] == 2 / 2.5
 
 
 def test_cache_replay_cuts_remote_rows_and_counts_fetches():
