@@ -61,12 +61,20 @@ class RoutingRecorder:
         return path
 
 
-def add_expert_statistics_hook(model, recorder: RoutingRecorder):
-    """Record routing of every MoE layer of a ``spec_ep`` model (or any module exposing
-    ``router_hook``); returns the hook handles."""
+def add_expert_statistics_hook(model, recorder):
+    """Record the routing of every MoE layer of a ``spec_ep`` model; returns the layers
+    hooked. ``recorder`` is a :class:`RoutingRecorder`, or, as in the reference
+    (src/utils_profile.py:16-26), any container indexed by layer (``sent[i]`` receives
+    that layer's int16 ``[T, K]`` expert ids on the host after each forward)."""
     handles = []
     for i, layer in enumerate(getattr(model, "layers", [])):
-        layer.routing_callback = (lambda e, i=i: recorder.record(i, e))
+        if isinstance(recorder, RoutingRecorder):
+            layer.routing_callback = (lambda e, i=i: recorder.record(i, e))
+        else:
+            def store(e, i=i):
+                recorder[i] = e.detach().to(torch.int16).cpu()
+
+            layer.routing_callback = store
         handles.append(layer)
     return handles
 

@@ -133,3 +133,26 @@ def test_flops_profile_file(tmp_path):
     text = path.read_text()
     assert path.name == "flops_profile_0.txt"
     assert "experts (SwiGLU)" in text and "TFLOP/s" in text and "total" in text
+
+
+def test_reference_import_paths_and_list_routing_hook():
+    """``spec_ep.utils`` and ``spec_ep.utils_profile`` expose the reference's names
+    (src/utils.py, src/utils_profile.py); the routing hook also fills a per-layer list as
+    the reference's does."""
+    from types import SimpleNamespace
+
+    import spec_ep.utils as u
+    import spec_ep.utils_profile as up
+
+    for name in ("print0", "shutdown_comm", "get_rank_and_world_size"):
+        assert callable(getattr(u, name))
+    for name in ("count_params", "add_expert_statistics_hook", "report_peak_mem", "start_flops_profile",
+                 "end_flops_profile", "torch_profile_ctx", "save_torch_profile"):
+        assert callable(getattr(up, name))
+    model = SimpleNamespace(layers=[SimpleNamespace(routing_callback=None) for _ in range(3)])
+    sent = [None] * 3
+    up.add_expert_statistics_hook(model, sent)
+    for i, layer in enumerate(model.layers):
+        layer.routing_callback(torch.full((4, 2), i + 5, dtype=torch.int32))
+    assert all(s.dtype == torch.int16 and s.device.type == "cpu" and int(s[0, 0]) == i + 5
+               for i, s in enumerate(sent))
