@@ -133,12 +133,17 @@ def _block_starts(counts: torch.Tensor) -> torch.Tensor:
     return torch.cumsum(counts, 0) - counts
 
 
-def _group_by_local_rank(rows, weights, experts, experts_per_rank, gpus_per_node):
+def _group_by_local_rank(copy_row, copy_weight, copy_expert, experts_per_rank, gpus_per_node):
     """Stable grouping of copies by the node-local rank owning their expert (src/rbd.py:148-175)."""
-    owner = torch.div(experts, experts_per_rank, rounding_mode="floor") % gpus_per_node
+    owner = torch.div(copy_expert, experts_per_rank, rounding_mode="floor") % gpus_per_node
     order = torch.sort(owner, stable=True).indices
     counts = torch.bincount(owner, minlength=gpus_per_node)
-    return rows[order], weights[order], experts[order], counts
+    return copy_row[order], copy_weight[order], copy_expert[order], counts
+
+
+# the reference's names for the two plan helpers (src/rbd.py:136-175), same contracts
+_start_offsets = _block_starts
+_sort_copies = _group_by_local_rank
 
 
 # ----------------------------------------------------------------------------------------

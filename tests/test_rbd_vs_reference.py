@@ -58,3 +58,32 @@ def test_outputs_match_the_reference_rbd(tmp_path, world, gpn):
     mp.spawn(_worker, args=(world, gpn, tmp_path / "init", q), nprocs=world, join=True)
     got = sorted(q.get() for _ in range(world))
     assert got == [(r, "ok") for r in range(world)]
+
+
+def test_same_api_surface_as_the_reference():
+    """Every function and plan type of the reference's rbd module exists here with the
+    same parameters in the same order (NamedTuple fields included), and the two plan
+    helpers agree on random inputs."""
+    import inspect
+
+    import spec_ep.rbd as ours
+
+    ref = _load_ref()
+    for name, obj in vars(ref).items():
+        if name.startswith("__") or getattr(obj, "__module__", "") != ref.__name__:
+            continue
+        if not (inspect.isfunction(obj) or inspect.isclass(obj)):
+            continue
+        mine = getattr(ours, name)
+        if hasattr(obj, "_fields"):
+            assert mine._fields == obj._fields, name
+        if inspect.isfunction(obj):
+            want = [p.name for p in inspect.signature(obj).parameters.values()]
+            got = [p.name for p in inspect.signature(mine).parameters.values()][:len(want)]
+            assert got == want, name
+    g = torch.Generator().manual_seed(3)
+    counts = torch.randint(0, 9, (6,), generator=g)
+    assert torch.equal(ours._start_offsets(counts), ref._start_offsets(counts))
+    rows, w, e = torch.arange(40), torch.rand(40, generator=g), torch.randint(0, 16, (40,), generator=g)
+    for a, b in zip(ours._sort_copies(rows, w, e, 4, 2), ref._sort_copies(rows, w, e, 4, 2)):
+        assert torch.equal(a, b)
