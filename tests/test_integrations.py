@@ -161,3 +161,28 @@ def test_sepx_placement_and_engine_options(tmp_path):
     assert all(len(part.holders_of(e)) == 2 for e in part.replicated)
     flat = plan_placement(load_config({}), 16, 4)
     assert flat.owner == [e // 4 for e in range(16)]
+
+
+def test_hf_example_builds_random_or_loaded_weights(tmp_path):
+    """examples/hf_qwen.py on the host: random weights from a checkpoint's config by
+    default, the checkpoint's own weights with --load-weights (the reference's flag)."""
+    import importlib.util
+
+    from spec_ep.integrations.hf_qwen import random_hf_model
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("hf_example", os.path.join(root, "examples", "hf_qwen.py"))
+    ex = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ex)
+    src = random_hf_model(num_layers=1, hidden=128, experts=4, inter=64, vocab=256, heads=2, kv_heads=1, seed=3)
+    src.save_pretrained(tmp_path / "ckpt")
+    loaded, tok = ex.build_model(str(tmp_path / "ckpt"), load_weights=True)
+    assert tok is None
+    w_src = src.model.layers[0].mlp.gate.weight
+    assert torch.equal(loaded.model.layers[0].mlp.gate.weight, w_src)
+    fresh, _ = ex.build_model(str(tmp_path / "ckpt"), load_weights=False)
+    assert fresh.config.num_experts == 4 and fresh.model.layers[0].mlp.gate.weight.shape == w_src.shape
+    assert fresh.model.layers[0].self_attn.q_proj.weight.dtype == torch.bfloat16
+    assert not torch.equal(fresh.model.layers[0].self_attn.q_proj.weight, src.model.layers[0].self_attn.q_proj.weight)
+    with pytest.raises(SystemExit):
+        ex.build_model(None, load_weights=True)
