@@ -23,10 +23,17 @@ static void check(const char* what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
-  uint4 v = *reinterpret_cast<const uint4*>(p);
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
   f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  unpack8(*reinterpret_cast<const uint4*>(p), f);
+}
+// An empty asm that claims to rewrite the registers: the compiler must unpack them again
+// afterwards instead of keeping the earlier unpacked floats live (values are unchanged).
+__device__ __forceinline__ void opaque(uint4& v) {
+  asm volatile("" : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w));
 }
 __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
   uint4 v;
@@ -99,31 +106,48 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
   for (int i = 0; i < VPL; ++i)
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+  // w, and each row's x and dy, stay packed as bf16 (4 registers per 8 elements instead
+  // of 8 floats), so they fit beside the dw accumulators without spilling; every use
+  // unpacks them to the same floats
+  uint4 wr[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) wr[i] = *reinterpret_cast<const uint4*>(w + (i * 32 + lane) * 8);
   for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < N; row += nw) {
     const float r = rstd[row];
-    float xv[VPL][8], g[VPL][8];
+    uint4 xr[VPL], gr[VPL];
     float dot = 0.f;
 #pragma unroll
+    for (int i = 0; i < VPL; ++i) opaque(wr[i]);
+#pragma unroll
     for (int i = 0; i < VPL; ++i) {
-      float wv[8];
-      load8(x + (size_t)row * D + (i * 32 + lane) * 8, xv[i]);
-      load8(dy + (size_t)row * D + (i * 32 + lane) * 8, g[i]);
-      load8(w + (i * 32 + lane) * 8, wv);
+      float xv[8], g[8], wv[8];
+      xr[i] = *reinterpret_cast<const uint4*>(x + (size_t)row * D + (i * 32 + lane) * 8);
+      gr[i] = *reinterpret_cast<const uint4*>(dy + (size_t)row * D + (i * 32 + lane) * 8);
+      unpack8(xr[i], xv);
+      unpack8(gr[i], g);
+      unpack8(wr[i], wv);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float xh = xv[i][e] * r;
-        acc[i][e] += g[i][e] * xh;
-        g[i][e] *= wv[e];
-        xv[i][e] = xh;
-        dot += xh * g[i][e];
+        const float xh = xv[e] * r;
+        acc[i][e] += g[e] * xh;
+        dot += xh * (g[e] * wv[e]);
       }
     }
     dot = warp_sum(dot) / D;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
-      float o[8];
+      opaque(xr[i]);
+      opaque(gr[i]);
+      opaque(wr[i]);
+    }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = r * (g[i][e] - xv[i][e] * dot);
+    for (int i = 0; i < VPL; ++i) {
+      float xv[8], g[8], wv[8], o[8];
+      unpack8(xr[i], xv);
+      unpack8(gr[i], g);
+      unpack8(wr[i], wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = r * (g[e] * wv[e] - (xv[e] * r) * dot);
       store8(dx + (size_t)row * D + (i * 32 + lane) * 8, o);
     }
   }
