@@ -62,8 +62,9 @@ def _static_unresolved(path: Path):
 
 
 def test_no_unresolved_names_in_gpu_only_code():
+    """Covers the GPU tests too: they only execute on a GPU box."""
     files = [ROOT / "bench.py", ROOT / "__graft_entry__.py", ROOT / "setup.py"]
-    for d in ("spec_ep", "benchmarks", "examples", "visualization"):
+    for d in ("spec_ep", "benchmarks", "examples", "visualization", "tests"):
         files += sorted((ROOT / d).rglob("*.py"))
     bad = [b for f in files for b in _static_unresolved(f)]
     assert bad == []
