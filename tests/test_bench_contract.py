@@ -68,3 +68,50 @@ def test_no_unresolved_names_in_gpu_only_code():
         files += sorted((ROOT / d).rglob("*.py"))
     bad = [b for f in files for b in _static_unresolved(f)]
     assert bad == []
+
+
+def test_no_undefined_self_attributes():
+    """Inside every class of the package, benchmarks, examples and tests, each
+    ``self.X`` that is read is assigned, defined or inherited somewhere (bases from
+    this repository or torch's Module / autograd Function)."""
+    import ast
+
+    import torch
+
+    external = {"nn.Module": set(dir(torch.nn.Module)), "torch.nn.Module": set(dir(torch.nn.Module)),
+                "torch.autograd.Function": set(dir(torch.autograd.Function)), "RuntimeError": set(dir(RuntimeError)),
+                "Exception": set(dir(Exception)), "NamedTuple": set(dir(tuple)), "object": set()}
+    classes = {}
+    for d in ("spec_ep", "benchmarks", "examples", "tests"):
+        for f in sorted((ROOT / d).rglob("*.py")):
+            for c in [n for n in ast.walk(ast.parse(f.read_text())) if isinstance(n, ast.ClassDef)]:
+                own = {n.name for n in c.body if isinstance(n, (ast.FunctionDef, ast.AsyncFunctionDef))}
+                for n in c.body:
+                    for t in (n.targets if isinstance(n, ast.Assign) else [n.target] if isinstance(n, ast.AnnAssign) else []):
+                        if isinstance(t, ast.Name):
+                            own.add(t.id)
+                for n in ast.walk(c):
+                    if (isinstance(n, ast.Attribute) and isinstance(n.value, ast.Name) and n.value.id == "self"
+                            and isinstance(n.ctx, (ast.Store, ast.Del))):
+                        own.add(n.attr)
+                bases = [b.id if isinstance(b, ast.Name) else ast.unparse(b) for b in c.bases]
+                classes[c.name] = (own, bases, c, f)
+
+    def defined(name, seen=()):
+        if name in external:
+            return external[name]
+        own, bases, _, _ = classes[name]
+        out = set(own)
+        for b in bases:
+            if b not in seen:
+                out |= defined(b, seen + (name,))
+        return out
+
+    bad = []
+    for name, (_, _, c, f) in classes.items():
+        full = defined(name)
+        for n in ast.walk(c):
+            if (isinstance(n, ast.Attribute) and isinstance(n.value, ast.Name) and n.value.id == "self"
+                    and isinstance(n.ctx, ast.Load) and n.attr not in full and not n.attr.startswith("__")):
+                bad.append(f"{f.relative_to(ROOT)}:{n.lineno}: {name}.{n.attr}")
+    assert len(classes) >= 40 and bad == []
