@@ -136,3 +136,32 @@ def test_corrupted_expert_ids_are_reported_not_followed():
     ep.combine_fwd(st.xp, st)
     ep.check()
     ep.close()
+
+
+def _placement_worker(rank, port, q):
+    from spec_ep.utils.dist import check_placement
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=4,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        hosts = check_placement(2)
+        errors = []
+        for gpn, nodes in ((3, 1), (2, 3)):
+            try:
+                check_placement(gpn, min_nodes=nodes)
+            except RuntimeError as e:
+                errors.append(str(e))
+        q.put((rank, len(hosts), len(set(hosts)), errors))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_check_placement_on_gloo_ranks():
+    """4 ranks on one host as 2 nodes x 2: accepted; 3 per node or 3 nodes: rejected."""
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.spawn(_placement_worker, args=(_free_port(), q), nprocs=4, join=True)
+    for _ in range(4):
+        rank, n, distinct, errors = q.get()
+        assert n == 4 and distinct == 1
+        assert len(errors) == 2 and "not a multiple" in errors[0] and "at least 3 nodes" in errors[1]
