@@ -115,3 +115,14 @@ def test_no_undefined_self_attributes():
                     and isinstance(n.ctx, ast.Load) and n.attr not in full and not n.attr.startswith("__")):
                 bad.append(f"{f.relative_to(ROOT)}:{n.lineno}: {name}.{n.attr}")
     assert len(classes) >= 40 and bad == []
+
+
+def test_entry_points_parse_their_command_lines():
+    """``--help`` of the benchmark, the training launcher and the CPU analysis tools exits
+    0 without a GPU (argument parsing comes before any CUDA work)."""
+    import subprocess
+    import sys
+
+    for cmd in (["bench.py"], ["-m", "spec_ep.run"], ["benchmarks/replay_routing.py"], ["benchmarks/roofline.py"]):
+        r = subprocess.run([sys.executable, *cmd, "--help"], cwd=ROOT, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0 and "usage" in r.stdout, (cmd, r.stderr[-500:])
