@@ -7,7 +7,7 @@ must cross NVLink under per-rank deduplication), so ``fraction = bound / measure
 at most about 1 for a kernel that does the work. The peaks come from a measured-peaks
 JSON (``hbm_gbs``, ``bf16_tflops``, ``bf16_tflops_sustained``); NVLink figures are the
 measured 8-rank all-reduce bus bandwidth (725 GB/s at 1 GiB) and peer copy (770 GB/s per
-direction) of an 8xB200 NVSwitch box, overridable.
+direction) of an 8xB200 NVSwitch system, overridable.
 
 The reference measures only wall-clock latency of its MoE forward
 (scripts/ds_moe.py:99-111) and GB/s of its all-to-alls
@@ -35,7 +35,7 @@ class Peaks:
 
     @classmethod
     def load(cls, path: str | Path | None = None) -> "Peaks":
-        """Peaks from a measured-peaks JSON; the pool's earlier measurement when absent."""
+        """Peaks from a measured-peaks JSON; an earlier B200 measurement when absent."""
         if path is not None and Path(path).is_file():
             d = json.loads(Path(path).read_text())
             return cls(float(d["hbm_gbs"]), float(d["bf16_tflops"]),

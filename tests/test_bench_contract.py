@@ -1,5 +1,5 @@
 """bench.py on the CPU: every name its functions read resolves (a typo or a variable
-from the other arm would only fail on the GPU box, after the timed region), and the
+from the other arm would only fail on a machine with a GPU, after the timed region), and the
 reference arm's JSON line has the contract's keys."""
 import builtins
 import importlib.util
@@ -62,7 +62,7 @@ def _static_unresolved(path: Path):
 
 
 def test_no_unresolved_names_in_gpu_only_code():
-    """Covers the GPU tests too: they only execute on a GPU box."""
+    """Covers the GPU tests too: they only execute on a machine with a GPU."""
     files = [ROOT / "bench.py", ROOT / "__graft_entry__.py", ROOT / "setup.py"]
     for d in ("spec_ep", "benchmarks", "examples", "visualization", "tests"):
         files += sorted((ROOT / d).rglob("*.py"))

@@ -2,7 +2,7 @@
 arguments as the bound C++ function takes.
 
 Bindings are plain function pointers without Python-side defaults, so a call with the
-wrong count raises only when it runs, which for these paths is on a GPU box. The C++
+wrong count raises only when it runs, which for these paths is on a machine with a GPU. The C++
 parameter lists come from the sources in csrc/ (free functions bound with ``m.def``,
 ``EpComm`` / ``SymmBuffer`` methods bound with ``.def``). The Python receivers tracked
 are: ``load()``, names and attributes assigned from ``load()``, and names and
