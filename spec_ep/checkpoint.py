@@ -12,6 +12,13 @@ expert from the file of its old owner, so expert weights and their optimizer sta
 the experts. 8-bit optimizer blocks are 32 elements and an expert holds a multiple of 32
 values, so block-wise state slices per expert exactly.
 
+The expert optimizer state precision is chosen per world size (fp32 where it fits,
+block-wise 8-bit otherwise), so a checkpoint may be resumed at another precision:
+``meta.json`` records each expert tensor's precision (``expert_state_precision``) and
+``load`` converts every expert's state to the resuming optimizer's precision (8-bit codes
+decoded to fp32 moments with the restored weight as the master, or fp32 moments encoded
+to 8-bit blocks).
+
 The reference keeps only HF checkpoints (scripts/ds_moe.py:28-34, scripts/hf_qwen.py:26-36);
 ``export_hf`` writes the transformers safetensors layout of ``Qwen3MoeForCausalLM``.
 """
@@ -23,6 +30,7 @@ import os
 import torch
 import torch.distributed as dist
 
+from .ops.optim import convert_state
 from .parallel.placement import Placement, contiguous
 
 
@@ -57,12 +65,14 @@ def save(path, model, trainer=None, step: int = 0):
     local = placement.local_experts[model.ep.rank]
     opt = trainer.opt if trainer is not None else None
     shard = {"experts": local, "layers": []}
-    for layer in model.layers:
+    precisions = {}
+    for li, layer in enumerate(model.layers):
         entry = {}
         for name in ("w_gu", "w_d"):
             p = getattr(layer, name)
             entry[name] = {e: p.detach()[i].cpu() for i, e in enumerate(local)}
             if opt is not None:
+                precisions[f"layers.{li}.{name}"] = opt.state[id(p)]["prec"]
                 sl = _expert_state_slices(opt, p, len(local))
                 entry[name + ".opt"] = {k: ({e: v[i].cpu() for i, e in enumerate(local)} if isinstance(v, list) else v)
                                         for k, v in sl.items()}
@@ -78,7 +88,8 @@ def save(path, model, trainer=None, step: int = 0):
                 dstate[n] = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in opt.state[id(p)].items()}
         torch.save({"params": dense, "opt": dstate, "opt_step": opt.step_count if opt else 0},
                    os.path.join(path, "dense.pt"))
-        meta = {"step": step, "world": world, "config": model.cfg.to_dict(), "placement": placement.to_dict()}
+        meta = {"step": step, "world": world, "config": model.cfg.to_dict(), "placement": placement.to_dict(),
+                "expert_state_precision": precisions}
         with open(os.path.join(path, "meta.json"), "w") as f:
             json.dump(meta, f)
     if dist.is_available() and dist.is_initialized():
@@ -104,13 +115,14 @@ def load(path, model, trainer=None) -> int:
                 p[i].copy_(shards[old.owner[e]]["layers"][li][name][e])
             if opt is not None and (name + ".opt") in shards[old.owner[need[0]]]["layers"][li]:
                 st = opt.state[id(p)]
-                for k, v in st.items():
-                    if not torch.is_tensor(v):
-                        continue
-                    rows = v.view(len(need), -1)
-                    for i, e in enumerate(need):
-                        src = shards[old.owner[e]]["layers"][li][name + ".opt"][k][e]
-                        rows[i].copy_(src.reshape(-1))
+                rows = {k: v.view(len(need), -1) for k, v in st.items() if torch.is_tensor(v)}
+                for i, e in enumerate(need):
+                    saved = shards[old.owner[e]]["layers"][li][name + ".opt"]
+                    src = {k: (v[e].reshape(-1) if isinstance(v, dict) else v) for k, v in saved.items()}
+                    src.setdefault("prec", meta.get("expert_state_precision", {}).get(f"layers.{li}.{name}", "fp32"))
+                    src = convert_state(src, st["prec"], p[i].detach().cpu())
+                    for k, r in rows.items():
+                        r[i].copy_(src[k].reshape(-1))
     dense = torch.load(os.path.join(path, "dense.pt"), weights_only=False)
     params = dict(model.named_parameters())
     for n, t in dense["params"].items():

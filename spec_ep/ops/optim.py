@@ -122,6 +122,53 @@ def adamw_reference(p, g, m, v, lr, b1, b2, eps, wd, step):
     return p, m, v
 
 
+def encode_8bit(m: torch.Tensor, v: torch.Tensor):
+    """fp32 moments -> the block-wise 8-bit codes the optimizer kernels read.
+
+    Blocks are 32 consecutive values: ``mq = round(m * 127 / max|m|)`` (int8, nearest),
+    ``vq = ceil(min(sqrt(v) * 255 / max sqrt(v), 255))`` (uint8, rounded up so a non-zero
+    second moment never decodes to 0), ``ms = max|m|``, ``vs = max sqrt(v)`` per block.
+    Returns ``(mq, ms, vq, vs)`` flattened; used to convert checkpointed state between
+    precisions (the kernels themselves encode on the device).
+    """
+    m = m.float().reshape(-1, 32)
+    sq = v.float().clamp_min(0).sqrt().reshape(-1, 32)
+    ms = m.abs().amax(1)
+    vs = sq.amax(1)
+    em = torch.where(ms > 0, 127.0 / ms, torch.zeros_like(ms))
+    ev = torch.where(vs > 0, 255.0 / vs, torch.zeros_like(vs))
+    mq = torch.round(m * em[:, None]).clamp(-127, 127).to(torch.int8)
+    vq = torch.ceil((sq * ev[:, None]).clamp(max=255.0)).to(torch.uint8)
+    return mq.reshape(-1), ms, vq.reshape(-1), vs
+
+
+def decode_8bit(mq: torch.Tensor, ms: torch.Tensor, vq: torch.Tensor, vs: torch.Tensor):
+    """Block-wise 8-bit codes -> fp32 ``(m, v)`` (flattened), the inverse of :func:`encode_8bit`."""
+    m = mq.reshape(-1, 32).float() * (ms.float() / 127.0)[:, None]
+    s = vq.reshape(-1, 32).float() * (vs.float() / 255.0)[:, None]
+    return m.reshape(-1), (s * s).reshape(-1)
+
+
+def convert_state(src: dict, dst_prec: str, weight: torch.Tensor) -> dict:
+    """One parameter's (or one expert's) optimizer state in another precision.
+
+    ``src`` holds ``prec`` and the flat tensors of that precision (``master, m, v`` or
+    ``mq, ms, vq, vs``); ``weight`` is the parameter's current (bf16) value, which becomes
+    the fp32 master when 8-bit state (which keeps none) is widened. The conversion is
+    lossy only where the narrower format is.
+    """
+    prec = src.get("prec", "fp32")
+    if prec == dst_prec:
+        return src
+    if prec == "8bit" and dst_prec == "fp32":
+        m, v = decode_8bit(src["mq"], src["ms"], src["vq"], src["vs"])
+        return {"prec": "fp32", "master": weight.float().reshape(-1), "m": m, "v": v}
+    if prec == "fp32" and dst_prec == "8bit":
+        mq, ms, vq, vs = encode_8bit(src["m"], src["v"])
+        return {"prec": "8bit", "mq": mq, "ms": ms, "vq": vq, "vs": vs}
+    raise ValueError(f"cannot convert optimizer state {prec!r} -> {dst_prec!r}")
+
+
 def bytes_per_param(precision: str) -> float:
     """Optimizer state bytes per parameter (excluding the bf16 weight itself)."""
     return {"fp32": 12.0, "8bit": 2.25}[precision]
