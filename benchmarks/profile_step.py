@@ -6,15 +6,46 @@ rank 0 prints its per-kernel table.
 
     python benchmarks/profile_step.py --layers 8 [--warmup 2]
     python benchmarks/profile_step.py --layers 48 --table   # per-kernel device time (torch profiler)
+    python benchmarks/profile_step.py --layers 48 --breakdown   # device time per kernel class
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/profile_step.py --layers 48 --table --expert-state fp32
+
+``--breakdown`` groups every kernel of one step by class (expert GEMMs, attention, dense
+GEMMs, optimizer, EP data plane, elementwise, collectives, other) and reports the
+device time of each class, the sum, and the step's wall time on the device minus that
+sum (launch gaps and waits; kernels on side streams can overlap, so the gap may be
+negative).
 """
 import argparse
 import os
+import re
 import sys
 
 import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+# (class, regex over the kernel name); first match wins
+CLASSES = [
+    ("ep: plan/dispatch/combine", r"route_plan|route_tables|dispatch_kernel|recv_|combine_kernel|source_reduce|"
+                                  r"wait_rows|count_publish"),
+    ("expert grouped GEMM (tcgen05)", r"gg_kernel|grouped_gemm|GroupedGemm|gemm_kernel<"),
+    ("attention fwd", r"attn_fwd|attention_fwd|flash_fprop|sdpa.*fprop|fmha.*fwd|flash_fwd"),
+    ("attention bwd", r"attn_bwd|attention_bwd|bprop|fmha.*bwd|flash_bwd|dot_do_o|convert_dq"),
+    ("dense GEMM (tcgen05)", r"dense_gemm|linear_kernel"),
+    ("dense GEMM (cuBLAS)", r"nvjet|cutlass|gemm|sm100_xmma|cublas"),
+    ("optimizer", r"adamw|adam"),
+    ("norm / rope / router / swiglu / xent", r"rmsnorm|rope|router|swiglu|xent|qk_norm"),
+    ("collectives (NCCL)", r"nccl"),
+    ("copies / fills / casts", r"elementwise_kernel|vectorized_elementwise|unrolled_elementwise|fill|copy|Memcpy|"
+                               r"Memset|reduce_kernel|index|scatter|gather|cat|embedding"),
+]
+
+
+def classify(name: str) -> str:
+    for cls, pat in CLASSES:
+        if re.search(pat, name, re.I):
+            return cls
+    return "other"
 
 
 def main():
@@ -25,6 +56,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--expert-state", default="8bit")
     ap.add_argument("--table", action="store_true", help="print per-kernel CUDA time of one step (torch profiler)")
+    ap.add_argument("--breakdown", action="store_true", help="print device time per kernel class of one step")
+    ap.add_argument("--out", default=None, help="also write the breakdown (markdown) to this file")
     args = ap.parse_args()
     from spec_ep.models.config import get_config
     from spec_ep.models.qwen3_moe import Qwen3MoeForCausalLM
@@ -56,21 +89,52 @@ def main():
     torch.cuda.profiler.stop()
     torch.cuda.synchronize()
     ep.check()
+    step_ms = s.elapsed_time(e)
     if rank == 0:
-        print(f"world={world} layers={args.layers} step_ms={s.elapsed_time(e):.2f} loss={loss.item():.4f}")
-    if args.table:
+        print(f"world={world} layers={args.layers} step_ms={step_ms:.2f} loss={loss.item():.4f}")
+    if args.table or args.breakdown:
         from torch.profiler import ProfilerActivity, profile
 
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
             tr.train_step(ids, lab, args.seq - 1)
             torch.cuda.synchronize()
-        if rank == 0:
-            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70))
+        if rank == 0 and args.table:
+            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=90))
+        if rank == 0 and args.breakdown:
+            text = breakdown(prof, step_ms, world, args)
+            print(text)
+            if args.out:
+                with open(args.out, "w") as f:
+                    f.write(text + "\n")
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
         dist.destroy_process_group()
+
+
+def breakdown(prof, step_ms, world, args) -> str:
+    per_cls: dict[str, list] = {}
+    for ev in prof.key_averages():
+        us = ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
+        if us <= 0:
+            continue
+        c = classify(ev.key)
+        d = per_cls.setdefault(c, [0.0, 0, []])
+        d[0] += us
+        d[1] += ev.count
+        d[2].append((us, ev.count, ev.key))
+    total_us = sum(v[0] for v in per_cls.values())
+    lines = [f"one training step, {args.model}, {args.layers} layers, seq {args.seq}, world {world}, "
+             f"expert state {args.expert_state}",
+             f"step (CUDA events, unprofiled run): {step_ms:.2f} ms; kernel time summed: {total_us / 1e3:.2f} ms; "
+             f"step minus kernel sum: {step_ms - total_us / 1e3:.2f} ms",
+             "", "| class | ms / step | share of kernel time | launches | top kernels (ms) |", "|---|---|---|---|---|"]
+    for c, (us, n, ks) in sorted(per_cls.items(), key=lambda kv: -kv[1][0]):
+        ks.sort(reverse=True)
+        top = "; ".join(f"{k[:60]} {u / 1e3:.2f}" for u, _, k in ks[:3])
+        lines.append(f"| {c} | {us / 1e3:.2f} | {100 * us / max(total_us, 1):.1f}% | {n} | {top} |")
+    return "\n".join(lines)
 
 
 if __name__ == "__main__":
