@@ -18,7 +18,13 @@
 //   row_w[p]     gate weight of the copy placed at row p (0 on padding rows)
 //   row_src[p]   token index of the copy at row p (-1 on padding rows)
 //   inv_rows     [T, k] row of each (token, choice) in xp (-1 if dropped)
-//   status       [1] int32 device word, set to 0, or to 3 if cap_rows was too small
+//   status       [1] int32 device word, set to 0 by the call; afterwards 3 if the rows
+//                did not fit cap_rows, or 5 if some expert id in topk_e was >= E or
+//                < -1 (corrupted routing; those choices are dropped)
+//
+// Expert ids: an id of -1 means "not routed": that choice is skipped silently (it gets
+// inv_rows = -1 and no row), which is how callers mask out choices. Ids >= E or < -1 are
+// also skipped, with inv_rows = -1, and additionally set status to 5.
 //
 // Limits (compile-time, the scratch array is sized for them):
 //   T <= 8192 tokens, 1 <= k <= 8, E <= 256 experts, H a multiple of 8,
@@ -27,12 +33,16 @@
 //
 // Return value: 0 on success; 1 T out of range; 2 k out of range; 3 E out of range;
 // 4 bad H; 5 cap_rows too small; 6 null pointer; 7 the scratch address could not be
-// obtained on the current device; 100 + cudaError_t for a launch failure. A one-line
-// message is also printed to stderr for every non-zero return.
+// obtained on the current device; 8 x or xp not 16-byte aligned (rows move as 16-byte
+// vectors); 9 a CUDA error from earlier, unrelated work was already pending on the
+// calling thread (it is left pending for the caller's own checks and nothing is
+// launched); 100 + cudaError_t for a launch failure of this call. A one-line message is
+// also printed to stderr for every non-zero return.
 //
 // Set-up: the first call on each device (with that device current) looks up the
-// scratch array's device address with cudaGetSymbolAddress and caches it. Make that
-// first call before any CUDA stream capture begins on the device.
+// scratch array's device address with cudaGetSymbolAddress and caches it, keyed by the
+// device's current context (after a cudaDeviceReset the next call looks it up again).
+// Make that first call before any CUDA stream capture begins on the device.
 //
 // Concurrency: all calls on a device share the one scratch array, and it keeps the last
 // call's contents. Calls that may run at the same time on the GPU (different streams

@@ -36,11 +36,13 @@ def _routing(T, E, k, H, seed):
     return x, e.int().contiguous(), (w / w.sum(-1, keepdim=True)).contiguous()
 
 
-def test_noalloc_permute_matches_allocating_dispatch_twice():
+@pytest.mark.parametrize("T,E,k,H", [(2048, 64, 8, 512), (8192, 256, 8, 256)])
+def test_noalloc_permute_matches_allocating_dispatch_twice(T, E, k, H):
+    """Two calls in a row, at a mid size and at the scratch array's limits (T = 8192,
+    E = 256), give the allocating dispatch's layout."""
     from spec_ep.parallel.ep import ExpertParallel
 
     f = _entry()
-    T, E, k, H = 2048, 64, 8, 512
     ep = ExpertParallel(E, k, H, max_tokens=T)
     R = ep.cap_rows
     stream = torch.cuda.current_stream().cuda_stream
@@ -80,3 +82,45 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     assert f(p, p, p, 1024, 8, 512, 257, p, 10**7, p, p, p, p, p, stream) == 3
     assert f(p, p, p, 1024, 8, 500, 64, p, 10**7, p, p, p, p, p, stream) == 4
     assert f(p, p, p, 1024, 8, 512, 64, p, 1024, p, p, p, p, p, stream) == 5
+    # rows move as 16-byte vectors: a misaligned x or xp is refused before any launch
+    assert f(p + 2, p, p, 1024, 8, 512, 64, p, 10**7, p, p, p, p, p, stream) == 8
+    assert f(p, p, p, 1024, 8, 512, 64, p + 8, 10**7, p, p, p, p, p, stream) == 8
+
+
+def test_noalloc_out_of_range_and_masked_expert_ids():
+    """An id >= E is reported (status 5) and dropped; an id of -1 is dropped silently;
+    every other choice is placed exactly as in a call without the bad entries."""
+    f = _entry()
+    T, E, k, H = 256, 16, 4, 64
+    x, te, tw = _routing(T, E, k, H, seed=3)
+    bad = te.clone()
+    bad[5, 1] = E + 3   # out of range: reported
+    bad[9, 2] = -1      # masked: silent
+    R = T * k + 64 * E
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run(ids):
+        xp = torch.empty(R, H, device="cuda", dtype=torch.bfloat16)
+        go = torch.empty(E + 1, device="cuda", dtype=torch.int32)
+        rw = torch.empty(R, device="cuda", dtype=torch.float32)
+        rs = torch.empty(R, device="cuda", dtype=torch.int32)
+        inv = torch.empty(T, k, device="cuda", dtype=torch.int32)
+        status = torch.full((1,), -1, device="cuda", dtype=torch.int32)
+        rc = f(x.data_ptr(), ids.data_ptr(), tw.data_ptr(), T, k, H, E, xp.data_ptr(), R, go.data_ptr(),
+               rw.data_ptr(), rs.data_ptr(), inv.data_ptr(), status.data_ptr(), stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        return int(status.item()), inv, go, rs, xp
+
+    st_bad, inv_bad, go_bad, rs_bad, xp_bad = run(bad)
+    assert st_bad == 5
+    assert int(inv_bad[5, 1]) == -1 and int(inv_bad[9, 2]) == -1
+    masked = bad.clone()
+    masked[5, 1] = -1  # the same routing with the bad entry masked instead
+    st_m, inv_m, go_m, rs_m, xp_m = run(masked)
+    assert st_m == 0
+    assert torch.equal(inv_bad, inv_m) and torch.equal(go_bad, go_m)
+    n = int(go_m[-1])
+    cnt = bad[(bad >= 0) & (bad < E)].long().bincount(minlength=E)
+    assert n == int(((cnt + 63) // 64 * 64).sum())
+    assert torch.equal(rs_bad[:n], rs_m[:n]) and torch.equal(xp_bad[:n], xp_m[:n])
