@@ -162,13 +162,16 @@ class EpComm {
                        const at::Tensor& self_tok, const at::Tensor& send_count, int G, int T, int cap_rows,
                        int64_t epoch, at::Tensor& rows_from, at::Tensor& chunk_cnt, at::Tensor& group_off,
                        at::Tensor& group_cnt, at::Tensor& pad_off, at::Tensor& done, at::Tensor& status,
-                       double timeout_s) {
+                       double timeout_s, const c10::optional<at::Tensor>& need,
+                       const c10::optional<at::Tensor>& miss) {
     auto a = call_args(T, 0, epoch, done, status, timeout_s);
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    int* need_p = need.has_value() ? need->data_ptr<int>() : nullptr;
+    int* miss_p = miss.has_value() ? miss->data_ptr<int>() : nullptr;
     sepx::ep_recv_count_scan(a, dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), topk_w.data_ptr<float>(),
                              self_tok.data_ptr<int>(), send_count.data_ptr<int>(), G, cap_rows,
                              rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(), group_off.data_ptr<int>(),
-                             group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(), st);
+                             group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(), st, need_p, miss_p);
   }
 
   void recv_permute_gather(const at::Tensor& x, const at::Tensor& dst_tk, const at::Tensor& meta_tk,

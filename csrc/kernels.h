@@ -44,9 +44,11 @@ void ep_dispatch(const EpArgs& a, const void* x, const int* dst_tk, const int* m
                  bool fp8 = false);
 // Receive plan in two halves so the caller can size buffers between them: count+scan
 // produce group_off (group_off[G] = rows needed), permute+gather fill them.
+// need / miss (optional): see recv_scan_kernel (row budgets that spare the host a wait).
 void ep_recv_count_scan(const EpArgs& a, const int* dst_tk, const int* meta_tk, const float* topk_w,
                         const int* self_tok, const int* send_count, int G, int cap_rows, int* rows_from,
-                        int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, cudaStream_t st);
+                        int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, cudaStream_t st,
+                        int* need = nullptr, int* miss = nullptr);
 void ep_recv_permute_gather(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk,
                             const float* topk_w, const int* self_tok, const int* send_count, int G,
                             const int* rows_from, const int* chunk_cnt, const int* group_off, const int* group_cnt,

@@ -120,6 +120,13 @@ __global__ void route_tables_kernel(const int* __restrict__ topk_e, const int* _
   }
 }
 
+// Bit mask of W ranks rotated right by r: bit i of the result is bit (i + r) % W of m.
+__device__ __forceinline__ unsigned long long rotr_mask(unsigned long long m, int r, int W) {
+  if (r == 0) return m;
+  const unsigned long long full = W >= 64 ? ~0ull : ((1ull << W) - 1ull);
+  return ((m >> r) | (m << (W - r))) & full;
+}
+
 // Epoch of this call: the host value plus the device counter when one is given.
 __device__ __forceinline__ uint32_t ep_epoch(const EpArgs& a) {
   return a.epoch_dev ? a.epoch + *a.epoch_dev : a.epoch;
@@ -177,6 +184,9 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
     }
     unsigned long long remote = m & ~(1ull << a.rank);
     if (!remote) continue;
+    // destinations are visited starting at a token-dependent rank (a rotation of the
+    // bit mask), so concurrent warps spread their stores over every peer's ingress
+    const int rot = (t + a.rank) % a.W;
     for (int c0 = 0; c0 < vec; c0 += 32 * 8) {
       uint4 r[8];
 #pragma unroll
@@ -213,10 +223,12 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
           }
           q[i] = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
         }
-        unsigned long long rm = remote;
+        unsigned long long rm = rotr_mask(remote, rot, a.W);
         while (rm) {
           int d = __ffsll(rm) - 1;
           rm &= rm - 1;
+          d += rot;
+          if (d >= a.W) d -= a.W;
           int s = __ldg(slot + (size_t)t * a.W + d);
           char* base = reinterpret_cast<char*>(a.peer_base[d]);
           uint2* dq = reinterpret_cast<uint2*>(base + a.off_recv_q) + ((size_t)a.rank * a.cap + s) * vec;
@@ -232,10 +244,12 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
         }
         continue;
       }
-      unsigned long long rm = remote;
+      unsigned long long rm = rotr_mask(remote, rot, a.W);
       while (rm) {
         int d = __ffsll(rm) - 1;
         rm &= rm - 1;
+        d += rot;
+        if (d >= a.W) d -= a.W;
         int s = __ldg(slot + (size_t)t * a.W + d);
         char* base = reinterpret_cast<char*>(a.peer_base[d]);
         uint4* dst = reinterpret_cast<uint4*>(base + a.off_recv_x) +
@@ -257,10 +271,12 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
       float wf[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) wf[q] = __shfl_sync(0xffffffffu, w, q);
-      unsigned long long rm = remote;
+      unsigned long long rm = rotr_mask(remote, rot, a.W);
       while (rm) {
-        const int d = __ffsll(rm) - 1;
+        int d = __ffsll(rm) - 1;
         rm &= rm - 1;
+        d += rot;
+        if (d >= a.W) d -= a.W;
         const int e = (owner == d) ? meta : -1;
         const uint32_t pair = ((uint32_t)e & 0xFFFFu) | ((uint32_t)__shfl_down_sync(0xffffffffu, e, 1) << 16);
         const uint32_t p1 = __shfl_sync(0xffffffffu, pair, 2), p2 = __shfl_sync(0xffffffffu, pair, 4),
@@ -281,10 +297,12 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
       const int owner = __ldg(dst_tk + t * a.k + j);
       const int meta = __ldg(meta_tk + t * a.k + j);
       const float w = __ldg(topk_w + t * a.k + j);
-      unsigned long long rm = remote;
+      unsigned long long rm = rotr_mask(remote, rot, a.W);
       while (rm) {
         int d = __ffsll(rm) - 1;
         rm &= rm - 1;
+        d += rot;
+        if (d >= a.W) d -= a.W;
         int s = __ldg(slot + (size_t)t * a.W + d);
         char* base = reinterpret_cast<char*>(a.peer_base[d]);
         int16_t* re = reinterpret_cast<int16_t*>(base + a.off_recv_e) + ((size_t)a.rank * a.cap + s) * a.k;
@@ -380,12 +398,18 @@ __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
   return v;
 }
 
+// cap_rows bounds the receive buffers. With `miss` given, cap_rows is the caller's row
+// budget for this call (buffers sized before the count is known, so the host never waits
+// for it): a total above it sets *miss = 1 instead of an error, the layout is emptied
+// (every later kernel of the call moves nothing) and the caller runs the pass again with
+// a larger budget. `need`, when given, receives the total rows the layout needs.
 __global__ void __launch_bounds__(1024) recv_scan_kernel(EpArgs a, int* __restrict__ chunk_cnt,
                                                          int nchunks, int G,
                                                          int* __restrict__ group_off,
                                                          int* __restrict__ group_cnt,
                                                          int* __restrict__ pad_off,
-                                                         int cap_rows) {
+                                                         int cap_rows, int* __restrict__ need = nullptr,
+                                                         int* __restrict__ miss = nullptr) {
   __shared__ int s_tot[1024];
   __shared__ int s_off[1024];
   __shared__ int s_pad[1024];
@@ -433,9 +457,14 @@ __global__ void __launch_bounds__(1024) recv_scan_kernel(EpArgs a, int* __restri
   __syncthreads();
   const int total = G > 0 ? s_off[G - 1] + ((s_tot[G - 1] + 63) & ~63) : 0;
   const int ptotal = G > 0 ? s_pad[G - 1] + (((s_tot[G - 1] + 63) & ~63) - s_tot[G - 1]) : 0;
+  if (threadIdx.x == 0 && need) *need = total;
   if (total > cap_rows) {
-    // cannot happen with the worst-case capacity; kept as a guard
-    if (threadIdx.x == 0) record_error(a.status, kErrOverflow);
+    // with the worst-case capacity this cannot happen (a guard); with a row budget it
+    // asks the caller for a larger one
+    if (threadIdx.x == 0) {
+      if (miss) atomicExch(miss, 1);
+      else record_error(a.status, kErrOverflow);
+    }
     if (g < G) {
       group_off[g] = 0;
       group_cnt[g] = 0;
@@ -618,11 +647,18 @@ __global__ void __launch_bounds__(256) combine_kernel(EpArgs a, const __nv_bfloa
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nw = (gridDim.x * blockDim.x) >> 5;
   const int vec = a.H / 8;
-  for (int src = 0; src < a.W; ++src) {
-    const int rows = rows_from[src];
-    char* dbase = reinterpret_cast<char*>(a.peer_base[src]);
-    uint4* ret = reinterpret_cast<uint4*>(dbase + a.off_ret_x) + (size_t)a.rank * a.cap * vec;
-    for (int s = gwarp; s < rows; s += nw) {
+  // Work items (src, slot) run slot-major, and each warp visits the sources in an order
+  // rotated by its own index and this rank: at any moment the warps of every rank write to
+  // all destinations at once, instead of every rank streaming into the same peer (which
+  // would leave one NVLink ingress saturated and the others idle).
+  int max_rows = 0;
+  for (int src = 0; src < a.W; ++src) max_rows = max(max_rows, rows_from[src]);
+  for (int s = gwarp; s < max_rows; s += nw) {
+    for (int i = 0; i < a.W; ++i) {
+      const int src = (a.rank + 1 + i + gwarp) % a.W;
+      if (s >= rows_from[src]) continue;
+      char* dbase = reinterpret_cast<char*>(a.peer_base[src]);
+      uint4* ret = reinterpret_cast<uint4*>(dbase + a.off_ret_x) + (size_t)a.rank * a.cap * vec;
       const int* inv = inv_rows + ((size_t)src * a.cap + s) * a.k;
       int plist[8];
       float wl[8];
@@ -780,14 +816,16 @@ void ep_dispatch(const EpArgs& a, const void* x, const int* dst_tk, const int* m
 
 void ep_recv_count_scan(const EpArgs& a, const int* dst_tk, const int* meta_tk, const float* topk_w,
                         const int* self_tok, const int* send_count, int G, int cap_rows, int* rows_from,
-                        int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, cudaStream_t st) {
+                        int* chunk_cnt, int* group_off, int* group_cnt, int* pad_off, cudaStream_t st,
+                        int* need, int* miss) {
   if (G > 1024) throw std::runtime_error("at most 1024 local experts");
   if (a.k > 8) throw std::runtime_error("top-k above 8 is not supported by the permute kernel");
   const int nchunks = ((a.cap + kChunk - 1) / kChunk) * a.W;
   recv_count_kernel<<<nchunks, kChunk, 0, st>>>(a, dst_tk, topk_w, self_tok, meta_tk, send_count, rows_from,
                                                 chunk_cnt, G);
   check_launch("recv_count");
-  recv_scan_kernel<<<1, 1024, 0, st>>>(a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows);
+  recv_scan_kernel<<<1, 1024, 0, st>>>(a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows, need,
+                                       miss);
   check_launch("recv_scan");
 }
 
@@ -894,18 +932,38 @@ __global__ void noalloc_init_kernel(int* scratch, int T, int k) {
   }
 }
 
+// The scratch array's device address on the current device. The address is looked up
+// once per device and primary context: a cudaDeviceReset destroys the context (and the
+// module holding the array), so the cache also remembers which context the address
+// belongs to and looks it up again when the current context is a different one.
 int* noalloc_scratch_for_current_device(int* dev_out) {
   static int* ptrs[64] = {nullptr};
+  static CUcontext ctxs[64] = {nullptr};
   static std::mutex mu;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   *dev_out = dev;
   std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
+  // cudaFree(0) makes the runtime create (or bind) this device's primary context, so the
+  // driver call below sees it
+  using CtxGetCurrent = CUresult (*)(CUcontext*);
+  static CtxGetCurrent get_ctx = nullptr;
+  if (!get_ctx) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return nullptr;
+    get_ctx = reinterpret_cast<CtxGetCurrent>(fn);
+  }
+  CUcontext ctx = nullptr;
+  if (cudaFree(nullptr) != cudaSuccess || get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return nullptr;
+  if (!ptrs[dev] || ctxs[dev] != ctx) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_sepx_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) return nullptr;
     ptrs[dev] = static_cast<int*>(p);
+    ctxs[dev] = ctx;
   }
   return ptrs[dev];
 }
@@ -928,6 +986,12 @@ extern "C" int sepx_moe_permute_noalloc(const void* x, const int* topk_e, const 
   if ((long long)cap_rows < (long long)T * k + 64LL * E) return noalloc_fail(5, "cap_rows must be >= T*k + 64*E");
   if (!x || !topk_e || !topk_w || !xp || !group_off || !row_w || !row_src || !inv_rows || !status)
     return noalloc_fail(6, "null pointer argument");
+  // rows of x and xp are read and written as 16-byte vectors
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(xp)) & 15)
+    return noalloc_fail(8, "x and xp must be 16-byte aligned");
+  // an error left by earlier work on this thread is not ours: report it without clearing it
+  if (cudaPeekAtLastError() != cudaSuccess)
+    return noalloc_fail(9, "a CUDA error from earlier work is pending on this thread");
   int dev = -1;
   int* s = noalloc_scratch_for_current_device(&dev);
   if (!s) return noalloc_fail(7, "cudaGetSymbolAddress failed for the scratch array on the current device");

@@ -137,6 +137,12 @@ class ExpertParallel:
             raise ValueError("fp8 dispatch needs hidden % 128 == 0")
         self.stats_on = False  # traffic statistics of forward dispatches (enable_stats)
         self._reset_stats()
+        # row budgets of a pass (begin_pass / end_pass): receive buffers sized ahead of
+        # the device-side count, so no layer waits for a device->host read
+        self._budget: list[int] = []
+        self._pass = None
+        self._need = torch.zeros(1024, dtype=torch.int32, device=self.device)
+        self._miss = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     # -------------------------------------------------------------------------------
     def _reset_stats(self):
@@ -206,6 +212,52 @@ class ExpertParallel:
     def _args(self):
         return self.done, self.status, self.timeout_s
 
+    # -------------------------------------------------------------------------------
+    # Row budgets: no host sync inside a pass
+    # -------------------------------------------------------------------------------
+    # budget = rows needed when learned x margin (64-row steps); after an overflow, the
+    # rows that call needed x the growth factor. Routing drifts while a model trains, so
+    # the margin is generous: a miss costs a second forward, the margin only memory.
+    budget_margin = 1.25
+    budget_growth = 1.5
+
+    def begin_pass(self):
+        """Start a pass of layer calls (e.g. one model forward). Inside a pass, the i-th
+        ``dispatch_fwd`` sizes its receive buffers (and so every saved activation of that
+        layer) from a row budget learned for call i instead of reading the received row
+        count back to the host, so the host never waits on the device between layers.
+        The first pass learns the budgets with exact sizes. A call whose rows exceed its
+        budget empties its layout and raises a device flag; ``end_pass`` reports it and
+        the caller runs the pass again, with the budget grown to fit."""
+        self._pass = 0
+
+    def _set_budget(self, idx: int, rows: int, margin: float):
+        want = min(self.cap_rows, (int(rows * margin) + 64 + 63) // 64 * 64)
+        while len(self._budget) <= idx:
+            self._budget.append(0)
+        self._budget[idx] = max(self._budget[idx], want)
+
+    def end_pass(self) -> bool:
+        """Close the pass; True if some call overflowed its budget (on any rank of the
+        default process group) and the pass must be run again. One small device->host
+        read (after a MAX all-reduce of the flag when ranks run together)."""
+        n, self._pass = self._pass, None
+        if not n:
+            return False
+        flag = self._miss.clone()
+        if dist.is_available() and dist.is_initialized():
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        vals = torch.cat([flag, self._need[:n]]).tolist()
+        self._miss.zero_()
+        missed, need = bool(vals[0]), vals[1:]
+        if self.stats_on:
+            self.stat_recv_rows.extend(need)
+        if missed:
+            for i, r in enumerate(need):
+                if i >= len(self._budget) or r > self._budget[i]:
+                    self._set_budget(i, r, self.budget_growth)
+        return missed
+
     def set_local_slots(self, G: int):
         """Number of local expert groups the receive side lays out (primaries plus, with
         speculative replication, the replica cache slots)."""
@@ -247,21 +299,33 @@ class ExpertParallel:
         group_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
         group_cnt = torch.empty(G, dtype=torch.int32, device=dev)
         pad_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
-        self.comm.recv_count_scan(dst_tk, meta_tk, topk_w, self_tok, send_count, G, T, self.cap_rows, ep,
-                                  rows_from, chunk_cnt, group_off, group_cnt, pad_off, self.done[0:1], self.status,
-                                  self.timeout_s)
-        # One small device->host read per layer sizes every buffer of this layer exactly
-        # (saved activations included); the receive capacity is the true worst case.
+        idx = self._pass
+        budget = 0
+        if idx is not None and not static_rows and idx < len(self._budget) and idx < self._need.numel():
+            budget = self._budget[idx]
+        need = self._need[idx:idx + 1] if budget else None
+        self.comm.recv_count_scan(dst_tk, meta_tk, topk_w, self_tok, send_count, G, T,
+                                  budget if budget else self.cap_rows, ep, rows_from, chunk_cnt, group_off, group_cnt,
+                                  pad_off, self.done[0:1], self.status, self.timeout_s, need,
+                                  self._miss if budget else None)
         if static_rows:
             R = self.cap_rows
+        elif budget:
+            R = budget  # inside a pass: no host sync; end_pass checks the budget held
         else:
+            # Outside a pass (or learning a budget): one small device->host read sizes every
+            # buffer of this layer exactly; the receive capacity is the true worst case.
             R = max(int(group_off[G].item()), 1)
             self.rows_last = R
+            if idx is not None and idx < self._need.numel():
+                self._set_budget(idx, R, self.budget_margin)
+        if idx is not None:
+            self._pass = idx + 1
         if self.stats_on:
             self.stat_sent += send_count
             self.stat_copies += ((dst_tk >= 0) & (dst_tk != self.rank)).sum()
             self.stat_tokens += T
-            if not static_rows:
+            if not static_rows and not budget:
                 self.stat_recv_rows.append(R)
         xp = torch.empty(R, self.H, dtype=torch.bfloat16, device=dev)
         row_w = torch.empty(R, dtype=torch.float32, device=dev)

@@ -10,7 +10,12 @@
   every rank) each see only the tokens routed to their copy; their gradients are summed
   over the EP group before the update, so every copy takes the same step.
 * Expert replicas across DP groups (EP < world) are all-reduced over the replica group
-  before their in-backward update.
+  before their in-backward update. The all-reduce of a layer's expert gradients runs
+  asynchronously on NCCL's stream while the backward of the next-lower layer computes;
+  the update of those weights is applied one layer later (and the last ones after the
+  backward), so the expert-DP traffic overlaps compute instead of blocking it. The fused
+  wgrad + 8-bit AdamW epilogue is not used in that case: it never materialises the
+  gradient, and the update needs the gradient summed over the replicas.
 * Optimizer state precision is chosen per parameter group to fit the memory budget:
   fp32 master + moments where they fit, block-wise 8-bit moments otherwise.
 """
@@ -52,7 +57,9 @@ class Trainer:
         if fuse_expert_optimizer is None:  # the 8-bit fused epilogue is the faster path
             fuse_expert_optimizer = expert_state == "8bit"
         self.fuse_expert_optimizer = fuse_expert_optimizer
-        model.set_grad_sink(_ExpertUpdater(self))
+        self.expert_updater = _ExpertUpdater(self)
+        model.set_grad_sink(self.expert_updater)
+        self.budget_retries = 0  # forwards run again because a row budget overflowed
         self.buckets = _GradBuckets(self.dense, self.dp_group, self.bucket_bytes) if self.world > 1 else None
 
     def _sync_dense_grads(self):
@@ -60,12 +67,30 @@ class Trainer:
         if self.buckets is not None:
             self.buckets.finish()
 
+    def _forward(self, input_ids, labels, num_valid):
+        """The loss, with the MoE layers' receive buffers sized by row budgets (no host
+        wait between layers). If some layer's rows outgrew its budget on any rank, the
+        forward is discarded (nothing was updated yet) and run again with the grown
+        budgets; the first step learns the budgets with exact sizes."""
+        ep = getattr(self.model, "ep", None)
+        if ep is None or not hasattr(ep, "begin_pass"):
+            return self.model(input_ids, labels, num_valid)
+        for _ in range(4):
+            ep.begin_pass()
+            loss = self.model(input_ids, labels, num_valid)
+            if not ep.end_pass():
+                return loss
+            self.budget_retries += 1
+            del loss
+        raise RuntimeError("MoE receive-row budgets kept overflowing")
+
     def train_step(self, input_ids, labels, num_valid=None):
         """One optimizer step on a device-resident batch; returns the (device) loss."""
         if self.buckets is not None:
             self.buckets.begin()
-        loss = self.model(input_ids, labels, num_valid)
+        loss = self._forward(input_ids, labels, num_valid)
         loss.backward()
+        self.expert_updater.flush()
         self._sync_dense_grads()
         self.opt.step()
         return loss.detach()
@@ -205,6 +230,10 @@ class _ExpertUpdater:
     gradient and the streaming optimizer kernel applies it.
     """
 
+    # gradients whose expert-DP all-reduce may still be in flight: one layer's two
+    # weights, while the next-lower layer's backward computes
+    depth = 2
+
     def __init__(self, trainer):
         self.t = trainer
         ep = getattr(trainer.model, "ep", None)
@@ -212,12 +241,27 @@ class _ExpertUpdater:
         self.ep_group = ep.group if ep is not None else None
         use = trainer.fuse_expert_optimizer and trainer.expert_world == 1 and not self.rep_slots
         self.fused_wgrad = trainer.opt.fused_wgrad if use else None
+        self.pending = []  # (param, grad, work) with the expert-DP all-reduce in flight
 
     def __call__(self, p, g):
         t = self.t
         if self.rep_slots:
             sum_replica_grads(g, self.rep_slots, self.ep_group)
         if t.expert_world > 1:
-            dist.all_reduce(g, group=t.expert_dp_group)
-            g.mul_(1.0 / t.expert_world)
+            # start the replica all-reduce now; apply the update once it is needed
+            work = dist.all_reduce(g, group=t.expert_dp_group, async_op=True)
+            self.pending.append((p, g, work))
+            while len(self.pending) > self.depth:
+                self._apply(*self.pending.pop(0))
+            return
         t.opt.apply_now(p, g)
+
+    def _apply(self, p, g, work):
+        work.wait()  # the compute stream waits for NCCL's; the host does not block
+        g.mul_(1.0 / self.t.expert_world)
+        self.t.opt.apply_now(p, g)
+
+    def flush(self):
+        """Apply every update still waiting for its all-reduce (end of the backward)."""
+        while self.pending:
+            self._apply(*self.pending.pop(0))

@@ -121,3 +121,47 @@ def test_ep_layers_replayed_as_cuda_graph_match_eager():
     del graph
     graph_ep.close()
     eager_ep.close()
+
+
+def test_row_budget_pass_matches_exact_sizes_and_recovers_from_overflow():
+    """Inside begin_pass / end_pass the receive buffers come from learned row budgets
+    (no device->host read per layer). The result equals the exact-size path bit for bit;
+    a budget that is too small empties the layer, raises the miss flag, and the pass
+    run again with the grown budget gives the exact result."""
+    from spec_ep.parallel.ep import ExpertParallel, ep_moe
+
+    torch.manual_seed(1)
+    T, E, k, H, I = 512, 16, 4, 256, 256
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    p = torch.softmax(torch.randn(T, E, device="cuda"), -1)
+    tw, te = p.topk(k, -1)
+    tw = tw / tw.sum(-1, keepdim=True)
+    w_gu = (torch.randn(E, 2 * I, H, device="cuda") / H**0.5).bfloat16()
+    w_d = (torch.randn(E, H, I, device="cuda") / I**0.5).bfloat16()
+    ep = ExpertParallel(E, k, H, max_tokens=T)
+
+    def layers():  # two layer calls per pass
+        y = ep_moe(x, te.int(), tw, w_gu, w_d, ep)
+        return ep_moe(y, te.int(), tw, w_gu, w_d, ep)
+
+    exact = layers()  # outside a pass: exact sizes
+    ep.begin_pass()
+    learn = layers()  # first pass: learns the budgets (exact sizes)
+    assert not ep.end_pass()
+    assert len(ep._budget) == 2 and all(b >= T * k for b in ep._budget)
+    ep.begin_pass()
+    budgeted = layers()  # no host read between the layers
+    assert not ep.end_pass()
+    assert torch.equal(learn, exact) and torch.equal(budgeted, exact)
+    ep._budget = [64, 64]  # far too small: the first call overflows
+    ep.begin_pass()
+    layers()
+    assert ep.end_pass()  # reported, and the budgets grown
+    assert all(b >= T * k for b in ep._budget)
+    ep.begin_pass()
+    again = layers()
+    assert not ep.end_pass()
+    torch.cuda.synchronize()
+    ep.check()  # an overflowed budget is not an error
+    assert torch.equal(again, exact)
+    ep.close()
