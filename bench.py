@@ -17,7 +17,16 @@ back to the host.
 ``dispatch_combine_us_per_layer`` is measured separately on the MoE-layer shape
 (hidden 2048, 4096 tokens/rank, 128 experts, top-8, Zipf s=1.0 routing) with identity
 experts, so it is the pure dispatch+combine cost, on the contiguous expert layout the
-reference uses. ``dispatch_combine_us_per_layer_planned`` repeats it with the
+reference uses; it is the mean over routing seeds 0-4 (per-seed values alongside).
+
+``check`` is a correctness figure taken on the same ranks before anything is timed: one
+small expert-parallel MoE forward + backward (512 tokens/rank, 16 experts, top-4, hidden
+512) through the fused kernels against an fp32 PyTorch MoE holding all experts; the
+largest relative error of the output and of every gradient, max over ranks.
+
+The expert optimizer state is block-wise 8-bit at every world size by default (the only
+precision that fits all experts of the model on one GPU), so every point of the scaling
+curve runs the same optimizer; ``--expert-state fp32`` selects fp32 state where it fits. ``dispatch_combine_us_per_layer_planned`` repeats it with the
 speculative placement: experts packed by the load of a *previous* batch's routing (seed
 1) and the 16 hottest replicated on every rank, measured on the seed-0 batch.
 
@@ -53,8 +62,12 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="override depth (smoke runs only; invalid for the bench)")
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--micro-batch", type=int, default=1)
-    ap.add_argument("--expert-state", choices=["auto", "fp32", "8bit"], default="auto")
+    ap.add_argument("--expert-state", choices=["auto", "fp32", "8bit"], default="8bit",
+                    help="expert optimizer state; 8bit (default) at every N keeps the scaling curve like for like")
     ap.add_argument("--dc-iters", type=int, default=20)
+    ap.add_argument("--ep", type=int, default=None,
+                    help="expert-parallel group size (default: every GPU); world / ep expert-data-parallel "
+                         "replicas, e.g. --gpus 8 --ep 4 for EP=4 x DP=2")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
@@ -115,22 +128,30 @@ def gpu_uuid(dev):
 
 
 # ---------------------------------------------------------------------------------------
-def dispatch_combine_us(ep, dev, rank, world, iters, seed=0):
-    """Identity-expert dispatch + combine on the MoE-layer shape; max over ranks."""
+def dispatch_combine_us(ep, dev, rank, world, iters, seeds=(0, 1, 2, 3, 4)):
+    """Identity-expert dispatch + combine on the MoE-layer shape, max over ranks, for each
+    routing seed; returns (mean µs, per-seed µs, rows per token of seed 0)."""
     from spec_ep.utils.routing import dedup_bound_rows, synthetic_routing
 
-    x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=seed, rank=rank, device=dev)
+    per_seed, bound = [], None
+    for seed in seeds:
+        x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=seed, rank=rank, device=dev)
 
-    def once():
-        st = ep.dispatch_fwd(x, te, tw)
-        ep.combine_fwd(st.xp, st)
+        def once():  # one layer call per pass, with the row budget the training step uses
+            ep.begin_pass()
+            st = ep.dispatch_fwd(x, te, tw)
+            ep.combine_fwd(st.xp, st)
 
-    for _ in range(3):
-        once()
-    ms = timed(once, iters, dev)
-    ep.check()
-    b = dedup_bound_rows(te.cpu(), 128 // world, rank, world)
-    return ms * 1000.0, b
+        for _ in range(3):
+            once()
+        ep.end_pass()  # learn / verify the budget before timing
+        per_seed.append(timed(once, iters, dev) * 1000.0)
+        if ep.end_pass():
+            raise RuntimeError("a dispatch outgrew its row budget inside the timed loop")
+        ep.check()
+        if bound is None:
+            bound = dedup_bound_rows(te.cpu(), 128 // world, rank, world)
+    return sum(per_seed) / len(per_seed), per_seed, bound
 
 
 def dispatch_combine_planned_us(dev, rank, world, iters):
@@ -148,12 +169,16 @@ def dispatch_combine_planned_us(dev, rank, world, iters):
     x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=0, rank=rank, device=dev)
 
     def once():
+        ep.begin_pass()
         st = ep.dispatch_fwd(x, te, tw)
         ep.combine_fwd(st.xp, st)
 
     for _ in range(3):
         once()
+    ep.end_pass()
     ms = timed(once, iters, dev)
+    if ep.end_pass():
+        raise RuntimeError("a dispatch outgrew its row budget inside the timed loop")
     ep.check()
     ep.close()
     return ms * 1000.0
@@ -169,14 +194,23 @@ def run_spec_ep(args):
     from spec_ep.utils.clocks import ClockSampler
 
     C = load()
+    from spec_ep.utils.selfcheck import ep_moe_check
+
+    check = ep_moe_check(dev)  # correctness on these ranks, before anything is timed
     cfg = get_config(args.model)
     if args.layers:
         cfg.num_layers = args.layers
     T = args.seq * args.micro_batch
-    ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=T, device=dev)
+    ep_size = args.ep or world
+    ep_group = dp_group = None
+    if ep_size != world:
+        from spec_ep.integrations.ds_moe import make_groups
+
+        ep_group, dp_group = make_groups(ep_size)
+    ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=T, device=dev, group=ep_group)
     total, expert = cfg.param_counts()
     dense = total - expert
-    local_expert = expert // world
+    local_expert = expert // ep_size
     # saved activations per layer: ~12 [T, H] tensors + the expert rows (x and gate|up),
     # with 1.5x headroom for routing imbalance
     rows = int(1.5 * T * cfg.top_k) + ep.G * 64
@@ -187,7 +221,7 @@ def run_spec_ep(args):
         prec = choose_state_precision(local_expert, dense, budget, act + (4 << 30))
     torch.manual_seed(1234)  # same dense init on every rank (replicated weights)
     model = Qwen3MoeForCausalLM(cfg, ep, device=dev)
-    trainer = Trainer(model, lr=1e-4, expert_state=prec)
+    trainer = Trainer(model, lr=1e-4, expert_state=prec, expert_dp_group=dp_group)
 
     g = torch.Generator().manual_seed(rank)
     ids_cpu = torch.randint(0, cfg.vocab_size, (args.micro_batch, args.seq), generator=g)
@@ -202,9 +236,11 @@ def run_spec_ep(args):
     ep.check()
 
     launches0 = C.launch_count()
+    retries0 = trainer.budget_retries
     with ClockSampler(gpu_uuid(dev)) as clk:
         ms = timed(lambda: trainer.train_step(ids, lab, num_valid), args.steps, dev)
     launches = (C.launch_count() - launches0)
+    retries_timed = trainer.budget_retries - retries0
     clocks = gather_clocks(clk.summary())
     ep.check()
     loss_dev = float(trainer.train_step(ids, lab, num_valid).item())
@@ -224,8 +260,8 @@ def run_spec_ep(args):
                "d2h_bytes_per_step": 4, "api": "spec_ep.train.Trainer.train_step_from_host",
                "last_loss": losses[-1] if losses else None}
 
-    dc_us, bound = dispatch_combine_us(ep, dev, rank, world, args.dc_iters)
-    dc_planned_us = dispatch_combine_planned_us(dev, rank, world, args.dc_iters)
+    dc_us, dc_seeds, bound = dispatch_combine_us(ep, dev, ep.rank, ep.world, args.dc_iters)
+    dc_planned_us = dispatch_combine_planned_us(dev, rank, world, args.dc_iters) if ep_size == world else None
     peak = torch.cuda.max_memory_allocated(dev) / 2**30
     peak = max_over_ranks(peak, dev)
     if rank == 0:
@@ -235,19 +271,31 @@ def run_spec_ep(args):
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform token ids, random-init weights)",
             "config": {"model": "Qwen3-30B-A3B", "global_batch": world * args.micro_batch, "seq_len": args.seq,
-                       "parallelism": f"ep{world}" + (f"+dp{world}(dense)" if world > 1 else ""),
+                       "parallelism": (f"ep{ep_size}" + (f"xdp{world // ep_size}(experts)" if ep_size != world else "")
+                                       + (f"+dp{world}(dense)" if world > 1 else "")),
                        "layers": cfg.num_layers, "experts": cfg.num_experts, "top_k": cfg.top_k,
                        "hidden": cfg.hidden_size, "moe_inter": cfg.moe_intermediate_size,
-                       "optimizer": "AdamW (dense: fp32 master+moments; experts: %s, updated in backward)" % prec,
+                       "optimizer": "AdamW (dense: fp32 master+moments; experts: %s state at every N, updated "
+                                    "in backward)" % prec,
                        "l2": "no flush: every step streams > 60 GB of weights and optimizer state (>> 126 MB L2)",
                        "attention": "torch SDPA (GQA, causal)"},
             "impl": "spec_ep",
             "dispatch_combine_us_per_layer": dc_us,
-            "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0, identity experts",
+            "dispatch_combine_us_per_seed": dc_seeds,
+            "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0 (seeds 0-4), "
+                                      "identity experts",
             "dispatch_combine_us_per_layer_planned": dc_planned_us,
+            "check": {"what": "ep_moe fwd+bwd, 512 tok/rank, 16 experts, top-4, hidden 512, vs fp32 torch MoE; "
+                              "max relative error over ranks",
+                      **check},
+            "check_max_rel_err": check["max"],
             "planned_placement": "LPT packing of the previous batch's loads + top-16 experts replicated on every rank",
             "rows_per_token": bound,
             "loss": loss_dev, "peak_mem_gib": peak,
+            "row_budget_retries": {"total": trainer.budget_retries, "in_timed_steps": retries_timed,
+                                   "what": "forwards run again because an MoE layer's received rows outgrew the "
+                                           "row budget its buffers were sized with (counted, and timed, as "
+                                           "part of the step)"},
             "gpu_launches": launches, "clocks": clocks, "e2e": e2e,
         }
         try:  # fraction of roofline (CPU arithmetic after the timed regions)
@@ -292,20 +340,24 @@ def run_reference(args):
         return
     from spec_ep.utils.routing import synthetic_routing
 
-    x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=0, rank=rank, device=dev)
     if world == 1:
         dist.init_process_group("nccl", init_method="tcp://127.0.0.1:29593", rank=0, world_size=1, device_id=dev)
     local_group, _ = dist.new_subgroups(group_size=world)
+    per_seed = []
+    for seed in range(5):
+        x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=seed, rank=rank, device=dev)
 
-    def once():
-        rbd.RBD_combine_dispatch(x, tw, lambda rows, ids: rows, te.long(), E=128, gpus_per_node=world,
-                                 local_group=local_group, concurrent=True)
+        def once():
+            rbd.RBD_combine_dispatch(x, tw, lambda rows, ids: rows, te.long(), E=128, gpus_per_node=world,
+                                     local_group=local_group, concurrent=True)
 
-    for _ in range(3):
-        once()
-    ms = timed(once, args.dc_iters, dev)
+        for _ in range(3):
+            once()
+        per_seed.append(timed(once, args.dc_iters, dev) * 1000.0)
     if rank == 0:
-        print(json.dumps(reference_record(world, ms * 1000.0, reason)), flush=True)
+        rec = reference_record(world, sum(per_seed) / len(per_seed), reason)
+        rec["dispatch_combine_us_per_seed"] = per_seed
+        print(json.dumps(rec), flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -316,7 +368,8 @@ def reference_record(world: int, dispatch_combine_us: float, reason: str) -> dic
     return {
         "impl": "reference", "metric": METRIC, "unavailable": reason, "n_gpus": world,
         "dispatch_combine_us_per_layer": dispatch_combine_us,
-        "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0, identity experts",
+        "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0 (seeds 0-4), "
+                                  "identity experts",
         "api": "spec_ep.rbd.RBD_combine_dispatch (reference, unmodified, NCCL)",
     }
 
