@@ -408,3 +408,69 @@ def test_replicated_experts_stay_identical_through_training():
     errq = ctx.SimpleQueue()
     mp.spawn(_replica_train_worker, args=(2, _free_port(), errq), nprocs=2, join=True)
     assert errq.empty()
+
+
+def _ep_dp_worker(rank, world, port, errq):
+    """EP over blocks of world / 2 ranks, expert data parallel over the 2 blocks."""
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        from spec_ep.integrations.ds_moe import make_groups
+        from spec_ep.models.config import get_config
+        from spec_ep.models.qwen3_moe import Qwen3MoeForCausalLM
+        from spec_ep.parallel.ep import ExpertParallel
+        from spec_ep.train import Trainer
+
+        ep_size = world // 2
+        ep_group, dp_group = make_groups(ep_size)
+        assert dp_group is not None and dist.get_world_size(dp_group) == 2
+        cfg = get_config("tiny", num_experts=8, top_k=2)
+        T = 256
+        ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=T, group=ep_group, device=dev)
+        torch.manual_seed(0)  # the same initial weights on every rank: replicas start equal
+        model = Qwen3MoeForCausalLM(cfg, ep, device=dev)
+        start = [p.detach().clone() for p in model.expert_parameters()]
+        trainer = Trainer(model, lr=1e-2, expert_state="8bit", expert_dp_group=dp_group)
+        assert trainer.expert_updater.fused_wgrad is None  # replicas need the summed gradient
+        ids = torch.randint(0, cfg.vocab_size, (1, T), device=dev,
+                            generator=torch.Generator(device=dev).manual_seed(10 + rank))
+        labels = torch.cat([ids[:, 1:], torch.full((1, 1), -1, device=dev)], 1).int()
+        losses = [float(trainer.train_step(ids, labels, T - 1)) for _ in range(3)]
+        torch.cuda.synchronize()
+        ep.check()
+        assert all(x == x for x in losses)
+        assert not trainer.expert_updater.pending
+        for p, p0 in zip(model.expert_parameters(), start):
+            got = [torch.empty_like(p) for _ in range(2)]
+            dist.all_gather(got, p.detach().contiguous(), group=dp_group)
+            assert torch.equal(got[0], got[1])  # the two replicas took the same steps
+            assert not torch.equal(p.detach(), p0)  # and the steps moved them
+        for p in model.dense_parameters():
+            got = [torch.empty_like(p) for _ in range(world)]
+            dist.all_gather(got, p.detach().contiguous())
+            for other in got[1:]:
+                assert torch.equal(other, got[0])
+        dist.barrier()
+        ep.close()
+        dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+def test_expert_data_parallel_replicas_stay_identical():
+    """EP x DP training (EP = 2 x DP = 2 on 4 GPUs, EP = 1 x DP = 2 on 2): the expert-DP
+    gradient all-reduce runs asynchronously inside the backward and every replica of an
+    expert takes the same update."""
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = 4 if n >= 4 else 2
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    mp.spawn(_ep_dp_worker, args=(world, _free_port(), errq), nprocs=world, join=True)
+    assert errq.empty()

@@ -245,7 +245,10 @@ def _multi_gpu_worker(rank, world, port, errq):
         from spec_ep.parallel.ep import ExpertParallel
         from spec_ep.parallel.speculative import enable_speculation, speculation_summary
 
-        cfg = get_config("tiny", num_experts=16, top_k=4)
+        # one layer: the speculative and the plain forward then route every token alike
+        # (with more layers, bf16 rounding of the regrouped partial sums can flip a later
+        # layer's top-k choice for near-tied tokens and the outputs stop being comparable)
+        cfg = get_config("tiny", num_experts=16, top_k=4, num_layers=1)
         T, S = 512, 3
         ep = ExpertParallel(cfg.num_experts, cfg.top_k, cfg.hidden_size, max_tokens=T, device=dev)
         torch.manual_seed(0)  # same dense weights on every rank
