@@ -39,8 +39,12 @@ def main():
     ap.add_argument("--rows", type=int, default=2048)
     ap.add_argument("--hidden", type=int, default=2048)
     ap.add_argument("--inter", type=int, default=768)
+    ap.add_argument("--pairs", type=int, default=1, help="256-column tiles on CTA pairs (1) or single CTAs (0)")
     args = ap.parse_args()
     from spec_ep.ops import grouped_gemm as gg
+    from spec_ep.ops._ext import load
+
+    load().gemm_set_pairs(bool(args.pairs))
 
     G, R, H, I = args.experts, args.rows, args.hidden, args.inter
     dev = "cuda"
@@ -89,7 +93,7 @@ def main():
     tb = timeit(lambda: torch.bmm(dy.view(G, R, H).transpose(1, 2), hw.view(G, R, I)), flush=flush)
     res["down_wgrad"] = dict(ms=t, tflops=f / t / 1e9, cublas_bmm_ms=tb, cublas_tflops=f / tb / 1e9)
 
-    print(json.dumps({"shape": dict(G=G, rows=R, hidden=H, inter=I), "results": res}, indent=1))
+    print(json.dumps({"shape": dict(G=G, rows=R, hidden=H, inter=I), "cta_pairs": bool(args.pairs), "results": res}))
 
 
 if __name__ == "__main__":

@@ -225,6 +225,7 @@ void register_kernels(pybind11::module& m);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "spec_ep sm_100a kernels";
   m.def("gg_fwd", &gg_fwd);
+  m.def("gemm_set_pairs", &sepx::gemm_set_pairs, "256-column GEMM tiles on CTA pairs (returns the previous setting)");
   m.def("gg_dgrad", &gg_dgrad);
   m.def("gg_swiglu_fwd", &gg_swiglu_fwd);
   m.def("gg_swiglu_bwd", &gg_swiglu_bwd);

@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -82,7 +83,8 @@ struct TileInfo {
   int num_kb;   // k-blocks
 };
 
-template <bool RAGGED_K, int BN>
+// TM: output rows per tile (128 for one CTA, 256 for a CTA pair).
+template <bool RAGGED_K, int BN, int TM = kBM>
 __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, const int* s_prefix) {
   TileInfo ti;
   if (!RAGGED_K) {
@@ -98,13 +100,13 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
     int n_tile = local - m_tile * p.n_tiles;
     int off0 = __ldg(p.group_off + g);
     ti.g = g;
-    ti.row0 = off0 + m_tile * kBM;
+    ti.row0 = off0 + m_tile * TM;
     ti.row_end = __ldg(p.group_off + g + 1);
     ti.n0 = n_tile * BN;
     ti.k0 = 0;
     ti.num_kb = p.K / kBK;
   } else {
-    int m_tiles = p.M / kBM;
+    int m_tiles = p.M / TM;
     int per_group = m_tiles * p.n_tiles;
     int g = t / per_group;
     int local = t - g * per_group;
@@ -113,7 +115,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
     int off0 = __ldg(p.group_off + g);
     int off1 = __ldg(p.group_off + g + 1);
     ti.g = g;
-    ti.row0 = m_tile * kBM;
+    ti.row0 = m_tile * TM;
     ti.row_end = p.M;
     ti.n0 = n_tile * BN;
     ti.k0 = off0;
@@ -123,6 +125,171 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+
+// One accumulator tile (128 rows x BN fp32 columns in TMEM at t_acc) through the
+// epilogue EPI by the 8 epilogue warps (warps 2..9): rows ti.row0 .. ti.row0 + 127 of the
+// output, valid below ti.row_end. Shared by the single-CTA and the CTA-pair kernels
+// (each CTA of a pair owns 128 rows of the 256-row tile). epi_smem: the CTA's epilogue
+// staging area (32 x 33 fp32 per warp for the transposing epilogues).
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInfo& ti, uint32_t t_acc, int warp,
+                                              int lane, uint8_t* epi_smem) {
+  const int q = warp & 3;            // TMEM lane quarter this warp may access
+  const int half = (warp - 2) >> 2;  // which of the two warps on this quarter
+  constexpr int kCStep = kEpiWarps / 4;
+  const int r = ti.row0 + q * 32 + lane;
+  const bool valid = r < ti.row_end;
+  const uint32_t t_row = t_acc + ((uint32_t)(q * 32) << 16);
+  const bool zero = ti.num_kb == 0;
+
+  if (EPI == kEpiBf16) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+    for (int c = half; c < BN / 32; c += kCStep) {
+      float v[32];
+      tmem_ld32(t_row + c * 32, v);
+      if (valid) {
+        uint4* dst = reinterpret_cast<uint4*>(out + (size_t)r * p.ldo + ti.n0 + c * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 w;
+          w.x = pack_bf16x2(zero ? 0.f : v[8 * j + 0], zero ? 0.f : v[8 * j + 1]);
+          w.y = pack_bf16x2(zero ? 0.f : v[8 * j + 2], zero ? 0.f : v[8 * j + 3]);
+          w.z = pack_bf16x2(zero ? 0.f : v[8 * j + 4], zero ? 0.f : v[8 * j + 5]);
+          w.w = pack_bf16x2(zero ? 0.f : v[8 * j + 6], zero ? 0.f : v[8 * j + 7]);
+          dst[j] = w;
+        }
+      }
+    }
+  } else if (EPI == kEpiF32) {
+    // Transpose each 32x32 fp32 block through shared memory so every store is one
+    // row's 32 contiguous floats (128 bytes per warp instruction).
+    float* out = reinterpret_cast<float*>(p.out);
+    float* tile = reinterpret_cast<float*>(epi_smem) + (warp - 2) * 32 * 33;
+    const size_t row_base = ((size_t)ti.g * p.M + ti.row0 + q * 32) * (size_t)p.ldo;
+#pragma unroll 1
+    for (int c = half; c < BN / 32; c += kCStep) {
+      float v[32];
+      tmem_ld32(t_row + c * 32, v);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) tile[lane * 33 + e] = zero ? 0.f : v[e];
+      __syncwarp();
+      float* dst = out + row_base + ti.n0 + c * 32 + lane;
+#pragma unroll 8
+      for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldo] = tile[i * 33 + lane];
+      __syncwarp();
+    }
+  } else if (EPI == kEpiSwigluFwd) {
+    // accumulator columns [0,128) = gate, [128,256) = up, for I-range [i0, i0+128)
+    const int i0 = ti.n0 / 2;
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out);
+    __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.aux);
+#pragma unroll 1
+    for (int c = half; c < 4; c += kCStep) {
+      float g[32], u[32];
+      tmem_ld32(t_row + c * 32, g);
+      tmem_ld32(t_row + 128 + c * 32, u);
+      if (valid) {
+        uint4* dh = reinterpret_cast<uint4*>(h + (size_t)r * p.ldo + i0 + c * 32);
+        uint4* dg = reinterpret_cast<uint4*>(gu + (size_t)r * p.ld_aux + i0 + c * 32);
+        uint4* du = reinterpret_cast<uint4*>(gu + (size_t)r * p.ld_aux + p.I + i0 + c * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float gg[8], uu[8], hh[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            // round g/u to bf16 first so h is consistent with the stored pre-activation
+            gg[e] = __bfloat162float(__float2bfloat16(g[8 * j + e]));
+            uu[e] = __bfloat162float(__float2bfloat16(u[8 * j + e]));
+            hh[e] = silu_f(gg[e]) * uu[e];
+          }
+          dg[j] = make_uint4(pack_bf16x2(gg[0], gg[1]), pack_bf16x2(gg[2], gg[3]),
+                             pack_bf16x2(gg[4], gg[5]), pack_bf16x2(gg[6], gg[7]));
+          du[j] = make_uint4(pack_bf16x2(uu[0], uu[1]), pack_bf16x2(uu[2], uu[3]),
+                             pack_bf16x2(uu[4], uu[5]), pack_bf16x2(uu[6], uu[7]));
+          dh[j] = make_uint4(pack_bf16x2(hh[0], hh[1]), pack_bf16x2(hh[2], hh[3]),
+                             pack_bf16x2(hh[4], hh[5]), pack_bf16x2(hh[6], hh[7]));
+        }
+      }
+    }
+  } else if (EPI == kEpiSwigluBwd) {
+    // accumulator = dh_unweighted[r, i0 : i0+BN]; gate weight w = row_w[r]
+    const int i0 = ti.n0;
+    const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux);
+    __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(p.out);
+    __nv_bfloat16* hw = reinterpret_cast<__nv_bfloat16*>(p.aux2);
+    const float w = valid ? __ldg(p.row_w + r) : 0.f;
+    float dw_part = 0.f;
+#pragma unroll 1
+    for (int c = half; c < BN / 32; c += kCStep) {
+      float d[32];
+      tmem_ld32(t_row + c * 32, d);
+      if (valid) {
+        const uint4* sg = reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + i0 + c * 32);
+        const uint4* su =
+            reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + p.I + i0 + c * 32);
+        uint4* og = reinterpret_cast<uint4*>(dgu + (size_t)r * p.ldo + i0 + c * 32);
+        uint4* ou = reinterpret_cast<uint4*>(dgu + (size_t)r * p.ldo + p.I + i0 + c * 32);
+        uint4* oh = reinterpret_cast<uint4*>(hw + (size_t)r * p.ld_aux2 + i0 + c * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 gv = sg[j], uv = su[j];
+          uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+          uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+          uint32_t rg[4], ru[4], rh[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 g2 = unpack_bf16x2(gw[e]);
+            float2 u2 = unpack_bf16x2(uw[e]);
+            float dd0 = d[8 * j + 2 * e], dd1 = d[8 * j + 2 * e + 1];
+            float s0 = 1.f / (1.f + __expf(-g2.x)), s1 = 1.f / (1.f + __expf(-g2.y));
+            float si0 = g2.x * s0, si1 = g2.y * s1;
+            float h0 = si0 * u2.x, h1 = si1 * u2.y;
+            dw_part += dd0 * h0 + dd1 * h1;
+            float wd0 = w * dd0, wd1 = w * dd1;
+            float dg0 = wd0 * u2.x * s0 * (1.f + g2.x * (1.f - s0));
+            float dg1 = wd1 * u2.y * s1 * (1.f + g2.y * (1.f - s1));
+            rg[e] = pack_bf16x2(dg0, dg1);
+            ru[e] = pack_bf16x2(wd0 * si0, wd1 * si1);
+            rh[e] = pack_bf16x2(w * h0, w * h1);
+          }
+          og[j] = make_uint4(rg[0], rg[1], rg[2], rg[3]);
+          ou[j] = make_uint4(ru[0], ru[1], ru[2], ru[3]);
+          oh[j] = make_uint4(rh[0], rh[1], rh[2], rh[3]);
+        }
+      }
+    }
+    if (valid && p.row_dw) atomicAdd(p.row_dw + r, dw_part);
+  } else if (EPI == kEpiAdamW) {
+    // fp32 state. The weight gradient never leaves the SM. Each 32x32 fp32 block (32
+    // rows of this warp's lane quarter x 32 columns) is transposed through shared
+    // memory so that the warp then updates one row's 32 contiguous weights per step,
+    // one per lane (coalesced).
+    float* tile = reinterpret_cast<float*>(epi_smem) + (warp - 2) * 32 * 33;
+    const size_t row_base = ((size_t)ti.g * p.M + ti.row0 + q * 32) * (size_t)p.N;
+#pragma unroll 1
+    for (int c = half; c < BN / 32; c += kCStep) {
+      float v[32];
+      tmem_ld32(t_row + c * 32, v);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) tile[lane * 33 + e] = zero ? 0.f : v[e];
+      __syncwarp();
+      const size_t col = (size_t)ti.n0 + c * 32 + lane;
+#pragma unroll 1
+      for (int i = 0; i < 32; i += 4) {
+        float g4[4];
+        size_t idx[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          g4[u] = tile[(i + u) * 33 + lane];
+          idx[u] = row_base + (size_t)(i + u) * p.N + col;
+        }
+        adamw_fp32_lanes<4>(g4, idx, p.opt);
+      }
+      __syncwarp();
+    }
+  }
+}
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -314,15 +481,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int njobs = my_tiles * J;
     const AdamCoef kc = adam_coef(p.opt);
     const int nb_row = p.N / 32;
-    auto job_pos = [&](int j, int& grow, int& col0, TileInfo& ti) {
-      ti = decode_tile<RAGGED_K, BN>((int)blockIdx.x + (j / J) * (int)gridDim.x, p, s_prefix);
-      grow = ti.g * p.M + ti.row0 + q * 32;
-      col0 = ti.n0 + (half + (j % J) * kCStep) * 32;
+    // Tile decoding (integer divisions, group offsets) happens once per tile and stream of
+    // jobs: the TMA issue, the scale prefetch and the update each walk the jobs in order,
+    // so each keeps the last tile it decoded.
+    struct TileMemo {
+      int tt = -1;
+      TileInfo ti;
     };
+    auto job_pos = [&](int j, int& grow, int& col0, TileInfo& ti, TileMemo& memo) {
+      const int tt = j / J;
+      if (tt != memo.tt) {
+        memo.ti = decode_tile<RAGGED_K, BN>((int)blockIdx.x + tt * (int)gridDim.x, p, s_prefix);
+        memo.tt = tt;
+      }
+      ti = memo.ti;
+      grow = ti.g * p.M + ti.row0 + q * 32;
+      col0 = ti.n0 + (half + (j - tt * J) * kCStep) * 32;
+    };
+    TileMemo memo_issue, memo_scale, memo_main;
     auto issue = [&](int j) {  // lane 0
       int grow, col0;
       TileInfo ti;
-      job_pos(j, grow, col0, ti);
+      job_pos(j, grow, col0, ti, memo_issue);
       const int s = j % kOptRing;
       uint8_t* b = ring + s * kOptJob;
       mbar_arrive_expect_tx(&obar[s], kOptJob);
@@ -335,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j >= njobs) return;
       int grow, col0;
       TileInfo ti;
-      job_pos(j, grow, col0, ti);
+      job_pos(j, grow, col0, ti, memo_scale);
       const size_t bi = (size_t)(grow + lane) * nb_row + col0 / 32;
       ms = p.opt.m_scale[bi];
       vs = p.opt.v_scale[bi];
@@ -351,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < njobs; ++j) {
       int grow, col0;
       TileInfo ti;
-      job_pos(j, grow, col0, ti);
+      job_pos(j, grow, col0, ti, memo_main);
       const int ci = j % J;
       float nms, nvs;
       load_scales(j + 1, nms, nvs);
@@ -436,167 +616,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // --------------------------------- epilogue --------------------------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;  // which of the two warps on this quarter
-    constexpr int kCStep = kEpiWarps / 4;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       TileInfo ti = decode_tile<RAGGED_K, BN>(t, p, s_prefix);
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, s_abort, p.status, p.timeout_ns)) break;
       tc_fence_after();
-      const int r = ti.row0 + q * 32 + lane;
-      const bool valid = r < ti.row_end;
-      const uint32_t t_row = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
-      const bool zero = ti.num_kb == 0;
-
-      if (EPI == kEpiBf16) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
-#pragma unroll 1
-        for (int c = half; c < BN / 32; c += kCStep) {
-          float v[32];
-          tmem_ld32(t_row + c * 32, v);
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(out + (size_t)r * p.ldo + ti.n0 + c * 32);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 w;
-              w.x = pack_bf16x2(zero ? 0.f : v[8 * j + 0], zero ? 0.f : v[8 * j + 1]);
-              w.y = pack_bf16x2(zero ? 0.f : v[8 * j + 2], zero ? 0.f : v[8 * j + 3]);
-              w.z = pack_bf16x2(zero ? 0.f : v[8 * j + 4], zero ? 0.f : v[8 * j + 5]);
-              w.w = pack_bf16x2(zero ? 0.f : v[8 * j + 6], zero ? 0.f : v[8 * j + 7]);
-              dst[j] = w;
-            }
-          }
-        }
-      } else if (EPI == kEpiF32) {
-        // Transpose each 32x32 fp32 block through shared memory so every store is one
-        // row's 32 contiguous floats (128 bytes per warp instruction).
-        float* out = reinterpret_cast<float*>(p.out);
-        float* tile = reinterpret_cast<float*>(smem + L::EPI_STAGE_OFF) + (warp - 2) * 32 * 33;
-        const size_t row_base = ((size_t)ti.g * p.M + ti.row0 + q * 32) * (size_t)p.ldo;
-#pragma unroll 1
-        for (int c = half; c < BN / 32; c += kCStep) {
-          float v[32];
-          tmem_ld32(t_row + c * 32, v);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) tile[lane * 33 + e] = zero ? 0.f : v[e];
-          __syncwarp();
-          float* dst = out + row_base + ti.n0 + c * 32 + lane;
-#pragma unroll 8
-          for (int i = 0; i < 32; ++i) dst[(size_t)i * p.ldo] = tile[i * 33 + lane];
-          __syncwarp();
-        }
-      } else if (EPI == kEpiSwigluFwd) {
-        // accumulator columns [0,128) = gate, [128,256) = up, for I-range [i0, i0+128)
-        const int i0 = ti.n0 / 2;
-        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out);
-        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(p.aux);
-#pragma unroll 1
-        for (int c = half; c < 4; c += kCStep) {
-          float g[32], u[32];
-          tmem_ld32(t_row + c * 32, g);
-          tmem_ld32(t_row + 128 + c * 32, u);
-          if (valid) {
-            uint4* dh = reinterpret_cast<uint4*>(h + (size_t)r * p.ldo + i0 + c * 32);
-            uint4* dg = reinterpret_cast<uint4*>(gu + (size_t)r * p.ld_aux + i0 + c * 32);
-            uint4* du = reinterpret_cast<uint4*>(gu + (size_t)r * p.ld_aux + p.I + i0 + c * 32);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float gg[8], uu[8], hh[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                // round g/u to bf16 first so h is consistent with the stored pre-activation
-                gg[e] = __bfloat162float(__float2bfloat16(g[8 * j + e]));
-                uu[e] = __bfloat162float(__float2bfloat16(u[8 * j + e]));
-                hh[e] = silu_f(gg[e]) * uu[e];
-              }
-              dg[j] = make_uint4(pack_bf16x2(gg[0], gg[1]), pack_bf16x2(gg[2], gg[3]),
-                                 pack_bf16x2(gg[4], gg[5]), pack_bf16x2(gg[6], gg[7]));
-              du[j] = make_uint4(pack_bf16x2(uu[0], uu[1]), pack_bf16x2(uu[2], uu[3]),
-                                 pack_bf16x2(uu[4], uu[5]), pack_bf16x2(uu[6], uu[7]));
-              dh[j] = make_uint4(pack_bf16x2(hh[0], hh[1]), pack_bf16x2(hh[2], hh[3]),
-                                 pack_bf16x2(hh[4], hh[5]), pack_bf16x2(hh[6], hh[7]));
-            }
-          }
-        }
-      } else if (EPI == kEpiSwigluBwd) {
-        // accumulator = dh_unweighted[r, i0 : i0+BN]; gate weight w = row_w[r]
-        const int i0 = ti.n0;
-        const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux);
-        __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(p.out);
-        __nv_bfloat16* hw = reinterpret_cast<__nv_bfloat16*>(p.aux2);
-        const float w = valid ? __ldg(p.row_w + r) : 0.f;
-        float dw_part = 0.f;
-#pragma unroll 1
-        for (int c = half; c < BN / 32; c += kCStep) {
-          float d[32];
-          tmem_ld32(t_row + c * 32, d);
-          if (valid) {
-            const uint4* sg = reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + i0 + c * 32);
-            const uint4* su =
-                reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + p.I + i0 + c * 32);
-            uint4* og = reinterpret_cast<uint4*>(dgu + (size_t)r * p.ldo + i0 + c * 32);
-            uint4* ou = reinterpret_cast<uint4*>(dgu + (size_t)r * p.ldo + p.I + i0 + c * 32);
-            uint4* oh = reinterpret_cast<uint4*>(hw + (size_t)r * p.ld_aux2 + i0 + c * 32);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 gv = sg[j], uv = su[j];
-              uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-              uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
-              uint32_t rg[4], ru[4], rh[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float2 g2 = unpack_bf16x2(gw[e]);
-                float2 u2 = unpack_bf16x2(uw[e]);
-                float dd0 = d[8 * j + 2 * e], dd1 = d[8 * j + 2 * e + 1];
-                float s0 = 1.f / (1.f + __expf(-g2.x)), s1 = 1.f / (1.f + __expf(-g2.y));
-                float si0 = g2.x * s0, si1 = g2.y * s1;
-                float h0 = si0 * u2.x, h1 = si1 * u2.y;
-                dw_part += dd0 * h0 + dd1 * h1;
-                float wd0 = w * dd0, wd1 = w * dd1;
-                float dg0 = wd0 * u2.x * s0 * (1.f + g2.x * (1.f - s0));
-                float dg1 = wd1 * u2.y * s1 * (1.f + g2.y * (1.f - s1));
-                rg[e] = pack_bf16x2(dg0, dg1);
-                ru[e] = pack_bf16x2(wd0 * si0, wd1 * si1);
-                rh[e] = pack_bf16x2(w * h0, w * h1);
-              }
-              og[j] = make_uint4(rg[0], rg[1], rg[2], rg[3]);
-              ou[j] = make_uint4(ru[0], ru[1], ru[2], ru[3]);
-              oh[j] = make_uint4(rh[0], rh[1], rh[2], rh[3]);
-            }
-          }
-        }
-        if (valid && p.row_dw) atomicAdd(p.row_dw + r, dw_part);
-      } else if (EPI == kEpiAdamW) {
-        // fp32 state. The weight gradient never leaves the SM. Each 32x32 fp32 block (32
-        // rows of this warp's lane quarter x 32 columns) is transposed through shared
-        // memory so that the warp then updates one row's 32 contiguous weights per step,
-        // one per lane (coalesced).
-        float* tile = reinterpret_cast<float*>(smem + L::EPI_STAGE_OFF) + (warp - 2) * 32 * 33;
-        const size_t row_base = ((size_t)ti.g * p.M + ti.row0 + q * 32) * (size_t)p.N;
-#pragma unroll 1
-        for (int c = half; c < BN / 32; c += kCStep) {
-          float v[32];
-          tmem_ld32(t_row + c * 32, v);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) tile[lane * 33 + e] = zero ? 0.f : v[e];
-          __syncwarp();
-          const size_t col = (size_t)ti.n0 + c * 32 + lane;
-#pragma unroll 1
-          for (int i = 0; i < 32; i += 4) {
-            float g4[4];
-            size_t idx[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              g4[u] = tile[(i + u) * 33 + lane];
-              idx[u] = row_base + (size_t)(i + u) * p.N + col;
-            }
-            adamw_fp32_lanes<4>(g4, idx, p.opt);
-          }
-          __syncwarp();
-        }
-      }
+      epilogue_tile<BN, EPI>(p, ti, tmem_base + acc * BN, warp, lane, smem + L::EPI_STAGE_OFF);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -618,6 +644,236 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
   }
+}
+
+// =====================================================================================
+// CTA-pair kernel: one tcgen05.mma.cta_group::2 per k-step over a 256-row x BN tile.
+//
+// A cluster of two CTAs on two SMs shares each MMA: every CTA TMA-loads its own 128 rows
+// of A and its own BN/2 rows (columns of the product) of B from this GPU's memory into
+// its own shared memory, and receives its 128 accumulator rows in its own TMEM. Per SM
+// the tensor core then streams half of the B tile a single-CTA MMA of the same output
+// width would, which is what keeps shared-memory bandwidth below the tensor-core rate at
+// N = 256 (a single CTA at M = 128, N = 256 needs 96 B/clk of operand reads plus the TMA
+// writes, beyond the SM's shared-memory bandwidth).
+//
+// Roles per CTA as in the single-CTA kernel (warp 0 TMA, warp 1 MMA, warps 2..9
+// epilogue), except that only the leader CTA (cluster rank 0) issues MMAs:
+//   full[s]   leader only; the leader's producer expects both CTAs' bytes, both CTAs'
+//             loads complete on it
+//   empty[s]  per CTA; the leader's MMA thread commits to both after the stage's MMAs
+//   tfull[a]  per CTA; committed to both when a tile's MMAs are done
+//   tempty[a] leader only; both CTAs' epilogue warps arrive (2 x 8 arrivals)
+// No load uses multicast; the only cross-CTA traffic is mbarrier arrivals and the MMA's
+// own reads of the peer's operand tiles.
+// =====================================================================================
+template <int BN, int STAGES, int EPI>
+struct PairSmem {
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = (BN / 2) * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI_STAGE_OFF = STAGES * STAGE_BYTES;
+  static constexpr int EPI_STAGE_BYTES = (EPI == kEpiAdamW || EPI == kEpiF32) ? kEpiWarps * 32 * 33 * 4 : 0;
+  static constexpr int BAR_OFF = EPI_STAGE_OFF + EPI_STAGE_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
+  static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
+  static constexpr int PREFIX_OFF = MISC_OFF + 16;
+  static size_t bytes(int G) { return 1024 + PREFIX_OFF + 4 * (size_t)(G + 1); }
+};
+
+constexpr int kPairM = 2 * kBM;
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                             const GemmParams p) {
+  static_assert(BN == 256, "the pair kernel covers 256 output columns per tile");
+  static_assert(EPI != kEpiAdamW8, "the 8-bit optimizer epilogue runs in the single-CTA kernel");
+  using L = PairSmem<BN, STAGES, EPI>;
+  constexpr int BH = BN / 2;  // B rows (product columns) held by each CTA
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+  int* s_prefix = reinterpret_cast<int*>(smem + L::PREFIX_OFF);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();
+  const bool leader = cta == 0;
+  const int cluster = (int)cluster_id_x();
+  const int nclusters = (int)num_clusters_x();
+
+  if (!RAGGED_K && threadIdx.x == 0) {
+    int acc = 0;
+    for (int g = 0; g < p.G; ++g) {
+      s_prefix[g] = acc;
+      const int rows = __ldg(p.group_off + g + 1) - __ldg(p.group_off + g);
+      acc += ((rows + kPairM - 1) / kPairM) * p.n_tiles;
+    }
+    s_prefix[p.G] = acc;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 2 * kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total_tiles = RAGGED_K ? p.G * (p.M / kPairM) * p.n_tiles : s_prefix[p.G];
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer -------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = cluster; t < total_tiles && ok; t += nclusters) {
+        const TileInfo ti = decode_tile<RAGGED_K, BN, kPairM>(t, p, s_prefix);
+        const int my_row0 = ti.row0 + (int)cta * kBM;  // this CTA's rows (ragged M) / m columns (ragged K)
+        for (int kb = 0; kb < ti.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, s_abort, p.status, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * L::STAGE_BYTES;
+          uint8_t* sB = sA + L::A_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::STAGE_BYTES);
+          const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (!A_MN) {
+            tma_load_2d_pair(sA, &tmA, fb, kb * kBK, my_row0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j)
+              tma_load_2d_pair(sA + j * 8192, &tmA, fb, my_row0 + j * 64, ti.k0 + kb * kBK);
+          }
+          if (!B_MN) {
+            int brow;
+            if (EPI == kEpiSwigluFwd) {  // leader: gate rows, peer: up rows of the same I range
+              brow = ti.g * p.b_rows_per_group + (int)cta * p.I + ti.n0 / 2;
+            } else {
+              brow = ti.g * p.b_rows_per_group + ti.n0 + (int)cta * BH;
+            }
+            tma_load_2d_pair(sB, &tmB, fb, kb * kBK, brow);
+          } else {
+            const int krow = RAGGED_K ? (ti.k0 + kb * kBK) : (ti.g * p.b_rows_per_group + kb * kBK);
+#pragma unroll
+            for (int j = 0; j < BH / 64; ++j)
+              tma_load_2d_pair(sB + j * 8192, &tmB, fb, ti.n0 + (int)cta * BH + j * 64, krow);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------- MMA issuer (leader CTA only) -------------------------
+    if (leader) {
+      constexpr uint32_t idesc = make_idesc_bf16(kPairM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = cluster; t < total_tiles && ok; t += nclusters) {
+        const TileInfo ti = decode_tile<RAGGED_K, BN, kPairM>(t, p, s_prefix);
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1, s_abort, p.status, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < ti.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, s_abort, p.status, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t a_addr = smem_u32(smem + stage * L::STAGE_BYTES);
+            const uint32_t b_addr = a_addr + L::A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              uint64_t adesc, bdesc;
+              if (!A_MN) adesc = make_smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+              else adesc = make_smem_desc_sw128(a_addr + kk * 2048, 8192, 1024);
+              if (!B_MN) bdesc = make_smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+              else bdesc = make_smem_desc_sw128(b_addr + kk * 2048, 8192, 1024);
+              umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            const uint32_t eb = smem_u32(&empty_bar[stage]);
+            umma_commit_pair(mapa_shared(eb, 0));
+            umma_commit_pair(mapa_shared(eb, 1));
+          }
+          __syncwarp();
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        if (lane == 0) {
+          const uint32_t tb = smem_u32(&tfull_bar[acc]);
+          umma_commit_pair(mapa_shared(tb, 0));
+          umma_commit_pair(mapa_shared(tb, 1));
+        }
+        __syncwarp();
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else {
+    // ----------------------------- epilogue (both CTAs) -----------------------------
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster; t < total_tiles; t += nclusters) {
+      TileInfo ti = decode_tile<RAGGED_K, BN, kPairM>(t, p, s_prefix);
+      ti.row0 += (int)cta * kBM;
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, s_abort, p.status, p.timeout_ns)) break;
+      tc_fence_after();
+      epilogue_tile<BN, EPI>(p, ti, tmem_base + acc * BN, warp, lane, smem + L::EPI_STAGE_OFF);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1 && leader && *s_abort) {
+    // drain: wait (bounded) for any MMA this thread issued before the TMEM is released
+    if (lane == 0) umma_commit_pair(mapa_shared(smem_u32(drain_bar), 0));
+    __syncwarp();
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(drain_bar, 0) && globaltimer_ns() - t0 < p.timeout_ns) {
+    }
+  }
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still read its operands or TMEM
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, 2 * BN);
 }
 
 // =====================================================================================
@@ -684,6 +940,39 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
   if (e != cudaSuccess) throw std::runtime_error(std::string("grouped_gemm launch: ") + cudaGetErrorString(e));
 }
 
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int max_tiles,
+                        cudaStream_t stream) {
+  using L = PairSmem<BN, STAGES, EPI>;
+  auto kern = grouped_gemm_pair_kernel<BN, STAGES, A_MN, B_MN, RAGGED_K, EPI>;
+  const size_t smem = L::bytes(p.G);
+  static unsigned long long smem_devices = 0;
+  smem_optin_once(kern, 232448, smem_devices);
+  int clusters = num_sms() / 2;
+  if (max_tiles > 0 && max_tiles < clusters) clusters = max_tiles;
+  if (clusters < 1) clusters = 1;
+  kern<<<2 * clusters, kThreads, smem, stream>>>(ta, tb, p);
+  note_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("grouped_gemm (pair) launch: ") + cudaGetErrorString(e));
+}
+
+// CTA pairs for the 256-column tiles: on unless SEPX_GEMM_PAIR=0 or gemm_set_pairs(false)
+// (single-CTA tiles, for comparison).
+static int g_pairs = -1;
+static bool use_pairs() {
+  if (g_pairs < 0) {
+    const char* v = std::getenv("SEPX_GEMM_PAIR");
+    g_pairs = (v && v[0] == '0') ? 0 : 1;
+  }
+  return g_pairs == 1;
+}
+bool gemm_set_pairs(bool on) {
+  const bool prev = use_pairs();
+  g_pairs = on ? 1 : 0;
+  return prev;
+}
+
 // ---------------------------------------------------------------------------------
 // Forward / dgrad: D[rows, N] = A[rows, K] . B_g   (ragged M)
 //   b_kmajor: B stored [G * N_b, K] (weights as [out, in]);  else B stored [G * K, N].
@@ -698,8 +987,13 @@ void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream) {
     if (!c.b_kmajor) throw std::runtime_error("swiglu fwd expects K-major weights");
     if (p.I % 128) throw std::runtime_error("SwiGLU intermediate must be a multiple of 128");
     p.n_tiles = p.I / 128;
-    max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
     CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
+    if (use_pairs()) {
+      launch_pair<256, 6, false, false, false, kEpiSwigluFwd>(ta, tb, p, (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles,
+                                                              stream);
+      return;
+    }
+    max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
     launch<256, 4, false, false, false, kEpiSwigluFwd>(ta, tb, p, max_tiles, stream);
     return;
   }
@@ -707,8 +1001,13 @@ void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream) {
     if (c.b_kmajor) throw std::runtime_error("swiglu bwd expects MN-major weights");
     if (p.N % 256) throw std::runtime_error("N must be a multiple of 256");
     p.n_tiles = p.N / 256;
-    max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
     CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
+    if (use_pairs()) {
+      launch_pair<256, 6, false, true, false, kEpiSwigluBwd>(ta, tb, p, (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles,
+                                                             stream);
+      return;
+    }
+    max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
     launch<256, 4, false, true, false, kEpiSwigluBwd>(ta, tb, p, max_tiles, stream);
     return;
   }
@@ -716,12 +1015,15 @@ void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream) {
   if (p.N % 256 == 0) {
     p.n_tiles = p.N / 256;
     max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
+    const int pair_tiles = (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles;
     if (c.b_kmajor) {
       CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
-      launch<256, 4, false, false, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
+      if (use_pairs()) launch_pair<256, 6, false, false, false, kEpiBf16>(ta, tb, p, pair_tiles, stream);
+      else launch<256, 4, false, false, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
     } else {
       CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
-      launch<256, 4, false, true, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
+      if (use_pairs()) launch_pair<256, 6, false, true, false, kEpiBf16>(ta, tb, p, pair_tiles, stream);
+      else launch<256, 4, false, true, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
     }
   } else if (p.N % 128 == 0) {
     p.n_tiles = p.N / 128;
@@ -749,6 +1051,10 @@ void grouped_gemm_ragged_k(const GemmCall& c, cudaStream_t stream) {
   CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
   if (p.N % 256 == 0) {
     p.n_tiles = p.N / 256;
+    if (use_pairs() && p.M % 256 == 0) {
+      launch_pair<256, 5, true, true, true, kEpiF32>(ta, tb, p, p.G * (p.M / 256) * p.n_tiles, stream);
+      return;
+    }
     int max_tiles = p.G * (p.M / 128) * p.n_tiles;
     launch<256, 3, true, true, true, kEpiF32>(ta, tb, p, max_tiles, stream);
   } else if (p.N % 128 == 0) {

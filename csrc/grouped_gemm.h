@@ -54,5 +54,8 @@ void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream);
 void grouped_gemm_ragged_k(const GemmCall& c, cudaStream_t stream);
 // weight gradient with the AdamW update fused into the epilogue (c.p.opt describes W)
 void grouped_gemm_wgrad_adamw(const GemmCall& c, cudaStream_t stream);
+// Whether 256-column tiles run on CTA pairs (tcgen05.mma.cta_group::2); returns the
+// previous setting.
+bool gemm_set_pairs(bool on);
 
 }  // namespace sepx

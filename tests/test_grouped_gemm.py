@@ -192,3 +192,59 @@ def test_wgrad_adamw_fused_matches_unfused(kind, M, N, G):
             assert torch.equal(o1.state[id(p1)][k_], o2.state[id(p2)][k_]), k_
     # the empty group still got weight decay + moment decay, and parameters moved
     assert not torch.equal(p1.detach(), w0)
+
+
+@pytest.mark.parametrize("mode", ["fwd", "dgrad", "swiglu_fwd", "swiglu_bwd", "wgrad"])
+def test_cta_pair_tiles_match_single_cta_tiles(mode):
+    """The 256-column tiles on CTA pairs (tcgen05.mma.cta_group::2) give the single-CTA
+    kernel's result on ragged groups, including groups shorter than one 128-row half."""
+    from spec_ep.ops import grouped_gemm as gg
+    from spec_ep.ops._ext import load
+
+    C = load()
+    torch.manual_seed(5)
+    sizes = [300, 0, 64, 1000, 130, 17]
+    off = _offsets(sizes, 64 if mode == "wgrad" else 1)
+    R, G, K, N, I = off[-1], len(sizes), 512, 512, 256
+    go = torch.tensor(off, dtype=torch.int32, device="cuda")
+    a = torch.randn(R, K, device="cuda").bfloat16()
+
+    def run():
+        st = _status()
+        if mode == "fwd":
+            out = gg.gg_fwd(a, (torch.randn(G, N, K, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+                                / K**0.5).bfloat16(), go, status=st)
+        elif mode == "dgrad":
+            out = gg.gg_dgrad(a, (torch.randn(G, K, N, device="cuda", generator=torch.Generator("cuda").manual_seed(2))
+                                  / K**0.5).bfloat16(), go, status=st)
+        elif mode == "swiglu_fwd":
+            w = (torch.randn(G, 2 * I, K, device="cuda", generator=torch.Generator("cuda").manual_seed(3))
+                 / K**0.5).bfloat16()
+            out = torch.cat(gg.gg_swiglu_fwd(a, w, go, status=st), 1)
+        elif mode == "swiglu_bwd":
+            wd = (torch.randn(G, K, I, device="cuda", generator=torch.Generator("cuda").manual_seed(4))
+                  / K**0.5).bfloat16()
+            gu = torch.randn(R, 2 * I, device="cuda", generator=torch.Generator("cuda").manual_seed(5)).bfloat16()
+            row_w = torch.rand(R, device="cuda", generator=torch.Generator("cuda").manual_seed(6))
+            dgu, hw, row_dw = gg.gg_swiglu_bwd(a, wd, go, gu, row_w, status=st)
+            out = torch.cat([dgu.float(), hw.float(), row_dw[:, None]], 1)
+        else:
+            b = torch.randn(R, N, device="cuda", generator=torch.Generator("cuda").manual_seed(7)).bfloat16()
+            out = gg.gg_wgrad(a, b, go, G, status=st)
+        torch.cuda.synchronize()
+        assert st.item() == 0
+        return out.float()
+
+    prev = C.gemm_set_pairs(True)
+    try:
+        paired = run()
+        C.gemm_set_pairs(False)
+        single = run()
+    finally:
+        C.gemm_set_pairs(prev)
+    valid = torch.ones(paired.shape[0], dtype=torch.bool, device="cuda")
+    if mode != "wgrad":  # rows of the ragged layout that belong to no group are not written
+        valid[:] = False
+        for g, s in enumerate(sizes):
+            valid[off[g]:off[g] + s] = True
+    torch.testing.assert_close(paired[valid], single[valid], rtol=1e-3, atol=1e-3)
