@@ -57,7 +57,33 @@ def main():
     with sdpa_kernel(SDPBackend.FLASH_ATTENTION):
         ms, mib = bench(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True))
     out["attention_sdpa_flash"] = {"ms": ms, "tflops": flops / ms / 1e9, "peak_mib": mib}
+    del q, k, v
+    out["model_projections"] = model_projections()
     print(json.dumps(out, indent=1))
+
+
+def model_projections(T=4096):
+    """The Qwen3-30B-A3B dense projections at 4096 tokens: forward, input gradient and
+    weight gradient on the tcgen05 GEMM (spec_ep.ops.linear) vs cuBLAS (torch.matmul)."""
+    from spec_ep.ops.linear import dense_dgrad, dense_fwd, dense_wgrad
+
+    res = {}
+    for name, K, N in (("qkv", 2048, 5120), ("o_proj", 4096, 2048), ("router", 2048, 128),
+                       ("lm_head", 2048, 151936)):
+        x = torch.randn(T, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+        gy = torch.randn(T, N, device="cuda", dtype=torch.bfloat16)
+        f = 2 * T * K * N
+        row = {}
+        for op, ours, lib in (("fwd", lambda: dense_fwd(x, w), lambda: x @ w.t()),
+                              ("dgrad", lambda: dense_dgrad(gy, w), lambda: gy @ w),
+                              ("wgrad", lambda: dense_wgrad(gy, x), lambda: gy.t() @ x)):
+            ms, _ = bench(ours)
+            ms_lib, _ = bench(lib)
+            row[op] = {"ms": ms, "tflops": f / ms / 1e9, "cublas_ms": ms_lib, "cublas_tflops": f / ms_lib / 1e9}
+        res[name] = row
+        del x, w, gy
+    return res
 
 
 if __name__ == "__main__":

@@ -104,12 +104,17 @@ __device__ __forceinline__ float enc_scale_v(float vmax) { return vmax > 0.f ? _
 
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
-// Two elements of one AdamW step in packed fp32x2 arithmetic (sm_100 FFMA2/FMUL2).
-__device__ __forceinline__ float2 adamw_step2(float2 w, float2 g, float2& m, float2& v, float2& sq,
-                                              const AdamCoef& k) {
+// Moment updates of two elements (packed fp32x2): m, v in place, sq = sqrt(v).
+__device__ __forceinline__ void adam_moments2(float2 g, float2& m, float2& v, float2& sq, const AdamCoef& k) {
   m = __ffma2_rn(f2(k.b1), m, __fmul2_rn(f2(k.c1), g));
   v = __ffma2_rn(f2(k.b2), v, __fmul2_rn(__fmul2_rn(f2(k.c2), g), g));
   sq = make_float2(sqrt_approx(v.x), sqrt_approx(v.y));
+}
+
+// Two elements of one AdamW step in packed fp32x2 arithmetic (sm_100 FFMA2/FMUL2).
+__device__ __forceinline__ float2 adamw_step2(float2 w, float2 g, float2& m, float2& v, float2& sq,
+                                              const AdamCoef& k) {
+  adam_moments2(g, m, v, sq, k);
   const float2 den = __ffma2_rn(sq, f2(k.bc2), f2(k.eps));
   const float2 r = make_float2(rcp_approx(den.x), rcp_approx(den.y));
   return __ffma2_rn(f2(-k.lr_bc1), __fmul2_rn(m, r), __fmul2_rn(w, f2(k.decay)));

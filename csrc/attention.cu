@@ -880,6 +880,12 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* 
 
 // =====================================================================================
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  // driver call: bind the device's primary context on this thread first (see grouped_gemm.cu)
+  static thread_local bool bound = false;
+  if (!bound) {
+    cudaFree(nullptr);
+    bound = true;
+  }
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     void* ptr = nullptr;

@@ -187,6 +187,38 @@ void gg_wgrad(const at::Tensor& A, const at::Tensor& B, const at::Tensor& group_
   sepx::grouped_gemm_ragged_k(c, cur_stream());
 }
 
+// out (bf16 [M, N]) = A^T . B over all rows, A [rows, M], B [rows, N]: the weight gradient
+// of a dense projection (one group; rows a multiple of 64).
+void gemm_wgrad_bf16(const at::Tensor& A, const at::Tensor& B, const at::Tensor& group_off, at::Tensor& out,
+                     const c10::optional<at::Tensor>& status) {
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_BF16(out);
+  CHECK_DTYPE(group_off, at::kInt);
+  TORCH_CHECK(A.size(0) == B.size(0) && A.size(0) % 64 == 0, "rows must match and be a multiple of 64");
+  TORCH_CHECK(group_off.numel() == 2, "group_off must be the device tensor [0, rows]");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const at::Tensor& go = group_off;
+  sepx::GemmCall c;
+  c.epi = sepx::kEpiBf16;
+  c.A = A.data_ptr();
+  c.a_rows = A.size(0);
+  c.lda = A.size(1);
+  c.B = B.data_ptr();
+  c.b_rows = B.size(0);
+  c.ldb = B.size(1);
+  c.b_kmajor = false;
+  c.p.group_off = go.data_ptr<int>();
+  c.p.G = 1;
+  c.p.M = out.size(0);
+  c.p.N = out.size(1);
+  TORCH_CHECK(A.size(1) == c.p.M && B.size(1) == c.p.N, "shape mismatch");
+  c.p.out = out.data_ptr();
+  c.p.ldo = out.size(1);
+  c.p.status = status_ptr(status);
+  sepx::grouped_gemm_ragged_k(c, cur_stream());
+}
+
 // W[g] <- AdamW(W[g], A[rows_g]^T . B[rows_g]): weight gradient with the optimizer update
 // fused into the GEMM epilogue (the gradient never reaches HBM). W is [G, M, N].
 void gg_wgrad_adamw(const at::Tensor& A, const at::Tensor& B, const at::Tensor& group_off, at::Tensor& W,
@@ -225,6 +257,7 @@ void register_kernels(pybind11::module& m);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "spec_ep sm_100a kernels";
   m.def("gg_fwd", &gg_fwd);
+  m.def("gemm_wgrad_bf16", &gemm_wgrad_bf16);
   m.def("gemm_set_pairs", &sepx::gemm_set_pairs, "256-column GEMM tiles on CTA pairs (returns the previous setting)");
   m.def("gg_dgrad", &gg_dgrad);
   m.def("gg_swiglu_fwd", &gg_swiglu_fwd);

@@ -44,6 +44,8 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kEpiWarps = 8;                 // two warps per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
+__host__ __device__ constexpr int epi_warps(int) { return kEpiWarps; }
+__host__ __device__ constexpr int threads_for(int epi) { return 64 + 32 * epi_warps(epi); }
 // fused 8-bit optimizer epilogue: one job = 32 rows x 32 columns of W (bf16, 64B-swizzled)
 // + m codes + v codes (uint8, 32B-swizzled), streamed by TMA three jobs deep per warp
 constexpr int kOptJob = 4096;  // w 2048 B @0, m 1024 B @2048, v 1024 B @3072
@@ -53,6 +55,14 @@ __host__ __device__ constexpr int opt_ring(int bn) { return bn == 256 ? 3 : 5; }
 struct OptMaps {  // kEpiAdamW8 state tensor maps over [G * M, N]
   CUtensorMap w, m, v;
 };
+
+// Output tensor maps of the TMA-store epilogues (bf16, box 32 columns x 32 rows, 64-byte
+// swizzle): out, aux, aux2 as in GemmParams.
+struct EpiMaps {
+  CUtensorMap out, aux, aux2;
+};
+// Per epilogue warp: three 32 x 32 bf16 staging blocks (2 KB each) for TMA stores.
+constexpr int kEpiStoreBytes = 3 * 2048;
 
 template <int BN, int STAGES, int EPI>
 struct GemmSmem {
@@ -66,7 +76,7 @@ struct GemmSmem {
   static constexpr int EPI_STAGE_BYTES =
       (EPI == kEpiAdamW || EPI == kEpiF32)
           ? kEpiWarps * 32 * 33 * 4
-          : (EPI == kEpiAdamW8 ? kEpiWarps * opt_ring(BN) * (kOptJob + 8) : 0);
+          : (EPI == kEpiAdamW8 ? epi_warps(EPI) * opt_ring(BN) * (kOptJob + 8) : 0);
   static constexpr int BAR_OFF = EPI_STAGE_OFF + EPI_STAGE_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
@@ -108,8 +118,9 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
   } else {
     int m_tiles = p.M / TM;
     int per_group = m_tiles * p.n_tiles;
-    int g = t / per_group;
-    int local = t - g * per_group;
+    int gi = t / per_group;
+    int local = t - gi * per_group;
+    const int g = s_prefix[gi];  // ragged K: groups in order of decreasing rows (group_order)
     int m_tile = local / p.n_tiles;
     int n_tile = local - m_tile * p.n_tiles;
     int off0 = __ldg(p.group_off + g);
@@ -122,6 +133,26 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmParams& p, cons
     ti.num_kb = (off1 - off0) / kBK;
   }
   return ti;
+}
+
+// Ragged K (weight gradients): a tile's MMA time grows with its group's rows, so the
+// persistent CTAs take tiles in order of decreasing group rows (ties by group index):
+// the long tiles are dealt out first, one per CTA, and the short ones even out the end
+// (longest-processing-time order for the static round-robin assignment). order[r] = group
+// of rank r. Every thread of the CTA calls it; scratch holds G ints and is free until the
+// first TMA load; the caller synchronises before order is read.
+__device__ __forceinline__ void group_order(const GemmParams& p, int* order, int* scratch) {
+  for (int i = threadIdx.x; i < p.G; i += blockDim.x) scratch[i] = __ldg(p.group_off + i + 1) - __ldg(p.group_off + i);
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.G; i += blockDim.x) {
+    const int si = scratch[i];
+    int rank = 0;
+    for (int j = 0; j < p.G; ++j) {
+      const int sj = scratch[j];
+      rank += (sj > si) || (sj == si && j < i);
+    }
+    order[rank] = i;
+  }
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
@@ -292,7 +323,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for(EPI), 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmParams p,
                         const __grid_constant__ OptMaps om) {
@@ -314,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---- tile prefix (ragged M): tiles of group g = ceil(rows_g / BM) * n_tiles ----
   int total_tiles;
+  if (RAGGED_K) group_order(p, s_prefix, reinterpret_cast<int*>(smem));
   if (!RAGGED_K) {
     if (threadIdx.x == 0) {
       int acc = 0;
@@ -333,12 +365,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], kEpiWarps);
+      mbar_init(&tempty_bar[a], epi_warps(EPI));
     }
     mbar_init(drain_bar, 1);
     if (EPI == kEpiAdamW8) {
-      uint64_t* obars = reinterpret_cast<uint64_t*>(smem + L::EPI_STAGE_OFF + kEpiWarps * opt_ring(BN) * kOptJob);
-      for (int i = 0; i < kEpiWarps * opt_ring(BN); ++i) mbar_init(&obars[i], 1);
+      uint64_t* obars = reinterpret_cast<uint64_t*>(smem + L::EPI_STAGE_OFF + epi_warps(EPI) * opt_ring(BN) * kOptJob);
+      for (int i = 0; i < epi_warps(EPI) * opt_ring(BN); ++i) mbar_init(&obars[i], 1);
     }
     *s_abort = 0;
     fence_barrier_init();
@@ -461,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
-  } else if (EPI == kEpiAdamW8) {
+  } else if constexpr (EPI == kEpiAdamW8) {
     // -------------------- epilogue: weight gradient -> 8-bit AdamW --------------------
     // Thread = one accumulator row (TMEM lane); one 32-column TMEM load = one 8-bit
     // quantisation block of W, so the update needs no shuffles. W, m and v of each
@@ -646,6 +678,142 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Writes one 32 x 32 bf16 block (this thread's row: 32 floats, scaled to bf16) into a
+// 64-byte-swizzled staging block: thread = row, 16-byte chunk c lands at chunk c ^ ((row >>
+// 1) & 3), which is the layout a SWIZZLE_64B tensor map stores from, and which spreads the
+// warp's 16-byte writes over all banks.
+__device__ __forceinline__ void stage_row_bf16(uint8_t* blk, int lane, const uint32_t (&w)[16]) {
+  const int sw = (lane >> 1) & 3;
+  uint8_t* row = blk + lane * 64;
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc)
+    *reinterpret_cast<uint4*>(row + ((cc ^ sw) << 4)) = make_uint4(w[4 * cc], w[4 * cc + 1], w[4 * cc + 2], w[4 * cc + 3]);
+}
+
+// One accumulator tile through a bf16-output epilogue whose rows leave by TMA stores:
+// each warp converts a 32-row x 32-column block, stages it in shared memory and one lane
+// stores it with cp.async.bulk.tensor (one 2 KB request instead of 32 rows of scattered
+// 16-byte stores). A warp's 32 rows go out by TMA only when they all lie inside the group;
+// the ragged end of a group takes the per-thread stores of epilogue_tile.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const EpiMaps& em, const TileInfo& ti,
+                                                  uint32_t t_acc, int warp, int lane, uint8_t* stage) {
+  static_assert(EPI == kEpiBf16 || EPI == kEpiSwigluFwd || EPI == kEpiSwigluBwd, "bf16-output epilogues only");
+  const int q = warp & 3;
+  const int half = (warp - 2) >> 2;
+  constexpr int kCStep = kEpiWarps / 4;
+  const int r0w = ti.row0 + q * 32;  // first row of this warp's slab
+  if (r0w >= ti.row_end) return;     // nothing of this warp's rows is in the group
+  if (r0w + 32 > ti.row_end) {       // ragged end of the group: per-thread stores
+    epilogue_tile<BN, EPI>(p, ti, t_acc, warp, lane, nullptr);
+    return;
+  }
+  const int r = r0w + lane;
+  const uint32_t t_row = t_acc + ((uint32_t)(q * 32) << 16);
+  const bool zero = ti.num_kb == 0;
+  auto wait_stage_free = [&]() {  // the previous block's TMA stores have read the staging area
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+  };
+  auto store_blocks = [&](int n, const CUtensorMap* const* maps, const int* cols) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) tma_store_2d(maps[i], stage + i * 2048, cols[i], r0w);
+      bulk_commit();
+    }
+  };
+  if (EPI == kEpiBf16) {
+#pragma unroll 1
+    for (int c = half; c < BN / 32; c += kCStep) {
+      float v[32];
+      tmem_ld32(t_row + c * 32, v);
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(zero ? 0.f : v[2 * j], zero ? 0.f : v[2 * j + 1]);
+      wait_stage_free();
+      stage_row_bf16(stage, lane, w);
+      const CUtensorMap* maps[1] = {&em.out};
+      const int cols[1] = {ti.n0 + c * 32};
+      store_blocks(1, maps, cols);
+    }
+  } else if (EPI == kEpiSwigluFwd) {
+    // accumulator columns [0,128) = gate, [128,256) = up, for I-range [i0, i0+128)
+    const int i0 = ti.n0 / 2;
+#pragma unroll 1
+    for (int c = half; c < 4; c += kCStep) {
+      float g[32], u[32];
+      tmem_ld32(t_row + c * 32, g);
+      tmem_ld32(t_row + 128 + c * 32, u);
+      uint32_t wg[16], wu[16], wh[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        // round g/u to bf16 first so h is consistent with the stored pre-activation
+        const float g0 = __bfloat162float(__float2bfloat16(g[2 * j])), g1 = __bfloat162float(__float2bfloat16(g[2 * j + 1]));
+        const float u0 = __bfloat162float(__float2bfloat16(u[2 * j])), u1 = __bfloat162float(__float2bfloat16(u[2 * j + 1]));
+        wg[j] = pack_bf16x2(g0, g1);
+        wu[j] = pack_bf16x2(u0, u1);
+        wh[j] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+      }
+      wait_stage_free();
+      stage_row_bf16(stage, lane, wg);
+      stage_row_bf16(stage + 2048, lane, wu);
+      stage_row_bf16(stage + 4096, lane, wh);
+      const CUtensorMap* maps[3] = {&em.aux, &em.aux, &em.out};
+      const int cols[3] = {i0 + c * 32, p.I + i0 + c * 32, i0 + c * 32};
+      store_blocks(3, maps, cols);
+    }
+  } else {
+    // SwiGLU backward: accumulator = dh_unweighted[r, i0 : i0+BN]; gate weight w = row_w[r]
+    const int i0 = ti.n0;
+    const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux);
+    const float wr = __ldg(p.row_w + r);
+    float dw_part = 0.f;
+#pragma unroll 1
+    for (int c = half; c < BN / 32; c += kCStep) {
+      const uint4* sg = reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + i0 + c * 32);
+      const uint4* su = reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + p.I + i0 + c * 32);
+      uint4 gv[4], uv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {  // issued before the TMEM load: their latency overlaps it
+        gv[j] = __ldg(sg + j);
+        uv[j] = __ldg(su + j);
+      }
+      float d[32];
+      tmem_ld32(t_row + c * 32, d);
+      uint32_t rg[16], ru[16], rh[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t gw[4] = {gv[j].x, gv[j].y, gv[j].z, gv[j].w};
+        const uint32_t uw[4] = {uv[j].x, uv[j].y, uv[j].z, uv[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 g2 = unpack_bf16x2(gw[e]);
+          const float2 u2 = unpack_bf16x2(uw[e]);
+          const float dd0 = zero ? 0.f : d[8 * j + 2 * e], dd1 = zero ? 0.f : d[8 * j + 2 * e + 1];
+          const float s0 = 1.f / (1.f + __expf(-g2.x)), s1 = 1.f / (1.f + __expf(-g2.y));
+          const float si0 = g2.x * s0, si1 = g2.y * s1;
+          const float h0 = si0 * u2.x, h1 = si1 * u2.y;
+          dw_part += dd0 * h0 + dd1 * h1;
+          const float wd0 = wr * dd0, wd1 = wr * dd1;
+          rg[4 * j + e] = pack_bf16x2(wd0 * u2.x * s0 * (1.f + g2.x * (1.f - s0)),
+                                      wd1 * u2.y * s1 * (1.f + g2.y * (1.f - s1)));
+          ru[4 * j + e] = pack_bf16x2(wd0 * si0, wd1 * si1);
+          rh[4 * j + e] = pack_bf16x2(wr * h0, wr * h1);
+        }
+      }
+      wait_stage_free();
+      stage_row_bf16(stage, lane, rg);
+      stage_row_bf16(stage + 2048, lane, ru);
+      stage_row_bf16(stage + 4096, lane, rh);
+      const CUtensorMap* maps[3] = {&em.out, &em.out, &em.aux2};
+      const int cols[3] = {i0 + c * 32, p.I + i0 + c * 32, i0 + c * 32};
+      store_blocks(3, maps, cols);
+    }
+    if (p.row_dw) atomicAdd(p.row_dw + r, dw_part);
+  }
+}
+
 // =====================================================================================
 // CTA-pair kernel: one tcgen05.mma.cta_group::2 per k-step over a 256-row x BN tile.
 //
@@ -673,7 +841,10 @@ struct PairSmem {
   static constexpr int B_BYTES = (BN / 2) * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_STAGE_OFF = STAGES * STAGE_BYTES;
-  static constexpr int EPI_STAGE_BYTES = (EPI == kEpiAdamW || EPI == kEpiF32) ? kEpiWarps * 32 * 33 * 4 : 0;
+  // fp32 epilogues transpose through 32 x 33 floats per warp; bf16 epilogues stage their
+  // TMA stores (kEpiStoreBytes per warp)
+  static constexpr int EPI_STAGE_BYTES =
+      (EPI == kEpiAdamW || EPI == kEpiF32) ? kEpiWarps * 32 * 33 * 4 : kEpiWarps * kEpiStoreBytes;
   static constexpr int BAR_OFF = EPI_STAGE_OFF + EPI_STAGE_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
@@ -682,11 +853,12 @@ struct PairSmem {
 };
 
 constexpr int kPairM = 2 * kBM;
+constexpr bool epi_tma_store(int epi) { return epi == kEpiBf16 || epi == kEpiSwigluFwd || epi == kEpiSwigluBwd; }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                             const GemmParams p) {
+                             const GemmParams p, const __grid_constant__ EpiMaps em) {
   static_assert(BN == 256, "the pair kernel covers 256 output columns per tile");
   static_assert(EPI != kEpiAdamW8, "the 8-bit optimizer epilogue runs in the single-CTA kernel");
   using L = PairSmem<BN, STAGES, EPI>;
@@ -710,6 +882,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int cluster = (int)cluster_id_x();
   const int nclusters = (int)num_clusters_x();
 
+  if (RAGGED_K) group_order(p, s_prefix, reinterpret_cast<int*>(smem));
   if (!RAGGED_K && threadIdx.x == 0) {
     int acc = 0;
     for (int g = 0; g < p.G; ++g) {
@@ -736,6 +909,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+  }
+  if (epi_tma_store(EPI) && warp >= 2 && lane == 0) {
+    tma_prefetch_desc(&em.out);
+    if (EPI != kEpiBf16) tma_prefetch_desc(EPI == kEpiSwigluFwd ? &em.aux : &em.aux2);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, 2 * BN);
@@ -852,13 +1029,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       ti.row0 += (int)cta * kBM;
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, s_abort, p.status, p.timeout_ns)) break;
       tc_fence_after();
-      epilogue_tile<BN, EPI>(p, ti, tmem_base + acc * BN, warp, lane, smem + L::EPI_STAGE_OFF);
+      if constexpr (epi_tma_store(EPI)) {
+        epilogue_tile_tma<BN, EPI>(p, em, ti, tmem_base + acc * BN, warp, lane,
+                                   smem + L::EPI_STAGE_OFF + (warp - 2) * kEpiStoreBytes);
+      } else {
+        epilogue_tile<BN, EPI>(p, ti, tmem_base + acc * BN, warp, lane, smem + L::EPI_STAGE_OFF);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (epi_tma_store(EPI) && lane == 0) bulk_wait_all();  // this warp's stores are done
+    __syncwarp();
   }
 
   __syncthreads();
@@ -881,6 +1065,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // =====================================================================================
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  // The encoder is a driver call and needs the device's context current on this thread.
+  // A thread that has only selected the device (e.g. autograd's backward worker on device
+  // 0) may not have bound it yet; a no-op runtime call binds the primary context.
+  static thread_local bool bound = false;
+  if (!bound) {
+    cudaFree(nullptr);
+    bound = true;
+  }
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     void* ptr = nullptr;
@@ -934,15 +1126,50 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
   int grid = num_sms();
   if (max_tiles > 0 && max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, p, om);
+  kern<<<grid, threads_for(EPI), smem, stream>>>(ta, tb, p, om);
   note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("grouped_gemm launch: ") + cudaGetErrorString(e));
 }
 
+// Tensor map of a bf16 output [rows, cols] (row stride ld elements) for the TMA-store
+// epilogues: 32 x 32 boxes, 64-byte swizzle (matching stage_row_bf16).
+static CUtensorMap make_tmap_out(const void* base, int64_t rows, int64_t cols, int64_t ld) {
+  CUtensorMap tm;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) & 15) || (cols % 32))
+    throw std::runtime_error("TMA-store output must be 16-byte aligned, 16-byte row stride, 32-column multiple");
+  CUresult r = get_encode_fn()(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return tm;
+}
+
+// Output maps of a call's bf16 epilogue: rows = the call's A rows (ragged M) or, for a
+// one-group weight gradient, M.
+static EpiMaps make_epi_maps(const GemmCall& c, int epi, int64_t rows = -1) {
+  EpiMaps em{};
+  const GemmParams& p = c.p;
+  if (rows < 0) rows = c.a_rows;
+  if (epi == kEpiBf16) {
+    em.out = make_tmap_out(p.out, rows, p.N, p.ldo);
+  } else if (epi == kEpiSwigluFwd) {
+    em.out = make_tmap_out(p.out, c.a_rows, p.I, p.ldo);
+    em.aux = make_tmap_out(p.aux, c.a_rows, 2 * p.I, p.ld_aux);
+  } else if (epi == kEpiSwigluBwd) {
+    em.out = make_tmap_out(p.out, c.a_rows, 2 * p.I, p.ldo);
+    em.aux2 = make_tmap_out(p.aux2, c.a_rows, p.I, p.ld_aux2);
+  }
+  return em;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool RAGGED_K, int EPI>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int max_tiles,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const EpiMaps& em = EpiMaps{}) {
   using L = PairSmem<BN, STAGES, EPI>;
   auto kern = grouped_gemm_pair_kernel<BN, STAGES, A_MN, B_MN, RAGGED_K, EPI>;
   const size_t smem = L::bytes(p.G);
@@ -951,7 +1178,7 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   int clusters = num_sms() / 2;
   if (max_tiles > 0 && max_tiles < clusters) clusters = max_tiles;
   if (clusters < 1) clusters = 1;
-  kern<<<2 * clusters, kThreads, smem, stream>>>(ta, tb, p);
+  kern<<<2 * clusters, kThreads, smem, stream>>>(ta, tb, p, em);
   note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("grouped_gemm (pair) launch: ") + cudaGetErrorString(e));
@@ -989,8 +1216,8 @@ void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream) {
     p.n_tiles = p.I / 128;
     CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
     if (use_pairs()) {
-      launch_pair<256, 6, false, false, false, kEpiSwigluFwd>(ta, tb, p, (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles,
-                                                              stream);
+      launch_pair<256, 5, false, false, false, kEpiSwigluFwd>(ta, tb, p, (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles,
+                                                              stream, make_epi_maps(c, kEpiSwigluFwd));
       return;
     }
     max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
@@ -1003,8 +1230,8 @@ void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream) {
     p.n_tiles = p.N / 256;
     CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
     if (use_pairs()) {
-      launch_pair<256, 6, false, true, false, kEpiSwigluBwd>(ta, tb, p, (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles,
-                                                             stream);
+      launch_pair<256, 5, false, true, false, kEpiSwigluBwd>(ta, tb, p, (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles,
+                                                             stream, make_epi_maps(c, kEpiSwigluBwd));
       return;
     }
     max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
@@ -1012,17 +1239,26 @@ void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream) {
     return;
   }
   if (c.epi != kEpiBf16) throw std::runtime_error("unsupported epilogue for ragged-M GEMM");
+  if (p.N % 256 != 0 && p.N % 32 == 0 && p.N > 256 && p.G == 1 && use_pairs() && c.b_kmajor) {
+    // one group (a dense projection) whose last 256-column tile is partial: B rows past N
+    // load as zeros and the TMA stores clip the output at N (e.g. a vocabulary)
+    p.n_tiles = (p.N + 255) / 256;
+    CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
+    launch_pair<256, 5, false, false, false, kEpiBf16>(ta, tb, p, (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles,
+                                                       stream, make_epi_maps(c, kEpiBf16));
+    return;
+  }
   if (p.N % 256 == 0) {
     p.n_tiles = p.N / 256;
     max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
     const int pair_tiles = (int)((c.a_rows + 255) / 256 + p.G) * p.n_tiles;
     if (c.b_kmajor) {
       CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
-      if (use_pairs()) launch_pair<256, 6, false, false, false, kEpiBf16>(ta, tb, p, pair_tiles, stream);
+      if (use_pairs()) launch_pair<256, 5, false, false, false, kEpiBf16>(ta, tb, p, pair_tiles, stream, make_epi_maps(c, kEpiBf16));
       else launch<256, 4, false, false, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
     } else {
       CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
-      if (use_pairs()) launch_pair<256, 6, false, true, false, kEpiBf16>(ta, tb, p, pair_tiles, stream);
+      if (use_pairs()) launch_pair<256, 5, false, true, false, kEpiBf16>(ta, tb, p, pair_tiles, stream, make_epi_maps(c, kEpiBf16));
       else launch<256, 4, false, true, false, kEpiBf16>(ta, tb, p, max_tiles, stream);
     }
   } else if (p.N % 128 == 0) {
@@ -1049,9 +1285,28 @@ void grouped_gemm_ragged_k(const GemmCall& c, cudaStream_t stream) {
   if (p.M % 128) throw std::runtime_error("M must be a multiple of 128");
   CUtensorMap ta = make_tmap_bf16(c.A, c.a_rows, p.M, c.lda, 64);
   CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.N, c.ldb, 64);
+  if (c.epi == kEpiBf16) {  // one group (a dense weight gradient), bf16 [M, N]
+    if (p.G != 1) throw std::runtime_error("bf16 weight gradients take a single group");
+    if (p.N % 256 == 0) {
+      p.n_tiles = p.N / 256;
+      if (use_pairs() && p.M % 256 == 0) {
+        launch_pair<256, 5, true, true, true, kEpiBf16>(ta, tb, p, (p.M / 256) * p.n_tiles, stream,
+                                                        make_epi_maps(c, kEpiBf16, p.M));
+        return;
+      }
+      launch<256, 3, true, true, true, kEpiBf16>(ta, tb, p, (p.M / 128) * p.n_tiles, stream);
+    } else if (p.N % 128 == 0) {
+      p.n_tiles = p.N / 128;
+      launch<128, 5, true, true, true, kEpiBf16>(ta, tb, p, (p.M / 128) * p.n_tiles, stream);
+    } else {
+      throw std::runtime_error("N must be a multiple of 128");
+    }
+    return;
+  }
   if (p.N % 256 == 0) {
     p.n_tiles = p.N / 256;
-    if (use_pairs() && p.M % 256 == 0) {
+    // pairs pay off when each group reduces over enough rows (per-tile fixed costs)
+    if (use_pairs() && p.M % 256 == 0 && c.a_rows >= 1024LL * p.G) {
       launch_pair<256, 5, true, true, true, kEpiF32>(ta, tb, p, p.G * (p.M / 256) * p.n_tiles, stream);
       return;
     }

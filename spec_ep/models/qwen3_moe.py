@@ -2,7 +2,7 @@
 
 Per layer:
     h = RMSNorm(x)
-    qkv = h @ W_qkv^T                              (one fused projection, cuBLAS)
+    qkv = h @ W_qkv^T                              (one fused projection, tcgen05 GEMM)
     q, k, v = qk_norm_rope(qkv)                    (per-head RMSNorm + RoPE, one kernel)
     x = x + attn(q, k, v) @ W_o^T                  (causal GQA)
     h = RMSNorm(x)
@@ -26,6 +26,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..ops.attention import causal_gqa_attention
+from ..ops.linear import dense_fwd, linear
 from ..ops.loss import lm_head_xent
 from ..ops.norm import rms_norm
 from ..ops.rope import qk_norm_rope
@@ -74,13 +75,13 @@ class Qwen3MoeLayer(nn.Module):
             spec.speculate(x, self.post_norm, self.w_router, cfg.top_k, cfg.rms_norm_eps, cfg.norm_topk_prob,
                            self.router_bias, self.router_logit_bias)
         h = rms_norm(x, self.input_norm, cfg.rms_norm_eps)
-        qkv = F.linear(h, self.w_qkv)
+        qkv = linear(h, self.w_qkv)
         q, k, v = qk_norm_rope(qkv, self.q_norm, self.k_norm, cfg.num_heads, cfg.num_kv_heads, cfg.rms_norm_eps,
                                cfg.rope_theta, pos)
         a = causal_gqa_attention(q, k, v)
-        x = x + F.linear(a, self.w_o)
+        x = x + linear(a, self.w_o)
         h = rms_norm(x, self.post_norm, cfg.rms_norm_eps)
-        logits = F.linear(h, self.w_router).float()
+        logits = linear(h, self.w_router).float()
         if self.router_logit_bias is not None:
             logits = logits + self.router_logit_bias
         topk_w, topk_e = router_topk(logits, cfg.top_k, cfg.norm_topk_prob, self.router_bias)
@@ -127,5 +128,5 @@ class Qwen3MoeForCausalLM(nn.Module):
     def forward(self, input_ids, labels=None, num_valid=None, pos=None):
         h = self.hidden_states(input_ids, pos)
         if labels is None:
-            return h @ self.lm_head.t()
+            return dense_fwd(h, self.lm_head)
         return lm_head_xent(h, self.lm_head, labels.view(-1), num_valid)

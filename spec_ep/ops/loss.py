@@ -1,7 +1,8 @@
 """Language-model head + cross-entropy with a fused loss/gradient kernel.
 
-The logits GEMM is a plain library GEMM (cuBLAS via torch); the softmax cross-entropy
-and its gradient run in one sm_100a kernel that overwrites the bf16 logits with
+The logits GEMM and both gradient GEMMs run on the tcgen05 GEMM (``spec_ep.ops.linear``;
+the vocabulary's last 256-column tile is partial); the softmax cross-entropy and its
+gradient run in one sm_100a kernel that overwrites the bf16 logits with
 ``(softmax - onehot) * scale`` so no fp32 copy of the [T, V] logits is ever stored.
 """
 from __future__ import annotations
@@ -9,13 +10,14 @@ from __future__ import annotations
 import torch
 
 from ._ext import load
+from .linear import dense_dgrad, dense_fwd, dense_wgrad
 
 
 class _LMHeadXent(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, w, labels, num_valid):
         C = load()
-        logits = h @ w.t()  # [T, V] bf16
+        logits = dense_fwd(h, w)  # [T, V] bf16
         loss = torch.empty(h.shape[0], device=h.device, dtype=torch.float32)
         if num_valid is not None:
             scale = 1.0 / max(int(num_valid), 1)
@@ -33,8 +35,8 @@ class _LMHeadXent(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         h, w, dlogits = ctx.saved_tensors
-        dh = dlogits @ w
-        dw = dlogits.t() @ h
+        dh = dense_dgrad(dlogits, w)
+        dw = dense_wgrad(dlogits, h)
         s = g if ctx.dev_scale is None else g * ctx.dev_scale
         return dh * s.to(dh.dtype), dw * s.to(dw.dtype), None, None
 
