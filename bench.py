@@ -17,7 +17,9 @@ back to the host.
 ``dispatch_combine_us_per_layer`` is measured separately on the MoE-layer shape
 (hidden 2048, 4096 tokens/rank, 128 experts, top-8, Zipf s=1.0 routing) with identity
 experts, so it is the pure dispatch+combine cost, on the contiguous expert layout the
-reference uses; it is the mean over routing seeds 0-4 (per-seed values alongside).
+reference uses; it is the mean over routing seeds 0-4 (per-seed values alongside), each
+layer call launched from the host as the training step does. ``..._graph`` replays the
+seed-0 layer from a CUDA graph: the device time alone, without per-call host cost.
 
 ``check`` is a correctness figure taken on the same ranks before anything is timed: one
 small expert-parallel MoE forward + backward (512 tokens/rank, 16 experts, top-4, hidden
@@ -154,6 +156,36 @@ def dispatch_combine_us(ep, dev, rank, world, iters, seeds=(0, 1, 2, 3, 4)):
     return sum(per_seed) / len(per_seed), per_seed, bound
 
 
+def dispatch_combine_graph_us(ep, dev, rank, iters):
+    """The same layer (seed 0) captured once in a CUDA graph and replayed: the device time
+    of dispatch + combine without the host's per-call launch cost (what the layer costs
+    inside a step whose host runs ahead of the GPU). Row budget as in training."""
+    from spec_ep.parallel.ep import EPGraph
+    from spec_ep.utils.routing import synthetic_routing
+
+    x, te, tw = synthetic_routing(4096, 2048, 128, 8, s=1.0, seed=0, rank=rank, device=dev)
+
+    def once():
+        ep.begin_pass()
+        st = ep.dispatch_fwd(x, te, tw)
+        out = ep.combine_fwd(st.xp, st)
+        ep._pass = None  # the replays run no host code; the miss flag is read below
+        return out
+
+    once()
+    ep.end_pass()
+    g = EPGraph(ep, once)
+    us = timed(g.replay, iters, dev) * 1000.0
+    torch.cuda.synchronize(dev)
+    missed = int(ep._miss.item())
+    del g
+    ep.graph_epochs(False)
+    ep.check()
+    if missed:
+        raise RuntimeError("a graph-replayed dispatch outgrew its row budget")
+    return us
+
+
 def dispatch_combine_planned_us(dev, rank, world, iters):
     """Same layer with the placement planned from the previous batch's expert loads."""
     from spec_ep.parallel.ep import ExpertParallel
@@ -261,6 +293,7 @@ def run_spec_ep(args):
                "last_loss": losses[-1] if losses else None}
 
     dc_us, dc_seeds, bound = dispatch_combine_us(ep, dev, ep.rank, ep.world, args.dc_iters)
+    dc_graph_us = dispatch_combine_graph_us(ep, dev, ep.rank, args.dc_iters)
     dc_planned_us = dispatch_combine_planned_us(dev, rank, world, args.dc_iters) if ep_size == world else None
     peak = torch.cuda.max_memory_allocated(dev) / 2**30
     peak = max_over_ranks(peak, dev)
@@ -282,6 +315,7 @@ def run_spec_ep(args):
             "impl": "spec_ep",
             "dispatch_combine_us_per_layer": dc_us,
             "dispatch_combine_us_per_seed": dc_seeds,
+            "dispatch_combine_us_per_layer_graph": dc_graph_us,
             "dispatch_combine_shape": "hidden 2048, 4096 tok/rank, 128 experts, top-8, Zipf s=1.0 (seeds 0-4), "
                                       "identity experts",
             "dispatch_combine_us_per_layer_planned": dc_planned_us,

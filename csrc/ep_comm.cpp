@@ -14,6 +14,8 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <tuple>
+
 #include <algorithm>
 #include <string>
 #include <vector>
@@ -200,6 +202,105 @@ class EpComm {
                          group_off.data_ptr<int>() + G, send_count.data_ptr<int>(), xp.data_ptr(), (int)xp.size(0), st);
   }
 
+  // The whole forward dispatch of one layer call in one host call (the per-call host cost
+  // bounds a layer when nothing else keeps the GPU busy): routing tables (unless given),
+  // route plan, dispatch, receive count + scan, buffer sizing, permute + gather.
+  //   rows_mode > 0: the caller's row budget (need / miss record the outcome);
+  //   rows_mode = 0: exact sizes (one small device->host read); rows_mode < 0: worst case.
+  // Returns (tensors, rows): slot, send_count, self_tok, rows_from, group_off, group_cnt,
+  // xp, row_w, row_src, inv_rows, dst_tk, meta_tk, topk_w (fp32), and the rows of xp.
+  std::tuple<std::vector<at::Tensor>, int64_t> dispatch_forward(
+      const at::Tensor& x, const at::Tensor& topk_e, const at::Tensor& topk_w_in, const at::Tensor& e2r,
+      const at::Tensor& e2l, const c10::optional<at::Tensor>& dst_in, const c10::optional<at::Tensor>& meta_in,
+      int G, int64_t epoch, int64_t rows_mode, int64_t cap_rows, const c10::optional<at::Tensor>& need,
+      const c10::optional<at::Tensor>& miss, at::Tensor& done, at::Tensor& status, double timeout_s, bool fp8) {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.size(1) == args_.H,
+                "x must be contiguous bf16 [T, H]");
+    const int64_t T = x.size(0), W = world_, k = args_.k, cap = args_.cap, H = args_.H;
+    TORCH_CHECK(T <= cap, "more tokens than the communicator capacity");
+    TORCH_CHECK(G >= 1 && G <= 1024, "1..1024 local expert groups");
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    auto i32 = x.options().dtype(at::kInt);
+    at::Tensor dst_tk, meta_tk;
+    if (dst_in.has_value()) {
+      dst_tk = *dst_in;
+      meta_tk = *meta_in;
+    } else {
+      TORCH_CHECK(topk_e.scalar_type() == at::kInt && topk_e.is_contiguous(), "topk_e must be contiguous int32");
+      dst_tk = at::empty({T, k}, i32);
+      meta_tk = at::empty({T, k}, i32);
+      sepx::ep_route_tables(topk_e.data_ptr<int>(), e2r.data_ptr<int>(), e2l.data_ptr<int>(), (int)(T * k),
+                            dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), st);
+    }
+    at::Tensor topk_w = topk_w_in.scalar_type() == at::kFloat && topk_w_in.is_contiguous()
+                            ? topk_w_in
+                            : topk_w_in.to(at::kFloat).contiguous();
+    // every small int32 array of the call in one allocation
+    const int64_t nchunks = W * ((cap + 127) / 128);
+    const int64_t sizes[] = {T * W, W, cap, W, nchunks * G, G + 1, G, G + 1};
+    int64_t total = 0;
+    for (int64_t n : sizes) total += (n + 3) / 4 * 4;  // 16-byte aligned views
+    at::Tensor ints = at::empty({total}, i32);
+    std::vector<at::Tensor> v;
+    int64_t off = 0;
+    for (int64_t n : sizes) {
+      v.push_back(ints.narrow(0, off, n));
+      off += (n + 3) / 4 * 4;
+    }
+    at::Tensor slot = v[0].view({T, W}), send_count = v[1], self_tok = v[2], rows_from = v[3], chunk_cnt = v[4],
+               group_off = v[5], group_cnt = v[6], pad_off = v[7];
+    sepx::ep_route_plan(dst_tk.data_ptr<int>(), (int)T, (int)k, (int)W, slot.data_ptr<int>(),
+                        send_count.data_ptr<int>(), st);
+    auto a = call_args((int)T, 0, epoch, done, status, timeout_s);
+    sepx::ep_dispatch(a, x.data_ptr(), dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), topk_w.data_ptr<float>(),
+                      slot.data_ptr<int>(), self_tok.data_ptr<int>(), send_count.data_ptr<int>(), true, st, fp8);
+    const bool budget = rows_mode > 0;
+    sepx::ep_recv_count_scan(a, dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), topk_w.data_ptr<float>(),
+                             self_tok.data_ptr<int>(), send_count.data_ptr<int>(), G,
+                             budget ? (int)rows_mode : (int)cap_rows, rows_from.data_ptr<int>(),
+                             chunk_cnt.data_ptr<int>(), group_off.data_ptr<int>(), group_cnt.data_ptr<int>(),
+                             pad_off.data_ptr<int>(), st, budget && need.has_value() ? need->data_ptr<int>() : nullptr,
+                             budget && miss.has_value() ? miss->data_ptr<int>() : nullptr);
+    int64_t R;
+    if (rows_mode > 0) {
+      R = rows_mode;
+    } else if (rows_mode < 0) {
+      R = cap_rows;
+    } else {
+      int h = 0;
+      CUDA_OK(cudaMemcpyAsync(&h, group_off.data_ptr<int>() + G, sizeof(int), cudaMemcpyDeviceToHost, st));
+      CUDA_OK(cudaStreamSynchronize(st));
+      R = std::max<int64_t>(h, 1);
+    }
+    at::Tensor xp = at::empty({R, H}, x.options());
+    at::Tensor row_w = at::empty({R}, x.options().dtype(at::kFloat));
+    at::Tensor row_src = at::empty({R}, i32);
+    at::Tensor inv_rows = at::empty({W, cap, k}, i32);
+    sepx::ep_recv_permute_gather(a, x.data_ptr(), dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(),
+                                 topk_w.data_ptr<float>(), self_tok.data_ptr<int>(), send_count.data_ptr<int>(), G,
+                                 rows_from.data_ptr<int>(), chunk_cnt.data_ptr<int>(), group_off.data_ptr<int>(),
+                                 group_cnt.data_ptr<int>(), pad_off.data_ptr<int>(), xp.data_ptr(),
+                                 row_w.data_ptr<float>(), row_src.data_ptr<int>(), inv_rows.data_ptr<int>(), st, fp8);
+    return {{slot, send_count, self_tok, rows_from, group_off, group_cnt, xp, row_w, row_src, inv_rows, dst_tk,
+             meta_tk, topk_w},
+            R};
+  }
+
+  // combine + source reduce of a forward call in one host call; returns the [T, H] output
+  at::Tensor combine_forward(const at::Tensor& y, const at::Tensor& inv_rows, const at::Tensor& row_w,
+                             const at::Tensor& rows_from, const at::Tensor& slot, const at::Tensor& dst_tk,
+                             const c10::optional<at::Tensor>& residual, int64_t T, int64_t epoch, at::Tensor& done,
+                             at::Tensor& status, double timeout_s) {
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    at::Tensor out = at::empty({T, (int64_t)args_.H}, y.options());
+    auto a = call_args((int)T, 1, epoch, done, status, timeout_s);
+    sepx::ep_combine(a, y.data_ptr(), inv_rows.data_ptr<int>(), row_w.data_ptr<float>(), rows_from.data_ptr<int>(),
+                     true, nullptr, st);
+    sepx::ep_source_reduce(a, slot.data_ptr<int>(), dst_tk.data_ptr<int>(),
+                           residual.has_value() ? residual->data_ptr() : nullptr, out.data_ptr(), nullptr, st);
+    return out;
+  }
+
   void wait_rows(const at::Tensor& send_count, at::Tensor& rows_from, int T, int phase, int64_t epoch,
                  at::Tensor& done, at::Tensor& status, double timeout_s) {
     auto a = call_args(T, phase, epoch, done, status, timeout_s);
@@ -299,6 +400,24 @@ class SymmBuffer {
                             cudaMemcpyDeviceToDevice, st));
   }
   int64_t size() const { return (int64_t)bytes_; }
+
+  // All-to-all write bandwidth probe: this rank writes `bytes_per_peer` of src into every
+  // other rank's buffer at offset rank * bytes_per_peer (mode 0: SM stores, 1: TMA bulk).
+  void p2p_write_bench(const at::Tensor& src, int64_t bytes_per_peer, int mode, int blocks,
+                       const at::Tensor& status) {
+    TORCH_CHECK(src.is_cuda() && src.is_contiguous() && src.numel() * src.element_size() >= bytes_per_peer,
+                "src must hold bytes_per_peer bytes");
+    TORCH_CHECK((int64_t)bytes_ >= bytes_per_peer * world_, "buffer too small");
+    sepx::P2PBenchArgs a;
+    for (int r = 0; r < 64; ++r) a.dst[r] = r < world_ ? static_cast<uint8_t*>(peers_[r]) : nullptr;
+    a.src = static_cast<const uint8_t*>(src.data_ptr());
+    a.bytes_per_peer = bytes_per_peer;
+    a.W = world_;
+    a.rank = rank_;
+    a.mode = mode;
+    a.status = status.data_ptr<int>();
+    sepx::p2p_write_bench(a, blocks, at::cuda::getCurrentCUDAStream().stream());
+  }
 
   // Speculative replication: copy the experts named by (fetch_rank[s], fetch_slot[s])
   // from their primary rank's buffer into local cache slot P + s of every region
@@ -422,6 +541,8 @@ void register_ep_comm(pybind11::module& m) {
       .def("route_plan", &EpComm::route_plan)
       .def("dispatch", &EpComm::dispatch)
       .def("recv_count_scan", &EpComm::recv_count_scan)
+      .def("dispatch_forward", &EpComm::dispatch_forward)
+      .def("combine_forward", &EpComm::combine_forward)
       .def("recv_permute_gather", &EpComm::recv_permute_gather)
       .def("recv_gather", &EpComm::recv_gather)
       .def("wait_rows", &EpComm::wait_rows)
@@ -436,5 +557,6 @@ void register_ep_comm(pybind11::module& m) {
       .def("local", &SymmBuffer::local)
       .def("put", &SymmBuffer::put)
       .def("fetch_experts", &SymmBuffer::fetch_experts)
+      .def("p2p_write_bench", &SymmBuffer::p2p_write_bench)
       .def("size", &SymmBuffer::size);
 }

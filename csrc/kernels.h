@@ -105,4 +105,15 @@ void spec_fetch(const SpecFetchArgs& a, int blocks_per_slot, cudaStream_t st);
 // Device timeline (trace.cu): ring[2 i] = tag, ring[2 i + 1] = %globaltimer ns.
 void trace_stamp(unsigned long long* ring, unsigned int* counter, int cap, int tag, cudaStream_t st);
 
+// All-to-all peer write bandwidth probe (p2p_bench.cu): dst[r] = rank r's buffer, each
+// rank writes bytes_per_peer from src to every other rank at offset rank * bytes_per_peer.
+struct P2PBenchArgs {
+  uint8_t* dst[64];
+  const uint8_t* src = nullptr;
+  long long bytes_per_peer = 0;
+  int W = 1, rank = 0, mode = 0;
+  int* status = nullptr;
+};
+void p2p_write_bench(const P2PBenchArgs& a, int blocks, cudaStream_t st);
+
 }  // namespace sepx

@@ -137,9 +137,10 @@ class ExpertParallel:
             raise ValueError("fp8 dispatch needs hidden % 128 == 0")
         self.stats_on = False  # traffic statistics of forward dispatches (enable_stats)
         self._reset_stats()
-        # row budgets of a pass (begin_pass / end_pass): receive buffers sized ahead of
-        # the device-side count, so no layer waits for a device->host read
-        self._budget: list[int] = []
+        # row budget of a pass (begin_pass / end_pass): receive buffers sized ahead of the
+        # device-side count, so no layer waits for a device->host read
+        self._budget = 0       # rows every call of a pass may receive (0: not learned yet)
+        self._seen = 0         # most rows a call needed in exact-size calls of this pass
         self._pass = None
         self._need = torch.zeros(1024, dtype=torch.int32, device=self.device)
         self._miss = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -215,27 +216,42 @@ class ExpertParallel:
     # -------------------------------------------------------------------------------
     # Row budgets: no host sync inside a pass
     # -------------------------------------------------------------------------------
-    # budget = rows needed when learned x margin (64-row steps); after an overflow, the
-    # rows that call needed x the growth factor. Routing drifts while a model trains, so
-    # the margin is generous: a miss costs a second forward, the margin only memory.
-    budget_margin = 1.25
-    budget_growth = 1.5
+    # One budget serves every call of a pass: the most rows any call has needed x margin
+    # (64-row steps, at most the worst case cap_rows); after an overflow, the most rows a
+    # call needed x growth. Routing drifts while a model trains (without a load-balancing
+    # loss a rank's share of the choices can grow step after step) and a rank's received
+    # rows vary from layer to layer; a budget per layer would be overflowed by one of
+    # dozens of layers x ranks nearly every step. A miss costs a second forward, the
+    # margin only memory (the saved expert activations of every layer).
+    budget_margin = 1.5
+    budget_growth = 2.0
 
     def begin_pass(self):
-        """Start a pass of layer calls (e.g. one model forward). Inside a pass, the i-th
-        ``dispatch_fwd`` sizes its receive buffers (and so every saved activation of that
-        layer) from a row budget learned for call i instead of reading the received row
-        count back to the host, so the host never waits on the device between layers.
-        The first pass learns the budgets with exact sizes. A call whose rows exceed its
-        budget empties its layout and raises a device flag; ``end_pass`` reports it and
-        the caller runs the pass again, with the budget grown to fit."""
+        """Start a pass of layer calls (e.g. one model forward). Inside a pass every
+        ``dispatch_fwd`` sizes its receive buffers (and so every saved activation of its
+        layer) from the learned row budget instead of reading the received row count back
+        to the host, so the host never waits on the device between layers. The first
+        pass learns the budget with exact sizes. A call whose rows exceed the budget
+        empties its layout and raises a device flag; ``end_pass`` reports it and the
+        caller runs the pass again, with the budget grown to fit."""
         self._pass = 0
+        self._seen = 0
 
-    def _set_budget(self, idx: int, rows: int, margin: float):
-        want = min(self.cap_rows, (int(rows * margin) + 64 + 63) // 64 * 64)
-        while len(self._budget) <= idx:
-            self._budget.append(0)
-        self._budget[idx] = max(self._budget[idx], want)
+    def _grow_budget(self, rows: int, factor: float):
+        want = min(self.cap_rows, (int(rows * factor) + 64 + 63) // 64 * 64)
+        self._budget = max(self._budget, want)
+
+    def run_pass(self, fn, retries: int = 3):
+        """``fn()`` (e.g. one model forward) inside a pass, run again while some layer's
+        rows outgrow their budget; returns its result. Collective over the default group
+        when ranks run together (every rank must call it)."""
+        for _ in range(retries + 1):
+            self.begin_pass()
+            out = fn()
+            if not self.end_pass():
+                return out
+            del out
+        raise EPError("MoE receive-row budgets kept overflowing")
 
     def end_pass(self) -> bool:
         """Close the pass; True if some call overflowed its budget (on any rank of the
@@ -244,6 +260,9 @@ class ExpertParallel:
         n, self._pass = self._pass, None
         if not n:
             return False
+        if self._seen:  # exact-size calls in this pass: learn the budget from them
+            self._grow_budget(self._seen, self.budget_margin)
+            self._seen = 0
         flag = self._miss.clone()
         if dist.is_available() and dist.is_initialized():
             dist.all_reduce(flag, op=dist.ReduceOp.MAX)
@@ -253,9 +272,7 @@ class ExpertParallel:
         if self.stats_on:
             self.stat_recv_rows.extend(need)
         if missed:
-            for i, r in enumerate(need):
-                if i >= len(self._budget) or r > self._budget[i]:
-                    self._set_budget(i, r, self.budget_growth)
+            self._grow_budget(max(need), self.budget_growth)
         return missed
 
     def set_local_slots(self, G: int):
@@ -281,44 +298,27 @@ class ExpertParallel:
         the received row count back to the host: no host sync, so the layer can be
         captured in a CUDA graph (inference; the expert GEMMs skip the unused rows).
         """
-        T, dev, W, k = x.shape[0], self.device, self.world, self.k
+        T = x.shape[0]
         if T > self.cap:
             raise ValueError(f"{T} tokens exceed the communicator capacity {self.cap}")
         ep = self._next_epoch()
-        slot = torch.empty(T, W, dtype=torch.int32, device=dev)
-        send_count = torch.empty(W, dtype=torch.int32, device=dev)
-        self_tok = torch.empty(self.cap, dtype=torch.int32, device=dev)
-        dst_tk, meta_tk = tables if tables is not None else self.route_tables(topk_e)
-        topk_w = topk_w.float().contiguous()
-        self.comm.route_plan(dst_tk, slot, send_count)
-        self.comm.dispatch(x, dst_tk, meta_tk, topk_w, slot, self_tok, send_count, True, ep,
-                           self.done[0:1], self.status, self.timeout_s, self.fp8_dispatch)
-        G = self.G
-        rows_from = torch.empty(W, dtype=torch.int32, device=dev)
-        chunk_cnt = torch.empty(self.nchunks * G, dtype=torch.int32, device=dev)
-        group_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
-        group_cnt = torch.empty(G, dtype=torch.int32, device=dev)
-        pad_off = torch.empty(G + 1, dtype=torch.int32, device=dev)
         idx = self._pass
         budget = 0
-        if idx is not None and not static_rows and idx < len(self._budget) and idx < self._need.numel():
-            budget = self._budget[idx]
-        need = self._need[idx:idx + 1] if budget else None
-        self.comm.recv_count_scan(dst_tk, meta_tk, topk_w, self_tok, send_count, G, T,
-                                  budget if budget else self.cap_rows, ep, rows_from, chunk_cnt, group_off, group_cnt,
-                                  pad_off, self.done[0:1], self.status, self.timeout_s, need,
-                                  self._miss if budget else None)
-        if static_rows:
-            R = self.cap_rows
-        elif budget:
-            R = budget  # inside a pass: no host sync; end_pass checks the budget held
-        else:
-            # Outside a pass (or learning a budget): one small device->host read sizes every
-            # buffer of this layer exactly; the receive capacity is the true worst case.
-            R = max(int(group_off[G].item()), 1)
+        if idx is not None and not static_rows and idx < self._need.numel():
+            budget = self._budget
+        rows_mode = -1 if static_rows else budget
+        dst_in, meta_in = tables if tables is not None else (None, None)
+        # one host call: tables, route plan, dispatch, receive count + scan, buffers sized
+        # by the budget (no host read), the worst case, or an exact read, permute + gather
+        (slot, send_count, self_tok, rows_from, group_off, group_cnt, xp, row_w, row_src, inv_rows, dst_tk, meta_tk,
+         topk_w), R = self.comm.dispatch_forward(
+            x, topk_e.int().contiguous(), topk_w, self.e2r, self.e2l, dst_in, meta_in, self.G, ep, rows_mode,
+            self.cap_rows, self._need[idx:idx + 1] if budget else None, self._miss if budget else None,
+            self.done[0:1], self.status, self.timeout_s, self.fp8_dispatch)
+        if not static_rows and not budget:
             self.rows_last = R
-            if idx is not None and idx < self._need.numel():
-                self._set_budget(idx, R, self.budget_margin)
+            if idx is not None:
+                self._seen = max(self._seen, R)
         if idx is not None:
             self._pass = idx + 1
         if self.stats_on:
@@ -327,23 +327,12 @@ class ExpertParallel:
             self.stat_tokens += T
             if not static_rows and not budget:
                 self.stat_recv_rows.append(R)
-        xp = torch.empty(R, self.H, dtype=torch.bfloat16, device=dev)
-        row_w = torch.empty(R, dtype=torch.float32, device=dev)
-        row_src = torch.empty(R, dtype=torch.int32, device=dev)
-        inv_rows = torch.empty(W, self.cap, k, dtype=torch.int32, device=dev)
-        self.comm.recv_permute_gather(x, dst_tk, meta_tk, topk_w, self_tok, send_count, G, ep, rows_from,
-                                      chunk_cnt, group_off, group_cnt, pad_off, xp, row_w, row_src, inv_rows,
-                                      self.done[0:1], self.status, self.timeout_s, self.fp8_dispatch)
         return EPState(T, slot, send_count, self_tok, dst_tk, meta_tk, topk_w, rows_from, group_off, group_cnt, xp,
                        row_w, row_src, inv_rows)
 
     def combine_fwd(self, y, st: EPState, residual=None):
-        out = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
-        self.comm.combine(y, st.inv_rows, st.row_w, st.rows_from, True, None, st.T, self.cur_epoch, self.done[1:2],
-                          self.status, self.timeout_s)
-        self.comm.source_reduce(st.slot, st.dst_tk, residual, out, None, self.cur_epoch, self.done[1:2],
-                                self.status, self.timeout_s)
-        return out
+        return self.comm.combine_forward(y, st.inv_rows, st.row_w, st.rows_from, st.slot, st.dst_tk, residual, st.T,
+                                         self.cur_epoch, self.done[1:2], self.status, self.timeout_s)
 
     def dispatch_bwd(self, dy, st: EPState):
         ep = self._next_epoch()
@@ -376,8 +365,10 @@ class ExpertParallel:
 class EPGraph:
     """A callable that runs expert-parallel inference layers, captured as one CUDA graph.
 
-    ``fn`` must call ``dispatch_fwd(..., static_rows=True)`` (no host sync) and read its
-    inputs from tensors that stay allocated; copy new inputs into them and ``replay()``.
+    ``fn`` must size its layers without a host read, with ``dispatch_fwd(...,
+    static_rows=True)`` (worst case) or inside a pass with a learned row budget, and read
+    its inputs from tensors that stay allocated; copy new inputs into them and
+    ``replay()``.
     Capture switches ``ep`` to device-side epochs (each replayed layer call bumps the
     counter on the device), runs ``warmup`` eager calls on a side stream, then captures
     one call. Every rank of the group must build and replay its graph in the same order.

@@ -73,16 +73,17 @@ class Trainer:
         forward is discarded (nothing was updated yet) and run again with the grown
         budgets; the first step learns the budgets with exact sizes."""
         ep = getattr(self.model, "ep", None)
-        if ep is None or not hasattr(ep, "begin_pass"):
+        if ep is None or not hasattr(ep, "run_pass"):
             return self.model(input_ids, labels, num_valid)
-        for _ in range(4):
-            ep.begin_pass()
-            loss = self.model(input_ids, labels, num_valid)
-            if not ep.end_pass():
-                return loss
-            self.budget_retries += 1
-            del loss
-        raise RuntimeError("MoE receive-row budgets kept overflowing")
+        calls = [0]
+
+        def fwd():
+            calls[0] += 1
+            return self.model(input_ids, labels, num_valid)
+
+        loss = ep.run_pass(fwd)
+        self.budget_retries += calls[0] - 1
+        return loss
 
     def train_step(self, input_ids, labels, num_valid=None):
         """One optimizer step on a device-resident batch; returns the (device) loss."""

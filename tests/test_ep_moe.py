@@ -148,16 +148,16 @@ def test_row_budget_pass_matches_exact_sizes_and_recovers_from_overflow():
     ep.begin_pass()
     learn = layers()  # first pass: learns the budgets (exact sizes)
     assert not ep.end_pass()
-    assert len(ep._budget) == 2 and all(b >= T * k for b in ep._budget)
+    assert ep._budget >= T * k
     ep.begin_pass()
     budgeted = layers()  # no host read between the layers
     assert not ep.end_pass()
     assert torch.equal(learn, exact) and torch.equal(budgeted, exact)
-    ep._budget = [64, 64]  # far too small: the first call overflows
+    ep._budget = 64  # far too small: the first call overflows
     ep.begin_pass()
     layers()
-    assert ep.end_pass()  # reported, and the budgets grown
-    assert all(b >= T * k for b in ep._budget)
+    assert ep.end_pass()  # reported, and the budget grown
+    assert ep._budget >= T * k
     ep.begin_pass()
     again = layers()
     assert not ep.end_pass()
