@@ -107,6 +107,20 @@ def main():
             ep.end_pass()  # learn the row budget (exact sizes once)
             r = {"seed": seed, "p2p_us": timed(p2p, args.iters)}
             assert not ep.end_pass(), "row budget outgrown inside the timed loop"
+            if seed == 0:
+                # host cost of issuing one layer call (no sync inside the loop): when it
+                # approaches p2p_us the layer is bound by the host, not the GPU
+                import time
+
+                torch.cuda.synchronize()
+                dist.barrier()
+                t0 = time.perf_counter()
+                for _ in range(args.iters):
+                    p2p()
+                r["host_issue_us"] = (time.perf_counter() - t0) * 1e6 / args.iters
+                torch.cuda.synchronize()
+                ep.end_pass()
+                r["host_cpus"] = os.cpu_count()
             r["nccl_naive_us"] = timed(lambda: naive_combine_dispatch(x, tw, ident, te.long(), 128), args.iters)
             if ref is not None:
                 r["reference_rbd_us"] = timed(lambda: ref.RBD_combine_dispatch(

@@ -7,6 +7,7 @@ rank 0 prints its per-kernel table.
     python benchmarks/profile_step.py --layers 8 [--warmup 2]
     python benchmarks/profile_step.py --layers 48 --table   # per-kernel device time (torch profiler)
     python benchmarks/profile_step.py --layers 48 --breakdown   # device time per kernel class
+    python benchmarks/profile_step.py --layers 48 --gaps        # device idle gaps by size
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/profile_step.py --layers 48 --table --expert-state fp32
 
 ``--breakdown`` groups every kernel of one step by class (expert GEMMs, attention, dense
@@ -57,6 +58,8 @@ def main():
     ap.add_argument("--expert-state", default="8bit")
     ap.add_argument("--table", action="store_true", help="print per-kernel CUDA time of one step (torch profiler)")
     ap.add_argument("--breakdown", action="store_true", help="print device time per kernel class of one step")
+    ap.add_argument("--gaps", action="store_true",
+                    help="list the device idle gaps of one step (between consecutive kernels) by size")
     ap.add_argument("--out", default=None, help="also write the breakdown (markdown) to this file")
     args = ap.parse_args()
     from spec_ep.models.config import get_config
@@ -92,7 +95,7 @@ def main():
     step_ms = s.elapsed_time(e)
     if rank == 0:
         print(f"world={world} layers={args.layers} step_ms={step_ms:.2f} loss={loss.item():.4f}")
-    if args.table or args.breakdown:
+    if args.table or args.breakdown or args.gaps:
         from torch.profiler import ProfilerActivity, profile
 
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
@@ -106,11 +109,51 @@ def main():
             if args.out:
                 with open(args.out, "w") as f:
                     f.write(text + "\n")
+        if rank == 0 and args.gaps:
+            text = gaps(prof)
+            print(text)
+            if args.out:
+                with open(args.out, "a") as f:
+                    f.write("\n" + text + "\n")
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
         dist.destroy_process_group()
+
+
+def gaps(prof, top=20) -> str:
+    """Device idle time of the profiled step: kernels (and memcpy / memset) sorted by start,
+    idle = time between the latest end so far and the next start. Lists the size histogram
+    and the largest gaps with the kernels on either side."""
+    evs = []
+    for ev in prof.events():
+        if getattr(ev, "device_type", None) is None or str(ev.device_type) != "DeviceType.CUDA":
+            continue
+        tr = ev.time_range
+        if tr.end > tr.start:
+            evs.append((tr.start, tr.end, ev.name))
+    evs.sort()
+    if not evs:
+        return "no device events"
+    found, end, prev = [], evs[0][1], evs[0][2]
+    for st, en, name in evs[1:]:
+        if st > end:
+            found.append((st - end, prev, name))
+        if en > end:
+            end, prev = en, name
+    span = end - evs[0][0]
+    idle = sum(g for g, _, _ in found)
+    bins = [(0, 5), (5, 20), (20, 100), (100, 1000), (1000, float("inf"))]
+    lines = [f"device span {span / 1e3:.2f} ms, idle {idle / 1e3:.2f} ms in {len(found)} gaps", "",
+             "| gap size (us) | gaps | idle ms |", "|---|---|---|"]
+    for lo, hi in bins:
+        sel = [g for g, _, _ in found if lo <= g < hi]
+        lines.append(f"| {lo}-{hi if hi != float('inf') else ''} | {len(sel)} | {sum(sel) / 1e3:.2f} |")
+    lines += ["", "| gap (us) | after | before |", "|---|---|---|"]
+    for g, a, b in sorted(found, reverse=True)[:top]:
+        lines.append(f"| {g:.1f} | {a[:60]} | {b[:60]} |")
+    return "\n".join(lines)
 
 
 def breakdown(prof, step_ms, world, args) -> str:

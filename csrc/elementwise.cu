@@ -200,9 +200,12 @@ void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy
 // Fused per-head RMSNorm + rotary embedding (rotate-half convention, Qwen3):
 //   in  qkv [T, (Hq + 2*Hkv) * 128]  (output of the fused QKV projection)
 //   out q [T, Hq, 128], k [T, Hkv, 128] normalised and rotated; v [T, Hkv, 128] copied.
-// One warp per (token, head); lane l owns elements {2l, 2l+1} and {64+2l, 64+2l+1}... we
-// use the pairing (i, i+64) of rotate-half: lane l owns i = 2l, 2l+1 and their partners.
+// One warp per token: lane l owns elements i = 2l, 2l+1 and their rotate-half partners
+// i + 64, so the lane's two rotation angles are computed once per token and reused by
+// every q / k head; heads go in batches of kRopeBatch with all their loads issued first.
 // =====================================================================================
+constexpr int kRopeBatch = 4;
+
 __device__ __forceinline__ void rope_cs(int pos, int i, float log2_theta, float* c, float* s) {
   // inv_freq_i = theta^(-2i/128), angle = pos * inv_freq
   const float inv = exp2f(-(2.f * i / 128.f) * log2_theta);
@@ -216,49 +219,61 @@ __global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(
     float* __restrict__ rstd_q, float* __restrict__ rstd_k, const int* __restrict__ pos_ids, int T, int Hq, int Hkv,
     float eps, float log2_theta) {
   const int lane = threadIdx.x & 31;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (t >= T) return;
   const int Ht = Hq + 2 * Hkv;
-  if (gw >= T * Ht) return;
-  const int t = gw / Ht, h = gw % Ht;
-  const __nv_bfloat16* src = qkv + ((size_t)t * Ht + h) * 128;
-  // lane owns lo = (2l, 2l+1) and hi = (64+2l, 64+2l+1)
-  float2 lo = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[lane]);
-  float2 hi = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src + 64)[lane]);
-  if (h >= Hq + Hkv) {  // value head: plain copy
-    __nv_bfloat16* dst = v + ((size_t)t * Hkv + (h - Hq - Hkv)) * 128;
-    reinterpret_cast<__nv_bfloat162*>(dst)[lane] = __floats2bfloat162_rn(lo.x, lo.y);
-    reinterpret_cast<__nv_bfloat162*>(dst + 64)[lane] = __floats2bfloat162_rn(hi.x, hi.y);
-    return;
-  }
-  const bool is_q = h < Hq;
-  const __nv_bfloat16* w = is_q ? wq : wk;
-  float ss = lo.x * lo.x + lo.y * lo.y + hi.x * hi.x + hi.y * hi.y;
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / 128.f + eps);
-  float2 wl = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(w)[lane]);
-  float2 wh = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(w + 64)[lane]);
-  float a0 = lo.x * r * wl.x, a1 = lo.y * r * wl.y, b0 = hi.x * r * wh.x, b1 = hi.y * r * wh.y;
   const int pos = pos_ids ? pos_ids[t] : t;
   float c0, s0, c1, s1;
   rope_cs(pos, 2 * lane, log2_theta, &c0, &s0);
   rope_cs(pos, 2 * lane + 1, log2_theta, &c1, &s1);
-  // out_lo = a*cos - b*sin ; out_hi = b*cos + a*sin
-  float o0 = a0 * c0 - b0 * s0, o1 = a1 * c1 - b1 * s1;
-  float p0 = b0 * c0 + a0 * s0, p1 = b1 * c1 + a1 * s1;
-  __nv_bfloat16* dst;
-  if (is_q) {
-    dst = q + ((size_t)t * Hq + h) * 128;
-    if (lane == 0) rstd_q[(size_t)t * Hq + h] = r;
-  } else {
-    dst = k + ((size_t)t * Hkv + (h - Hq)) * 128;
-    if (lane == 0) rstd_k[(size_t)t * Hkv + (h - Hq)] = r;
+  const float2 wql = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wq)[lane]);
+  const float2 wqh = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wq + 64)[lane]);
+  const float2 wkl = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wk)[lane]);
+  const float2 wkh = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wk + 64)[lane]);
+  const __nv_bfloat162* row = reinterpret_cast<const __nv_bfloat162*>(qkv + (size_t)t * Ht * 128);
+  for (int h0 = 0; h0 < Ht; h0 += kRopeBatch) {
+    __nv_bfloat162 lo[kRopeBatch], hi[kRopeBatch];
+#pragma unroll
+    for (int b = 0; b < kRopeBatch; ++b) {
+      const int h = min(h0 + b, Ht - 1);
+      lo[b] = row[h * 64 + lane];
+      hi[b] = row[h * 64 + 32 + lane];
+    }
+#pragma unroll
+    for (int b = 0; b < kRopeBatch; ++b) {
+      const int h = h0 + b;
+      if (h >= Ht) break;
+      const float2 l = __bfloat1622float2(lo[b]), u = __bfloat1622float2(hi[b]);
+      if (h >= Hq + Hkv) {  // value head: plain copy
+        __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(v + ((size_t)t * Hkv + (h - Hq - Hkv)) * 128);
+        dst[lane] = lo[b];
+        dst[32 + lane] = hi[b];
+        continue;
+      }
+      const bool is_q = h < Hq;
+      const float2 wl = is_q ? wql : wkl, wh = is_q ? wqh : wkh;
+      const float r = rsqrtf(warp_sum(l.x * l.x + l.y * l.y + u.x * u.x + u.y * u.y) / 128.f + eps);
+      const float a0 = l.x * r * wl.x, a1 = l.y * r * wl.y, b0 = u.x * r * wh.x, b1 = u.y * r * wh.y;
+      // out_lo = a*cos - b*sin ; out_hi = b*cos + a*sin
+      const float o0 = a0 * c0 - b0 * s0, o1 = a1 * c1 - b1 * s1;
+      const float p0 = b0 * c0 + a0 * s0, p1 = b1 * c1 + a1 * s1;
+      __nv_bfloat162* dst;
+      if (is_q) {
+        dst = reinterpret_cast<__nv_bfloat162*>(q + ((size_t)t * Hq + h) * 128);
+        if (lane == 0) rstd_q[(size_t)t * Hq + h] = r;
+      } else {
+        dst = reinterpret_cast<__nv_bfloat162*>(k + ((size_t)t * Hkv + (h - Hq)) * 128);
+        if (lane == 0) rstd_k[(size_t)t * Hkv + (h - Hq)] = r;
+      }
+      dst[lane] = __floats2bfloat162_rn(o0, o1);
+      dst[32 + lane] = __floats2bfloat162_rn(p0, p1);
+    }
   }
-  reinterpret_cast<__nv_bfloat162*>(dst)[lane] = __floats2bfloat162_rn(o0, o1);
-  reinterpret_cast<__nv_bfloat162*>(dst + 64)[lane] = __floats2bfloat162_rn(p0, p1);
 }
 
 // Backward: dq/dk (post-rotation) -> un-rotate -> RMSNorm backward -> dqkv; dv copied.
-// dwq/dwk accumulate per-element weight gradients (fp32).
+// dwq/dwk accumulate per-element weight gradients (fp32). One warp per token (grid-stride
+// over tokens), heads in batches as in the forward.
 __global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(
     const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ wq, const __nv_bfloat16* __restrict__ wk,
     const float* __restrict__ rstd_q, const float* __restrict__ rstd_k, const __nv_bfloat16* __restrict__ dq,
@@ -271,50 +286,72 @@ __global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(
   const int lane = threadIdx.x & 31;
   const int Ht = Hq + 2 * Hkv;
   const int nw = gridDim.x * (blockDim.x >> 5);
+  const float2 wql = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wq)[lane]);
+  const float2 wqh = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wq + 64)[lane]);
+  const float2 wkl = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wk)[lane]);
+  const float2 wkh = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wk + 64)[lane]);
   float aq[4] = {0, 0, 0, 0}, ak[4] = {0, 0, 0, 0};
-  for (int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); gw < T * Ht; gw += nw) {
-    const int t = gw / Ht, h = gw % Ht;
-    __nv_bfloat16* out = dqkv + ((size_t)t * Ht + h) * 128;
-    if (h >= Hq + Hkv) {
-      const __nv_bfloat16* g = dv + ((size_t)t * Hkv + (h - Hq - Hkv)) * 128;
-      reinterpret_cast<__nv_bfloat162*>(out)[lane] = reinterpret_cast<const __nv_bfloat162*>(g)[lane];
-      reinterpret_cast<__nv_bfloat162*>(out + 64)[lane] = reinterpret_cast<const __nv_bfloat162*>(g + 64)[lane];
-      continue;
-    }
-    const bool is_q = h < Hq;
-    const __nv_bfloat16* w = is_q ? wq : wk;
-    const __nv_bfloat16* g = is_q ? dq + ((size_t)t * Hq + h) * 128 : dk + ((size_t)t * Hkv + (h - Hq)) * 128;
-    const float r = is_q ? rstd_q[(size_t)t * Hq + h] : rstd_k[(size_t)t * Hkv + (h - Hq)];
-    float2 glo = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(g)[lane]);
-    float2 ghi = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(g + 64)[lane]);
+  for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += nw) {
     const int pos = pos_ids ? pos_ids[t] : t;
     float c0, s0, c1, s1;
     rope_cs(pos, 2 * lane, log2_theta, &c0, &s0);
     rope_cs(pos, 2 * lane + 1, log2_theta, &c1, &s1);
-    // inverse rotation: da = glo*cos + ghi*sin ; db = ghi*cos - glo*sin
-    float da0 = glo.x * c0 + ghi.x * s0, da1 = glo.y * c1 + ghi.y * s1;
-    float db0 = ghi.x * c0 - glo.x * s0, db1 = ghi.y * c1 - glo.y * s1;
-    const __nv_bfloat16* src = qkv + ((size_t)t * Ht + h) * 128;
-    float2 lo = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[lane]);
-    float2 hi = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src + 64)[lane]);
-    float2 wl = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(w)[lane]);
-    float2 wh = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(w + 64)[lane]);
-    float xh[4] = {lo.x * r, lo.y * r, hi.x * r, hi.y * r};
-    float gy[4] = {da0, da1, db0, db1};
-    float wv[4] = {wl.x, wl.y, wh.x, wh.y};
-    float dot = 0.f;
+    const __nv_bfloat162* xrow = reinterpret_cast<const __nv_bfloat162*>(qkv + (size_t)t * Ht * 128);
+    __nv_bfloat162* orow = reinterpret_cast<__nv_bfloat162*>(dqkv + (size_t)t * Ht * 128);
+    for (int h0 = 0; h0 < Ht; h0 += kRopeBatch) {
+      __nv_bfloat162 glo[kRopeBatch], ghi[kRopeBatch], xlo[kRopeBatch], xhi[kRopeBatch];
+      float rr[kRopeBatch];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (is_q) aq[e] += gy[e] * xh[e]; else ak[e] += gy[e] * xh[e];
-      gy[e] *= wv[e];
-      dot += gy[e] * xh[e];
+      for (int b = 0; b < kRopeBatch; ++b) {
+        const int h = min(h0 + b, Ht - 1);
+        const __nv_bfloat162* g;
+        if (h < Hq) {
+          g = reinterpret_cast<const __nv_bfloat162*>(dq + ((size_t)t * Hq + h) * 128);
+          rr[b] = rstd_q[(size_t)t * Hq + h];
+        } else if (h < Hq + Hkv) {
+          g = reinterpret_cast<const __nv_bfloat162*>(dk + ((size_t)t * Hkv + (h - Hq)) * 128);
+          rr[b] = rstd_k[(size_t)t * Hkv + (h - Hq)];
+        } else {
+          g = reinterpret_cast<const __nv_bfloat162*>(dv + ((size_t)t * Hkv + (h - Hq - Hkv)) * 128);
+          rr[b] = 0.f;
+        }
+        glo[b] = g[lane];
+        ghi[b] = g[32 + lane];
+        if (h < Hq + Hkv) {
+          xlo[b] = xrow[h * 64 + lane];
+          xhi[b] = xrow[h * 64 + 32 + lane];
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kRopeBatch; ++b) {
+        const int h = h0 + b;
+        if (h >= Ht) break;
+        if (h >= Hq + Hkv) {  // value head: the gradient is copied
+          orow[h * 64 + lane] = glo[b];
+          orow[h * 64 + 32 + lane] = ghi[b];
+          continue;
+        }
+        const bool is_q = h < Hq;
+        const float2 gl = __bfloat1622float2(glo[b]), gh = __bfloat1622float2(ghi[b]);
+        const float2 lo = __bfloat1622float2(xlo[b]), hi = __bfloat1622float2(xhi[b]);
+        const float r = rr[b];
+        // inverse rotation: da = glo*cos + ghi*sin ; db = ghi*cos - glo*sin
+        float gy[4] = {gl.x * c0 + gh.x * s0, gl.y * c1 + gh.y * s1, gh.x * c0 - gl.x * s0, gh.y * c1 - gl.y * s1};
+        const float xh[4] = {lo.x * r, lo.y * r, hi.x * r, hi.y * r};
+        const float2 wl = is_q ? wql : wkl, wh = is_q ? wqh : wkh;
+        const float wv[4] = {wl.x, wl.y, wh.x, wh.y};
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (is_q) aq[e] += gy[e] * xh[e]; else ak[e] += gy[e] * xh[e];
+          gy[e] *= wv[e];
+          dot += gy[e] * xh[e];
+        }
+        dot = warp_sum(dot) / 128.f;
+        orow[h * 64 + lane] = __floats2bfloat162_rn(r * (gy[0] - xh[0] * dot), r * (gy[1] - xh[1] * dot));
+        orow[h * 64 + 32 + lane] = __floats2bfloat162_rn(r * (gy[2] - xh[2] * dot), r * (gy[3] - xh[3] * dot));
+      }
     }
-    dot = warp_sum(dot) / 128.f;
-    float o[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[e] = r * (gy[e] - xh[e] * dot);
-    reinterpret_cast<__nv_bfloat162*>(out)[lane] = __floats2bfloat162_rn(o[0], o[1]);
-    reinterpret_cast<__nv_bfloat162*>(out + 64)[lane] = __floats2bfloat162_rn(o[2], o[3]);
   }
   atomicAdd(&s_dw[0][2 * lane], aq[0]);
   atomicAdd(&s_dw[0][2 * lane + 1], aq[1]);
@@ -334,8 +371,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(
 void qk_norm_rope_fwd(const void* qkv, const void* wq, const void* wk, void* q, void* k, void* v, float* rstd_q,
                       float* rstd_k, const int* pos_ids, int T, int Hq, int Hkv, float eps, float theta,
                       cudaStream_t st) {
-  const int warps = T * (Hq + 2 * Hkv);
-  qk_norm_rope_fwd_kernel<<<(warps + 7) / 8, 256, 0, st>>>(
+  qk_norm_rope_fwd_kernel<<<(T + 7) / 8, 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(wq),
       reinterpret_cast<const __nv_bfloat16*>(wk), reinterpret_cast<__nv_bfloat16*>(q),
       reinterpret_cast<__nv_bfloat16*>(k), reinterpret_cast<__nv_bfloat16*>(v), rstd_q, rstd_k, pos_ids, T, Hq, Hkv,
@@ -346,8 +382,7 @@ void qk_norm_rope_fwd(const void* qkv, const void* wq, const void* wk, void* q, 
 void qk_norm_rope_bwd(const void* qkv, const void* wq, const void* wk, const float* rstd_q, const float* rstd_k,
                       const void* dq, const void* dk, const void* dv, void* dqkv, float* dwq, float* dwk,
                       const int* pos_ids, int T, int Hq, int Hkv, float theta, int num_sms, cudaStream_t st) {
-  const int warps = T * (Hq + 2 * Hkv);
-  const int blocks = std::min((warps + 7) / 8, num_sms * 4);
+  const int blocks = std::max(1, std::min((T + 7) / 8, num_sms * 4));
   qk_norm_rope_bwd_kernel<<<blocks, 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<const __nv_bfloat16*>(wq),
       reinterpret_cast<const __nv_bfloat16*>(wk), rstd_q, rstd_k, reinterpret_cast<const __nv_bfloat16*>(dq),

@@ -50,7 +50,8 @@ __host__ __device__ constexpr int threads_for(int epi) { return 64 + 32 * epi_wa
 // + m codes + v codes (uint8, 32B-swizzled), streamed by TMA three jobs deep per warp
 constexpr int kOptJob = 4096;  // w 2048 B @0, m 1024 B @2048, v 1024 B @3072
 // ring depth per epilogue warp: what fits next to two mainloop stages
-__host__ __device__ constexpr int opt_ring(int bn) { return bn == 256 ? 3 : 5; }
+// (three mainloop stages, for long reductions, leave room for two jobs per warp)
+__host__ __device__ constexpr int opt_ring(int bn, int stages) { return bn == 256 ? (stages >= 3 ? 2 : 3) : 5; }
 
 struct OptMaps {  // kEpiAdamW8 state tensor maps over [G * M, N]
   CUtensorMap w, m, v;
@@ -76,7 +77,7 @@ struct GemmSmem {
   static constexpr int EPI_STAGE_BYTES =
       (EPI == kEpiAdamW || EPI == kEpiF32)
           ? kEpiWarps * 32 * 33 * 4
-          : (EPI == kEpiAdamW8 ? epi_warps(EPI) * opt_ring(BN) * (kOptJob + 8) : 0);
+          : (EPI == kEpiAdamW8 ? epi_warps(EPI) * opt_ring(BN, STAGES) * (kOptJob + 8) : 0);
   static constexpr int BAR_OFF = EPI_STAGE_OFF + EPI_STAGE_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;  // full, empty, tfull[2], tempty[2], drain
   static constexpr int MISC_OFF = BAR_OFF + NUM_BARS * 8;
@@ -369,8 +370,9 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     }
     mbar_init(drain_bar, 1);
     if (EPI == kEpiAdamW8) {
-      uint64_t* obars = reinterpret_cast<uint64_t*>(smem + L::EPI_STAGE_OFF + epi_warps(EPI) * opt_ring(BN) * kOptJob);
-      for (int i = 0; i < epi_warps(EPI) * opt_ring(BN); ++i) mbar_init(&obars[i], 1);
+      uint64_t* obars =
+          reinterpret_cast<uint64_t*>(smem + L::EPI_STAGE_OFF + epi_warps(EPI) * opt_ring(BN, STAGES) * kOptJob);
+      for (int i = 0; i < epi_warps(EPI) * opt_ring(BN, STAGES); ++i) mbar_init(&obars[i], 1);
     }
     *s_abort = 0;
     fence_barrier_init();
@@ -504,7 +506,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     const int half = (warp - 2) >> 2;
     constexpr int kCStep = kEpiWarps / 4;
     constexpr int J = BN / 32 / kCStep;  // jobs per tile for this warp
-    constexpr int kOptRing = opt_ring(BN);
+    constexpr int kOptRing = opt_ring(BN, STAGES);
     const int ew = warp - 2;
     uint8_t* ring = smem + L::EPI_STAGE_OFF + ew * kOptRing * kOptJob;
     uint64_t* obar =
@@ -832,7 +834,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Epi
 //   empty[s]  per CTA; the leader's MMA thread commits to both after the stage's MMAs
 //   tfull[a]  per CTA; committed to both when a tile's MMAs are done
 //   tempty[a] leader only; both CTAs' epilogue warps arrive (2 x 8 arrivals)
-// No load uses multicast; the only cross-CTA traffic is mbarrier arrivals and the MMA's
+// Every load fills only its own CTA's shared memory; the only cross-CTA traffic is mbarrier arrivals and the MMA's
 // own reads of the peer's operand tiles.
 // =====================================================================================
 template <int BN, int STAGES, int EPI>
@@ -1356,7 +1358,12 @@ void grouped_gemm_wgrad_adamw(const GemmCall& c, cudaStream_t stream) {
     om.v = make_tmap_state(p.opt.v, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, p.N, CU_TENSOR_MAP_SWIZZLE_32B);
     if (p.N % 256 == 0) {
       p.n_tiles = p.N / 256;
-      launch<256, 2, true, true, true, kEpiAdamW8>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream, om);
+      // long reductions (many rows per expert: the MMA bounds the tile) take a third
+      // mainloop stage; short ones (the optimizer stream bounds it) a deeper state ring
+      if (c.a_rows >= 512LL * p.G)
+        launch<256, 3, true, true, true, kEpiAdamW8>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream, om);
+      else
+        launch<256, 2, true, true, true, kEpiAdamW8>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream, om);
     } else if (p.N % 128 == 0) {
       p.n_tiles = p.N / 128;
       launch<128, 2, true, true, true, kEpiAdamW8>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream, om);

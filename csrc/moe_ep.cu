@@ -64,46 +64,98 @@ __device__ __forceinline__ bool wait_header(const uint64_t* hdr, uint32_t epoch,
 // none of t's choices goes to d). dst_tk[t][j] is the destination rank of choice j (-1:
 // not sent). Single block; T up to a few 10^4 tokens.
 // ------------------------------------------------------------------------------------
+// Inclusive scan of one int per lane of a full warp.
+__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
+
+// Destination mask of token t: bit d set when any choice goes to rank d. KV > 0: k == KV
+// is known at compile time and each row is read with KV / 4 16-byte loads.
+template <int KV>
+__device__ __forceinline__ unsigned long long token_mask(const int* __restrict__ dst_tk, int t, int T, int k) {
+  unsigned long long m = 0;
+  if (t >= T) return 0;
+  if constexpr (KV > 0) {
+    const int4* p = reinterpret_cast<const int4*>(dst_tk + (size_t)t * KV);
+#pragma unroll
+    for (int q = 0; q < KV / 4; ++q) {
+      const int4 v = __ldg(p + q);
+      m |= (v.x >= 0 ? 1ull << v.x : 0ull) | (v.y >= 0 ? 1ull << v.y : 0ull) |
+           (v.z >= 0 ? 1ull << v.z : 0ull) | (v.w >= 0 ? 1ull << v.w : 0ull);
+    }
+  } else {
+    for (int j = 0; j < k; ++j) {
+      const int d = __ldg(dst_tk + (size_t)t * k + j);
+      if (d >= 0) m |= 1ull << d;
+    }
+  }
+  return m;
+}
+
+constexpr int kPlanRounds = 4;  // rounds of 1024 tokens whose loads are issued together
+
+template <int KV>
 __global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict__ dst_tk, int T,
                                                           int k, int W, int* __restrict__ slot,
                                                           int* __restrict__ send_count) {
-  // One token per thread per round of 1024 tokens; per destination, a warp ballot gives
-  // each token its rank among the warp's senders, per-warp totals are scanned in shared
-  // memory, and a running base per destination carries across rounds. Slots follow
-  // token order (deterministic).
-  __shared__ int s_warp[32][kMaxW];
+  // Tokens in passes of kPlanRounds x 1024 (one per thread per round, every load of a pass
+  // in flight at once). Per destination, a warp ballot gives each token its rank among the
+  // warp's senders; the 128 per-warp totals of a pass (round-major, so token order) are
+  // scanned by one warp per destination, and a running base per destination carries
+  // across passes. Slots follow token order (deterministic).
+  __shared__ int s_warp[kPlanRounds * 32][kMaxW];
   __shared__ int s_base[kMaxW];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   if (tid < W) s_base[tid] = 0;
   __syncthreads();
-  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
-    const int t = t0 + tid;
-    unsigned long long m = 0;
-    if (t < T) {
-      for (int j = 0; j < k; ++j) {
-        const int d = __ldg(dst_tk + (size_t)t * k + j);
-        if (d >= 0) m |= 1ull << d;
+  for (int t0 = 0; t0 < T; t0 += blockDim.x * kPlanRounds) {
+    unsigned long long m[kPlanRounds];
+#pragma unroll
+    for (int r = 0; r < kPlanRounds; ++r) m[r] = token_mask<KV>(dst_tk, t0 + r * blockDim.x + tid, T, k);
+#pragma unroll
+    for (int r = 0; r < kPlanRounds; ++r)
+      for (int d = 0; d < W; ++d) {
+        const unsigned b = __ballot_sync(0xffffffffu, (m[r] >> d) & 1ull);
+        if (lane == 0) s_warp[r * nwarps + warp][d] = __popc(b);
       }
-    }
-    for (int d = 0; d < W; ++d) {
-      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1ull);
-      if (lane == 0) s_warp[warp][d] = __popc(b);
+    __syncthreads();
+    // exclusive scan of the kPlanRounds * nwarps totals of destination d, one warp each
+    const int n = kPlanRounds * nwarps, per = (n + 31) / 32;
+    for (int d = warp; d < W; d += nwarps) {
+      int v[kPlanRounds];
+      int sum = 0;
+#pragma unroll
+      for (int i = 0; i < kPlanRounds; ++i) {
+        const int e = lane * per + i;
+        v[i] = (i < per && e < n) ? s_warp[e][d] : 0;
+        sum += v[i];
+      }
+      const int incl = warp_incl_scan(sum, lane);
+      int acc = s_base[d] + incl - sum;
+      const int total = __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+      for (int i = 0; i < kPlanRounds; ++i) {
+        const int e = lane * per + i;
+        if (i < per && e < n) s_warp[e][d] = acc;
+        acc += v[i];
+      }
+      __syncwarp();
+      if (lane == 0) s_base[d] += total;
     }
     __syncthreads();
-    if (tid < W) {  // exclusive scan of the 32 warp totals of destination tid
-      int acc = s_base[tid];
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-        const int v = s_warp[w][tid];
-        s_warp[w][tid] = acc;
-        acc += v;
+#pragma unroll
+    for (int r = 0; r < kPlanRounds; ++r) {
+      const int t = t0 + r * blockDim.x + tid;
+      for (int d = 0; d < W; ++d) {  // every lane takes part in the ballot; only real tokens store
+        const unsigned b = __ballot_sync(0xffffffffu, (m[r] >> d) & 1ull);
+        const int before = __popc(b & ((1u << lane) - 1u));
+        if (t < T) slot[(size_t)t * W + d] = ((m[r] >> d) & 1ull) ? s_warp[r * nwarps + warp][d] + before : -1;
       }
-      s_base[tid] = acc;
-    }
-    __syncthreads();
-    for (int d = 0; d < W; ++d) {  // every lane takes part in the ballot; only real tokens store
-      const unsigned b = __ballot_sync(0xffffffffu, (m >> d) & 1ull);
-      const int before = __popc(b & ((1u << lane) - 1u));
-      if (t < T) slot[(size_t)t * W + d] = ((m >> d) & 1ull) ? s_warp[warp][d] + before : -1;
     }
     __syncthreads();
   }
@@ -317,7 +369,6 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
 
 // ------------------------------------------------------------------------------------
 // Receive side. Rows are enumerated src-major: (src, slot) for slot < rows_from[src].
-// K4a count: per chunk of 128 rows, rows per local expert -> chunk_cnt[chunk][G].
 // ------------------------------------------------------------------------------------
 __device__ __forceinline__ void row_meta(const EpArgs& a, const int* dst_tk, const float* topk_w,
                                          const int* self_tok, const int* meta_tk,
@@ -335,8 +386,43 @@ __device__ __forceinline__ void row_meta(const EpArgs& a, const int* dst_tk, con
   }
 }
 
+// All k (local expert, weight) entries of received row (src, s), loaded at once (the
+// permute kernel's passes over the choices then wait on no memory). k <= 8.
+__device__ __forceinline__ void row_meta_all(const EpArgs& a, const int* dst_tk, const float* topk_w,
+                                             const int* self_tok, const int* meta_tk, int src, int s,
+                                             int (&le)[8], float (&w)[8]) {
+  if (src == a.rank) {
+    const int t = self_tok[s];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < a.k) {
+        le[j] = (__ldg(dst_tk + t * a.k + j) == a.rank) ? __ldg(meta_tk + t * a.k + j) : -1;
+        w[j] = __ldg(topk_w + t * a.k + j);
+      }
+    }
+  } else {
+    const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
+    const int16_t* re = reinterpret_cast<const int16_t*>(base + a.off_recv_e) + ((size_t)src * a.cap + s) * a.k;
+    const float* rw = reinterpret_cast<const float*>(base + a.off_recv_w) + ((size_t)src * a.cap + s) * a.k;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < a.k) {
+        le[j] = re[j];
+        w[j] = rw[j];
+      }
+    }
+  }
+}
+
 constexpr int kChunk = 128;
 
+// Chunk counts the scan stages in shared memory (dynamic, with the kernel's static
+// shared memory under 48 KB); larger layouts are scanned in place in global memory.
+constexpr int kScanSmemEntries = 8192;
+__host__ __device__ constexpr int scan_smem_words(int n) { return n + (n >> 5) + 1; }
+
+
+// K4a count: per chunk of 128 rows, rows per local expert -> chunk_cnt[g][chunk].
 __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int* __restrict__ dst_tk,
                                                             const float* __restrict__ topk_w,
                                                             const int* __restrict__ self_tok,
@@ -370,10 +456,13 @@ __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int*
   __syncthreads();
   const int s = chunk * kChunk + threadIdx.x;
   if (s < s_rows) {
-    for (int j = 0; j < a.k; ++j) {
-      int le;
-      float w;
-      row_meta(a, dst_tk, topk_w, self_tok, meta_tk, src, s, j, &le, &w);
+    int le_all[8];
+    float w_all[8];
+    row_meta_all(a, dst_tk, topk_w, self_tok, meta_tk, src, s, le_all, w_all);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= a.k) break;
+      const int le = le_all[j];
       if (le >= G || le < -1) {
         record_error(a.status, kErrCorrupt);  // corrupted metadata: the entry is dropped
       } else if (le >= 0) {
@@ -383,19 +472,183 @@ __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int*
   }
   __syncthreads();
   for (int g = threadIdx.x; g < G; g += blockDim.x)
-    chunk_cnt[(size_t)blockIdx.x * G + g] = s_cnt[g];
+    chunk_cnt[(size_t)g * gridDim.x + blockIdx.x] = s_cnt[g];
 }
 
-// K4b scan (one block of 1024 threads): chunk_base[chunk][g] = group_off[g] + rows of g in
-// earlier chunks. One warp per expert group scans its chunk counts 32 at a time; the group
-// totals are then scanned block-wide into 64-row-aligned group offsets.
-__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += n;
+// K4b scan. chunk_cnt is laid out [G][nchunks] (each group's chunk counts contiguous).
+// Per group: exclusive scan over chunks (in place) and the group's total; then an
+// exclusive scan of the 64-row-padded group totals gives group_off / pad_off, and the
+// chunk entries become absolute row offsets. Any block size that is a multiple of 32.
+
+// Block-wide exclusive scan of one int per thread; *total (shared) gets the sum.
+__device__ __forceinline__ int block_excl_scan(int v, int* s_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int incl = warp_incl_scan(v, lane);
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int x = lane < nw ? s_warp[lane] : 0;
+    const int sx = warp_incl_scan(x, lane);
+    if (lane < nw) s_warp[lane] = sx - x;
+    if (lane == 31) *total = sx;
   }
-  return v;
+  __syncthreads();
+  const int r = s_warp[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
+// Segmented-scan operator on (segment started, value) pairs, a before b.
+__device__ __forceinline__ void seg_combine(bool fa, int va, bool& fb, int& vb) {
+  if (!fb) vb += va;
+  fb = fb || fa;
+}
+
+__device__ void scan_groups(const EpArgs& a, int* __restrict__ chunk_cnt, int nchunks, int G,
+                            int* __restrict__ group_off, int* __restrict__ group_cnt, int* __restrict__ pad_off,
+                            int cap_rows, int* __restrict__ need, int* __restrict__ miss, int* s_cc) {
+  __shared__ int s_tot[1024];
+  __shared__ int s_off[1024];
+  __shared__ int s_warp[32];
+  __shared__ int s_wv[32];
+  __shared__ bool s_wf[32];
+  __shared__ int s_sum[2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int n = nchunks * G;
+  auto P = [](int i) { return i + (i >> 5); };  // one pad word per 32: conflict-free runs
+  if (s_cc) {
+    // 1) staged: load all counts (written by other blocks: read from L2), then one
+    //    segmented exclusive scan over the flattened [G][nchunks] array, each thread a
+    //    contiguous run of it, a segment per group
+#pragma unroll 8
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s_cc[P(i)] = __ldcg(chunk_cnt + i);
+    __syncthreads();
+    const int per = (n + blockDim.x - 1) / blockDim.x;
+    const int i0 = min(n, (int)threadIdx.x * per), i1 = min(n, i0 + per);
+    bool f = false;
+    int v = 0;
+    for (int i = i0; i < i1; ++i) {
+      if (i % nchunks == 0) {
+        v = 0;
+        f = true;
+      }
+      v += s_cc[P(i)];
+    }
+    // inclusive warp scan of (f, v), then exclusive per thread
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const bool nf = __shfl_up_sync(0xffffffffu, f, o);
+      const int nv = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) seg_combine(nf, nv, f, v);
+    }
+    bool ef = __shfl_up_sync(0xffffffffu, f, 1);
+    int ev = __shfl_up_sync(0xffffffffu, v, 1);
+    if (lane == 0) {
+      ef = false;
+      ev = 0;
+    }
+    if (lane == 31) {
+      s_wf[warp] = f;
+      s_wv[warp] = v;
+    }
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the warp aggregates
+      bool wf = lane < nw ? s_wf[lane] : false;
+      int wv = lane < nw ? s_wv[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const bool nf = __shfl_up_sync(0xffffffffu, wf, o);
+        const int nv = __shfl_up_sync(0xffffffffu, wv, o);
+        if (lane >= o) seg_combine(nf, nv, wf, wv);
+      }
+      const bool xf = __shfl_up_sync(0xffffffffu, wf, 1);
+      const int xv = __shfl_up_sync(0xffffffffu, wv, 1);
+      if (lane < nw) {
+        s_wf[lane] = lane == 0 ? false : xf;
+        s_wv[lane] = lane == 0 ? 0 : xv;
+      }
+    }
+    __syncthreads();
+    bool cf = s_wf[warp];
+    int carry = s_wv[warp];
+    seg_combine(cf, carry, ef, ev);  // prefix of the warp, then of the lanes before
+    int run = ev;
+    for (int i = i0; i < i1; ++i) {
+      if (i % nchunks == 0) run = 0;
+      const int x = s_cc[P(i)];
+      s_cc[P(i)] = run;
+      run += x;
+      if ((i + 1) % nchunks == 0) s_tot[i / nchunks] = run;
+    }
+  } else {
+    // 1) in place in global memory: per group (one warp each, coalesced over its
+    //    contiguous chunk counts)
+    for (int g = warp; g < G; g += nw) {
+      int carry = 0;
+      int* row = chunk_cnt + (size_t)g * nchunks;
+      for (int c0 = 0; c0 < nchunks; c0 += 32) {
+        const int c = c0 + lane;
+        const int v = c < nchunks ? __ldcg(row + c) : 0;  // written by other blocks: read from L2
+        const int incl = warp_incl_scan(v, lane);
+        if (c < nchunks) row[c] = carry + incl - v;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) s_tot[g] = carry;
+    }
+  }
+  __syncthreads();
+  // 2) padded totals and padding counts, scanned over groups: each thread takes a
+  //    contiguous run of groups
+  const int per = (G + blockDim.x - 1) / blockDim.x;
+  const int g0 = min(G, (int)threadIdx.x * per), g1 = min(G, g0 + per);
+  int sp = 0, sq = 0;
+  for (int g = g0; g < g1; ++g) {
+    const int padded = (s_tot[g] + 63) & ~63;
+    sp += padded;
+    sq += padded - s_tot[g];
+  }
+  int base_p = block_excl_scan(sp, s_warp, &s_sum[0]);
+  int base_q = block_excl_scan(sq, s_warp, &s_sum[1]);
+  for (int g = g0; g < g1; ++g) {
+    const int padded = (s_tot[g] + 63) & ~63;
+    s_off[g] = base_p;
+    group_cnt[g] = s_tot[g];
+    pad_off[g] = base_q;
+    base_p += padded;
+    base_q += padded - s_tot[g];
+  }
+  __syncthreads();
+  const int total = s_sum[0], ptotal = s_sum[1];
+  if (threadIdx.x == 0 && need) *need = total;
+  if (total > cap_rows) {
+    // with the worst-case capacity this cannot happen (a guard); with a row budget it
+    // asks the caller for a larger one: the layout is emptied
+    if (threadIdx.x == 0) {
+      if (miss) atomicExch(miss, 1);
+      else record_error(a.status, kErrOverflow);
+    }
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+      group_off[g] = 0;
+      group_cnt[g] = 0;
+      pad_off[g] = 0;
+    }
+    if (threadIdx.x == 0) {
+      group_off[G] = 0;
+      pad_off[G] = 0;
+    }
+    return;
+  }
+  for (int g = threadIdx.x; g < G; g += blockDim.x) group_off[g] = s_off[g];
+  if (threadIdx.x == 0) {
+    group_off[G] = total;
+    pad_off[G] = ptotal;
+  }
+  // 3) chunk bases become absolute row offsets
+  if (s_cc) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) chunk_cnt[i] = s_cc[P(i)] + s_off[i / nchunks];
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) chunk_cnt[i] += s_off[i / nchunks];
+  }
 }
 
 // cap_rows bounds the receive buffers. With `miss` given, cap_rows is the caller's row
@@ -409,84 +662,10 @@ __global__ void __launch_bounds__(1024) recv_scan_kernel(EpArgs a, int* __restri
                                                          int* __restrict__ group_cnt,
                                                          int* __restrict__ pad_off,
                                                          int cap_rows, int* __restrict__ need = nullptr,
-                                                         int* __restrict__ miss = nullptr) {
-  __shared__ int s_tot[1024];
-  __shared__ int s_off[1024];
-  __shared__ int s_pad[1024];
-  __shared__ int s_wsum[2][32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  // 1) per group: exclusive scan over chunks (in place), total rows of the group
-  for (int g = warp; g < G; g += nw) {
-    int carry = 0;
-    for (int c0 = 0; c0 < nchunks; c0 += 32) {
-      const int c = c0 + lane;
-      const int v = c < nchunks ? chunk_cnt[(size_t)c * G + g] : 0;
-      const int incl = warp_incl_scan(v, lane);
-      if (c < nchunks) chunk_cnt[(size_t)c * G + g] = carry + incl - v;
-      carry += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) s_tot[g] = carry;
-  }
-  __syncthreads();
-  // 2) block-wide exclusive scan of padded totals and of padding counts
-  const int g = threadIdx.x;
-  const int tot = g < G ? s_tot[g] : 0;
-  const int padded = (tot + 63) & ~63;
-  const int pad = padded - tot;
-  int ip = warp_incl_scan(padded, lane), iq = warp_incl_scan(pad, lane);
-  if (lane == 31) {
-    s_wsum[0][warp] = ip;
-    s_wsum[1][warp] = iq;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    int vp = lane < nw ? s_wsum[0][lane] : 0, vq = lane < nw ? s_wsum[1][lane] : 0;
-    int sp = warp_incl_scan(vp, lane), sq = warp_incl_scan(vq, lane);
-    if (lane < nw) {
-      s_wsum[0][lane] = sp - vp;
-      s_wsum[1][lane] = sq - vq;
-    }
-  }
-  __syncthreads();
-  const int off = s_wsum[0][warp] + ip - padded;
-  const int poff = s_wsum[1][warp] + iq - pad;
-  if (g < G) {
-    s_off[g] = off;
-    s_pad[g] = poff;
-  }
-  __syncthreads();
-  const int total = G > 0 ? s_off[G - 1] + ((s_tot[G - 1] + 63) & ~63) : 0;
-  const int ptotal = G > 0 ? s_pad[G - 1] + (((s_tot[G - 1] + 63) & ~63) - s_tot[G - 1]) : 0;
-  if (threadIdx.x == 0 && need) *need = total;
-  if (total > cap_rows) {
-    // with the worst-case capacity this cannot happen (a guard); with a row budget it
-    // asks the caller for a larger one
-    if (threadIdx.x == 0) {
-      if (miss) atomicExch(miss, 1);
-      else record_error(a.status, kErrOverflow);
-    }
-    if (g < G) {
-      group_off[g] = 0;
-      group_cnt[g] = 0;
-      pad_off[g] = 0;
-    }
-    if (threadIdx.x == 0) {
-      group_off[G] = 0;
-      pad_off[G] = 0;
-    }
-    return;
-  }
-  if (g < G) {
-    group_off[g] = s_off[g];
-    group_cnt[g] = s_tot[g];
-    pad_off[g] = s_pad[g];
-  }
-  if (threadIdx.x == 0) {
-    group_off[G] = total;
-    pad_off[G] = ptotal;
-  }
-  // 3) chunk bases become absolute row offsets
-  for (int i = threadIdx.x; i < nchunks * G; i += blockDim.x) chunk_cnt[i] += s_off[i % G];
+                                                         int* __restrict__ miss = nullptr, int smem = 0) {
+  extern __shared__ int s_dyn[];
+  scan_groups(a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows, need, miss,
+              smem ? s_dyn : nullptr);
 }
 
 // K4c permute: place every (row, local choice) at its deterministic position inside its
@@ -505,7 +684,7 @@ __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
   const int s = chunk * kChunk + threadIdx.x;
   const int rows = rows_from[src];
   __shared__ int s_base[1024];
-  for (int g = threadIdx.x; g < G; g += blockDim.x) s_base[g] = chunk_base[(size_t)blockIdx.x * G + g];
+  for (int g = threadIdx.x; g < G; g += blockDim.x) s_base[g] = chunk_base[(size_t)g * gridDim.x + blockIdx.x];
   __syncthreads();
   // per-warp entry counts of each group in the current pass (zero between passes)
   constexpr int kWarpsPerChunk = kChunk / 32;
@@ -517,10 +696,25 @@ __global__ void __launch_bounds__(kChunk) recv_permute_kernel(
   // Positions are deterministic: within an expert group, entries of this chunk are
   // ordered by (choice j, slot). Each pass j ranks the block's threads sharing a group:
   // within a warp by __match_any_sync, across warps by per-warp group counts.
+  int le_all[8];
+  float w_all[8];
+  if (s < rows) row_meta_all(a, dst_tk, topk_w, self_tok, meta_tk, src, s, le_all, w_all);
   for (int j = 0; j < a.k; ++j) {
     int le = -1;
     float w = 0.f;
-    if (s < rows) row_meta(a, dst_tk, topk_w, self_tok, meta_tk, src, s, j, &le, &w);
+    if (s < rows) {
+      // registers indexed by the loop counter: the loop is unrolled over k <= 8
+      switch (j) {
+        case 0: le = le_all[0]; w = w_all[0]; break;
+        case 1: le = le_all[1]; w = w_all[1]; break;
+        case 2: le = le_all[2]; w = w_all[2]; break;
+        case 3: le = le_all[3]; w = w_all[3]; break;
+        case 4: le = le_all[4]; w = w_all[4]; break;
+        case 5: le = le_all[5]; w = w_all[5]; break;
+        case 6: le = le_all[6]; w = w_all[6]; break;
+        default: le = le_all[7]; w = w_all[7]; break;
+      }
+    }
     if (le >= G || le < -1) le = -1;  // corrupted entry (recorded by the count kernel)
     const unsigned peers = __match_any_sync(0xffffffffu, le);
     const bool leader = (__ffs(peers) - 1) == lane;
@@ -785,7 +979,10 @@ static int sm_count() {
 
 void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_count, cudaStream_t st) {
   if (W > kMaxW) throw std::runtime_error("EP world size above 64 is not supported");
-  route_plan_kernel<<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count);
+  if (k == 8 && (reinterpret_cast<uintptr_t>(dst_tk) & 15) == 0)
+    route_plan_kernel<8><<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count);
+  else
+    route_plan_kernel<0><<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count);
   check_launch("route_plan");
 }
 
@@ -821,11 +1018,12 @@ void ep_recv_count_scan(const EpArgs& a, const int* dst_tk, const int* meta_tk, 
   if (G > 1024) throw std::runtime_error("at most 1024 local experts");
   if (a.k > 8) throw std::runtime_error("top-k above 8 is not supported by the permute kernel");
   const int nchunks = ((a.cap + kChunk - 1) / kChunk) * a.W;
+  const bool staged = nchunks * G <= kScanSmemEntries;
   recv_count_kernel<<<nchunks, kChunk, 0, st>>>(a, dst_tk, topk_w, self_tok, meta_tk, send_count, rows_from,
                                                 chunk_cnt, G);
   check_launch("recv_count");
-  recv_scan_kernel<<<1, 1024, 0, st>>>(a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows, need,
-                                       miss);
+  recv_scan_kernel<<<1, 1024, staged ? scan_smem_words(nchunks * G) * sizeof(int) : 0, st>>>(
+      a, chunk_cnt, nchunks, G, group_off, group_cnt, pad_off, cap_rows, need, miss, staged ? 1 : 0);
   check_launch("recv_scan");
 }
 
@@ -1011,7 +1209,7 @@ extern "C" int sepx_moe_permute_noalloc(const void* x, const int* topk_e, const 
 
   cudaMemsetAsync(status, 0, sizeof(int), stream);
   noalloc_init_kernel<<<(kNaMaxT * 8 + 255) / 256, 256, 0, stream>>>(s, T, k);
-  route_plan_kernel<<<1, 1024, 0, stream>>>(s + kNaDst, T, k, 1, s + kNaSlot, s + kNaSendCount);
+  route_plan_kernel<0><<<1, 1024, 0, stream>>>(s + kNaDst, T, k, 1, s + kNaSlot, s + kNaSendCount);
   // local slot of each choice = its expert id (all experts on this GPU)
   recv_count_kernel<<<nchunks, kChunk, 0, stream>>>(a, s + kNaDst, topk_w, s + kNaSelfTok, topk_e,
                                                     s + kNaSendCount, s + kNaRowsFrom, s + kNaChunkCnt, E);

@@ -285,7 +285,7 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // The leader (cluster rank 0) issues the MMAs; each CTA holds half of the A rows and
 // half of the B columns in its own shared memory at the same offsets, and gets its
 // half of the accumulator rows in its own TMEM. Operands are loaded by each CTA from
-// this GPU's own global memory, into its own shared memory (no multicast).
+// this GPU's own global memory, into its own shared memory only.
 // ----------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -148,19 +148,22 @@ def test_large_fwd_perf_sanity():
     assert _rel_err(gu, ref) < 1e-2
 
 
-@pytest.mark.parametrize("kind,M,N,G", [("fp32", 256, 384, 4), ("8bit", 256, 384, 4), ("8bit", 256, 512, 4),
-                                         ("8bit", 512, 768, 40)])
-def test_wgrad_adamw_fused_matches_unfused(kind, M, N, G):
+@pytest.mark.parametrize("kind,M,N,G,mult", [("fp32", 256, 384, 4, 1), ("8bit", 256, 384, 4, 1),
+                                              ("8bit", 256, 512, 4, 1), ("8bit", 512, 768, 40, 1),
+                                              ("8bit", 256, 512, 4, 8)])
+def test_wgrad_adamw_fused_matches_unfused(kind, M, N, G, mult):
     """AdamW applied in the wgrad epilogue == wgrad to HBM followed by the standalone update.
 
     N = 384 takes 128-column tiles, 512 / 768 take 256-column tiles; G = 40 gives every
-    CTA several tiles (the 8-bit epilogue's TMA ring wraps many times).
+    CTA several tiles (the 8-bit epilogue's TMA ring wraps many times); mult = 8 makes the
+    reduction long enough (>= 512 rows per group on average) for the three-stage operand
+    ring with a two-deep epilogue ring.
     """
     from spec_ep.ops.grouped_gemm import gg_wgrad
     from spec_ep.ops.optim import FusedAdamW
 
     torch.manual_seed(6)
-    sizes = ([128, 0, 64, 300] * ((G + 3) // 4))[:G]
+    sizes = [s * mult for s in ([128, 0, 64, 300] * ((G + 3) // 4))[:G]]
     off = _offsets(sizes, 64)
     R = off[-1]
     a = torch.zeros(R, M, device="cuda")
