@@ -177,6 +177,13 @@ def breakdown(prof, step_ms, world, args) -> str:
         ks.sort(reverse=True)
         top = "; ".join(f"{k[:60]} {u / 1e3:.2f}" for u, _, k in ks[:3])
         lines.append(f"| {c} | {us / 1e3:.2f} | {100 * us / max(total_us, 1):.1f}% | {n} | {top} |")
+    # the kernels of the largest class by full template name (instances differ by tile
+    # width, stage count, operand majorness and epilogue)
+    big = max(per_cls.items(), key=lambda kv: kv[1][0])
+    lines += ["", f"{big[0]}, per kernel:", "", "| kernel | ms / step | launches |", "|---|---|---|"]
+    for u, cnt, k in sorted(big[1][2], reverse=True)[:10]:
+        name = k.split("(")[0].replace("void ", "").replace("sepx::", "")
+        lines.append(f"| `{name}` | {u / 1e3:.2f} | {cnt} |")
     return "\n".join(lines)
 
 

@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* _
 // dx = r * (w*dy - xhat * mean(xhat * w*dy)); dw += sum_rows dy * xhat (fp32, per-block
 // reduction in shared memory then one atomicAdd per element per block).
 template <int VPL>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(256, 2) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ w,
                                                           const float* __restrict__ rstd,
                                                           const __nv_bfloat16* __restrict__ dy,
@@ -106,26 +106,21 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
   for (int i = 0; i < VPL; ++i)
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
-  // w, and each row's x and dy, stay packed as bf16 (4 registers per 8 elements instead
-  // of 8 floats), so they fit beside the dw accumulators without spilling; every use
-  // unpacks them to the same floats
-  uint4 wr[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) wr[i] = *reinterpret_cast<const uint4*>(w + (i * 32 + lane) * 8);
+  // Only the dw accumulators stay in registers across rows: the second pass over a row
+  // reads x and dy again (L1 / L2 hits: the warp read them a moment before) and w comes
+  // from L1, so a thread needs about half the registers of holding the row, and twice the
+  // warps fit on an SM to hide the loads.
   for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < N; row += nw) {
     const float r = rstd[row];
-    uint4 xr[VPL], gr[VPL];
+    const __nv_bfloat16* xrow = x + (size_t)row * D;
+    const __nv_bfloat16* grow = dy + (size_t)row * D;
     float dot = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) opaque(wr[i]);
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       float xv[8], g[8], wv[8];
-      xr[i] = *reinterpret_cast<const uint4*>(x + (size_t)row * D + (i * 32 + lane) * 8);
-      gr[i] = *reinterpret_cast<const uint4*>(dy + (size_t)row * D + (i * 32 + lane) * 8);
-      unpack8(xr[i], xv);
-      unpack8(gr[i], g);
-      unpack8(wr[i], wv);
+      unpack8(*reinterpret_cast<const uint4*>(xrow + (i * 32 + lane) * 8), xv);
+      unpack8(*reinterpret_cast<const uint4*>(grow + (i * 32 + lane) * 8), g);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(w + (i * 32 + lane) * 8)), wv);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float xh = xv[e] * r;
@@ -134,18 +129,15 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
       }
     }
     dot = warp_sum(dot) / D;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      opaque(xr[i]);
-      opaque(gr[i]);
-      opaque(wr[i]);
-    }
+    // opaque pointers: the compiler must read the row again instead of keeping the first
+    // pass's values live in registers
+    asm volatile("" : "+l"(xrow), "+l"(grow));
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       float xv[8], g[8], wv[8], o[8];
-      unpack8(xr[i], xv);
-      unpack8(gr[i], g);
-      unpack8(wr[i], wv);
+      unpack8(*reinterpret_cast<const uint4*>(xrow + (i * 32 + lane) * 8), xv);
+      unpack8(*reinterpret_cast<const uint4*>(grow + (i * 32 + lane) * 8), g);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(w + (i * 32 + lane) * 8)), wv);
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = r * (g[e] * wv[e] - (xv[e] * r) * dot);
       store8(dx + (size_t)row * D + (i * 32 + lane) * 8, o);
@@ -402,7 +394,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfl
     load8(gu + row * 2 * I + c, g);
     load8(gu + row * 2 * I + I + c, u);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = g[e] / (1.f + __expf(-g[e])) * u[e];
+    for (int e = 0; e < 8; ++e) o[e] = __fdividef(g[e], 1.f + __expf(-g[e])) * u[e];
     store8(h + row * I + c, o);
   }
 }
@@ -417,7 +409,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __
     load8(dh + row * I + c, d);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float s = 1.f / (1.f + __expf(-g[e]));
+      const float s = __fdividef(1.f, 1.f + __expf(-g[e]));
       og[e] = d[e] * u[e] * s * (1.f + g[e] * (1.f - s));
       ou[e] = d[e] * g[e] * s;
     }

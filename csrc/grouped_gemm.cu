@@ -44,14 +44,22 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kEpiWarps = 8;                 // two warps per TMEM lane quarter
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer + MMA + epilogue
-__host__ __device__ constexpr int epi_warps(int) { return kEpiWarps; }
+// Epilogue warps of the fused 8-bit optimizer. Twelve (three per TMEM lane quarter, 128
+// registers, two-job rings) measured slower than eight (168 registers, three-job rings):
+// 1.10 vs 0.96 ms for the 128 x 1536 x 2048 gate|up update at 256 rows per expert.
+constexpr int kOptEpiWarps = 8;
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == kEpiAdamW8 ? kOptEpiWarps : kEpiWarps; }
 __host__ __device__ constexpr int threads_for(int epi) { return 64 + 32 * epi_warps(epi); }
 // fused 8-bit optimizer epilogue: one job = 32 rows x 32 columns of W (bf16, 64B-swizzled)
-// + m codes + v codes (uint8, 32B-swizzled), streamed by TMA three jobs deep per warp
+// + m codes + v codes (uint8, 32B-swizzled), streamed by TMA a few jobs deep per warp
 constexpr int kOptJob = 4096;  // w 2048 B @0, m 1024 B @2048, v 1024 B @3072
-// ring depth per epilogue warp: what fits next to two mainloop stages
-// (three mainloop stages, for long reductions, leave room for two jobs per warp)
+// ring depth per epilogue warp: what fits next to the mainloop stages. With two stages
+// the three-job ring measured fastest for the 128 x 1536 x 2048 gate|up update at 256
+// rows per expert: 0.956 ms, against 1.088 (two jobs) and 1.201 (four jobs, which leaves
+// the SM 28 KB of L1 instead of 60 KB). Three stages (long reductions, or group tables
+// too large for two) leave room for two jobs.
 __host__ __device__ constexpr int opt_ring(int bn, int stages) { return bn == 256 ? (stages >= 3 ? 2 : 3) : 5; }
+constexpr size_t kMaxSmem = 232448;  // dynamic shared memory per block (opt-in)
 
 struct OptMaps {  // kEpiAdamW8 state tensor maps over [G * M, N]
   CUtensorMap w, m, v;
@@ -156,7 +164,10 @@ __device__ __forceinline__ void group_order(const GemmParams& p, int* order, int
   }
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.f + __expf(-x)); }
+// SiLU and the logistic function with the fast division intrinsic (for exp(-x) beyond
+// 2^126 it returns 0, which is the limit of both); epilogues round the results to bf16
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 // One accumulator tile (128 rows x BN fp32 columns in TMEM at t_acc) through the
 // epilogue EPI by the 8 epilogue warps (warps 2..9): rows ti.row0 .. ti.row0 + 127 of the
@@ -274,7 +285,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
             float2 g2 = unpack_bf16x2(gw[e]);
             float2 u2 = unpack_bf16x2(uw[e]);
             float dd0 = d[8 * j + 2 * e], dd1 = d[8 * j + 2 * e + 1];
-            float s0 = 1.f / (1.f + __expf(-g2.x)), s1 = 1.f / (1.f + __expf(-g2.y));
+            float s0 = sigmoid_f(g2.x), s1 = sigmoid_f(g2.y);
             float si0 = g2.x * s0, si1 = g2.y * s1;
             float h0 = si0 * u2.x, h1 = si1 * u2.y;
             dw_part += dd0 * h0 + dd1 * h1;
@@ -502,17 +513,33 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     // 32x32 job arrive by TMA (swizzled, so the per-row 16-byte reads are bank-conflict
     // free) several jobs ahead of the one being computed, the block scales a job ahead, and
     // the updated W / m / v leave by TMA stores. The gradient never reaches HBM.
+    // Jobs: each tile has NJ = BN / 32 column blocks per TMEM lane quarter, shared by the
+    // NWQ warps of the quarter. Column block c of the CTA's tile tt goes to warp
+    // (tt * NJ + c) % NWQ, so over NWQ tiles every warp gets NJ jobs even when NWQ does not
+    // divide NJ; every warp has at least one job in every tile (NJ >= NWQ).
+    constexpr int NWQ = epi_warps(EPI) / 4;
+    constexpr int NJ = BN / 32;
+    static_assert(NJ >= NWQ, "every epilogue warp needs a job in every tile");
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
-    constexpr int kCStep = kEpiWarps / 4;
-    constexpr int J = BN / 32 / kCStep;  // jobs per tile for this warp
+    const int half = (warp - 2) >> 2;  // warp within its lane quarter
     constexpr int kOptRing = opt_ring(BN, STAGES);
     const int ew = warp - 2;
     uint8_t* ring = smem + L::EPI_STAGE_OFF + ew * kOptRing * kOptJob;
     uint64_t* obar =
-        reinterpret_cast<uint64_t*>(smem + L::EPI_STAGE_OFF + kEpiWarps * kOptRing * kOptJob) + ew * kOptRing;
+        reinterpret_cast<uint64_t*>(smem + L::EPI_STAGE_OFF + epi_warps(EPI) * kOptRing * kOptJob) + ew * kOptRing;
     const int my_tiles = total_tiles > (int)blockIdx.x ? (total_tiles - (int)blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-    const int njobs = my_tiles * J;
+    const int njobs = my_tiles * NJ > half ? (my_tiles * NJ - half + NWQ - 1) / NWQ : 0;
+    // tile (in this CTA's sequence) and column block of this warp's job j
+    auto job_tc = [&](int j, int& tt, int& c) {
+      const int x = (j / NJ) * (NWQ * NJ) + (j % NJ) * NWQ + half;
+      tt = x / NJ;
+      c = x - tt * NJ;
+    };
+    auto job_tile = [&](int j) {
+      int tt, c;
+      job_tc(j, tt, c);
+      return tt;
+    };
     const AdamCoef kc = adam_coef(p.opt);
     const int nb_row = p.N / 32;
     // Tile decoding (integer divisions, group offsets) happens once per tile and stream of
@@ -522,21 +549,22 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
       int tt = -1;
       TileInfo ti;
     };
-    auto job_pos = [&](int j, int& grow, int& col0, TileInfo& ti, TileMemo& memo) {
-      const int tt = j / J;
+    auto job_pos = [&](int j, int& grow, int& col0, int& c, TileInfo& ti, TileMemo& memo) {
+      int tt;
+      job_tc(j, tt, c);
       if (tt != memo.tt) {
         memo.ti = decode_tile<RAGGED_K, BN>((int)blockIdx.x + tt * (int)gridDim.x, p, s_prefix);
         memo.tt = tt;
       }
       ti = memo.ti;
       grow = ti.g * p.M + ti.row0 + q * 32;
-      col0 = ti.n0 + (half + (j - tt * J) * kCStep) * 32;
+      col0 = ti.n0 + c * 32;
     };
     TileMemo memo_issue, memo_scale, memo_main;
     auto issue = [&](int j) {  // lane 0
-      int grow, col0;
+      int grow, col0, c;
       TileInfo ti;
-      job_pos(j, grow, col0, ti, memo_issue);
+      job_pos(j, grow, col0, c, ti, memo_issue);
       const int s = j % kOptRing;
       uint8_t* b = ring + s * kOptJob;
       mbar_arrive_expect_tx(&obar[s], kOptJob);
@@ -547,9 +575,9 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     auto load_scales = [&](int j, float& ms, float& vs) {
       ms = vs = 0.f;
       if (j >= njobs) return;
-      int grow, col0;
+      int grow, col0, c;
       TileInfo ti;
-      job_pos(j, grow, col0, ti, memo_scale);
+      job_pos(j, grow, col0, c, ti, memo_scale);
       const size_t bi = (size_t)(grow + lane) * nb_row + col0 / 32;
       ms = p.opt.m_scale[bi];
       vs = p.opt.v_scale[bi];
@@ -562,14 +590,17 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     float msc, vsc;
     load_scales(0, msc, vsc);
     const int sw = (lane >> 1) & 3, sc = (lane >> 2) & 1;  // swizzled 16-byte chunk of this row
+    int cur_tile = -1;
     for (int j = 0; j < njobs; ++j) {
-      int grow, col0;
+      int grow, col0, c;
       TileInfo ti;
-      job_pos(j, grow, col0, ti, memo_main);
-      const int ci = j % J;
+      job_pos(j, grow, col0, c, ti, memo_main);
+      const bool first_of_tile = memo_main.tt != cur_tile;
+      cur_tile = memo_main.tt;
+      const bool last_of_tile = j + 1 == njobs || job_tile(j + 1) != cur_tile;
       float nms, nvs;
       load_scales(j + 1, nms, nvs);
-      if (ci == 0) {
+      if (first_of_tile) {
         if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, s_abort, p.status, p.timeout_ns)) break;
         tc_fence_after();
       }
@@ -578,7 +609,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
       ++consumed;
       uint8_t* b = ring + s * kOptJob;
       float g[32];
-      tmem_ld32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + (half + ci * kCStep) * 32, g);
+      tmem_ld32(tmem_base + acc * BN + ((uint32_t)(q * 32) << 16) + c * 32, g);
       if (ti.num_kb == 0) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) g[e] = 0.f;
@@ -627,7 +658,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
         }
       }
       __syncwarp();
-      if (ci == J - 1) {
+      if (last_of_tile) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -771,16 +802,30 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Epi
     const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(p.aux);
     const float wr = __ldg(p.row_w + r);
     float dw_part = 0.f;
+    // gate|up of this row's next 32 columns are loaded one job ahead, so their latency
+    // overlaps the current job's TMEM load, math and stores (two jobs ahead spills: ten
+    // warps leave 168 registers a thread)
+    const __nv_bfloat16* grow = gu + (size_t)r * p.ld_aux + i0;
+    uint4 gn[4], un[4];
+    auto load_gu = [&](int c) {
+      const uint4* sg = reinterpret_cast<const uint4*>(grow + c * 32);
+      const uint4* su = reinterpret_cast<const uint4*>(grow + p.I + c * 32);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        gn[j] = __ldg(sg + j);
+        un[j] = __ldg(su + j);
+      }
+    };
+    load_gu(half);
 #pragma unroll 1
     for (int c = half; c < BN / 32; c += kCStep) {
-      const uint4* sg = reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + i0 + c * 32);
-      const uint4* su = reinterpret_cast<const uint4*>(gu + (size_t)r * p.ld_aux + p.I + i0 + c * 32);
       uint4 gv[4], uv[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {  // issued before the TMEM load: their latency overlaps it
-        gv[j] = __ldg(sg + j);
-        uv[j] = __ldg(su + j);
+      for (int j = 0; j < 4; ++j) {
+        gv[j] = gn[j];
+        uv[j] = un[j];
       }
+      if (c + kCStep < BN / 32) load_gu(c + kCStep);
       float d[32];
       tmem_ld32(t_row + c * 32, d);
       uint32_t rg[16], ru[16], rh[16];
@@ -793,7 +838,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Epi
           const float2 g2 = unpack_bf16x2(gw[e]);
           const float2 u2 = unpack_bf16x2(uw[e]);
           const float dd0 = zero ? 0.f : d[8 * j + 2 * e], dd1 = zero ? 0.f : d[8 * j + 2 * e + 1];
-          const float s0 = 1.f / (1.f + __expf(-g2.x)), s1 = 1.f / (1.f + __expf(-g2.y));
+          const float s0 = sigmoid_f(g2.x), s1 = sigmoid_f(g2.y);
           const float si0 = g2.x * s0, si1 = g2.y * s1;
           const float h0 = si0 * u2.x, h1 = si1 * u2.y;
           dw_part += dd0 * h0 + dd1 * h1;
@@ -1123,8 +1168,9 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
   using L = GemmSmem<BN, STAGES, EPI>;
   auto kern = grouped_gemm_kernel<BN, STAGES, A_MN, B_MN, RAGGED_K, EPI>;
   size_t smem = L::bytes(p.G);
+  if (smem > kMaxSmem) throw std::runtime_error("grouped_gemm: too many groups for this kernel's shared memory");
   static unsigned long long smem_devices = 0;
-  smem_optin_once(kern, 232448, smem_devices);
+  smem_optin_once(kern, kMaxSmem, smem_devices);
   int grid = num_sms();
   if (max_tiles > 0 && max_tiles < grid) grid = max_tiles;
   if (grid < 1) grid = 1;
@@ -1360,7 +1406,7 @@ void grouped_gemm_wgrad_adamw(const GemmCall& c, cudaStream_t stream) {
       p.n_tiles = p.N / 256;
       // long reductions (many rows per expert: the MMA bounds the tile) take a third
       // mainloop stage; short ones (the optimizer stream bounds it) a deeper state ring
-      if (c.a_rows >= 512LL * p.G)
+      if (c.a_rows >= 512LL * p.G || GemmSmem<256, 2, kEpiAdamW8>::bytes(p.G) > kMaxSmem)
         launch<256, 3, true, true, true, kEpiAdamW8>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream, om);
       else
         launch<256, 2, true, true, true, kEpiAdamW8>(ta, tb, p, p.G * (p.M / 128) * p.n_tiles, stream, om);
