@@ -63,14 +63,58 @@ def dense_dgrad(gy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return out
 
 
+_SM_COUNT: dict = {}
+
+
+def _sm_count(device) -> int:
+    key = str(device)
+    if key not in _SM_COUNT:
+        _SM_COUNT[key] = torch.cuda.get_device_properties(device).multi_processor_count
+    return _SM_COUNT[key]
+
+
+def _split_offsets(rows: int, parts: int, device) -> torch.Tensor:
+    """Cached device tensor of ``parts`` equal row ranges of ``rows`` (multiples of 64)."""
+    key = ("split", rows, parts, str(device))
+    t = _OFFSETS.get(key)
+    if t is None:
+        step = rows // parts
+        t = torch.tensor([i * step for i in range(parts)] + [rows], dtype=torch.int32, device=device)
+        _OFFSETS[key] = t
+    return t
+
+
+def wgrad_split(N: int, K: int, T: int, sms: int) -> int:
+    """Reduction splits for a weight gradient with an ``N x K`` output over ``T`` tokens:
+    1 when its 128 x 256 output tiles already fill half the SMs, else enough equal token
+    ranges (of at least 256 rows, each a multiple of 64) to give about one tile per SM."""
+    tiles = -(-N // 128) * -(-K // 256)
+    if 2 * tiles >= sms or T < 512:
+        return 1
+    parts = min(T // 256, -(-sms // tiles))
+    while parts > 1 and (T % parts or (T // parts) % 64):
+        parts -= 1
+    return max(parts, 1)
+
+
 def dense_wgrad(gy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """``gy [T, N].T @ x [T, K] -> [N, K]`` (weight gradient of ``x @ w.T``, bf16). Rows of
-    the output come in 128-row tiles and tokens in 64-row steps: others are zero-padded."""
+    the output come in 128-row tiles and tokens in 64-row steps: others are zero-padded.
+
+    An output too small to fill the GPU (the router's 128 x 2048: 8 tiles) splits the
+    token dimension: each token range is one group of the ragged-K GEMM writing an fp32
+    partial, and the partials are summed in fp32 before the one rounding to bf16."""
     N, T = gy.shape[1], gy.shape[0]
     gyp = _pad0(_pad1(gy.contiguous(), 128), 64).contiguous()
     xp = _pad0(x.contiguous(), 64).contiguous()
-    out = torch.empty(gyp.shape[1], x.shape[1], device=x.device, dtype=torch.bfloat16)
-    load().gemm_wgrad_bf16(gyp, xp, _rows_offsets(xp.shape[0], x.device), out, None)
+    parts = wgrad_split(gyp.shape[1], x.shape[1], xp.shape[0], _sm_count(x.device))
+    if parts > 1:
+        part = torch.empty(parts, gyp.shape[1], x.shape[1], device=x.device, dtype=torch.float32)
+        load().gg_wgrad(gyp, xp, _split_offsets(xp.shape[0], parts, x.device), part, None)
+        out = part.sum(0).to(torch.bfloat16)
+    else:
+        out = torch.empty(gyp.shape[1], x.shape[1], device=x.device, dtype=torch.bfloat16)
+        load().gemm_wgrad_bf16(gyp, xp, _rows_offsets(xp.shape[0], x.device), out, None)
     return out if gyp.shape[1] == N else out[:N]
 
 

@@ -1,7 +1,8 @@
 """Dense projections on the tcgen05 GEMM (``spec_ep.ops.linear``) against fp32 PyTorch:
 forward, input gradient and weight gradient, at the model's projection shapes (fused
 QKV, attention output, router with 128 outputs, and a vocabulary whose last 256-column
-tile is partial), plus small routers and token counts that take the zero-padded path."""
+tile is partial), plus small routers and token counts that take the zero-padded path;
+(4096, 2048, 128) and (4160, 512, 8) take the weight gradient split over token ranges."""
 import pytest
 import torch
 
@@ -13,7 +14,8 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("T,K,N", [(512, 512, 1280), (512, 1024, 512), (256, 512, 128), (256, 512, 4224),
-                                   (384, 256, 256), (256, 512, 8), (200, 512, 48)])
+                                   (384, 256, 256), (256, 512, 8), (200, 512, 48), (4096, 2048, 128),
+                                   (4160, 512, 8)])
 def test_linear_forward_backward_matches_fp32(T, K, N):
     from spec_ep.ops.linear import linear
 
@@ -32,6 +34,15 @@ def test_linear_forward_backward_matches_fp32(T, K, N):
     assert _rel(y, yr) < 1e-2
     assert _rel(x.grad, xr.grad) < 1e-2
     assert _rel(w.grad, wr.grad) < 1e-2
+
+
+def test_wgrad_split_choice():
+    from spec_ep.ops.linear import wgrad_split
+
+    assert wgrad_split(128, 2048, 4096, 148) == 16  # router: 8 tiles -> 128
+    assert wgrad_split(5120, 2048, 4096, 148) == 1  # QKV fills the GPU
+    assert wgrad_split(128, 2048, 4160, 148) == 13  # 320-row ranges (multiples of 64)
+    assert wgrad_split(128, 2048, 448, 148) == 1  # too few tokens to split
 
 
 def test_lm_head_xent_on_own_gemm_matches_reference():
