@@ -79,7 +79,10 @@ def main():
     torch.manual_seed(0)
     model = Qwen3MoeForCausalLM(cfg, ep, device=dev)
     tr = Trainer(model, lr=1e-4, expert_state=args.expert_state)
-    ids = torch.randint(0, cfg.vocab_size, (1, args.seq), device=dev)
+    # different tokens on every rank (as in bench.py): identical batches would route every
+    # rank's copy of a token to the same experts and pile the rows onto a few ranks
+    gen = torch.Generator().manual_seed(rank)
+    ids = torch.randint(0, cfg.vocab_size, (1, args.seq), generator=gen).to(dev)
     lab = torch.cat([ids[:, 1:], torch.full((1, 1), -1, device=dev)], 1).int()
     for _ in range(args.warmup):
         tr.train_step(ids, lab, args.seq - 1)
