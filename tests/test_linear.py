@@ -36,14 +36,6 @@ def test_linear_forward_backward_matches_fp32(T, K, N):
     assert _rel(w.grad, wr.grad) < 1e-2
 
 
-def test_wgrad_split_choice():
-    from spec_ep.ops.linear import wgrad_split
-
-    assert wgrad_split(128, 2048, 4096, 148) == 16  # router: 8 tiles -> 128
-    assert wgrad_split(5120, 2048, 4096, 148) == 1  # QKV fills the GPU
-    assert wgrad_split(128, 2048, 4160, 148) == 13  # 320-row ranges (multiples of 64)
-    assert wgrad_split(128, 2048, 448, 148) == 1  # too few tokens to split
-
 
 def test_lm_head_xent_on_own_gemm_matches_reference():
     from spec_ep.ops.loss import lm_head_xent, lm_head_xent_reference
