@@ -370,22 +370,6 @@ __global__ void __launch_bounds__(256) dispatch_kernel(EpArgs a, const __nv_bflo
 // ------------------------------------------------------------------------------------
 // Receive side. Rows are enumerated src-major: (src, slot) for slot < rows_from[src].
 // ------------------------------------------------------------------------------------
-__device__ __forceinline__ void row_meta(const EpArgs& a, const int* dst_tk, const float* topk_w,
-                                         const int* self_tok, const int* meta_tk,
-                                         int src, int s, int j, int* le, float* w) {
-  if (src == a.rank) {
-    const int t = self_tok[s];
-    *le = (__ldg(dst_tk + t * a.k + j) == a.rank) ? __ldg(meta_tk + t * a.k + j) : -1;
-    *w = __ldg(topk_w + t * a.k + j);
-  } else {
-    const char* base = reinterpret_cast<const char*>(a.peer_base[a.rank]);
-    const int16_t* re = reinterpret_cast<const int16_t*>(base + a.off_recv_e) + ((size_t)src * a.cap + s) * a.k;
-    const float* rw = reinterpret_cast<const float*>(base + a.off_recv_w) + ((size_t)src * a.cap + s) * a.k;
-    *le = re[j];
-    *w = rw[j];
-  }
-}
-
 // All k (local expert, weight) entries of received row (src, s), loaded at once (the
 // permute kernel's passes over the choices then wait on no memory). k <= 8.
 __device__ __forceinline__ void row_meta_all(const EpArgs& a, const int* dst_tk, const float* topk_w,
@@ -420,7 +404,6 @@ constexpr int kChunk = 128;
 // shared memory under 48 KB); larger layouts are scanned in place in global memory.
 constexpr int kScanSmemEntries = 8192;
 __host__ __device__ constexpr int scan_smem_words(int n) { return n + (n >> 5) + 1; }
-
 
 // K4a count: per chunk of 128 rows, rows per local expert -> chunk_cnt[g][chunk].
 __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int* __restrict__ dst_tk,
@@ -475,11 +458,6 @@ __global__ void __launch_bounds__(kChunk) recv_count_kernel(EpArgs a, const int*
     chunk_cnt[(size_t)g * gridDim.x + blockIdx.x] = s_cnt[g];
 }
 
-// K4b scan. chunk_cnt is laid out [G][nchunks] (each group's chunk counts contiguous).
-// Per group: exclusive scan over chunks (in place) and the group's total; then an
-// exclusive scan of the 64-row-padded group totals gives group_off / pad_off, and the
-// chunk entries become absolute row offsets. Any block size that is a multiple of 32.
-
 // Block-wide exclusive scan of one int per thread; *total (shared) gets the sum.
 __device__ __forceinline__ int block_excl_scan(int v, int* s_warp, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -504,6 +482,13 @@ __device__ __forceinline__ void seg_combine(bool fa, int va, bool& fb, int& vb) 
   fb = fb || fa;
 }
 
+// K4b scan. chunk_cnt is laid out [G][nchunks] (each group's chunk counts contiguous).
+// Per group: exclusive scan over chunks and the group's total; then an exclusive scan of
+// the 64-row-padded group totals gives group_off / pad_off, and the chunk entries become
+// absolute row offsets. With s_cc (shared memory for scan_smem_words(G * nchunks) words)
+// the counts are staged and scanned as one segmented scan, each thread a contiguous run;
+// without it, one warp per group scans in place in global memory. Any block size that is
+// a multiple of 32.
 __device__ void scan_groups(const EpArgs& a, int* __restrict__ chunk_cnt, int nchunks, int G,
                             int* __restrict__ group_off, int* __restrict__ group_cnt, int* __restrict__ pad_off,
                             int cap_rows, int* __restrict__ need, int* __restrict__ miss, int* s_cc) {

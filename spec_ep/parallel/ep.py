@@ -124,8 +124,6 @@ class ExpertParallel:
             dist.barrier(group=group)
         # worst case: every token of every source routes all k choices here
         self.cap_rows = self.world * max_tokens * top_k + self.G * 64
-        self.rows_last = 0
-        self.nchunks = self.world * ((max_tokens + 127) // 128)
         self.timeout_s = float(timeout_s)
         self.epoch = 0
         self.cur_epoch = 0
@@ -209,9 +207,6 @@ class ExpertParallel:
             self.epoch += 1
             self.cur_epoch = self.epoch
         return self.cur_epoch
-
-    def _args(self):
-        return self.done, self.status, self.timeout_s
 
     # -------------------------------------------------------------------------------
     # Row budgets: no host sync inside a pass
@@ -315,10 +310,8 @@ class ExpertParallel:
             x, topk_e.int().contiguous(), topk_w, self.e2r, self.e2l, dst_in, meta_in, self.G, ep, rows_mode,
             self.cap_rows, self._need[idx:idx + 1] if budget else None, self._miss if budget else None,
             self.done[0:1], self.status, self.timeout_s, self.fp8_dispatch)
-        if not static_rows and not budget:
-            self.rows_last = R
-            if idx is not None:
-                self._seen = max(self._seen, R)
+        if not static_rows and not budget and idx is not None:
+            self._seen = max(self._seen, R)
         if idx is not None:
             self._pass = idx + 1
         if self.stats_on:
