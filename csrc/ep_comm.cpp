@@ -294,6 +294,12 @@ class EpComm {
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
     at::Tensor out = at::empty({T, (int64_t)args_.H}, y.options());
     auto a = call_args((int)T, 1, epoch, done, status, timeout_s);
+    if (world_ == 1) {  // every expert row is local: one kernel, no return slab
+      sepx::ep_combine_local(a, y.data_ptr(), inv_rows.data_ptr<int>(), row_w.data_ptr<float>(),
+                             slot.data_ptr<int>(), dst_tk.data_ptr<int>(), true, nullptr,
+                             residual.has_value() ? residual->data_ptr() : nullptr, out.data_ptr(), nullptr, st);
+      return out;
+    }
     sepx::ep_combine(a, y.data_ptr(), inv_rows.data_ptr<int>(), row_w.data_ptr<float>(), rows_from.data_ptr<int>(),
                      true, nullptr, st);
     sepx::ep_source_reduce(a, slot.data_ptr<int>(), dst_tk.data_ptr<int>(),
@@ -326,6 +332,24 @@ class EpComm {
     cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
     sepx::ep_combine(a, y.data_ptr(), inv_rows.data_ptr<int>(), row_w.data_ptr<float>(), rows_from.data_ptr<int>(),
                      weighted, row_val.has_value() ? row_val->data_ptr<float>() : nullptr, st);
+  }
+
+  // World size 1: combine + source reduce in one kernel into out [T, H] (and the
+  // per-choice values into val [T, k]); the same bits as combine followed by source_reduce.
+  void combine_local(const at::Tensor& y, const at::Tensor& inv_rows, const at::Tensor& row_w,
+                     const at::Tensor& slot, const at::Tensor& dst_tk, bool weighted,
+                     const c10::optional<at::Tensor>& row_val, const c10::optional<at::Tensor>& residual,
+                     at::Tensor& out, const c10::optional<at::Tensor>& val, at::Tensor& status) {
+    TORCH_CHECK(world_ == 1, "combine_local runs at world size 1");
+    TORCH_CHECK(out.is_contiguous() && out.size(1) == args_.H, "out must be contiguous [T, H]");
+    sepx::EpArgs a = args_;
+    a.T = (int)out.size(0);
+    a.status = status.data_ptr<int>();
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    sepx::ep_combine_local(a, y.data_ptr(), inv_rows.data_ptr<int>(), row_w.data_ptr<float>(), slot.data_ptr<int>(),
+                           dst_tk.data_ptr<int>(), weighted, row_val.has_value() ? row_val->data_ptr<float>() : nullptr,
+                           residual.has_value() ? residual->data_ptr() : nullptr, out.data_ptr(),
+                           val.has_value() ? val->data_ptr<float>() : nullptr, st);
   }
 
   void source_reduce(const at::Tensor& slot, const at::Tensor& dst_tk, const c10::optional<at::Tensor>& residual,
@@ -548,6 +572,7 @@ void register_ep_comm(pybind11::module& m) {
       .def("wait_rows", &EpComm::wait_rows)
       .def("slabs", &EpComm::slabs)
       .def("combine", &EpComm::combine)
+      .def("combine_local", &EpComm::combine_local)
       .def("source_reduce", &EpComm::source_reduce);
   py::class_<SymmBuffer>(m, "SymmBuffer")
       .def(py::init<int, int, int64_t, int>(), py::arg("world"), py::arg("rank"), py::arg("bytes"), py::arg("device"))

@@ -61,6 +61,10 @@ void ep_recv_gather(const EpArgs& a, const void* x, const int* self_tok, const i
 void ep_wait_rows(const EpArgs& a, const int* send_count, int* rows_from, cudaStream_t st);
 void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float* row_w,
                 const int* rows_from, bool weighted, const float* row_val, cudaStream_t st);
+// World size 1: combine and source reduce in one kernel (same bits as the pair).
+void ep_combine_local(const EpArgs& a, const void* y, const int* inv_rows, const float* row_w, const int* slot,
+                      const int* dst_tk, bool weighted, const float* row_val, const void* residual, void* out,
+                      float* val, cudaStream_t st);
 void ep_source_reduce(const EpArgs& a, const int* slot, const int* dst_tk, const void* residual, void* out,
                       float* val, cudaStream_t st);
 

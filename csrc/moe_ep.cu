@@ -943,6 +943,88 @@ __global__ void __launch_bounds__(256) source_reduce_kernel(EpArgs a, const int*
   }
 }
 
+// ------------------------------------------------------------------------------------
+// K5 + K7 on one rank (W == 1): every expert row is local, so each token's gate-weighted
+// sum goes straight to out, plus the residual, with no return slab, no header and no
+// second kernel. The sum is rounded to bf16 before the residual is added, as the combine
+// and source-reduce kernels do, so the result has the same bits as that pair.
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) local_combine_kernel(EpArgs a, const __nv_bfloat16* __restrict__ y,
+                                                            const int* __restrict__ inv_rows,
+                                                            const float* __restrict__ row_w,
+                                                            const int* __restrict__ slot,
+                                                            const int* __restrict__ dst_tk, int weighted,
+                                                            const float* __restrict__ row_val,
+                                                            const __nv_bfloat16* __restrict__ residual,
+                                                            __nv_bfloat16* __restrict__ out,
+                                                            float* __restrict__ val) {
+  const int lane = threadIdx.x & 31;
+  const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int vec = a.H / 8;
+  for (int t = gwarp; t < a.T; t += nw) {
+    const int s = __ldg(slot + t);
+    const int* inv = inv_rows + (size_t)(s < 0 ? 0 : s) * a.k;
+    int plist[8];
+    float wl[8];
+    int np = 0;
+    if (s >= 0) {
+      for (int j = 0; j < a.k && j < 8; ++j) {
+        const int p = inv[j];
+        if (p >= 0) {
+          plist[np] = p;
+          wl[np] = weighted ? row_w[p] : 1.f;
+          ++np;
+        }
+      }
+    }
+    if (val && lane < a.k) {
+      const int j = lane;
+      const int p = (s >= 0 && __ldg(dst_tk + t * a.k + j) >= 0) ? inv[j] : -1;
+      val[t * a.k + j] = p >= 0 ? row_val[p] : 0.f;
+    }
+    for (int c = lane; c < vec; c += 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < np) v[q] = reinterpret_cast<const uint4*>(y + (size_t)plist[q] * a.H)[c];
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (q >= np) break;
+        float2 f0 = unpack_bf16x2(v[q].x), f1 = unpack_bf16x2(v[q].y), f2 = unpack_bf16x2(v[q].z),
+               f3 = unpack_bf16x2(v[q].w);
+        const float w = wl[q];
+        acc[0] += w * f0.x; acc[1] += w * f0.y; acc[2] += w * f1.x; acc[3] += w * f1.y;
+        acc[4] += w * f2.x; acc[5] += w * f2.y; acc[6] += w * f3.x; acc[7] += w * f3.y;
+      }
+      float r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (residual) {
+        const uint4 x = reinterpret_cast<const uint4*>(residual + (size_t)t * a.H)[c];
+        float2 f0 = unpack_bf16x2(x.x), f1 = unpack_bf16x2(x.y), f2 = unpack_bf16x2(x.z), f3 = unpack_bf16x2(x.w);
+        r[0] = f0.x; r[1] = f0.y; r[2] = f1.x; r[3] = f1.y;
+        r[4] = f2.x; r[5] = f2.y; r[6] = f3.x; r[7] = f3.y;
+      }
+      if (s >= 0) {  // the partial as the two-kernel path stores it (bf16), then the sum
+        const uint32_t pk[4] = {pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7])};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(pk[e]);
+          r[2 * e] += f.x;
+          r[2 * e + 1] += f.y;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(r[0], r[1]);
+      o.y = pack_bf16x2(r[2], r[3]);
+      o.z = pack_bf16x2(r[4], r[5]);
+      o.w = pack_bf16x2(r[6], r[7]);
+      reinterpret_cast<uint4*>(out + (size_t)t * a.H)[c] = o;
+    }
+  }
+}
+
 // =====================================================================================
 // launchers
 // =====================================================================================
@@ -1064,6 +1146,20 @@ void ep_combine(const EpArgs& a, const void* y, const int* inv_rows, const float
   combine_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(y), inv_rows, row_w, rows_from,
                                          weighted ? 1 : 0, row_val, nullptr);
   check_launch("combine");
+}
+
+void ep_combine_local(const EpArgs& a, const void* y, const int* inv_rows, const float* row_w, const int* slot,
+                      const int* dst_tk, bool weighted, const float* row_val, const void* residual, void* out,
+                      float* val, cudaStream_t st) {
+  if (a.W != 1) throw std::runtime_error("the local combine is for world size 1");
+  if (a.k > 8) throw std::runtime_error("top-k above 8 is not supported by the combine");
+  if (a.T == 0) return;
+  const int blocks = std::max(1, std::min(sm_count() * 2, (a.T + 7) / 8));
+  local_combine_kernel<<<blocks, 256, 0, st>>>(a, reinterpret_cast<const __nv_bfloat16*>(y), inv_rows, row_w, slot,
+                                               dst_tk, weighted ? 1 : 0, row_val,
+                                               reinterpret_cast<const __nv_bfloat16*>(residual),
+                                               reinterpret_cast<__nv_bfloat16*>(out), val);
+  check_launch("local_combine");
 }
 
 void ep_source_reduce(const EpArgs& a, const int* slot, const int* dst_tk, const void* residual, void* out,

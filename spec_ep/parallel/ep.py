@@ -71,6 +71,7 @@ class EPState:
     row_w: torch.Tensor
     row_src: torch.Tensor
     inv_rows: torch.Tensor
+    local_bwd: tuple | None = None  # world size 1: (input-gradient rows, router-weight grads) for the finish
 
 
 class ExpertParallel:
@@ -342,7 +343,11 @@ class ExpertParallel:
 
     def combine_bwd_send(self, dxp, row_dw, st: EPState):
         """Store this rank's input-gradient partials (and router-weight gradients) into the
-        source ranks' return slabs; independent local work can run before the finish."""
+        source ranks' return slabs; independent local work can run before the finish. At
+        world size 1 nothing leaves the GPU: the finish does both steps in one kernel."""
+        if self.world == 1:
+            st.local_bwd = (dxp, row_dw)
+            return
         self.comm.combine(dxp, st.inv_rows, st.row_w, st.rows_from, False, row_dw, st.T, self.cur_epoch,
                           self.done[1:2], self.status, self.timeout_s)
 
@@ -350,6 +355,12 @@ class ExpertParallel:
         """Wait for every rank's partials of this layer and sum them per token."""
         dx = torch.empty(st.T, self.H, dtype=torch.bfloat16, device=self.device)
         dw = torch.empty(st.T, self.k, dtype=torch.float32, device=self.device)
+        if self.world == 1:
+            dxp, row_dw = st.local_bwd
+            st.local_bwd = None
+            self.comm.combine_local(dxp, st.inv_rows, st.row_w, st.slot, st.dst_tk, False, row_dw, None, dx, dw,
+                                    self.status)
+            return dx, dw
         self.comm.source_reduce(st.slot, st.dst_tk, None, dx, dw, self.cur_epoch, self.done[1:2],
                                 self.status, self.timeout_s)
         return dx, dw
