@@ -250,10 +250,12 @@ class EpComm {
     at::Tensor slot = v[0].view({T, W}), send_count = v[1], self_tok = v[2], rows_from = v[3], chunk_cnt = v[4],
                group_off = v[5], group_cnt = v[6], pad_off = v[7];
     sepx::ep_route_plan(dst_tk.data_ptr<int>(), (int)T, (int)k, (int)W, slot.data_ptr<int>(),
-                        send_count.data_ptr<int>(), st);
+                        send_count.data_ptr<int>(), st, self_tok.data_ptr<int>(), rank_);
     auto a = call_args((int)T, 0, epoch, done, status, timeout_s);
-    sepx::ep_dispatch(a, x.data_ptr(), dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), topk_w.data_ptr<float>(),
-                      slot.data_ptr<int>(), self_tok.data_ptr<int>(), send_count.data_ptr<int>(), true, st, fp8);
+    // at world size 1 nothing is sent: the plan's self_tok is all the dispatch would write
+    if (W > 1)
+      sepx::ep_dispatch(a, x.data_ptr(), dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), topk_w.data_ptr<float>(),
+                        slot.data_ptr<int>(), self_tok.data_ptr<int>(), send_count.data_ptr<int>(), true, st, fp8);
     const bool budget = rows_mode > 0;
     sepx::ep_recv_count_scan(a, dst_tk.data_ptr<int>(), meta_tk.data_ptr<int>(), topk_w.data_ptr<float>(),
                              self_tok.data_ptr<int>(), send_count.data_ptr<int>(), G,

@@ -38,7 +38,9 @@ struct EpArgs {
 // meta_tk[t][j] = value delivered with the row (local expert slot on that rank).
 void ep_route_tables(const int* topk_e, const int* e2r, const int* e2l, int n, int* dst, int* meta,
                      cudaStream_t st);
-void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_count, cudaStream_t st);
+// self_tok (optional): also the map slot -> token of the rows that stay on `rank`.
+void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_count, cudaStream_t st,
+                   int* self_tok = nullptr, int rank = 0);
 void ep_dispatch(const EpArgs& a, const void* x, const int* dst_tk, const int* meta_tk, const float* topk_w,
                  const int* slot, int* self_tok, const int* send_count, bool with_meta, cudaStream_t st,
                  bool fp8 = false);

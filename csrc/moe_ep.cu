@@ -99,10 +99,14 @@ __device__ __forceinline__ unsigned long long token_mask(const int* __restrict__
 
 constexpr int kPlanRounds = 4;  // rounds of 1024 tokens whose loads are issued together
 
+// self_tok (optional): also writes self_tok[slot[t][rank]] = t for the tokens that stay on
+// this rank (the receive side's map of its own rows), which at world size 1 is all the
+// dispatch kernel would do.
 template <int KV>
 __global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict__ dst_tk, int T,
                                                           int k, int W, int* __restrict__ slot,
-                                                          int* __restrict__ send_count) {
+                                                          int* __restrict__ send_count,
+                                                          int* __restrict__ self_tok = nullptr, int rank = 0) {
   // Tokens in passes of kPlanRounds x 1024 (one per thread per round, every load of a pass
   // in flight at once). Per destination, a warp ballot gives each token its rank among the
   // warp's senders; the 128 per-warp totals of a pass (round-major, so token order) are
@@ -154,7 +158,10 @@ __global__ void __launch_bounds__(1024) route_plan_kernel(const int* __restrict_
       for (int d = 0; d < W; ++d) {  // every lane takes part in the ballot; only real tokens store
         const unsigned b = __ballot_sync(0xffffffffu, (m[r] >> d) & 1ull);
         const int before = __popc(b & ((1u << lane) - 1u));
-        if (t < T) slot[(size_t)t * W + d] = ((m[r] >> d) & 1ull) ? s_warp[r * nwarps + warp][d] + before : -1;
+        const bool sent = (m[r] >> d) & 1ull;
+        const int sl = s_warp[r * nwarps + warp][d] + before;
+        if (t < T) slot[(size_t)t * W + d] = sent ? sl : -1;
+        if (self_tok && d == rank && sent && t < T) self_tok[sl] = t;
       }
     }
     __syncthreads();
@@ -1044,12 +1051,13 @@ static int sm_count() {
   return n;
 }
 
-void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_count, cudaStream_t st) {
+void ep_route_plan(const int* dst_tk, int T, int k, int W, int* slot, int* send_count, cudaStream_t st,
+                   int* self_tok, int rank) {
   if (W > kMaxW) throw std::runtime_error("EP world size above 64 is not supported");
   if (k == 8 && (reinterpret_cast<uintptr_t>(dst_tk) & 15) == 0)
-    route_plan_kernel<8><<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count);
+    route_plan_kernel<8><<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count, self_tok, rank);
   else
-    route_plan_kernel<0><<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count);
+    route_plan_kernel<0><<<1, 1024, 0, st>>>(dst_tk, T, k, W, slot, send_count, self_tok, rank);
   check_launch("route_plan");
 }
 

@@ -330,8 +330,9 @@ class ExpertParallel:
 
     def dispatch_bwd(self, dy, st: EPState):
         ep = self._next_epoch()
-        self.comm.dispatch(dy, st.dst_tk, st.meta_tk, st.topk_w, st.slot, st.self_tok, st.send_count,
-                           False, ep, self.done[0:1], self.status, self.timeout_s, False)
+        if self.world > 1:  # at world size 1 the gather reads dy's rows in place
+            self.comm.dispatch(dy, st.dst_tk, st.meta_tk, st.topk_w, st.slot, st.self_tok, st.send_count,
+                               False, ep, self.done[0:1], self.status, self.timeout_s, False)
         dyp = torch.empty(st.xp.shape[0], self.H, dtype=torch.bfloat16, device=self.device)
         self.comm.recv_gather(dy, st.self_tok, st.row_src, st.group_off, st.send_count, dyp, ep, self.done[0:1],
                               self.status, self.timeout_s)
