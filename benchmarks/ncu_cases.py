@@ -105,8 +105,8 @@ def main():
         labels = torch.randint(0, 151936, (4096,), device=dev).int()
         loss = torch.empty(4096, device=dev)
         for _ in range(args.reps):
-            C.rmsnorm_fwd(x, w, y, rstd, 1e-6)
-            C.rmsnorm_bwd(x, w, rstd, y, dx, dw)
+            C.rmsnorm_fwd(x, w, y, rstd, 1e-6, None, None)
+            C.rmsnorm_bwd(x, w, rstd, y, dx, dw, None)
             q, kk, v = qk_norm_rope(qkv.requires_grad_(), wq, wk, 32, 4)
             torch.autograd.backward([q, kk, v], [torch.ones_like(q), torch.ones_like(kk), torch.ones_like(v)])
             C.router_topk(logits, None, 8, True, te, tw, probs)

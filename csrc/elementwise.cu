@@ -57,11 +57,15 @@ __device__ __forceinline__ float warp_max(float v) {
 // =====================================================================================
 // RMSNorm: y = w * x * rsqrt(mean(x^2) + eps). One warp per row; D % 256 == 0, D <= 8192.
 // =====================================================================================
+// With `add` (and `sum`): the input is s = x + add, rounded to bf16 as a bf16 tensor add
+// rounds it, and s is written to `sum` (the residual stream) before it is normalised.
 template <int VPL>  // 8-element vectors per lane
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ w,
                                                           __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
-                                                          int N, int D, float eps) {
+                                                          int N, int D, float eps,
+                                                          const __nv_bfloat16* __restrict__ add = nullptr,
+                                                          __nv_bfloat16* __restrict__ sum = nullptr) {
   const int lane = threadIdx.x & 31;
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (row >= N) return;
@@ -69,7 +73,15 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* _
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    load8(x + (size_t)row * D + (i * 32 + lane) * 8, v[i]);
+    const size_t off = (size_t)row * D + (i * 32 + lane) * 8;
+    load8(x + off, v[i]);
+    if (add) {
+      float a[8];
+      load8(add + off, a);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = __bfloat162float(__float2bfloat16(v[i][e] + a[e]));
+      store8(sum + off, v[i]);
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
   }
@@ -94,7 +106,8 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_kernel(const __nv_bfloat16
                                                           const float* __restrict__ rstd,
                                                           const __nv_bfloat16* __restrict__ dy,
                                                           __nv_bfloat16* __restrict__ dx, float* __restrict__ dw,
-                                                          int N, int D) {
+                                                          int N, int D,
+                                                          const __nv_bfloat16* __restrict__ dres = nullptr) {
   extern __shared__ float s_dw[];  // [D]
   for (int i = threadIdx.x; i < D; i += blockDim.x) s_dw[i] = 0.f;
   __syncthreads();
@@ -140,6 +153,12 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_kernel(const __nv_bfloat16
       unpack8(__ldg(reinterpret_cast<const uint4*>(w + (i * 32 + lane) * 8)), wv);
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = r * (g[e] * wv[e] - (xv[e] * r) * dot);
+      if (dres) {  // the input's other gradient, added as a bf16 tensor add would
+        float d[8];
+        load8(dres + (size_t)row * D + (i * 32 + lane) * 8, d);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = __bfloat162float(__float2bfloat16(o[e])) + d[e];
+      }
       store8(dx + (size_t)row * D + (i * 32 + lane) * 8, o);
     }
   }
@@ -151,38 +170,43 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_kernel(const __nv_bfloat16
   for (int i = threadIdx.x; i < D; i += blockDim.x) atomicAdd(dw + i, s_dw[i]);
 }
 
-void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int N, int D, float eps, cudaStream_t st) {
+void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int N, int D, float eps, cudaStream_t st,
+                 const void* add, void* sum) {
   if (D % 256 || D > 8192) throw std::runtime_error("rmsnorm: D must be a multiple of 256, <= 8192");
+  if ((add == nullptr) != (sum == nullptr)) throw std::runtime_error("rmsnorm: add and sum go together");
   const int blocks = (N + 7) / 8;
   auto X = reinterpret_cast<const __nv_bfloat16*>(x);
   auto Wt = reinterpret_cast<const __nv_bfloat16*>(w);
   auto Y = reinterpret_cast<__nv_bfloat16*>(y);
+  auto A = reinterpret_cast<const __nv_bfloat16*>(add);
+  auto S = reinterpret_cast<__nv_bfloat16*>(sum);
   switch (D / 256) {
-    case 1: rmsnorm_fwd_kernel<1><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
-    case 2: rmsnorm_fwd_kernel<2><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
-    case 4: rmsnorm_fwd_kernel<4><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
-    case 8: rmsnorm_fwd_kernel<8><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
-    case 16: rmsnorm_fwd_kernel<16><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
-    case 32: rmsnorm_fwd_kernel<32><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps); break;
+    case 1: rmsnorm_fwd_kernel<1><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps, A, S); break;
+    case 2: rmsnorm_fwd_kernel<2><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps, A, S); break;
+    case 4: rmsnorm_fwd_kernel<4><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps, A, S); break;
+    case 8: rmsnorm_fwd_kernel<8><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps, A, S); break;
+    case 16: rmsnorm_fwd_kernel<16><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps, A, S); break;
+    case 32: rmsnorm_fwd_kernel<32><<<blocks, 256, 0, st>>>(X, Wt, Y, rstd, N, D, eps, A, S); break;
     default: throw std::runtime_error("rmsnorm: unsupported D");
   }
   check("rmsnorm_fwd");
 }
 
 void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, void* dx, float* dw, int N, int D,
-                 int num_sms, cudaStream_t st) {
+                 int num_sms, cudaStream_t st, const void* dres) {
   if (D % 256 || D > 8192) throw std::runtime_error("rmsnorm: D must be a multiple of 256, <= 8192");
   const int blocks = std::min((N + 7) / 8, num_sms * 2);
   auto X = reinterpret_cast<const __nv_bfloat16*>(x);
   auto Wt = reinterpret_cast<const __nv_bfloat16*>(w);
   auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
   auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
+  auto DR = reinterpret_cast<const __nv_bfloat16*>(dres);
   const size_t sm = D * sizeof(float);
   switch (D / 256) {
-    case 1: rmsnorm_bwd_kernel<1><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D); break;
-    case 2: rmsnorm_bwd_kernel<2><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D); break;
-    case 4: rmsnorm_bwd_kernel<4><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D); break;
-    case 8: rmsnorm_bwd_kernel<8><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D); break;
+    case 1: rmsnorm_bwd_kernel<1><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D, DR); break;
+    case 2: rmsnorm_bwd_kernel<2><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D, DR); break;
+    case 4: rmsnorm_bwd_kernel<4><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D, DR); break;
+    case 8: rmsnorm_bwd_kernel<8><<<blocks, 256, sm, st>>>(X, Wt, rstd, DY, DX, dw, N, D, DR); break;
     default: throw std::runtime_error("rmsnorm_bwd: unsupported D");
   }
   check("rmsnorm_bwd");

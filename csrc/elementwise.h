@@ -8,9 +8,12 @@
 
 namespace sepx {
 
-void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int N, int D, float eps, cudaStream_t st);
+// add / sum (optional, together): normalise s = x + add and write s to sum.
+void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int N, int D, float eps, cudaStream_t st,
+                 const void* add = nullptr, void* sum = nullptr);
+// dres (optional): the input's gradient from its other uses, added to dx (as a bf16 add).
 void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, void* dx, float* dw, int N, int D,
-                 int num_sms, cudaStream_t st);
+                 int num_sms, cudaStream_t st, const void* dres = nullptr);
 void qk_norm_rope_fwd(const void* qkv, const void* wq, const void* wk, void* q, void* k, void* v, float* rstd_q,
                       float* rstd_k, const int* pos_ids, int T, int Hq, int Hkv, float eps, float theta,
                       cudaStream_t st);

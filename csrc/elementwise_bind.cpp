@@ -26,26 +26,40 @@ void req(const at::Tensor& t, at::ScalarType dt, const char* name) {
 const int* opt_int(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr<int>() : nullptr; }
 const float* opt_f(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr<float>() : nullptr; }
 
-void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, double eps) {
+// add / sum (optional, together): y = rmsnorm(x + add), with x + add written to sum.
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, double eps,
+                 const c10::optional<at::Tensor>& add, const c10::optional<at::Tensor>& sum) {
   req(x, at::kBFloat16, "x");
   req(w, at::kBFloat16, "w");
   req(y, at::kBFloat16, "y");
   req(rstd, at::kFloat, "rstd");
+  TORCH_CHECK(add.has_value() == sum.has_value(), "add and sum go together");
+  if (add.has_value()) {
+    req(*add, at::kBFloat16, "add");
+    req(*sum, at::kBFloat16, "sum");
+    TORCH_CHECK(add->numel() == x.numel() && sum->numel() == x.numel(), "add / sum must match x");
+  }
   const int D = x.size(-1);
   const int N = x.numel() / D;
-  sepx::rmsnorm_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr<float>(), N, D, (float)eps, cs());
+  sepx::rmsnorm_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr<float>(), N, D, (float)eps, cs(),
+                    add.has_value() ? add->data_ptr() : nullptr, sum.has_value() ? sum->data_ptr() : nullptr);
 }
 
+// dres (optional): gradient of x from its other uses, added into dx.
 void rmsnorm_bwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd, const at::Tensor& dy, at::Tensor& dx,
-                 at::Tensor& dw) {
+                 at::Tensor& dw, const c10::optional<at::Tensor>& dres) {
   req(x, at::kBFloat16, "x");
   req(dy, at::kBFloat16, "dy");
   req(dx, at::kBFloat16, "dx");
   req(dw, at::kFloat, "dw");
+  if (dres.has_value()) {
+    req(*dres, at::kBFloat16, "dres");
+    TORCH_CHECK(dres->numel() == x.numel(), "dres must match x");
+  }
   const int D = x.size(-1);
   const int N = x.numel() / D;
   sepx::rmsnorm_bwd(x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(), dx.data_ptr(),
-                    dw.data_ptr<float>(), N, D, num_sms(), cs());
+                    dw.data_ptr<float>(), N, D, num_sms(), cs(), dres.has_value() ? dres->data_ptr() : nullptr);
 }
 
 void qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, at::Tensor& q, at::Tensor& k,

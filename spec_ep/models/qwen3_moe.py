@@ -28,7 +28,7 @@ import torch.nn.functional as F
 from ..ops.attention import causal_gqa_attention
 from ..ops.linear import dense_fwd, linear
 from ..ops.loss import lm_head_xent
-from ..ops.norm import rms_norm
+from ..ops.norm import add_rms_norm, rms_norm, rms_norm_res
 from ..ops.rope import qk_norm_rope
 from ..ops.router import router_topk
 from ..parallel.ep import ExpertParallel, ep_moe
@@ -74,13 +74,14 @@ class Qwen3MoeLayer(nn.Module):
             # fetch runs on a side stream while the attention below executes
             spec.speculate(x, self.post_norm, self.w_router, cfg.top_k, cfg.rms_norm_eps, cfg.norm_topk_prob,
                            self.router_bias, self.router_logit_bias)
-        h = rms_norm(x, self.input_norm, cfg.rms_norm_eps)
+        # the residual adds and the gradient sums of the residual stream ride in the norm
+        # kernels (rms_norm_res, add_rms_norm)
+        h, x = rms_norm_res(x, self.input_norm, cfg.rms_norm_eps)
         qkv = linear(h, self.w_qkv)
         q, k, v = qk_norm_rope(qkv, self.q_norm, self.k_norm, cfg.num_heads, cfg.num_kv_heads, cfg.rms_norm_eps,
                                cfg.rope_theta, pos)
         a = causal_gqa_attention(q, k, v)
-        x = x + linear(a, self.w_o)
-        h = rms_norm(x, self.post_norm, cfg.rms_norm_eps)
+        x, h = add_rms_norm(x, linear(a, self.w_o), self.post_norm, cfg.rms_norm_eps)
         logits = linear(h, self.w_router).float()
         if self.router_logit_bias is not None:
             logits = logits + self.router_logit_bias

@@ -27,6 +27,39 @@ def test_rmsnorm_fwd_bwd(D):
     assert _rel(w.grad, wr.grad) < 2e-2
 
 
+def test_residual_norms_equal_the_unfused_ops():
+    """rms_norm_res / add_rms_norm (the residual add and the residual-gradient sums folded
+    into the norm kernels) give the same bits as writing them as separate tensor ops, in
+    the pre-norm block pattern of the model."""
+    from spec_ep.ops.norm import add_rms_norm, rms_norm, rms_norm_res
+
+    torch.manual_seed(3)
+    T, D = 512, 2048
+    x0 = torch.randn(T, D, device="cuda").bfloat16()
+    w1 = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16()
+    w2 = (1 + 0.1 * torch.randn(D, device="cuda")).bfloat16()
+    proj = (torch.randn(D, D, device="cuda") / D**0.5).bfloat16()
+    g_out = torch.randn(T, D, device="cuda").bfloat16()
+
+    def block(fused):
+        x = x0.clone().requires_grad_()
+        a1 = w1.clone().requires_grad_()
+        a2 = w2.clone().requires_grad_()
+        if fused:
+            h, r = rms_norm_res(x, a1)
+            s, h2 = add_rms_norm(r, h @ proj, a2)
+        else:
+            h = rms_norm(x, a1)
+            s = x + h @ proj
+            h2 = rms_norm(s, a2)
+        out = s + h2 @ proj  # s is used twice downstream of the second norm, as in the model
+        out.backward(g_out)
+        return out.detach(), x.grad, a1.grad, a2.grad
+
+    for got, want in zip(block(True), block(False)):
+        assert torch.equal(got, want)
+
+
 def test_qk_norm_rope_fwd_bwd():
     from spec_ep.ops.rope import qk_norm_rope, qk_norm_rope_reference
 
