@@ -57,69 +57,6 @@ void gg_fwd(const at::Tensor& A, const at::Tensor& W, const at::Tensor& group_of
   sepx::grouped_gemm_ragged_m(c, cur_stream());
 }
 
-// MoE router front in one launch: logits = h [T, H] . w [128, H]^T on the tcgen05 GEMM,
-// whose epilogue applies the softmax / top-k / renormalisation (probs, topk_e, topk_w)
-// and, with e2r / e2l, writes the expert-parallel routing tables (dst, meta).
-void gemm_router(const at::Tensor& h, const at::Tensor& w, const at::Tensor& group_off,
-                 const c10::optional<at::Tensor>& logit_bias, const c10::optional<at::Tensor>& sel_bias, int64_t k,
-                 bool renorm, const c10::optional<at::Tensor>& e2r, const c10::optional<at::Tensor>& e2l,
-                 at::Tensor& probs, at::Tensor& topk_e, at::Tensor& topk_w, const c10::optional<at::Tensor>& dst,
-                 const c10::optional<at::Tensor>& meta, const c10::optional<at::Tensor>& status) {
-  CHECK_BF16(h);
-  CHECK_BF16(w);
-  CHECK_DTYPE(group_off, at::kInt);
-  TORCH_CHECK(w.dim() == 2 && w.size(0) == 128 && w.size(1) == h.size(1), "router weight must be [128, H]");
-  const int64_t T = h.size(0);
-  TORCH_CHECK(probs.is_contiguous() && probs.scalar_type() == at::kFloat && probs.size(0) == T && probs.size(1) == 128,
-              "probs must be fp32 [T, 128]");
-  TORCH_CHECK(topk_e.is_contiguous() && topk_e.scalar_type() == at::kInt && topk_e.numel() == T * k, "topk_e [T, k] int32");
-  TORCH_CHECK(topk_w.is_contiguous() && topk_w.scalar_type() == at::kFloat && topk_w.numel() == T * k, "topk_w [T, k] fp32");
-  TORCH_CHECK(e2r.has_value() == e2l.has_value() && e2r.has_value() == dst.has_value() &&
-                  dst.has_value() == meta.has_value(),
-              "e2r, e2l, dst and meta go together");
-  const c10::cuda::CUDAGuard guard(h.device());
-  sepx::GemmCall c;
-  c.epi = sepx::kEpiRouter;
-  c.A = h.data_ptr();
-  c.a_rows = T;
-  c.lda = h.size(1);
-  c.B = w.data_ptr();
-  c.b_rows = w.size(0);
-  c.ldb = w.size(1);
-  c.b_kmajor = true;
-  c.p.group_off = group_off.data_ptr<int>();
-  c.p.G = 1;
-  c.p.N = 128;
-  c.p.K = h.size(1);
-  c.p.b_rows_per_group = 128;
-  c.p.status = status_ptr(status);
-  sepx::RouterEpi& r = c.p.router;
-  auto fptr = [](const c10::optional<at::Tensor>& t) -> const float* {
-    if (!t.has_value()) return nullptr;
-    TORCH_CHECK(t->is_contiguous() && t->scalar_type() == at::kFloat && t->numel() == 128, "biases must be fp32 [128]");
-    return t->data_ptr<float>();
-  };
-  r.logit_bias = fptr(logit_bias);
-  r.sel_bias = fptr(sel_bias);
-  r.probs = probs.data_ptr<float>();
-  r.topk_e = topk_e.data_ptr<int>();
-  r.topk_w = topk_w.data_ptr<float>();
-  if (e2r.has_value()) {
-    TORCH_CHECK(e2r->scalar_type() == at::kInt && e2l->scalar_type() == at::kInt && e2r->numel() == 128 &&
-                    e2l->numel() == 128, "e2r / e2l must be int32 [128]");
-    TORCH_CHECK(dst->is_contiguous() && meta->is_contiguous() && dst->scalar_type() == at::kInt &&
-                    meta->scalar_type() == at::kInt && dst->numel() == T * k && meta->numel() == T * k,
-                "dst / meta must be int32 [T, k]");
-    r.e2r = e2r->data_ptr<int>();
-    r.e2l = e2l->data_ptr<int>();
-    r.dst = dst->data_ptr<int>();
-    r.meta = meta->data_ptr<int>();
-  }
-  r.k = (int)k;
-  r.renorm = renorm ? 1 : 0;
-  sepx::grouped_gemm_ragged_m(c, cur_stream());
-}
-
 // out[rows, N] = A[rows, K] . W[g] with W stored [G, K, N] (MN-major weights, dgrad).
 void gg_dgrad(const at::Tensor& A, const at::Tensor& W, const at::Tensor& group_off,
               at::Tensor& out, const c10::optional<at::Tensor>& status) {
@@ -320,7 +257,6 @@ void register_kernels(pybind11::module& m);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "spec_ep sm_100a kernels";
   m.def("gg_fwd", &gg_fwd);
-  m.def("gemm_router", &gemm_router);
   m.def("gemm_wgrad_bf16", &gemm_wgrad_bf16);
   m.def("gemm_set_pairs", &sepx::gemm_set_pairs, "256-column GEMM tiles on CTA pairs (returns the previous setting)");
   m.def("gg_dgrad", &gg_dgrad);

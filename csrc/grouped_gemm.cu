@@ -185,79 +185,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
   const uint32_t t_row = t_acc + ((uint32_t)(q * 32) << 16);
   const bool zero = ti.num_kb == 0;
 
-  if constexpr (EPI == kEpiRouter) {
-    // One thread per logit row (E = BN = 128 experts); the second warp of each lane
-    // quarter has nothing to do. Softmax in fp32 over the bf16-rounded logits, top-k by
-    // repeated scans (lowest expert index wins ties), optional renormalisation.
-    static_assert(BN == 128, "the router epilogue takes all 128 experts of a row in one tile");
-    if (half != 0) return;
-    float v[4][32];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) tmem_ld32(t_row + c * 32, v[c]);
-    if (!valid) return;
-    const RouterEpi& R = p.router;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        float l = zero ? 0.f : __bfloat162float(__float2bfloat16(v[c][e]));
-        if (R.logit_bias) l += __ldg(R.logit_bias + c * 32 + e);
-        v[c][e] = l;
-        mx = fmaxf(mx, l);
-      }
-    float s = 0.f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        v[c][e] = __expf(v[c][e] - mx);
-        s += v[c][e];
-      }
-    const float inv = 1.f / s;
-    float4* prow = reinterpret_cast<float4*>(R.probs + (size_t)r * 128);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) v[c][e] *= inv;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) prow[c * 8 + e] = make_float4(v[c][4 * e], v[c][4 * e + 1], v[c][4 * e + 2], v[c][4 * e + 3]);
-    }
-    uint32_t taken[4] = {0u, 0u, 0u, 0u};
-    float sel_sum = 0.f;
-    int* te = R.topk_e + (size_t)r * R.k;
-    float* tw = R.topk_w + (size_t)r * R.k;
-#pragma unroll 1
-    for (int j = 0; j < R.k; ++j) {
-      float best = -INFINITY, bp = 0.f;
-      int bi = 0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float sc = ((taken[c] >> e) & 1u) ? -INFINITY
-                                                  : v[c][e] + (R.sel_bias ? __ldg(R.sel_bias + c * 32 + e) : 0.f);
-          if (sc > best) {
-            best = sc;
-            bi = c * 32 + e;
-            bp = v[c][e];
-          }
-        }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) taken[c] |= (bi >> 5) == c ? 1u << (bi & 31) : 0u;
-      sel_sum += bp;
-      te[j] = bi;
-      tw[j] = bp;
-    }
-    for (int j = 0; j < R.k; ++j) {
-      if (R.renorm) tw[j] = tw[j] / sel_sum;
-      if (R.e2r) {
-        const int e = te[j];
-        R.dst[(size_t)r * R.k + j] = __ldg(R.e2r + e);
-        R.meta[(size_t)r * R.k + j] = __ldg(R.e2l + e);
-      }
-    }
-  } else if (EPI == kEpiBf16) {
+  if (EPI == kEpiBf16) {
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 1
     for (int c = half; c < BN / 32; c += kCStep) {
@@ -1356,14 +1284,6 @@ void grouped_gemm_ragged_m(const GemmCall& c, cudaStream_t stream) {
     }
     max_tiles = (int)((c.a_rows + 127) / 128 + p.G) * p.n_tiles;
     launch<256, 4, false, true, false, kEpiSwigluBwd>(ta, tb, p, max_tiles, stream);
-    return;
-  }
-  if (c.epi == kEpiRouter) {
-    if (p.G != 1 || p.N != 128 || !c.b_kmajor || p.router.k < 1 || p.router.k > 32)
-      throw std::runtime_error("router epilogue: one group, 128 experts, K-major weights, 1 <= top-k <= 32");
-    p.n_tiles = 1;
-    CUtensorMap tb = make_tmap_bf16(c.B, c.b_rows, p.K, c.ldb, 128);
-    launch<128, 6, false, false, false, kEpiRouter>(ta, tb, p, (int)((c.a_rows + 127) / 128 + p.G), stream);
     return;
   }
   if (c.epi != kEpiBf16) throw std::runtime_error("unsupported epilogue for ragged-M GEMM");

@@ -14,24 +14,6 @@ enum : int {
   kEpiF32 = 3,        // D -> fp32 [G, M, ldo] (weight gradients)
   kEpiAdamW = 4,      // D = weight gradient -> AdamW update of W[G, M, N] in place (fp32 state)
   kEpiAdamW8 = 5,     // same, 8-bit state, with the state streamed through a TMA ring
-  kEpiRouter = 6,     // D = router logits [T, 128] -> softmax, top-k, routing tables (RouterEpi)
-};
-
-// kEpiRouter: the MoE router's softmax / top-k / renormalisation (and, with e2r / e2l, the
-// expert-parallel routing tables) applied to each logit row straight from TMEM. Logits are
-// rounded to bf16 first, as a bf16 projection followed by the standalone router would.
-struct RouterEpi {
-  const float* logit_bias = nullptr;  // [E] added to the logits (optional)
-  const float* sel_bias = nullptr;    // [E] added to the probabilities for the selection only (optional)
-  float* probs = nullptr;             // [T, E] softmax, kept for the backward
-  int* topk_e = nullptr;              // [T, k]
-  float* topk_w = nullptr;            // [T, k]
-  const int* e2r = nullptr;           // [E] expert -> rank, and local slot (optional, together)
-  const int* e2l = nullptr;
-  int* dst = nullptr;                 // [T, k] destination rank / local slot per choice (with e2r)
-  int* meta = nullptr;
-  int k = 0;
-  int renorm = 1;
 };
 
 struct GemmParams {
@@ -54,7 +36,6 @@ struct GemmParams {
   int* status = nullptr;
   unsigned long long timeout_ns = 2000000000ull;
   OptHyper opt;  // kEpiAdamW
-  RouterEpi router;  // kEpiRouter
 };
 
 struct GemmCall {

@@ -30,7 +30,7 @@ from ..ops.linear import dense_fwd, linear
 from ..ops.loss import lm_head_xent
 from ..ops.norm import add_rms_norm, rms_norm, rms_norm_res
 from ..ops.rope import qk_norm_rope
-from ..ops.router import router_front, router_front_supported, router_topk
+from ..ops.router import router_topk
 from ..parallel.ep import ExpertParallel, ep_moe
 from .config import MoEModelConfig
 
@@ -82,26 +82,16 @@ class Qwen3MoeLayer(nn.Module):
                                cfg.rope_theta, pos)
         a = causal_gqa_attention(q, k, v)
         x, h = add_rms_norm(x, linear(a, self.w_o), self.post_norm, cfg.rms_norm_eps)
-        tables = None
-        if router_front_supported(self.w_router, h):
-            # projection, softmax / top-k and (without speculation) the routing tables in
-            # one launch
-            out = router_front(h, self.w_router, cfg.top_k, cfg.norm_topk_prob, self.router_bias,
-                               self.router_logit_bias, None if spec is not None else (self.ep.e2r, self.ep.e2l))
-            topk_w, topk_e = out[0], out[1]
-            if spec is None:
-                tables = (out[2], out[3])
-        else:
-            logits = linear(h, self.w_router).float()
-            if self.router_logit_bias is not None:
-                logits = logits + self.router_logit_bias
-            topk_w, topk_e = router_topk(logits, cfg.top_k, cfg.norm_topk_prob, self.router_bias)
+        logits = linear(h, self.w_router).float()
+        if self.router_logit_bias is not None:
+            logits = logits + self.router_logit_bias
+        topk_w, topk_e = router_topk(logits, cfg.top_k, cfg.norm_topk_prob, self.router_bias)
         if self.routing_callback is not None:
             self.routing_callback(topk_e)
         if spec is not None:
             spec.observe(x_in, topk_e)
             return ep_moe(h, topk_e, topk_w, spec.w_gu, spec.w_d, self.ep, None, residual=x, route=spec.tables())
-        return ep_moe(h, topk_e, topk_w, self.w_gu, self.w_d, self.ep, self.grad_sink, residual=x, tables=tables)
+        return ep_moe(h, topk_e, topk_w, self.w_gu, self.w_d, self.ep, self.grad_sink, residual=x)
 
 
 class Qwen3MoeForCausalLM(nn.Module):

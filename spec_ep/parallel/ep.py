@@ -400,10 +400,9 @@ class EPGraph:
 
 class _EPMoE(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, topk_w, w_gu, w_d, topk_e, ep: ExpertParallel, grad_sink, residual, route, tables):
+    def forward(ctx, x, topk_w, w_gu, w_d, topk_e, ep: ExpertParallel, grad_sink, residual, route):
         with stage("ep.dispatch"):
-            if route is not None:
-                tables = ep.route_tables(topk_e, *route)
+            tables = ep.route_tables(topk_e, *route) if route is not None else None
             st = ep.dispatch_fwd(x.contiguous(), topk_e, topk_w, tables=tables)
         with stage("ep.experts"):
             h, gu = gg.gg_swiglu_fwd(st.xp, w_gu, st.group_off, status=ep.status)
@@ -451,18 +450,16 @@ class _EPMoE(torch.autograd.Function):
             dx, dtopk_w = ep.combine_bwd_finish(st)
         ctx.st = None
         dres = dout if ctx.has_residual else None
-        return dx, dtopk_w, g_gu, g_d, None, None, None, dres, None, None
+        return dx, dtopk_w, g_gu, g_d, None, None, None, dres, None
 
 
-def ep_moe(x, topk_e, topk_w, w_gu, w_d, ep: ExpertParallel, grad_sink=None, residual=None, route=None,
-           tables=None):
+def ep_moe(x, topk_e, topk_w, w_gu, w_d, ep: ExpertParallel, grad_sink=None, residual=None, route=None):
     """Expert-parallel SwiGLU MoE: ``out[t] = residual[t] + sum_j w[t,j] * FFN_{e[t,j]}(x[t])``.
 
     ``w_gu [G, 2I, H]`` and ``w_d [G, H, I]`` hold this rank's ``G`` local experts.
     ``grad_sink(param, fp32_grad)``, when given, receives the expert weight gradients
     (e.g. an optimizer applying them immediately) instead of autograd. ``route``
     optionally gives per-call ``(e2r, e2l)`` device tables (speculative replicas)
-    instead of the communicator's placement; ``tables`` the already computed per-choice
-    ``(dst, meta)`` routing tables (e.g. from ``ops.router.router_front``).
+    instead of the communicator's placement.
     """
-    return _EPMoE.apply(x, topk_w, w_gu, w_d, topk_e, ep, grad_sink, residual, route, tables)
+    return _EPMoE.apply(x, topk_w, w_gu, w_d, topk_e, ep, grad_sink, residual, route)

@@ -55,41 +55,3 @@ def test_lm_head_xent_on_own_gemm_matches_reference():
     assert abs(loss.item() - ref.item()) < 2e-2 * abs(ref.item())
     assert _rel(h.grad, hr.grad) < 3e-2
     assert _rel(w.grad, wr.grad) < 3e-2
-
-
-@pytest.mark.parametrize("bias", [False, True])
-def test_router_front_matches_projection_then_router(bias):
-    """One launch (router GEMM whose epilogue does softmax / top-k / renormalisation and the
-    routing tables) against the projection followed by the standalone router kernel and
-    the table lookup: same experts, weights and gradients to fp32 rounding."""
-    from spec_ep.ops.linear import linear
-    from spec_ep.ops.router import router_front, router_topk
-
-    torch.manual_seed(4)
-    T, H, E, k = 1000, 2048, 128, 8
-    h = torch.randn(T, H, device="cuda").bfloat16()
-    w = (torch.randn(E, H, device="cuda") / H**0.5).bfloat16()
-    sel = (0.01 * torch.rand(E, device="cuda")) if bias else None
-    lgb = (0.5 * torch.randn(E, device="cuda")) if bias else None
-    e2r = (torch.arange(E, device="cuda") // 16).int()
-    e2l = (torch.arange(E, device="cuda") % 16).int()
-    g = torch.randn(T, k, device="cuda")
-
-    h1, w1 = h.clone().requires_grad_(), w.clone().requires_grad_()
-    tw1, te1, dst, meta = router_front(h1, w1, k, True, sel, lgb, (e2r, e2l))
-    (tw1 * g).sum().backward()
-
-    h2, w2 = h.clone().requires_grad_(), w.clone().requires_grad_()
-    logits = linear(h2, w2).float()
-    if lgb is not None:
-        logits = logits + lgb
-    tw2, te2 = router_topk(logits, k, True, sel)
-    (tw2 * g).sum().backward()
-    torch.cuda.synchronize()
-
-    same = (te1 == te2).all(1)
-    assert same.float().mean().item() > 0.995  # near-ties may order differently
-    assert torch.equal(dst[same], e2r[te1[same].long()]) and torch.equal(meta[same], e2l[te1[same].long()])
-    assert (tw1[same] - tw2[same]).abs().max().item() < 1e-5
-    assert _rel(h1.grad[same], h2.grad[same]) < 2e-2 and _rel(w1.grad, w2.grad) < 2e-2
-
