@@ -286,13 +286,12 @@ class SpeculativeExperts:
 
 def predict_topk(x_prev, post_norm, w_router, top_k, eps, renorm=True, bias=None, logit_bias=None):
     """Predicted expert ids [T, k]: the layer's router on RMSNorm(x_prev; post_norm)."""
-    import torch.nn.functional as F
-
+    from ..ops.linear import dense_fwd
     from ..ops.norm import rms_norm
     from ..ops.router import router_topk
 
     h = rms_norm(x_prev, post_norm, eps)
-    logits = F.linear(h, w_router).float()
+    logits = dense_fwd(h, w_router).float()  # the tcgen05 GEMM, on the caller's (side) stream
     if logit_bias is not None:
         logits = logits + logit_bias
     _, e = router_topk(logits, top_k, renorm, bias)
